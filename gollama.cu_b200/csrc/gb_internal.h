@@ -1,0 +1,209 @@
+// gb_internal.h -- host-side internals shared by the library's translation
+// units: error reporting, kernel launch entry points, GGUF reader/writer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/gollama_b200.h"
+#include "gb_formats.h"
+
+// ---- errors: each entry point returns a status and leaves a message in
+// the calling thread's slot, worded like the reference's wrapped Go errors.
+int gb_fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int gb_cuda_fail(cudaError_t e, const char *what);
+void gb_clear_error();
+
+#define GB_CUDA(call, what)                              \
+  do {                                                   \
+    cudaError_t e_ = (call);                             \
+    if (e_ != cudaSuccess) return gb_cuda_fail(e_, what); \
+  } while (0)
+
+// ---- the limb pack of a device vector (see gb_device.cuh)
+struct GbXPackBuf {
+  int n = 0;
+  int8_t *a = nullptr, *b = nullptr, *c = nullptr;
+  float *s = nullptr, *sum16 = nullptr, *ssq = nullptr;
+};
+int gb_xpack_alloc(GbXPackBuf *p, int n);
+void gb_xpack_free(GbXPackBuf *p);
+
+// ---- tiled GEMV (gb_gemv.cu)
+enum GbEpi {
+  GB_EPI_PLAIN = 0,   // y[r] = W x
+  GB_EPI_QKV = 1,     // RoPE q,k; q -> qbuf, k,v -> KV cache at *pos
+  GB_EPI_RESID = 2,   // x[r] += y; pack x*wnorm (+ssq) for the next layer
+  GB_EPI_SWIGLU = 3,  // gate/up tile pairs -> act = silu(g)*u, packed
+  GB_EPI_LOGITS = 4,  // logits[r] = y; argmax candidates; last CTA -> token
+};
+
+struct GbGemvPlan {
+  int warps = 8;    // warps per CTA
+  int rb = 1;       // row tiles per CTA
+  int ks = 1;       // K splits across CTAs
+  int stages = 3;   // sb-blocks in flight per warp
+};
+
+struct GbEpiArgs {
+  // QKV
+  float *q_out = nullptr;
+  void *kcache = nullptr, *vcache = nullptr;  // head-major caches
+  int q_rows = 0, kv_rows = 0, head_dim = 0, max_len = 0, kv_f16 = 1;
+  const double *rope_cs = nullptr;  // [max_len][head_dim/2][2] (cos, sin)
+  const int32_t *pos = nullptr;
+  // RESID
+  float *x = nullptr;
+  const float *wnorm = nullptr;
+  GbXPackBuf out_pack;
+  // LOGITS / PLAIN
+  float *y = nullptr;
+  unsigned long long *best = nullptr;     // running argmax key (zero between launches)
+  unsigned long long *key_out = nullptr;  // tensor parallel: final local key
+  unsigned *counter = nullptr;            // finished row-blocks (zero between launches)
+  int32_t *token_out = nullptr;   // argmax result (device)
+  int32_t *token_hist = nullptr;  // optional history slot base ([max_len]); indexed by *pos
+  int row_offset = 0;             // global index of local row 0 (vocab shard)
+  int vocab_total = 0;
+  unsigned *err = nullptr;
+  // K-split scratch
+  float *part = nullptr;          // [ntiles][ks][32]
+  unsigned *tile_counter = nullptr;
+};
+
+struct GbGemvArgs {
+  const uint8_t *w = nullptr;  // tiled weights
+  int type_a = GB_T_Q4_K, type_b = GB_T_Q4_K;
+  int split_tile = 1 << 30;    // tiles >= split_tile use type_b
+  int rows = 0, ntiles = 0, nsb = 0;
+  GbXPackBuf in;               // input pack
+  const float *in_ssq = nullptr;  // non-null: the input is RMS-normalised (ssq partials)
+  float eps = 1e-5f;
+  int epi = GB_EPI_PLAIN;
+  GbEpiArgs e;
+};
+
+int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &p, cudaStream_t st, bool pdl);
+GbGemvPlan gb_gemv_plan(int ntiles, int nsb, int epi, int sms);
+size_t gb_tiled_bytes(int typ, int rows, int cols);
+int gb_repack_launch(int typ, const uint8_t *raw, int rows, int cols, uint8_t *tiled,
+                     cudaStream_t st);
+int gb_pack_launch(const float *x, int n, const GbXPackBuf &p, cudaStream_t st);
+int gb_gemv_scratch_floats(int ntiles, const GbGemvPlan &p);
+
+// ---- attention (gb_attn.cu)
+struct GbAttnArgs {
+  const float *q = nullptr;
+  const void *k = nullptr, *v = nullptr;
+  int kv_f16 = 0;
+  // element strides (in elements of the cache type)
+  long long k_sh = 0, k_sd = 0, k_st = 0;  // head, 16-byte dim chunk, position
+  long long v_sh = 0, v_st = 0;            // head, position (dims contiguous)
+  int n_heads = 0, n_kv = 0, head_dim = 0;
+  float scale = 1.f;
+  int kv_len = 0;                // used when kv_len_pos is null
+  const int32_t *kv_len_pos = nullptr;  // kv_len = *kv_len_pos + 1
+  int max_len = 0;
+  int splits = 1;
+  float *out = nullptr;          // [n_heads*head_dim]
+  GbXPackBuf out_pack;           // optional pack of out (model path)
+  float *part = nullptr;         // [n_kv][splits][group*(head_dim+2)]
+  unsigned *counter = nullptr;   // [n_kv], zero between launches
+  unsigned *err = nullptr;
+};
+int gb_attn_launch(const GbAttnArgs &a, cudaStream_t st, bool pdl);
+int gb_attn_splits(int n_kv, int max_len, int sms);
+size_t gb_attn_part_floats(int n_kv, int splits, int group, int head_dim);
+
+// ---- misc kernels (gb_ops.cu)
+int gb_embed_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
+                    int vocab, float *x, const float *wnorm, const GbXPackBuf &pk,
+                    unsigned *err, cudaStream_t st, bool pdl);
+int gb_resid_pack_launch(float *x, const float *y, const float *wnorm, int n,
+                         const GbXPackBuf &pk, cudaStream_t st, bool pdl);
+// Reduce n per-rank argmax keys (tensor-parallel lm_head) to the token.
+int gb_argmax_keys_launch(const unsigned long long *keys, int n, int32_t *token, int32_t *hist,
+                          const int32_t *pos, int max_len, cudaStream_t st);
+int gb_advance_pos_launch(int32_t *pos, cudaStream_t st);
+
+// ---- GGUF (gb_gguf.cpp): reader restating gguf/gguf.go:62 Parse and
+// writer restating gguf/writer.go.
+struct GbTensor {
+  std::string name;
+  std::vector<uint64_t> dims;  // ggml order, innermost first
+  int type = 0;
+  uint64_t offset = 0;
+  const uint8_t *data = nullptr;
+  uint64_t bytes = 0;
+  int rows() const { return dims.size() >= 2 ? (int)dims[1] : 1; }
+  int cols() const { return dims.empty() ? 0 : (int)dims[0]; }
+  uint64_t numel() const {
+    uint64_t n = 1;
+    for (auto d : dims) n *= d;
+    return n;
+  }
+};
+
+struct GbValue {
+  int type = 0;  // gguf value type
+  uint64_t u = 0;
+  double f = 0;
+  std::string s;
+  int elem = 0;
+  std::vector<GbValue> arr;
+  // gguf/gguf.go:223 IsInt: the eight integer value types.
+  bool is_int() const { return (type >= 0 && type <= 5) || type == 10 || type == 11; }
+};
+
+struct GbGguf {
+  uint32_t version = 0, alignment = 32;
+  std::vector<std::pair<std::string, GbValue>> kv;
+  std::vector<GbTensor> tensors;
+  const uint8_t *data = nullptr;
+  size_t len = 0;
+  uint64_t data_offset = 0;
+  // mmap bookkeeping (Open)
+  void *map = nullptr;
+  size_t map_len = 0;
+  ~GbGguf();
+  const GbValue *get(const std::string &k) const;
+  uint64_t get_uint(const std::string &k, uint64_t def) const;
+  double get_float(const std::string &k, double def) const;
+  std::string get_string(const std::string &k, const std::string &def) const;
+  const GbTensor *tensor(const std::string &name) const;
+};
+// Parse a GGUF image (not copied). Returns nullptr and sets the error.
+GbGguf *gb_gguf_parse(const uint8_t *data, size_t len);
+GbGguf *gb_gguf_open(const char *path);
+
+struct GbGgufWriter {
+  std::vector<std::pair<std::string, GbValue>> kv;
+  struct T {
+    std::string name;
+    std::vector<uint64_t> dims;
+    int type = 0;
+    uint64_t bytes = 0;
+    std::vector<uint8_t> data;  // may stay empty until the image is filled
+  };
+  std::vector<T> tensors;
+  uint32_t alignment = 32;
+  void set_u32(const std::string &k, uint32_t v);
+  void set_f32(const std::string &k, float v);
+  void set_str(const std::string &k, const std::string &v);
+  int add_tensor(const std::string &name, const std::vector<int> &shape, int type,
+                 std::vector<uint8_t> &&data);
+  // Header bytes (padded to the alignment), per-tensor data offsets and the
+  // total image size; tensor bytes go at header.size() + offsets[i].
+  std::vector<uint8_t> layout(std::vector<uint64_t> *offsets, uint64_t *total) const;
+  std::vector<uint8_t> write() const;
+};
+
+// ---- synthetic data (gb_synth.cpp)
+uint64_t gb_splitmix64(uint64_t *state);
+uint64_t gb_stream_seed(uint64_t seed, uint64_t tensor, uint64_t block);
+int gb_host_threads();

@@ -1,0 +1,1041 @@
+// gb_model.cu -- the decode-step runtime: model.Load / (*Model).Forward /
+// Close (model/model.go:160-392) on B200, plus model.Linear (model/model.go:67-126).
+//
+// Load reads the GGUF (mmap'd file or a memory image), checks the config
+// like model.ConfigFrom (model/model.go:35), uploads each quantized matrix
+// and repacks it on the device into the 32-row tiled layout (gb_formats.h),
+// uploads float32 norms, and allocates head-major KV caches. Tensor
+// parallelism (tp_world > 1): q/k/v and gate/up rows are split by heads /
+// FFN rows, o and down by input columns, the lm_head by vocabulary rows;
+// the two row-split projections of each layer are summed with an NCCL
+// all-reduce and the greedy token is the maximum of the per-rank argmax
+// keys (one 8-byte all-gather).
+//
+// One decode step is 5 launches per layer plus 3 (embedding, lm_head with
+// the argmax, position advance), each a persistent kernel launched with
+// programmatic dependent launch so the next kernel's weight copies start
+// while the previous one finishes; the whole step is captured once into a
+// CUDA graph whose kernels read the token and position from device memory.
+#include <dlfcn.h>
+#include <math.h>
+#include <nccl.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <memory>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "gb_internal.h"
+
+// ---- NCCL through dlopen: the library loads without NCCL on one GPU, and
+// reuses the libnccl.so.2 a host process (e.g. torch) already mapped.
+namespace {
+struct NcclApi {
+  void *h = nullptr;
+  ncclResult_t (*getUniqueId)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*commInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*allReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*allGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  const char *(*getErrorString)(ncclResult_t) = nullptr;
+};
+NcclApi *nccl() {
+  static NcclApi api;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    api.h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (api.h) {
+      api.getUniqueId = (decltype(api.getUniqueId))dlsym(api.h, "ncclGetUniqueId");
+      api.commInitRank = (decltype(api.commInitRank))dlsym(api.h, "ncclCommInitRank");
+      api.allReduce = (decltype(api.allReduce))dlsym(api.h, "ncclAllReduce");
+      api.allGather = (decltype(api.allGather))dlsym(api.h, "ncclAllGather");
+      api.commDestroy = (decltype(api.commDestroy))dlsym(api.h, "ncclCommDestroy");
+      api.getErrorString = (decltype(api.getErrorString))dlsym(api.h, "ncclGetErrorString");
+    }
+  }
+  return api.h && api.commInitRank && api.allReduce && api.allGather ? &api : nullptr;
+}
+#define GB_NCCL(call, what)                                                                  \
+  do {                                                                                       \
+    ncclResult_t r_ = (call);                                                                \
+    if (r_ != ncclSuccess)                                                                   \
+      return gb_fail(GB_ERR_NCCL, "%s: %s", what,                                            \
+                     nccl()->getErrorString ? nccl()->getErrorString(r_) : "nccl error");    \
+  } while (0)
+
+float host_half(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000) << 16, exp = (h >> 10) & 0x1f, mant = h & 0x3ff, b;
+  if (exp == 0) {
+    if (mant == 0) {
+      b = sign;
+    } else {
+      uint32_t e = 127 - 15 + 1;
+      while (!(mant & 0x400)) { mant <<= 1; e--; }
+      b = sign | e << 23 | (mant & 0x3ff) << 13;
+    }
+  } else if (exp == 0x1f) {
+    b = sign | 0x7f800000 | mant << 13;
+  } else {
+    b = sign | (exp + 127 - 15) << 23 | mant << 13;
+  }
+  float f;
+  memcpy(&f, &b, 4);
+  return f;
+}
+
+uint16_t host_f16(float x) {
+  uint32_t b;
+  memcpy(&b, &x, 4);
+  uint16_t sign = (uint16_t)(b >> 16) & 0x8000;
+  int32_t exp = (int32_t)((b >> 23) & 0xff) - 127;
+  uint32_t mant = b & 0x7fffff;
+  if (exp == 128) return mant ? (uint16_t)(sign | 0x7e00) : (uint16_t)(sign | 0x7c00);
+  if (exp > 15) return (uint16_t)(sign | 0x7c00);
+  if (exp >= -14) {
+    uint32_t m = mant >> 13, rem = mant & 0x1fff;
+    if (rem > 0x1000 || (rem == 0x1000 && (m & 1))) m++;
+    return (uint16_t)((uint16_t)(sign | (uint16_t)((uint32_t)(exp + 15) << 10)) + (uint16_t)m);
+  }
+  if (exp >= -25) {
+    uint32_t full = mant | 0x800000, shift = (uint32_t)(-exp - 1);
+    uint32_t m = full >> shift, rem = full & ((1u << shift) - 1), half = 1u << (shift - 1);
+    if (rem > half || (rem == half && (m & 1))) m++;
+    return (uint16_t)(sign | (uint16_t)m);
+  }
+  return sign;
+}
+
+const char *tname(int t) {
+  switch (t) {
+    case GB_T_F32: return "F32";
+    case GB_T_F16: return "F16";
+    case GB_T_Q4_0: return "Q4_0";
+    case GB_T_Q8_0: return "Q8_0";
+    case GB_T_Q4_K: return "Q4_K";
+    case GB_T_Q6_K: return "Q6_K";
+    case GB_T_BF16: return "BF16";
+  }
+  return "?";
+}
+
+// A tiled matrix on the device (possibly several row segments concatenated).
+struct Tiled {
+  uint8_t *w = nullptr;
+  int type_a = 0, type_b = 0, split_tile = 1 << 30;
+  int rows = 0, cols = 0, ntiles = 0, nsb = 0;
+  size_t bytes = 0;
+  bool owned = true;
+};
+
+enum { K_QKV = 0, K_ATTN, K_O, K_GU, K_DOWN, K_HEAD, K_OTHER, K_CLASSES };
+
+}  // namespace
+
+struct gb_linear {
+  int device = 0;
+  Tiled t;
+  GbXPackBuf pack;
+  float *part = nullptr;
+  unsigned *tile_counter = nullptr;
+};
+
+struct gb_model {
+  gb_config c{};
+  gb_model_opts o{};
+  int q_local = 0, kv_local = 0, ffn_local = 0, vocab_local = 0, vocab_off = 0;
+  int embd_type = 0, embd_nsb = 0;
+  struct Layer {
+    float *attn_norm = nullptr, *ffn_norm = nullptr;
+    Tiled qkv, wo, gu, down;
+    void *kc = nullptr, *vc = nullptr;
+  };
+  std::vector<Layer> layers;
+  Tiled embd, head;
+  float *out_norm = nullptr;
+  double *rope_cs = nullptr;
+  // work
+  float *x = nullptr, *q = nullptr, *attn = nullptr, *logits = nullptr, *logits_full = nullptr,
+        *ypart = nullptr;
+  GbXPackBuf pack_dim, pack_q, pack_ffn;
+  int32_t *token = nullptr, *pos = nullptr, *gen = nullptr;
+  unsigned *err = nullptr;
+  float *gemv_part = nullptr;
+  unsigned *tile_counter = nullptr;
+  float *attn_part = nullptr;
+  unsigned *attn_counter = nullptr;
+  unsigned long long *best = nullptr, *key_local = nullptr, *keys = nullptr;
+  unsigned *done = nullptr;
+  int attn_splits = 1;
+  GbGemvPlan plan_plain, plan_gu;
+  cudaStream_t st = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  ncclComm_t comm = nullptr;
+  int32_t *h_stage = nullptr;  // pinned: token, pos, next, err
+  float *h_logits = nullptr;   // pinned vocab floats
+  std::vector<void *> allocs;
+  int launches = 0;
+  int sms = 148;
+};
+
+namespace {
+
+template <class T>
+int dalloc(gb_model *m, T **p, size_t n, const char *what) {
+  void *q = nullptr;
+  GB_CUDA(cudaMalloc(&q, n * sizeof(T) > 0 ? n * sizeof(T) : 16), what);
+  GB_CUDA(cudaMemset(q, 0, n * sizeof(T) > 0 ? n * sizeof(T) : 16), what);
+  m->allocs.push_back(q);
+  *p = (T *)q;
+  return GB_OK;
+}
+
+// Host decode of a norm-like tensor (model/model.go:186 norm(): quant.Dequantize).
+int host_vector(const GbTensor *t, int n, std::vector<float> &out, const char *name) {
+  if (!t) return gb_fail(GB_ERR_IO, "model: no tensor %s", name);
+  if ((int)t->numel() != n)
+    return gb_fail(GB_ERR_INVALID, "model: %s has %llu elements, want %d", name,
+                   (unsigned long long)t->numel(), n);
+  out.resize((size_t)n);
+  switch (t->type) {
+    case GB_T_F32: memcpy(out.data(), t->data, sizeof(float) * (size_t)n); break;
+    case GB_T_F16:
+      for (int i = 0; i < n; i++) out[i] = host_half((uint16_t)(t->data[2 * i] | t->data[2 * i + 1] << 8));
+      break;
+    case GB_T_BF16:
+      for (int i = 0; i < n; i++) {
+        uint32_t b = (uint32_t)(t->data[2 * i] | t->data[2 * i + 1] << 8) << 16;
+        memcpy(&out[i], &b, 4);
+      }
+      break;
+    default: return gb_fail(GB_ERR_UNSUPPORTED, "model: %s: %s norms not supported", name, tname(t->type));
+  }
+  return GB_OK;
+}
+
+int upload_vec(gb_model *m, const std::vector<float> &v, float **dst, const char *what) {
+  int rc = dalloc(m, dst, v.size(), what);
+  if (rc) return rc;
+  GB_CUDA(cudaMemcpy(*dst, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice), what);
+  return GB_OK;
+}
+
+// Upload rows [r0, r0+nr) and column super-blocks [c0, c0+nc) (in elements,
+// multiples of 256) of a raw matrix into tiles [tile0, ...) of dst.
+int upload_tiles(const GbTensor *t, int r0, int nr, int c0, int nc, uint8_t *dst_base,
+                 int dst_tile0, int dst_tile_mul, cudaStream_t st, uint8_t *staging,
+                 size_t staging_bytes) {
+  const int typ = t->type;
+  const size_t rb = (size_t)gb_row_bytes(typ, t->cols());
+  const size_t sub_rb = (size_t)gb_row_bytes(typ, nc), coff = (size_t)gb_row_bytes(typ, c0);
+  const size_t need = sub_rb * (size_t)nr;
+  if (need > staging_bytes) return gb_fail(GB_ERR_INVALID, "model: staging buffer too small");
+  std::vector<uint8_t> host(need);
+  for (int r = 0; r < nr; r++) memcpy(host.data() + (size_t)r * sub_rb, t->data + (size_t)(r0 + r) * rb + coff, sub_rb);
+  GB_CUDA(cudaMemcpyAsync(staging, host.data(), need, cudaMemcpyHostToDevice, st), "model: upload");
+  const int nsb = nc / 256, ntiles = (nr + 31) / 32;
+  const size_t sbb = (size_t)gb_tiled_sb_bytes(typ);
+  if (dst_tile_mul == 1) {
+    int rc = gb_repack_launch(typ, staging, nr, nc, dst_base + (size_t)dst_tile0 * nsb * sbb, st);
+    if (rc) return rc;
+  } else {
+    // interleaved destination (gate/up pairs): repack into a scratch region
+    // after the raw bytes, then place each tile
+    uint8_t *tmp = staging + ((need + 255) / 256) * 256;
+    size_t tb = (size_t)ntiles * nsb * sbb;
+    if (((need + 255) / 256) * 256 + tb > staging_bytes)
+      return gb_fail(GB_ERR_INVALID, "model: staging buffer too small");
+    int rc = gb_repack_launch(typ, staging, nr, nc, tmp, st);
+    if (rc) return rc;
+    for (int i = 0; i < ntiles; i++)
+      GB_CUDA(cudaMemcpyAsync(dst_base + (size_t)(dst_tile0 + i * dst_tile_mul) * nsb * sbb,
+                              tmp + (size_t)i * nsb * sbb, (size_t)nsb * sbb, cudaMemcpyDeviceToDevice, st),
+              "model: place tiles");
+  }
+  GB_CUDA(cudaStreamSynchronize(st), "model: upload");
+  return GB_OK;
+}
+
+int check_matrix(const GbGguf *f, const std::string &name, int rows, int cols, const GbTensor **out) {
+  const GbTensor *t = f->tensor(name);
+  if (!t) return gb_fail(GB_ERR_IO, "model: no tensor %s", name.c_str());
+  if (t->dims.size() != 2) return gb_fail(GB_ERR_INVALID, "model: %s: not a matrix", name.c_str());
+  if (t->rows() != rows || t->cols() != cols)
+    return gb_fail(GB_ERR_INVALID, "model: %s is [%d][%d], want [%d][%d]", name.c_str(), t->rows(),
+                   t->cols(), rows, cols);
+  if (!gb_tiled_type(t->type))
+    return gb_fail(GB_ERR_UNSUPPORTED, "model: %s: no kernel for %s weights", name.c_str(), tname(t->type));
+  if (cols % 256)
+    return gb_fail(GB_ERR_UNSUPPORTED, "model: %s: %d columns is not a multiple of 256", name.c_str(), cols);
+  *out = t;
+  return GB_OK;
+}
+
+int alloc_tiled(gb_model *m, Tiled *T, int ta, int tb, int split_tile, int ntiles, int nsb, int rows, int cols) {
+  T->type_a = ta;
+  T->type_b = tb;
+  T->split_tile = split_tile;
+  T->ntiles = ntiles;
+  T->nsb = nsb;
+  T->rows = rows;
+  T->cols = cols;
+  size_t na = (size_t)(split_tile < ntiles ? split_tile : ntiles) * nsb * gb_tiled_sb_bytes(ta);
+  size_t nb = split_tile < ntiles ? (size_t)(ntiles - split_tile) * nsb * gb_tiled_sb_bytes(tb) : 0;
+  T->bytes = na + nb;
+  return dalloc(m, &T->w, T->bytes, "model: weights");
+}
+
+// ---- the decode step --------------------------------------------------------
+
+struct Hook {
+  cudaEvent_t ev[1024];
+  int cls[1024];
+  int n = 0;
+};
+
+GbGemvArgs gemv_args(const Tiled &t, const GbXPackBuf &in, const float *in_ssq, float eps, int epi,
+                     gb_model *m) {
+  GbGemvArgs a;
+  a.w = t.w;
+  a.type_a = t.type_a;
+  a.type_b = t.type_b;
+  a.split_tile = t.split_tile;
+  a.rows = t.rows;
+  a.ntiles = t.ntiles;
+  a.nsb = t.nsb;
+  a.in = in;
+  a.in_ssq = in_ssq;
+  a.eps = eps;
+  a.epi = epi;
+  a.e.err = m->err;
+  a.e.part = m->gemv_part;
+  a.e.tile_counter = m->tile_counter;
+  a.e.pos = m->pos;
+  a.e.max_len = m->c.max_len;
+  return a;
+}
+
+int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
+  const gb_config &c = m->c;
+  const bool pdl = true;
+  const bool tp = c.tp_world > 1;
+  int n = 0;
+  auto mark = [&](int cls) -> int {
+    n++;
+    if (hook && hook->n < 1024) {
+      hook->cls[hook->n] = cls;
+      GB_CUDA(cudaEventRecord(hook->ev[hook->n], st), "model: profile event");
+      hook->n++;
+    }
+    return GB_OK;
+  };
+  int rc;
+  if (hook) {
+    hook->cls[hook->n] = -1;
+    GB_CUDA(cudaEventRecord(hook->ev[hook->n++], st), "model: profile event");
+  }
+  rc = gb_embed_launch(m->embd_type, m->embd.w, m->embd_nsb, c.dim, m->token, c.vocab, m->x,
+                       m->layers[0].attn_norm, m->pack_dim, m->err, st, pdl);
+  if (rc || (rc = mark(K_OTHER))) return rc;
+  for (int l = 0; l < c.layers; l++) {
+    gb_model::Layer &L = m->layers[l];
+    const float *next_norm = l + 1 < c.layers ? m->layers[l + 1].attn_norm : m->out_norm;
+    // q, k, v with RoPE and the KV-cache store fused in the epilogue
+    GbGemvArgs a = gemv_args(L.qkv, m->pack_dim, m->pack_dim.ssq, c.eps, GB_EPI_QKV, m);
+    a.e.q_out = m->q;
+    a.e.kcache = L.kc;
+    a.e.vcache = L.vc;
+    a.e.q_rows = m->q_local;
+    a.e.kv_rows = m->kv_local;
+    a.e.head_dim = c.head_dim;
+    a.e.kv_f16 = c.kv_f16;
+    a.e.rope_cs = m->rope_cs;
+    if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_QKV))) return rc;
+    // attention over the cache, output packed for the o projection
+    GbAttnArgs at;
+    at.q = m->q;
+    at.k = L.kc;
+    at.v = L.vc;
+    at.kv_f16 = c.kv_f16;
+    const int V = c.kv_f16 ? 8 : 4;
+    at.k_sh = (long long)c.head_dim * c.max_len;
+    at.k_sd = (long long)c.max_len * V;
+    at.k_st = V;
+    at.v_sh = (long long)c.max_len * c.head_dim;
+    at.v_st = c.head_dim;
+    at.n_heads = m->q_local / c.head_dim;
+    at.n_kv = m->kv_local / c.head_dim;
+    at.head_dim = c.head_dim;
+    at.scale = (float)(1 / sqrt((double)c.head_dim));  // model/model.go:322
+    at.kv_len_pos = m->pos;
+    at.max_len = c.max_len;
+    at.splits = m->attn_splits;
+    at.out = m->attn;
+    at.out_pack = m->pack_q;
+    at.part = m->attn_part;
+    at.counter = m->attn_counter;
+    at.err = m->err;
+    if ((rc = gb_attn_launch(at, st, pdl)) || (rc = mark(K_ATTN))) return rc;
+    // o projection + residual (+ pack for the FFN norm)
+    if (!tp) {
+      a = gemv_args(L.wo, m->pack_q, nullptr, c.eps, GB_EPI_RESID, m);
+      a.e.x = m->x;
+      a.e.wnorm = L.ffn_norm;
+      a.e.out_pack = m->pack_dim;
+      if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_O))) return rc;
+    } else {
+      a = gemv_args(L.wo, m->pack_q, nullptr, c.eps, GB_EPI_PLAIN, m);
+      a.e.y = m->ypart;
+      if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_O))) return rc;
+      GB_NCCL(nccl()->allReduce(m->ypart, m->ypart, (size_t)c.dim, ncclFloat, ncclSum, m->comm, st),
+              "model: all-reduce");
+      if ((rc = gb_resid_pack_launch(m->x, m->ypart, L.ffn_norm, c.dim, m->pack_dim, st, false)) ||
+          (rc = mark(K_OTHER)))
+        return rc;
+    }
+    // gate/up + SwiGLU
+    a = gemv_args(L.gu, m->pack_dim, m->pack_dim.ssq, c.eps, GB_EPI_SWIGLU, m);
+    a.e.out_pack = m->pack_ffn;
+    if ((rc = gb_gemv_launch(a, m->plan_gu, st, pdl)) || (rc = mark(K_GU))) return rc;
+    // down + residual (+ pack for the next layer's norm)
+    if (!tp) {
+      a = gemv_args(L.down, m->pack_ffn, nullptr, c.eps, GB_EPI_RESID, m);
+      a.e.x = m->x;
+      a.e.wnorm = next_norm;
+      a.e.out_pack = m->pack_dim;
+      if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_DOWN))) return rc;
+    } else {
+      a = gemv_args(L.down, m->pack_ffn, nullptr, c.eps, GB_EPI_PLAIN, m);
+      a.e.y = m->ypart;
+      if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_DOWN))) return rc;
+      GB_NCCL(nccl()->allReduce(m->ypart, m->ypart, (size_t)c.dim, ncclFloat, ncclSum, m->comm, st),
+              "model: all-reduce");
+      if ((rc = gb_resid_pack_launch(m->x, m->ypart, next_norm, c.dim, m->pack_dim, st, false)) ||
+          (rc = mark(K_OTHER)))
+        return rc;
+    }
+  }
+  // lm_head + argmax (model.Argmax on the device)
+  GbGemvArgs a = gemv_args(m->head, m->pack_dim, m->pack_dim.ssq, c.eps, GB_EPI_LOGITS, m);
+  a.e.y = m->logits;
+  a.e.best = m->best;
+  a.e.counter = m->done;
+  a.e.row_offset = m->vocab_off;
+  a.e.vocab_total = c.vocab;
+  if (!tp) {
+    a.e.token_out = m->token;
+    a.e.token_hist = m->gen;
+  } else {
+    a.e.key_out = m->key_local;
+  }
+  if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_HEAD))) return rc;
+  if (tp) {
+    GB_NCCL(nccl()->allGather(m->key_local, m->keys, 1, ncclUint64, m->comm, st), "model: all-gather");
+    if ((rc = gb_argmax_keys_launch(m->keys, c.tp_world, m->token, m->gen, m->pos, c.max_len, st)) ||
+        (rc = mark(K_OTHER)))
+      return rc;
+  }
+  if ((rc = gb_advance_pos_launch(m->pos, st)) || (rc = mark(K_OTHER))) return rc;
+  m->launches = n;
+  return GB_OK;
+}
+
+int capture(gb_model *m) {
+  cudaGraph_t g = nullptr;
+  GB_CUDA(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal), "model: graph capture");
+  int rc = enqueue_step(m, m->st, nullptr);
+  cudaError_t e = cudaStreamEndCapture(m->st, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return gb_cuda_fail(e, "model: graph capture");
+  e = cudaGraphInstantiate(&m->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return gb_cuda_fail(e, "model: graph instantiate");
+  return GB_OK;
+}
+
+int run_step(gb_model *m) {
+  if (m->graph) {
+    GB_CUDA(cudaGraphLaunch(m->graph, m->st), "model: graph launch");
+    return GB_OK;
+  }
+  return enqueue_step(m, m->st, nullptr);
+}
+
+int check_err(gb_model *m) {
+  GB_CUDA(cudaMemcpyAsync(m->h_stage + 3, m->err, sizeof(unsigned), cudaMemcpyDeviceToHost, m->st),
+          "model: status");
+  GB_CUDA(cudaStreamSynchronize(m->st), "model: forward");
+  unsigned e = (unsigned)m->h_stage[3];
+  if (e) {
+    GB_CUDA(cudaMemsetAsync(m->err, 0, sizeof(unsigned), m->st), "model: status");
+    GB_CUDA(cudaStreamSynchronize(m->st), "model: status");
+    if (e & GB_DEVERR_TIMEOUT) return gb_fail(GB_ERR_TIMEOUT, "model: a bounded device wait timed out");
+    if (e & GB_DEVERR_POS) return gb_fail(GB_ERR_DEVICE, "model: position outside the KV cache");
+    return gb_fail(GB_ERR_DEVICE, "model: token outside the vocabulary");
+  }
+  return GB_OK;
+}
+
+int set_token_pos(gb_model *m, int32_t token, int pos) {
+  // model/model.go:315-320
+  if (pos < 0 || pos >= m->c.max_len)
+    return gb_fail(GB_ERR_INVALID, "model: position %d outside the %d-token cache", pos, m->c.max_len);
+  if (token < 0 || token >= m->c.vocab)
+    return gb_fail(GB_ERR_INVALID, "model: token %d outside the vocabulary", token);
+  m->h_stage[0] = token;
+  m->h_stage[1] = pos;
+  GB_CUDA(cudaMemcpyAsync(m->token, m->h_stage, sizeof(int32_t), cudaMemcpyHostToDevice, m->st), "model: token");
+  GB_CUDA(cudaMemcpyAsync(m->pos, m->h_stage + 1, sizeof(int32_t), cudaMemcpyHostToDevice, m->st), "model: position");
+  return GB_OK;
+}
+
+void free_model(gb_model *m) {
+  if (!m) return;
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  if (m->comm && nccl() && nccl()->commDestroy) nccl()->commDestroy(m->comm);
+  for (void *p : m->allocs) cudaFree(p);
+  gb_xpack_free(&m->pack_dim);
+  gb_xpack_free(&m->pack_q);
+  gb_xpack_free(&m->pack_ffn);
+  if (m->h_stage) cudaFreeHost(m->h_stage);
+  if (m->h_logits) cudaFreeHost(m->h_logits);
+  if (m->st) cudaStreamDestroy(m->st);
+  delete m;
+}
+
+int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
+  gb_model_opts o;
+  gb_model_opts_default(&o);
+  if (opts) o = *opts;
+  // model/model.go:35 ConfigFrom
+  std::string arch = f->get_string("general.architecture", "");
+  if (arch != "llama") return gb_fail(GB_ERR_INVALID, "model: architecture \"%s\" is not llama", arch.c_str());
+  gb_config c{};
+  c.layers = (int)f->get_uint("llama.block_count", 0);
+  c.dim = (int)f->get_uint("llama.embedding_length", 0);
+  c.ffn = (int)f->get_uint("llama.feed_forward_length", 0);
+  c.heads = (int)f->get_uint("llama.attention.head_count", 0);
+  c.ctx_len = (int)f->get_uint("llama.context_length", 2048);
+  c.rope_base = (float)f->get_float("llama.rope.freq_base", 10000);
+  c.eps = (float)f->get_float("llama.attention.layer_norm_rms_epsilon", 1e-5);
+  c.kv_heads = (int)f->get_uint("llama.attention.head_count_kv", (uint64_t)c.heads);
+  if (c.layers == 0 || c.dim == 0 || c.ffn == 0 || c.heads == 0)
+    return gb_fail(GB_ERR_INVALID, "model: incomplete llama metadata");
+  c.head_dim = (int)f->get_uint("llama.attention.key_length", (uint64_t)(c.dim / c.heads));
+  if (c.kv_heads == 0 || c.heads % c.kv_heads != 0)
+    return gb_fail(GB_ERR_INVALID, "model: %d heads is not a multiple of %d KV heads", c.heads, c.kv_heads);
+  const GbTensor *embd = f->tensor("token_embd.weight");
+  if (!embd) return gb_fail(GB_ERR_IO, "model: no token_embd.weight");
+  if (embd->dims.size() != 2 || embd->cols() != c.dim)
+    return gb_fail(GB_ERR_INVALID, "model: token_embd.weight is not [vocab][%d]", c.dim);
+  c.vocab = embd->rows();
+  // model/model.go:165: maxLen <= 0 or beyond the trained context -> context length
+  c.max_len = (o.max_len <= 0 || o.max_len > c.ctx_len) ? c.ctx_len : o.max_len;
+  c.kv_f16 = o.kv_f16 ? 1 : 0;
+  c.tp_rank = o.tp_rank;
+  c.tp_world = o.tp_world < 1 ? 1 : o.tp_world;
+  const int N = c.tp_world, R = c.tp_rank;
+  if (R < 0 || R >= N) return gb_fail(GB_ERR_INVALID, "model: rank %d outside world %d", R, N);
+  if (c.head_dim != 64 && c.head_dim != 128)
+    return gb_fail(GB_ERR_UNSUPPORTED, "model: head_dim %d (64 or 128 supported)", c.head_dim);
+  if (c.heads % N || c.kv_heads % N || c.ffn % (256 * N) || (c.heads / N * c.head_dim) % 256 ||
+      c.vocab % N || c.dim % 256)
+    return gb_fail(GB_ERR_UNSUPPORTED, "model: shape does not split over %d GPUs", N);
+  if (N > 1 && !nccl()) return gb_fail(GB_ERR_NCCL, "model: libnccl.so.2 not found");
+
+  gb_model *m = new gb_model();
+  m->c = c;
+  m->o = o;
+  int rc = GB_OK;
+  auto fail = [&](int r) {
+    free_model(m);
+    return r;
+  };
+  if (cudaSetDevice(o.device) != cudaSuccess) return fail(gb_fail(GB_ERR_CUDA, "model: no device %d", o.device));
+  cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, o.device);
+  if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess)
+    return fail(gb_fail(GB_ERR_CUDA, "model: stream"));
+  const int hd = c.head_dim, kv_dim = c.kv_heads * hd;
+  m->q_local = c.heads / N * hd;
+  m->kv_local = c.kv_heads / N * hd;
+  m->ffn_local = c.ffn / N;
+  m->vocab_local = c.vocab / N;
+  m->vocab_off = R * m->vocab_local;
+  (void)kv_dim;
+
+  // staging for uploads: the largest raw shard plus its tiled copy
+  size_t staging_bytes = 0;
+  for (auto &t : f->tensors) staging_bytes = std::max<size_t>(staging_bytes, (size_t)t.bytes);
+  staging_bytes = staging_bytes * 2 + (1 << 20);
+  uint8_t *staging = nullptr;
+  if ((rc = dalloc(m, &staging, staging_bytes, "model: staging"))) return fail(rc);
+
+  // token embedding (full, for the lookup) -- tiled
+  if (!gb_tiled_type(embd->type))
+    return fail(gb_fail(GB_ERR_UNSUPPORTED, "model: token_embd.weight: no kernel for %s", tname(embd->type)));
+  m->embd_type = embd->type;
+  m->embd_nsb = c.dim / 256;
+  {
+    int nt = (c.vocab + 31) / 32;
+    if ((rc = alloc_tiled(m, &m->embd, embd->type, embd->type, 1 << 30, nt, c.dim / 256, c.vocab, c.dim)))
+      return fail(rc);
+    // upload in row chunks to bound the staging size
+    int chunk = (int)std::max<size_t>(32, (staging_bytes / 2 / (size_t)gb_row_bytes(embd->type, c.dim)) / 32 * 32);
+    for (int r0 = 0; r0 < c.vocab; r0 += chunk) {
+      int nr = std::min(chunk, c.vocab - r0);
+      if ((rc = upload_tiles(embd, r0, nr, 0, c.dim, m->embd.w, r0 / 32, 1, m->st, staging, staging_bytes)))
+        return fail(rc);
+    }
+  }
+
+  m->layers.resize((size_t)c.layers);
+  std::vector<float> hv;
+  for (int l = 0; l < c.layers; l++) {
+    gb_model::Layer &L = m->layers[(size_t)l];
+    std::string p = "blk." + std::to_string(l) + ".";
+    if ((rc = host_vector(f->tensor(p + "attn_norm.weight"), c.dim, hv, (p + "attn_norm.weight").c_str())) ||
+        (rc = upload_vec(m, hv, &L.attn_norm, "model: norm")))
+      return fail(rc);
+    if ((rc = host_vector(f->tensor(p + "ffn_norm.weight"), c.dim, hv, (p + "ffn_norm.weight").c_str())) ||
+        (rc = upload_vec(m, hv, &L.ffn_norm, "model: norm")))
+      return fail(rc);
+    const GbTensor *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    if ((rc = check_matrix(f, p + "attn_q.weight", c.heads * hd, c.dim, &wq)) ||
+        (rc = check_matrix(f, p + "attn_k.weight", c.kv_heads * hd, c.dim, &wk)) ||
+        (rc = check_matrix(f, p + "attn_v.weight", c.kv_heads * hd, c.dim, &wv)) ||
+        (rc = check_matrix(f, p + "attn_output.weight", c.dim, c.heads * hd, &wo)) ||
+        (rc = check_matrix(f, p + "ffn_gate.weight", c.ffn, c.dim, &wg)) ||
+        (rc = check_matrix(f, p + "ffn_up.weight", c.ffn, c.dim, &wu)) ||
+        (rc = check_matrix(f, p + "ffn_down.weight", c.dim, c.ffn, &wd)))
+      return fail(rc);
+    if (wq->type != wk->type)
+      return fail(gb_fail(GB_ERR_UNSUPPORTED, "model: %sattn_q and attn_k types differ", p.c_str()));
+    if (wg->type != wu->type)
+      return fail(gb_fail(GB_ERR_UNSUPPORTED, "model: %sffn_gate and ffn_up types differ", p.c_str()));
+    // q | k | v rows of this rank, one tiled buffer (q,k type_a; v type_b)
+    const int tq = m->q_local / 32, tk = m->kv_local / 32, tv = m->kv_local / 32;
+    if ((rc = alloc_tiled(m, &L.qkv, wq->type, wv->type, wv->type == wq->type ? (1 << 30) : tq + tk,
+                          tq + tk + tv, c.dim / 256, m->q_local + 2 * m->kv_local, c.dim)))
+      return fail(rc);
+    const size_t sba = (size_t)gb_tiled_sb_bytes(wq->type) * (c.dim / 256);
+    if ((rc = upload_tiles(wq, R * m->q_local, m->q_local, 0, c.dim, L.qkv.w, 0, 1, m->st, staging, staging_bytes)) ||
+        (rc = upload_tiles(wk, R * m->kv_local, m->kv_local, 0, c.dim, L.qkv.w, tq, 1, m->st, staging, staging_bytes)) ||
+        (rc = upload_tiles(wv, R * m->kv_local, m->kv_local, 0, c.dim, L.qkv.w + (size_t)(tq + tk) * sba, 0, 1,
+                           m->st, staging, staging_bytes)))
+      return fail(rc);
+    // o: all dim rows, this rank's input columns
+    if ((rc = alloc_tiled(m, &L.wo, wo->type, wo->type, 1 << 30, c.dim / 32, m->q_local / 256, c.dim, m->q_local)) ||
+        (rc = upload_tiles(wo, 0, c.dim, R * m->q_local, m->q_local, L.wo.w, 0, 1, m->st, staging, staging_bytes)))
+      return fail(rc);
+    // gate/up: this rank's FFN rows, tiles interleaved gate0 up0 gate1 up1 ...
+    const int tf = m->ffn_local / 32;
+    if ((rc = alloc_tiled(m, &L.gu, wg->type, wg->type, 1 << 30, 2 * tf, c.dim / 256, 2 * m->ffn_local, c.dim)) ||
+        (rc = upload_tiles(wg, R * m->ffn_local, m->ffn_local, 0, c.dim, L.gu.w, 0, 2, m->st, staging, staging_bytes)) ||
+        (rc = upload_tiles(wu, R * m->ffn_local, m->ffn_local, 0, c.dim, L.gu.w, 1, 2, m->st, staging, staging_bytes)))
+      return fail(rc);
+    // down: all dim rows, this rank's FFN columns
+    if ((rc = alloc_tiled(m, &L.down, wd->type, wd->type, 1 << 30, c.dim / 32, m->ffn_local / 256, c.dim, m->ffn_local)) ||
+        (rc = upload_tiles(wd, 0, c.dim, R * m->ffn_local, m->ffn_local, L.down.w, 0, 1, m->st, staging, staging_bytes)))
+      return fail(rc);
+    // KV caches, head-major (see gb_attn.cu)
+    const size_t elems = (size_t)(m->kv_local) * c.max_len;
+    const size_t esz = c.kv_f16 ? 2 : 4;
+    uint8_t *kc = nullptr, *vc = nullptr;
+    if ((rc = dalloc(m, &kc, elems * esz, "model: KV cache")) || (rc = dalloc(m, &vc, elems * esz, "model: KV cache")))
+      return fail(rc);
+    L.kc = kc;
+    L.vc = vc;
+  }
+  if ((rc = host_vector(f->tensor("output_norm.weight"), c.dim, hv, "output_norm.weight")) ||
+      (rc = upload_vec(m, hv, &m->out_norm, "model: norm")))
+    return fail(rc);
+  // lm_head: output.weight, or tied to token_embd (model/model.go:263-267)
+  const GbTensor *head = f->tensor("output.weight");
+  if (head) {
+    const GbTensor *h2;
+    if ((rc = check_matrix(f, "output.weight", c.vocab, c.dim, &h2))) return fail(rc);
+    if ((rc = alloc_tiled(m, &m->head, head->type, head->type, 1 << 30, (m->vocab_local + 31) / 32, c.dim / 256,
+                          m->vocab_local, c.dim)))
+      return fail(rc);
+    int chunk = (int)std::max<size_t>(32, (staging_bytes / 2 / (size_t)gb_row_bytes(head->type, c.dim)) / 32 * 32);
+    for (int r0 = 0; r0 < m->vocab_local; r0 += chunk) {
+      int nr = std::min(chunk, m->vocab_local - r0);
+      if ((rc = upload_tiles(head, m->vocab_off + r0, nr, 0, c.dim, m->head.w, r0 / 32, 1, m->st, staging,
+                             staging_bytes)))
+        return fail(rc);
+    }
+  } else {
+    if (m->vocab_off % 32 || (N > 1 && m->vocab_local % 32))
+      return fail(gb_fail(GB_ERR_UNSUPPORTED, "model: tied head shard is not tile aligned"));
+    m->head = m->embd;
+    m->head.owned = false;
+    m->head.w = m->embd.w + (size_t)(m->vocab_off / 32) * m->embd.nsb * gb_tiled_sb_bytes(m->embd.type_a);
+    m->head.rows = m->vocab_local;
+    m->head.ntiles = (m->vocab_local + 31) / 32;
+  }
+  // RoPE angles (cpu.RoPE, backend/cpu/cpu.go:69) in float64 on the host
+  {
+    std::vector<float> freq((size_t)hd / 2, 1.f);
+    bool has_freq = false;
+    if (const GbTensor *ft = f->tensor("rope_freqs.weight")) {
+      if ((rc = host_vector(ft, hd / 2, freq, "rope_freqs.weight"))) return fail(rc);
+      has_freq = true;
+    }
+    std::vector<double> cs((size_t)c.max_len * (hd / 2) * 2);
+    for (int p = 0; p < c.max_len; p++)
+      for (int j = 0; j < hd / 2; j++) {
+        double theta = (double)p * pow((double)c.rope_base, -2 * (double)j / (double)hd);
+        if (has_freq) theta /= (double)freq[(size_t)j];
+        cs[((size_t)p * (hd / 2) + j) * 2] = cos(theta);
+        cs[((size_t)p * (hd / 2) + j) * 2 + 1] = sin(theta);
+      }
+    if ((rc = dalloc(m, &m->rope_cs, cs.size(), "model: rope table"))) return fail(rc);
+    if (cudaMemcpy(m->rope_cs, cs.data(), cs.size() * sizeof(double), cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(gb_fail(GB_ERR_CUDA, "model: rope table upload"));
+  }
+  // work buffers
+  if ((rc = dalloc(m, &m->x, (size_t)c.dim, "model: work")) || (rc = dalloc(m, &m->q, (size_t)m->q_local, "model: work")) ||
+      (rc = dalloc(m, &m->attn, (size_t)m->q_local, "model: work")) ||
+      (rc = dalloc(m, &m->logits, (size_t)m->vocab_local, "model: work")) ||
+      (rc = dalloc(m, &m->logits_full, (size_t)c.vocab, "model: work")) ||
+      (rc = dalloc(m, &m->ypart, (size_t)c.dim, "model: work")) ||
+      (rc = dalloc(m, &m->token, 4, "model: work")) || (rc = dalloc(m, &m->pos, 4, "model: work")) ||
+      (rc = dalloc(m, &m->gen, (size_t)c.max_len, "model: work")) || (rc = dalloc(m, &m->err, 4, "model: work")) ||
+      (rc = dalloc(m, &m->best, 1, "model: work")) || (rc = dalloc(m, &m->key_local, 1, "model: work")) ||
+      (rc = dalloc(m, &m->keys, (size_t)N, "model: work")) || (rc = dalloc(m, &m->done, 1, "model: work")))
+    return fail(rc);
+  if ((rc = gb_xpack_alloc(&m->pack_dim, c.dim)) || (rc = gb_xpack_alloc(&m->pack_q, m->q_local)) ||
+      (rc = gb_xpack_alloc(&m->pack_ffn, m->ffn_local)))
+    return fail(rc);
+  m->plan_plain = gb_gemv_plan(0, 0, GB_EPI_PLAIN, m->sms);
+  m->plan_gu = gb_gemv_plan(0, 0, GB_EPI_SWIGLU, m->sms);
+  int max_tiles = std::max(std::max(m->head.ntiles, (m->q_local + 2 * m->kv_local) / 32),
+                           std::max(c.dim / 32, 2 * m->ffn_local / 32));
+  if ((rc = dalloc(m, &m->gemv_part, (size_t)gb_gemv_scratch_floats(0, m->plan_plain) * 2, "model: scratch")) ||
+      (rc = dalloc(m, &m->tile_counter, (size_t)max_tiles + 64, "model: scratch")))
+    return fail(rc);
+  m->attn_splits = gb_attn_splits(m->kv_local / hd, c.max_len, m->sms);
+  if ((rc = dalloc(m, &m->attn_part,
+                   gb_attn_part_floats(m->kv_local / hd, m->attn_splits, c.heads / c.kv_heads, hd), "model: scratch")) ||
+      (rc = dalloc(m, &m->attn_counter, (size_t)(m->kv_local / hd), "model: scratch")))
+    return fail(rc);
+  if (cudaMallocHost(&m->h_stage, 64) != cudaSuccess || cudaMallocHost(&m->h_logits, sizeof(float) * (size_t)c.vocab) != cudaSuccess)
+    return fail(gb_fail(GB_ERR_CUDA, "model: pinned host buffers"));
+  // the staging buffer is no longer needed
+  cudaFree(staging);
+  m->allocs.erase(std::find(m->allocs.begin(), m->allocs.end(), (void *)staging));
+  if (N > 1) {
+    if (!o.nccl_id) return fail(gb_fail(GB_ERR_INVALID, "model: tp_world %d needs an NCCL id", N));
+    ncclUniqueId id;
+    memcpy(&id, o.nccl_id, sizeof id);
+    ncclResult_t r = nccl()->commInitRank(&m->comm, N, id, R);
+    if (r != ncclSuccess) return fail(gb_fail(GB_ERR_NCCL, "model: NCCL init: %s", nccl()->getErrorString(r)));
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) return fail(gb_fail(GB_ERR_CUDA, "model: load"));
+  // embedding, 5 per layer (+2 per layer for the collectives' residual
+  // kernels under tensor parallelism), lm_head, (+key reduce), advance
+  m->launches = 1 + c.layers * (5 + (N > 1 ? 2 : 0)) + 1 + (N > 1 ? 1 : 0) + 1;
+  if (o.use_graph && (rc = capture(m))) return fail(rc);
+  *out = m;
+  return GB_OK;
+}
+
+}  // namespace
+
+// ---- C ABI: model -------------------------------------------------------------
+extern "C" {
+
+void gb_model_opts_default(gb_model_opts *o) {
+  memset(o, 0, sizeof *o);
+  o->device = 0;
+  o->max_len = 0;
+  o->kv_f16 = 1;
+  o->use_graph = 1;
+  o->tp_rank = 0;
+  o->tp_world = 1;
+}
+
+int gb_model_load(const char *path, const gb_model_opts *opts, gb_model **out) {
+  gb_clear_error();
+  if (!path || !out) return gb_fail(GB_ERR_INVALID, "model: null argument");
+  std::unique_ptr<GbGguf> f(gb_gguf_open(path));
+  if (!f) return GB_ERR_IO;
+  return load_model(f.get(), opts, out);
+}
+
+int gb_model_load_mem(const void *gguf, size_t len, const gb_model_opts *opts, gb_model **out) {
+  gb_clear_error();
+  if (!gguf || !out) return gb_fail(GB_ERR_INVALID, "model: null argument");
+  std::unique_ptr<GbGguf> f(gb_gguf_parse((const uint8_t *)gguf, len));
+  if (!f) return GB_ERR_IO;
+  return load_model(f.get(), opts, out);
+}
+
+int gb_model_config(const gb_model *m, gb_config *c) {
+  gb_clear_error();
+  if (!m || !c) return gb_fail(GB_ERR_INVALID, "model: null argument");
+  *c = m->c;
+  return GB_OK;
+}
+
+int gb_model_forward(gb_model *m, int32_t token, int pos, float *host_logits) {
+  gb_clear_error();
+  if (!m) return gb_fail(GB_ERR_INVALID, "model: null model");
+  int rc = set_token_pos(m, token, pos);
+  if (rc || (rc = run_step(m))) return rc;
+  const float *src = m->logits;
+  if (m->c.tp_world > 1) {
+    GB_NCCL(nccl()->allGather(m->logits, m->logits_full, (size_t)m->vocab_local, ncclFloat, m->comm, m->st),
+            "model: logits all-gather");
+    src = m->logits_full;
+  }
+  if (host_logits)
+    GB_CUDA(cudaMemcpyAsync(m->h_logits, src, sizeof(float) * (size_t)m->c.vocab, cudaMemcpyDeviceToHost, m->st),
+            "model: logits");
+  if ((rc = check_err(m))) return rc;
+  if (host_logits) memcpy(host_logits, m->h_logits, sizeof(float) * (size_t)m->c.vocab);
+  return GB_OK;
+}
+
+int gb_model_next(gb_model *m, int32_t token, int pos, int32_t *next) {
+  gb_clear_error();
+  if (!m || !next) return gb_fail(GB_ERR_INVALID, "model: null argument");
+  int rc = set_token_pos(m, token, pos);
+  if (rc || (rc = run_step(m))) return rc;
+  GB_CUDA(cudaMemcpyAsync(m->h_stage + 2, m->token, sizeof(int32_t), cudaMemcpyDeviceToHost, m->st), "model: token");
+  if ((rc = check_err(m))) return rc;
+  *next = m->h_stage[2];
+  return GB_OK;
+}
+
+int gb_model_generate(gb_model *m, int32_t token, int pos, int n, int32_t *out_tokens) {
+  gb_clear_error();
+  if (!m || n < 0 || (n > 0 && !out_tokens)) return gb_fail(GB_ERR_INVALID, "model: bad generate arguments");
+  if (pos + n > m->c.max_len)
+    return gb_fail(GB_ERR_INVALID, "model: %d steps from position %d exceed the %d-token cache", n, pos, m->c.max_len);
+  int rc = set_token_pos(m, token, pos);
+  if (rc) return rc;
+  for (int i = 0; i < n; i++)
+    if ((rc = run_step(m))) return rc;
+  if (n > 0)
+    GB_CUDA(cudaMemcpyAsync(out_tokens, m->gen + pos, sizeof(int32_t) * (size_t)n, cudaMemcpyDeviceToHost, m->st),
+            "model: tokens");
+  return check_err(m);
+}
+
+int gb_model_fill_kv_normal(gb_model *m, uint64_t seed, int n_pos) {
+  gb_clear_error();
+  if (!m || n_pos < 0 || n_pos > m->c.max_len) return gb_fail(GB_ERR_INVALID, "model: bad KV fill");
+  const gb_config &c = m->c;
+  const int hd = c.head_dim, kv_dim = c.kv_heads * hd, kvl = m->kv_local, h0 = c.tp_rank * kvl;
+  const size_t esz = c.kv_f16 ? 2 : 4, elems = (size_t)kvl * c.max_len;
+  std::vector<float> k((size_t)n_pos * kv_dim), v((size_t)n_pos * kv_dim);
+  std::vector<uint8_t> kd(elems * esz, 0), vd(elems * esz, 0);
+  const int V = c.kv_f16 ? 8 : 4;
+  for (int l = 0; l < c.layers; l++) {
+    int rc = gb_synth_kv_normal(seed, l, 0, n_pos, kv_dim, c.kv_f16, k.data(), v.data());
+    if (rc) return rc;
+    for (int t = 0; t < n_pos; t++)
+      for (int j = 0; j < kvl; j++) {
+        int h = j / hd, d = j % hd;
+        float kx = k[(size_t)t * kv_dim + h0 + j], vx = v[(size_t)t * kv_dim + h0 + j];
+        size_t ki = (((size_t)h * (hd / V) + d / V) * c.max_len + t) * V + d % V;
+        size_t vi = ((size_t)h * c.max_len + t) * hd + d;
+        if (c.kv_f16) {
+          ((uint16_t *)kd.data())[ki] = host_f16(kx);
+          ((uint16_t *)vd.data())[vi] = host_f16(vx);
+        } else {
+          ((float *)kd.data())[ki] = kx;
+          ((float *)vd.data())[vi] = vx;
+        }
+      }
+    GB_CUDA(cudaMemcpy(m->layers[(size_t)l].kc, kd.data(), kd.size(), cudaMemcpyHostToDevice), "model: KV fill");
+    GB_CUDA(cudaMemcpy(m->layers[(size_t)l].vc, vd.data(), vd.size(), cudaMemcpyHostToDevice), "model: KV fill");
+  }
+  return GB_OK;
+}
+
+int gb_model_read_kv(gb_model *m, int layer, int pos0, int n, float *k_out, float *v_out) {
+  gb_clear_error();
+  if (!m || layer < 0 || layer >= m->c.layers || pos0 < 0 || n < 0 || pos0 + n > m->c.max_len)
+    return gb_fail(GB_ERR_INVALID, "model: bad KV read");
+  const gb_config &c = m->c;
+  const int hd = c.head_dim, kvl = m->kv_local, V = c.kv_f16 ? 8 : 4;
+  const size_t esz = c.kv_f16 ? 2 : 4, elems = (size_t)kvl * c.max_len;
+  std::vector<uint8_t> kd(elems * esz), vd(elems * esz);
+  GB_CUDA(cudaStreamSynchronize(m->st), "model: KV read");
+  GB_CUDA(cudaMemcpy(kd.data(), m->layers[(size_t)layer].kc, kd.size(), cudaMemcpyDeviceToHost), "model: KV read");
+  GB_CUDA(cudaMemcpy(vd.data(), m->layers[(size_t)layer].vc, vd.size(), cudaMemcpyDeviceToHost), "model: KV read");
+  for (int t = 0; t < n; t++)
+    for (int j = 0; j < kvl; j++) {
+      int h = j / hd, d = j % hd, p = pos0 + t;
+      size_t ki = (((size_t)h * (hd / V) + d / V) * c.max_len + p) * V + d % V;
+      size_t vi = ((size_t)h * c.max_len + p) * hd + d;
+      k_out[(size_t)t * kvl + j] = c.kv_f16 ? host_half(((uint16_t *)kd.data())[ki]) : ((float *)kd.data())[ki];
+      v_out[(size_t)t * kvl + j] = c.kv_f16 ? host_half(((uint16_t *)vd.data())[vi]) : ((float *)vd.data())[vi];
+    }
+  return GB_OK;
+}
+
+void *gb_model_stream(gb_model *m) { return m ? (void *)m->st : nullptr; }
+
+int gb_model_profile_step(gb_model *m, int32_t token, int pos, float *ms_out, int *launches) {
+  gb_clear_error();
+  if (!m || !ms_out) return gb_fail(GB_ERR_INVALID, "model: null argument");
+  std::unique_ptr<Hook> h(new Hook());
+  for (int i = 0; i < 1024; i++) GB_CUDA(cudaEventCreate(&h->ev[i]), "model: profile events");
+  int rc = set_token_pos(m, token, pos);
+  if (!rc) rc = enqueue_step(m, m->st, h.get());
+  if (!rc) rc = check_err(m);
+  for (int c = 0; c < K_CLASSES; c++) {
+    ms_out[c] = 0.f;
+    if (launches) launches[c] = 0;
+  }
+  if (!rc) {
+    for (int i = 1; i < h->n; i++) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, h->ev[i - 1], h->ev[i]);
+      int c = h->cls[i];
+      if (c >= 0 && c < K_CLASSES) {
+        ms_out[c] += ms;
+        if (launches) launches[c]++;
+      }
+    }
+  }
+  for (int i = 0; i < 1024; i++) cudaEventDestroy(h->ev[i]);
+  return rc;
+}
+
+int gb_model_step_bytes(const gb_model *m, int kv_len, double *bytes_per_token, double *gateup_bytes) {
+  gb_clear_error();
+  if (!m) return gb_fail(GB_ERR_INVALID, "model: null model");
+  const gb_config &c = m->c;
+  double w = 0;
+  for (auto &L : m->layers) w += (double)L.qkv.bytes + L.wo.bytes + L.gu.bytes + L.down.bytes;
+  // tiled bytes include row padding only when rows are not multiples of 32
+  w += (double)gb_row_bytes(m->head.type_a, c.dim) * m->vocab_local;
+  double norms = 4.0 * c.dim * (2.0 * c.layers + 1);
+  double esz = c.kv_f16 ? 2.0 : 4.0;
+  double kv = (double)c.layers * (double)kv_len * 2.0 * m->kv_local * esz + (double)c.layers * 2.0 * m->kv_local * esz;
+  double emb = (double)gb_row_bytes(m->embd_type, c.dim);
+  if (bytes_per_token) *bytes_per_token = w + norms + kv + emb;
+  if (gateup_bytes) *gateup_bytes = m->layers.empty() ? 0 : (double)m->layers[0].gu.bytes;
+  return GB_OK;
+}
+
+int gb_model_launches_per_step(const gb_model *m) { return m ? m->launches : 0; }
+
+int gb_model_close(gb_model *m) {
+  gb_clear_error();
+  if (m) {
+    cudaStreamSynchronize(m->st);
+    free_model(m);
+  }
+  return GB_OK;
+}
+
+int gb_tp_unique_id(uint8_t out[128]) {
+  gb_clear_error();
+  if (!nccl() || !nccl()->getUniqueId) return gb_fail(GB_ERR_NCCL, "tp: libnccl.so.2 not found");
+  ncclUniqueId id;
+  GB_NCCL(nccl()->getUniqueId(&id), "tp: unique id");
+  memcpy(out, &id, 128);
+  return GB_OK;
+}
+
+// ---- model.Linear ------------------------------------------------------------
+
+int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes, int rows, int cols,
+                     gb_linear **out) {
+  gb_clear_error();
+  if (!out || !host_bytes || rows <= 0 || cols <= 0) return gb_fail(GB_ERR_INVALID, "model: linear: bad arguments");
+  if (!gb_tiled_type(typ)) return gb_fail(GB_ERR_UNSUPPORTED, "model: linear: no kernel for %s weights", tname(typ));
+  if (cols % 256) return gb_fail(GB_ERR_UNSUPPORTED, "model: linear: %d columns is not a multiple of 256", cols);
+  if (nbytes != (size_t)gb_row_bytes(typ, cols) * rows)
+    return gb_fail(GB_ERR_INVALID, "model: linear: %zu bytes, want %lld", nbytes, (long long)gb_row_bytes(typ, cols) * rows);
+  GB_CUDA(cudaSetDevice(device), "model: linear");
+  gb_linear *l = new gb_linear();
+  l->device = device;
+  Tiled &t = l->t;
+  t.type_a = t.type_b = typ;
+  t.rows = rows;
+  t.cols = cols;
+  t.ntiles = (rows + 31) / 32;
+  t.nsb = cols / 256;
+  t.bytes = gb_tiled_bytes(typ, rows, cols);
+  uint8_t *raw = nullptr;
+  cudaError_t e = cudaMalloc(&t.w, t.bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&raw, nbytes);
+  if (e == cudaSuccess) e = cudaMemcpy(raw, host_bytes, nbytes, cudaMemcpyHostToDevice);
+  int rc = e == cudaSuccess ? gb_repack_launch(typ, raw, rows, cols, t.w, 0) : gb_cuda_fail(e, "model: linear upload");
+  if (!rc) {
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) rc = gb_cuda_fail(e, "model: linear repack");
+  }
+  if (raw) cudaFree(raw);
+  if (!rc) rc = gb_xpack_alloc(&l->pack, cols);
+  GbGemvPlan plan = gb_gemv_plan(t.ntiles, t.nsb, GB_EPI_PLAIN, 148);
+  if (!rc && cudaMalloc(&l->part, sizeof(float) * (size_t)gb_gemv_scratch_floats(t.ntiles, plan) * 2) != cudaSuccess)
+    rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
+  if (!rc && cudaMalloc(&l->tile_counter, sizeof(unsigned) * (size_t)(t.ntiles + 64)) != cudaSuccess)
+    rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
+  if (!rc && cudaMemset(l->tile_counter, 0, sizeof(unsigned) * (size_t)(t.ntiles + 64)) != cudaSuccess)
+    rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
+  if (rc) {
+    gb_linear_free(l);
+    return rc;
+  }
+  *out = l;
+  return GB_OK;
+}
+
+int gb_linear_matvec(gb_linear *l, void *stream, const float *x, float *y) {
+  gb_clear_error();
+  if (!l) return gb_fail(GB_ERR_INVALID, "model: linear: null handle");
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = gb_pack_launch(x, l->t.cols, l->pack, st);
+  if (rc) return rc;
+  GbGemvArgs a;
+  a.w = l->t.w;
+  a.type_a = a.type_b = l->t.type_a;
+  a.rows = l->t.rows;
+  a.ntiles = l->t.ntiles;
+  a.nsb = l->t.nsb;
+  a.in = l->pack;
+  a.epi = GB_EPI_PLAIN;
+  a.e.y = y;
+  a.e.part = l->part;
+  a.e.tile_counter = l->tile_counter;
+  return gb_gemv_launch(a, gb_gemv_plan(l->t.ntiles, l->t.nsb, GB_EPI_PLAIN, 148), st, false);
+}
+
+int gb_linear_info(const gb_linear *l, int *typ, int *rows, int *cols, size_t *weight_bytes) {
+  gb_clear_error();
+  if (!l) return gb_fail(GB_ERR_INVALID, "model: linear: null handle");
+  if (typ) *typ = l->t.type_a;
+  if (rows) *rows = l->t.rows;
+  if (cols) *cols = l->t.cols;
+  if (weight_bytes) *weight_bytes = (size_t)gb_row_bytes(l->t.type_a, l->t.cols) * l->t.rows;
+  return GB_OK;
+}
+
+int gb_linear_free(gb_linear *l) {
+  gb_clear_error();
+  if (!l) return GB_OK;
+  if (l->t.w) cudaFree(l->t.w);
+  gb_xpack_free(&l->pack);
+  if (l->part) cudaFree(l->part);
+  if (l->tile_counter) cudaFree(l->tile_counter);
+  delete l;
+  return GB_OK;
+}
+
+}  // extern "C"

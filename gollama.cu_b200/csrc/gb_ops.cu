@@ -1,0 +1,628 @@
+// gb_ops.cu -- the per-kernel launch API of backend/gpu (backend/gpu/gpu.go:35-167)
+// as sm_100a kernels behind a C ABI, plus the small kernels of the decode
+// step (embedding lookup, residual+pack, argmax) and the library's error slot.
+//
+// Per-op kernels keep the reference's argument meaning (same buffers, same
+// row/column conventions, in-place use allowed where the reference allows it)
+// and follow backend/cpu/cpu.go's arithmetic where it is cheap to do so
+// (float64 reductions for RMSNorm/Softmax, float64 exp/pow/sincos), so they
+// meet the reference's tolerances with margin.
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <string>
+
+#include "gb_device.cuh"
+#include "gb_internal.h"
+
+// ---- error slot -----------------------------------------------------------
+static thread_local std::string g_err;
+
+int gb_fail(int code, const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+int gb_cuda_fail(cudaError_t e, const char *what) {
+  return gb_fail(GB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+void gb_clear_error() { g_err.clear(); }
+
+namespace {
+
+// ---- per-op kernels ----------------------------------------------------------
+
+// kernels.RMSNorm (kernels/rows.go:7), with cpu.RMSNorm's float64 sum.
+__global__ void rmsnorm_kernel(const float *x, const float *w, float *out, int n, float eps) {
+  const float *xr = x + (size_t)blockIdx.x * n;
+  float *o = out + (size_t)blockIdx.x * n;
+  __shared__ double red[32];
+  double ss = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) ss += (double)xr[i] * (double)xr[i];
+  for (int k = 16; k > 0; k >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, k);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += red[i];
+    red[0] = t;
+  }
+  __syncthreads();
+  float inv = (float)(1.0 / sqrt(red[0] / (double)n + (double)eps));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+}
+
+// kernels.Softmax (kernels/rows.go:23), with cpu.Softmax's float64 exp and sum.
+__global__ void softmax_kernel(const float *x, float *out, int n) {
+  const float *xr = x + (size_t)blockIdx.x * n;
+  float *o = out + (size_t)blockIdx.x * n;
+  __shared__ float fred[32];
+  __shared__ double dred[32];
+  __shared__ int nan_seen;
+  if (threadIdx.x == 0) nan_seen = 0;
+  __syncthreads();
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = xr[i];
+    if (isnan(v)) nan_seen = 1;  // Go's max propagates NaN
+    m = fmaxf(m, v);
+  }
+  m = gb_warp_max(m);
+  if ((threadIdx.x & 31) == 0) fred[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = -INFINITY;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) t = fmaxf(t, fred[i]);
+    fred[0] = nan_seen ? NAN : t;
+  }
+  __syncthreads();
+  m = fred[0];
+  double s = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float e = (float)exp((double)(xr[i] - m));
+    o[i] = e;
+    s += (double)e;
+  }
+  for (int k = 16; k > 0; k >>= 1) s += __shfl_xor_sync(0xffffffffu, s, k);
+  if ((threadIdx.x & 31) == 0) dred[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += dred[i];
+    dred[0] = t;
+  }
+  __syncthreads();
+  float inv = (float)(1.0 / dred[0]);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = o[i] * inv;
+}
+
+// kernels.SiluMul (kernels/rows.go:45).
+__global__ void silu_mul_kernel(const float *g, const float *u, float *out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    float gv = g[i];
+    float e = (float)exp(-(double)gv);
+    out[i] = gv / (1.f + e) * u[i];
+  }
+}
+
+// kernels.Add (kernels/rows.go:54).
+__global__ void add_kernel(const float *a, const float *b, float *out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = a[i] + b[i];
+}
+
+// kernels.RoPE (kernels/rows.go:67), angles and rotation in float64 as in
+// cpu.RoPE (backend/cpu/cpu.go:69).
+__global__ void rope_kernel(float *x, const int32_t *pos, const float *freq, int n_heads,
+                            int head_dim, float base) {
+  const int r = blockIdx.x, half = head_dim / 2;
+  const double p = (double)pos[r];
+  float *row = x + (size_t)r * n_heads * head_dim;
+  for (int i = threadIdx.x; i < n_heads * half; i += blockDim.x) {
+    int h = i / half, j = i % half;
+    double theta = p * pow((double)base, -2.0 * (double)j / (double)head_dim);
+    theta = theta / (double)freq[j];
+    double s, c;
+    sincos(theta, &s, &c);
+    float *pr = row + h * head_dim + 2 * j;
+    double x0 = pr[0], x1 = pr[1];
+    pr[0] = (float)__dsub_rn(__dmul_rn(x0, c), __dmul_rn(x1, s));
+    pr[1] = (float)__dadd_rn(__dmul_rn(x0, s), __dmul_rn(x1, c));
+  }
+}
+
+// kernels.MatVecF16 / MatVecF32 (kernels/matvec.go:10,30): one warp per row.
+template <bool F16>
+__global__ void matvec_dense_kernel(const void *w, const float *x, float *y, int rows, int cols) {
+  int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int b = blockIdx.y, lane = threadIdx.x & 31;
+  const float *xb = x + (size_t)b * cols;
+  double acc = 0;
+  for (int c = lane; c < cols; c += 32) {
+    float wv = F16 ? gb_half_to_float(((const uint16_t *)w)[(size_t)r * cols + c])
+                   : ((const float *)w)[(size_t)r * cols + c];
+    acc += (double)wv * (double)xb[c];
+  }
+  for (int k = 16; k > 0; k >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, k);
+  if (lane == 0) y[(size_t)b * rows + r] = (float)acc;
+}
+
+// kernels.MatVecQ4_0/Q4K/Q6K on raw ggml bytes (kernels/quantmv.go:18-136):
+// one warp per (row, batch vector); each lane decodes whole blocks with the
+// bit-exact decoder and accumulates in float64 like cpu.MatVecQ.
+__global__ void matvec_q_raw_kernel(int typ, const uint8_t *w, const float *x, float *y, int rows,
+                                    int cols) {
+  int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int b = blockIdx.y, lane = threadIdx.x & 31;
+  const int bs = gb_block_size(typ), ts = gb_type_size(typ), nb = cols / bs;
+  const uint8_t *wr = w + (size_t)r * nb * ts;
+  const float *xb = x + (size_t)b * cols;
+  double acc = 0;
+  for (int blk = lane; blk < nb; blk += 32) {
+    const uint8_t *p = wr + (size_t)blk * ts;
+    float part = 0.f;
+    for (int e = 0; e < bs; e++) part = fmaf(gb_dequant_elem(typ, p, e), xb[blk * bs + e], part);
+    acc += (double)part;
+  }
+  for (int k = 16; k > 0; k >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, k);
+  if (lane == 0) y[(size_t)b * rows + r] = (float)acc;
+}
+
+// quant.Row on the device (quant/quant.go:135): bit-exact.
+__global__ void dequant_rows_kernel(int typ, const uint8_t *w, int cols, int row0, int nrows,
+                                    float *out) {
+  const int bs = gb_block_size(typ), ts = gb_type_size(typ);
+  const long long rb = (long long)(cols / bs) * ts;
+  long long total = (long long)nrows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    int r = (int)(i / cols), c = (int)(i % cols);
+    const uint8_t *blk = w + (long long)(row0 + r) * rb + (long long)(c / bs) * ts;
+    out[i] = gb_dequant_elem(typ, blk, c % bs);
+  }
+}
+
+// Single-CTA argmax with model.Argmax's rule (model/model.go:376).
+__global__ void argmax_kernel(const float *x, int n, int32_t *out) {
+  __shared__ unsigned long long red[32];
+  unsigned long long best = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = x[i];
+    if (isnan(v)) v = i == 0 ? INFINITY : -INFINITY;
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    unsigned long long k = ((unsigned long long)b << 32) | (0xFFFFFFFFull - (unsigned)i);
+    best = k > best ? k : best;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+    best = k > best ? k : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) t = red[i] > t ? red[i] : t;
+    *out = (int32_t)(0xFFFFFFFFu - (uint32_t)(t & 0xFFFFFFFFull));
+  }
+}
+
+// Reduce per-rank argmax keys (tensor-parallel lm_head) to the token.
+__global__ void argmax_keys_kernel(const unsigned long long *keys, int n, int32_t *token,
+                                   int32_t *hist, const int32_t *pos, int max_len) {
+  unsigned long long t = 0;
+  for (int i = 0; i < n; i++) t = keys[i] > t ? keys[i] : t;
+  int32_t tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(t & 0xFFFFFFFFull));
+  *token = tok;
+  if (hist) {
+    int p = *pos;
+    if (p >= 0 && p < max_len) hist[p] = tok;
+  }
+}
+
+__global__ void advance_pos_kernel(int32_t *pos) { *pos += 1; }
+
+// Embedding lookup (model/model.go:326 quant.Row on the host, moved on the
+// device): row *token of the tiled token_embd, bit-exact, into x; packs
+// x*wnorm and the per-group sums of squares for the first RMSNorm.
+__global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
+                             int vocab, float *x, const float *wnorm, GbXPackBuf pk,
+                             unsigned *err) {
+  __shared__ __align__(16) uint8_t blk[8][224];
+  gb_grid_dep_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (g >= dim / 32) return;
+  int tok = *token;
+  if (tok < 0 || tok >= vocab) {
+    if (g == 0 && lane == 0 && err) atomicOr(err, GB_DEVERR_TOKEN);
+    tok = 0;
+  }
+  const int tile = tok / 32, tl = tok % 32, sb = g / 8;
+  const int sbb = gb_tiled_sb_bytes(typ), raw = gb_sb_raw_bytes(typ);
+  const uint8_t *base = tiled + ((size_t)tile * nsb + sb) * sbb;
+  for (int b = lane; b < raw; b += 32) blk[warp][b] = base[gb_tiled_offset(typ, tl, b)];
+  __syncwarp();
+  int e = (g % 8) * 32 + lane;  // element within the super-block
+  float v = typ == GB_T_Q4_0 ? gb_dequant_elem(typ, blk[warp] + 18 * (e / 32), e % 32)
+                             : gb_dequant_elem(typ, blk[warp], e);
+  int c = g * 32 + lane;
+  x[c] = v;
+  GbXPack p{pk.a, pk.b, pk.c, pk.s, pk.sum16, pk.ssq};
+  gb_pack_group(p, g, v * wnorm[c]);
+  float ss = gb_warp_sum(v * v);
+  if (lane == 0) pk.ssq[g] = ss;
+  gb_grid_dep_launch();
+}
+
+// x += y, then pack x*wnorm (+ per-group sums of squares): the residual
+// epilogue when the projection's sum arrives from a collective.
+__global__ void resid_pack_kernel(float *x, const float *y, const float *wnorm, int n, GbXPackBuf pk) {
+  gb_grid_dep_wait();
+  const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (g >= n / 32) return;
+  int c = g * 32 + lane;
+  float xn = x[c] + y[c];
+  x[c] = xn;
+  GbXPack p{pk.a, pk.b, pk.c, pk.s, pk.sum16, pk.ssq};
+  gb_pack_group(p, g, xn * wnorm[c]);
+  float ss = gb_warp_sum(xn * xn);
+  if (lane == 0) pk.ssq[g] = ss;
+  gb_grid_dep_launch();
+}
+
+__global__ void fill_kernel(float *p, int n, float v) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = v;
+}
+
+cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAttribute *attr,
+                            bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cfg;
+}
+
+int blocks_for(long long n, int threads) {
+  long long b = (n + threads - 1) / threads;
+  if (b > 148 * 32) b = 148 * 32;
+  return b < 1 ? 1 : (int)b;
+}
+
+const char *type_name(int t) {
+  switch (t) {
+    case GB_T_F32: return "F32";
+    case GB_T_F16: return "F16";
+    case GB_T_Q4_0: return "Q4_0";
+    case GB_T_Q8_0: return "Q8_0";
+    case GB_T_Q4_K: return "Q4_K";
+    case GB_T_Q6_K: return "Q6_K";
+    case GB_T_BF16: return "BF16";
+  }
+  return "unknown";
+}
+
+}  // namespace
+
+// ---- internal launchers -----------------------------------------------------
+
+int gb_xpack_alloc(GbXPackBuf *p, int n) {
+  p->n = n;
+  GB_CUDA(cudaMalloc(&p->a, 3 * (size_t)n), "gpu: alloc pack");
+  p->b = p->a + n;
+  p->c = p->b + n;
+  GB_CUDA(cudaMalloc(&p->s, sizeof(float) * (size_t)(n / 32 + n / 16 + n / 32)), "gpu: alloc pack");
+  p->sum16 = p->s + n / 32;
+  p->ssq = p->sum16 + n / 16;
+  GB_CUDA(cudaMemset(p->a, 0, 3 * (size_t)n), "gpu: clear pack");
+  GB_CUDA(cudaMemset(p->s, 0, sizeof(float) * (size_t)(n / 32 + n / 16 + n / 32)), "gpu: clear pack");
+  return GB_OK;
+}
+void gb_xpack_free(GbXPackBuf *p) {
+  if (p->a) cudaFree(p->a);
+  if (p->s) cudaFree(p->s);
+  *p = GbXPackBuf();
+}
+
+int gb_embed_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
+                    int vocab, float *x, const float *wnorm, const GbXPackBuf &pk, unsigned *err,
+                    cudaStream_t st, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  int groups = dim / 32;
+  cudaLaunchConfig_t cfg = make_cfg(dim3((groups + 7) / 8), dim3(256), st, attr, pdl);
+  GB_CUDA(cudaLaunchKernelEx(&cfg, embed_kernel, typ, tiled, nsb, dim, token, vocab, x, wnorm, pk, err),
+          "gpu: embed");
+  return GB_OK;
+}
+
+int gb_resid_pack_launch(float *x, const float *y, const float *wnorm, int n, const GbXPackBuf &pk,
+                         cudaStream_t st, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  int groups = n / 32;
+  cudaLaunchConfig_t cfg = make_cfg(dim3((groups + 7) / 8), dim3(256), st, attr, pdl);
+  GB_CUDA(cudaLaunchKernelEx(&cfg, resid_pack_kernel, x, y, wnorm, n, pk), "gpu: residual");
+  return GB_OK;
+}
+
+int gb_argmax_keys_launch(const unsigned long long *keys, int n, int32_t *token, int32_t *hist,
+                          const int32_t *pos, int max_len, cudaStream_t st) {
+  argmax_keys_kernel<<<1, 1, 0, st>>>(keys, n, token, hist, pos, max_len);
+  GB_CUDA(cudaGetLastError(), "gpu: argmax reduce");
+  return GB_OK;
+}
+
+int gb_advance_pos_launch(int32_t *pos, cudaStream_t st) {
+  advance_pos_kernel<<<1, 1, 0, st>>>(pos);
+  GB_CUDA(cudaGetLastError(), "gpu: advance position");
+  return GB_OK;
+}
+
+// ---- C ABI: backend/gpu ------------------------------------------------------
+
+struct gb_kernels {
+  int device = 0;
+  float *ws = nullptr;  // attention partials + counters
+  size_t ws_floats = 0;
+  unsigned *ws_counter = nullptr;
+  int ws_nkv = 0;
+};
+
+// The kernel names backend/gpu binds (backend/gpu/gpu.go:24); each has an
+// entry point here.
+static const char *const k_names[] = {"RMSNorm", "Softmax", "SiluMul", "Add", "RoPE", "MatVecF16",
+                                      "MatVecF32", "MatVecQ4_0", "MatVecQ4K", "MatVecQ6K", "AttnDecode"};
+static const int k_count = (int)(sizeof k_names / sizeof k_names[0]);
+
+extern "C" {
+
+const char *gb_last_error(void) { return g_err.c_str(); }
+const char *gb_version(void) { return "gollama-b200 0.1 (sm_100a)"; }
+
+int gb_gpu_load(int device, gb_kernels **out) {
+  gb_clear_error();
+  if (!out) return gb_fail(GB_ERR_INVALID, "gpu: load kernels: null handle");
+  int n = 0;
+  GB_CUDA(cudaGetDeviceCount(&n), "gpu: load kernels");
+  if (device < 0 || device >= n) return gb_fail(GB_ERR_INVALID, "gpu: load kernels: no device %d", device);
+  GB_CUDA(cudaSetDevice(device), "gpu: load kernels");
+  cudaDeviceProp prop;
+  GB_CUDA(cudaGetDeviceProperties(&prop, device), "gpu: load kernels");
+  if (prop.major != 10)
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: load kernels: device is sm_%d%d, the kernels are sm_100a",
+                   prop.major, prop.minor);
+  cudaFuncAttributes fa;
+  GB_CUDA(cudaFuncGetAttributes(&fa, rmsnorm_kernel), "gpu: load kernels");
+  gb_kernels *k = new gb_kernels();
+  k->device = device;
+  *out = k;
+  return GB_OK;
+}
+
+int gb_gpu_len(const gb_kernels *k) { return k && k_names[0] ? k_count : 0; }
+
+int gb_gpu_close(gb_kernels *k) {
+  gb_clear_error();
+  if (!k) return GB_OK;
+  if (k->ws) cudaFree(k->ws);
+  if (k->ws_counter) cudaFree(k->ws_counter);
+  delete k;
+  return GB_OK;
+}
+
+#define GB_NEED(k)                                                        \
+  do {                                                                    \
+    if (!(k)) return gb_fail(GB_ERR_INVALID, "gpu: kernels not loaded"); \
+  } while (0)
+
+int gb_gpu_rmsnorm(gb_kernels *k, void *stream, const float *x, const float *w, float *out,
+                   int rows, int n, float eps) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (rows <= 0 || n <= 0) return GB_OK;
+  rmsnorm_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(x, w, out, n, eps);
+  GB_CUDA(cudaGetLastError(), "gpu: RMSNorm");
+  return GB_OK;
+}
+
+int gb_gpu_softmax(gb_kernels *k, void *stream, const float *x, float *out, int rows, int n) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (rows <= 0 || n <= 0) return GB_OK;
+  softmax_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(x, out, n);
+  GB_CUDA(cudaGetLastError(), "gpu: Softmax");
+  return GB_OK;
+}
+
+int gb_gpu_silu_mul(gb_kernels *k, void *stream, const float *gate, const float *up, float *out, int n) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (n <= 0) return GB_OK;
+  silu_mul_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(gate, up, out, n);
+  GB_CUDA(cudaGetLastError(), "gpu: SiluMul");
+  return GB_OK;
+}
+
+int gb_gpu_add(gb_kernels *k, void *stream, const float *a, const float *b, float *out, int n) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (n <= 0) return GB_OK;
+  add_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(a, b, out, n);
+  GB_CUDA(cudaGetLastError(), "gpu: Add");
+  return GB_OK;
+}
+
+int gb_gpu_rope(gb_kernels *k, void *stream, float *x, const int32_t *pos, const float *freq,
+                int rows, int n_heads, int head_dim, float base) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (head_dim % 2) return gb_fail(GB_ERR_INVALID, "gpu: RoPE: odd head_dim %d", head_dim);
+  if (rows <= 0) return GB_OK;
+  rope_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(x, pos, freq, n_heads, head_dim, base);
+  GB_CUDA(cudaGetLastError(), "gpu: RoPE");
+  return GB_OK;
+}
+
+int gb_gpu_attn_decode(gb_kernels *k, void *stream, const float *q, const float *kcache,
+                       const float *vcache, float *out, int kv_len, int n_heads, int n_kv,
+                       int head_dim, float scale) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (kv_len <= 0) return gb_fail(GB_ERR_INVALID, "gpu: AttnDecode: kv_len %d", kv_len);
+  if (n_kv <= 0 || n_heads % n_kv)
+    return gb_fail(GB_ERR_INVALID, "gpu: AttnDecode: %d heads is not a multiple of %d KV heads", n_heads, n_kv);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, k->device);
+  int splits = (2 * sms + n_kv - 1) / n_kv;
+  if (splits > 128) splits = 128;
+  if (splits > kv_len) splits = kv_len;
+  while ((kv_len + splits - 1) / splits > 2048) splits++;
+  const int G = n_heads / n_kv;
+  size_t need = gb_attn_part_floats(n_kv, splits, G, head_dim);
+  if (need > k->ws_floats || n_kv > k->ws_nkv) {
+    if (k->ws) cudaFree(k->ws);
+    if (k->ws_counter) cudaFree(k->ws_counter);
+    k->ws = nullptr;
+    k->ws_counter = nullptr;
+    k->ws_floats = 0;
+    k->ws_nkv = 0;
+    GB_CUDA(cudaMalloc(&k->ws, need * sizeof(float)), "gpu: AttnDecode: workspace");
+    GB_CUDA(cudaMalloc(&k->ws_counter, sizeof(unsigned) * (size_t)n_kv), "gpu: AttnDecode: workspace");
+    GB_CUDA(cudaMemset(k->ws_counter, 0, sizeof(unsigned) * (size_t)n_kv), "gpu: AttnDecode: workspace");
+    k->ws_floats = need;
+    k->ws_nkv = n_kv;
+  }
+  GbAttnArgs a;
+  a.q = q;
+  a.k = kcache;
+  a.v = vcache;
+  a.kv_f16 = 0;
+  const long long kv_dim = (long long)n_kv * head_dim;
+  a.k_sh = head_dim;
+  a.k_sd = 4;
+  a.k_st = kv_dim;
+  a.v_sh = head_dim;
+  a.v_st = kv_dim;
+  a.n_heads = n_heads;
+  a.n_kv = n_kv;
+  a.head_dim = head_dim;
+  a.scale = scale;
+  a.kv_len = kv_len;
+  a.splits = splits;
+  a.out = out;
+  a.part = k->ws;
+  a.counter = k->ws_counter;
+  return gb_attn_launch(a, (cudaStream_t)stream, false);
+}
+
+int gb_gpu_matvec_f16(gb_kernels *k, void *stream, const uint16_t *w, const float *x, float *y,
+                      int rows, int cols, int batch) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (rows <= 0 || batch <= 0) return GB_OK;
+  matvec_dense_kernel<true><<<dim3((rows + 7) / 8, batch), 256, 0, (cudaStream_t)stream>>>(w, x, y, rows, cols);
+  GB_CUDA(cudaGetLastError(), "gpu: MatVecF16");
+  return GB_OK;
+}
+
+int gb_gpu_matvec_f32(gb_kernels *k, void *stream, const float *w, const float *x, float *y,
+                      int rows, int cols, int batch) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (rows <= 0 || batch <= 0) return GB_OK;
+  matvec_dense_kernel<false><<<dim3((rows + 7) / 8, batch), 256, 0, (cudaStream_t)stream>>>(w, x, y, rows, cols);
+  GB_CUDA(cudaGetLastError(), "gpu: MatVecF32");
+  return GB_OK;
+}
+
+// backend/gpu/gpu.go:137-153: type dispatch and the block-multiple check.
+int gb_gpu_matvec_q(gb_kernels *k, void *stream, int typ, const uint8_t *w, const float *x,
+                    float *y, int rows, int cols, int batch) {
+  gb_clear_error();
+  GB_NEED(k);
+  const char *name;
+  switch (typ) {
+    case GB_T_Q4_0: name = "MatVecQ4_0"; break;
+    case GB_T_Q4_K: name = "MatVecQ4K"; break;
+    case GB_T_Q6_K: name = "MatVecQ6K"; break;
+    default: return gb_fail(GB_ERR_UNSUPPORTED, "gpu: no matvec kernel for %s", type_name(typ));
+  }
+  if (cols % gb_block_size(typ) != 0)
+    return gb_fail(GB_ERR_INVALID, "gpu: %s: %d columns is not a multiple of the block (%d)", name,
+                   cols, gb_block_size(typ));
+  if (rows <= 0 || batch <= 0) return GB_OK;
+  matvec_q_raw_kernel<<<dim3((rows + 7) / 8, batch), 256, 0, (cudaStream_t)stream>>>(typ, w, x, y, rows, cols);
+  GB_CUDA(cudaGetLastError(), name);
+  return GB_OK;
+}
+
+int gb_gpu_ones(int n, float **out) {
+  gb_clear_error();
+  if (!out || n < 0) return gb_fail(GB_ERR_INVALID, "gpu: Ones: bad arguments");
+  float *p = nullptr;
+  GB_CUDA(cudaMalloc(&p, sizeof(float) * (size_t)(n > 0 ? n : 1)), "gpu: Ones");
+  if (n > 0) {
+    fill_kernel<<<blocks_for(n, 256), 256>>>(p, n, 1.f);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      return gb_cuda_fail(e, "gpu: Ones");
+    }
+  }
+  *out = p;
+  return GB_OK;
+}
+
+int gb_free(void *p) {
+  gb_clear_error();
+  if (p) GB_CUDA(cudaFree(p), "gpu: free");
+  return GB_OK;
+}
+
+int gb_gpu_dequant_rows(gb_kernels *k, void *stream, int typ, const uint8_t *w, int rows, int cols,
+                        int row0, int nrows, float *out) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (row0 < 0 || nrows < 0 || (long long)row0 + nrows > rows)
+    return gb_fail(GB_ERR_INVALID, "quant: rows [%d, %d) outside the %d-row matrix", row0, row0 + nrows, rows);
+  if (gb_block_size(typ) == 0) return gb_fail(GB_ERR_UNSUPPORTED, "quant: %s not supported", type_name(typ));
+  if (cols % gb_block_size(typ))
+    return gb_fail(GB_ERR_INVALID, "quant: %d elements is not a multiple of the %s block (%d)", cols,
+                   type_name(typ), gb_block_size(typ));
+  if (nrows <= 0) return GB_OK;
+  dequant_rows_kernel<<<blocks_for((long long)nrows * cols, 256), 256, 0, (cudaStream_t)stream>>>(
+      typ, w, cols, row0, nrows, out);
+  GB_CUDA(cudaGetLastError(), "gpu: dequant");
+  return GB_OK;
+}
+
+int gb_gpu_argmax(gb_kernels *k, void *stream, const float *x, int n, int32_t *out) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (n <= 0) return gb_fail(GB_ERR_INVALID, "gpu: argmax: empty vector");
+  argmax_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, out);
+  GB_CUDA(cudaGetLastError(), "gpu: argmax");
+  return GB_OK;
+}
+
+// model.Argmax, model/model.go:376.
+int32_t gb_argmax(const float *logits, int64_t n) {
+  int64_t best = 0;
+  for (int64_t i = 0; i < n; i++)
+    if (logits[i] > logits[best]) best = i;
+  return (int32_t)best;
+}
+
+}  // extern "C"
