@@ -602,12 +602,19 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   if (grid < 1) grid = 1;
   if (grid * warps > (long long)gb_gemv_scratch_floats(a.ntiles, plan) / 128)
     grid = gb_gemv_scratch_floats(a.ntiles, plan) / 128 / warps;
-  static bool attr_set = false;
-  if (!attr_set) {
-    GB_CUDA(cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024),
+  static int smem_cap = 0;
+  if (!smem_cap) {
+    int dev = 0, optin = 0;
+    cudaFuncAttributes fa;
+    GB_CUDA(cudaGetDevice(&dev), "gpu: gemv");
+    GB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev), "gpu: gemv");
+    GB_CUDA(cudaFuncGetAttributes(&fa, gemv_kernel), "gpu: gemv");
+    int cap = optin - (int)fa.sharedSizeBytes;
+    GB_CUDA(cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cap),
             "gpu: gemv: shared memory attribute");
-    attr_set = true;
+    smem_cap = cap;
   }
+  if (smem > (size_t)smem_cap) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: %zu bytes of shared memory", smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3((unsigned)(warps * 32));

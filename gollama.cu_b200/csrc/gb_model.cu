@@ -953,6 +953,15 @@ int gb_tp_unique_id(uint8_t out[128]) {
 
 // ---- model.Linear ------------------------------------------------------------
 
+static void free_linear(gb_linear *l) {
+  if (!l) return;
+  if (l->t.w) cudaFree(l->t.w);
+  gb_xpack_free(&l->pack);
+  if (l->part) cudaFree(l->part);
+  if (l->tile_counter) cudaFree(l->tile_counter);
+  delete l;
+}
+
 int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes, int rows, int cols,
                      gb_linear **out) {
   gb_clear_error();
@@ -990,7 +999,7 @@ int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes,
   if (!rc && cudaMemset(l->tile_counter, 0, sizeof(unsigned) * (size_t)(t.ntiles + 64)) != cudaSuccess)
     rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
   if (rc) {
-    gb_linear_free(l);
+    free_linear(l);  // keeps the error message of the failed step
     return rc;
   }
   *out = l;
@@ -1029,12 +1038,7 @@ int gb_linear_info(const gb_linear *l, int *typ, int *rows, int *cols, size_t *w
 
 int gb_linear_free(gb_linear *l) {
   gb_clear_error();
-  if (!l) return GB_OK;
-  if (l->t.w) cudaFree(l->t.w);
-  gb_xpack_free(&l->pack);
-  if (l->part) cudaFree(l->part);
-  if (l->tile_counter) cudaFree(l->tile_counter);
-  delete l;
+  free_linear(l);
   return GB_OK;
 }
 

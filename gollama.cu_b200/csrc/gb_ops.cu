@@ -29,6 +29,7 @@ int gb_fail(int code, const char *fmt, ...) {
   return code;
 }
 int gb_cuda_fail(cudaError_t e, const char *what) {
+  (void)cudaGetLastError();  // a non-sticky error must not resurface at the next launch check
   return gb_fail(GB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 void gb_clear_error() { g_err.clear(); }
