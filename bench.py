@@ -1,0 +1,424 @@
+#!/usr/bin/env python3
+"""Decode tokens/s at batch 1 for the B200 path of gollama.cu (one JSON line).
+
+Default workload (1 GPU): a Llama-3.1-8B-shaped Q4_K_M model
+with seeded random-init weights, the KV cache prefilled with seeded N(0,1)
+fp16 values for positions 0..8191, then greedy decode steps at positions
+8192..8319 (a 128-position window that repeats for longer runs). A step is one
+decode token: embedding, 32 layers, lm_head and the argmax, as one CUDA graph
+replay with the token and position resident on the device.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config 8b|1b|3b|70b]
+  python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...   # tensor parallel
+  python bench.py --impl reference ...   # the reference's CPU path (the C restatement of
+                                         # backend/cpu + cpuForward), all host threads
+
+`value` is device time (CUDA events on the model's stream, max over ranks);
+`e2e` goes through the reference-facing call (gb_model_forward: token and
+position copied in, the vocabulary logits copied out, host argmax) every step.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "gollama.cu_b200")
+sys.path.insert(0, PKG)
+
+CONFIGS = {
+    # name: preset, KV setup, first decode position, window of positions, cache
+    "8b": dict(preset=8, prefill=8192, prompt=0, window=128, kv_f16=1, max_len=8320,
+               workload="llama-3.1-8b Q4_K_M decode, KV prefilled N(0,1) fp16 to 8192, positions 8192-8319"),
+    "1b": dict(preset=1, prefill=0, prompt=16, window=64, kv_f16=0, max_len=512,
+               workload="llama-3.2-1b Q4_0 decode after a 16-token prompt, f32 KV, positions 16-79"),
+    "3b": dict(preset=3, prefill=0, prompt=32, window=256, kv_f16=1, max_len=4096,
+               workload="llama-3.2-3b Q4_K_M decode after a 32-token prompt, fp16 KV, positions 32-287"),
+    "70b": dict(preset=70, prefill=0, prompt=64, window=128, kv_f16=1, max_len=8192,
+                workload="llama-3.1-70b Q4_K_M decode after a 64-token prompt, fp16 KV, positions 64-191"),
+}
+SEED = 0
+KV_SEED = 1
+METRIC = "decode tokens/s at batch 1"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy burst)"
+    except Exception:
+        return 6650.0, "fallback 6.65 TB/s (no MEASURED_PEAKS.json)"
+
+
+def ncu_traffic(config):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d.get(config, {}).get("gateup_dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=self.out, stderr=subprocess.DEVNULL)
+            time.sleep(0.2)
+        except Exception:
+            self.proc = None
+        self.t0 = time.time()
+
+    def mark(self):
+        self.t0 = time.time()
+
+    def stop(self):
+        t1 = time.time()
+        if not self.proc:
+            return None
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                try:
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    rows.append((ts, int(parts[1]), float(parts[2]), float(parts[3]), parts[6:10]))
+                except ValueError:
+                    continue
+        os.unlink(self.path)
+        inside = [r for r in rows if self.t0 - 0.06 <= r[0] <= t1 + 0.06 and r[1] in self.gpus]
+        if not inside:
+            inside = [r for r in rows if r[1] in self.gpus][-3:]
+        if not inside:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[4]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[2] for r in inside), "sm_max_mhz": max(r[3] for r in inside),
+                "reasons": reasons, "samples": len(inside)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def build_image(gb, cfg, world, rank):
+    """A synthetic GGUF image: in memory for one GPU, a shared file for several ranks."""
+    spec = gb.synth_preset(cfg["preset"], seed=SEED)
+    if cfg.get("layers"):
+        spec.layers = cfg["layers"]  # profiling captures only: same shapes, fewer layers
+    if world == 1:
+        return gb.SynthImage(spec), spec
+    path = os.path.join(tempfile.gettempdir(), f"gollama_b200_{cfg['preset']}_{SEED}.gguf")
+    if rank == 0 and not os.path.exists(path):
+        tmp = path + ".part"
+        gb._check(gb.lib().gb_synth_model_file(gb.C.byref(spec), tmp.encode()))
+        os.replace(tmp, path)
+    barrier(world)
+    return path, spec
+
+
+def prompt_tokens(spec, n):
+    rng = np.random.default_rng(SEED)
+    return [int(t) for t in rng.integers(0, spec.vocab, n)]
+
+
+def run_ours(args, cfg, world, rank, local):
+    import torch
+
+    import gollama_b200 as gb
+
+    os.environ.setdefault("GB_HOST_THREADS", str(max(1, (os.cpu_count() or 8) // world)))
+    nccl_id = None
+    if world > 1:
+        import torch.distributed as dist
+
+        obj = [gb.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    src, spec = build_image(gb, cfg, world, rank)
+    opts = dict(device=local, max_len=cfg["max_len"], kv_f16=cfg["kv_f16"], tp_rank=rank, tp_world=world)
+    if nccl_id is not None:
+        opts["nccl_id"] = nccl_id
+    m = gb.Model(src, **opts)
+    c = m.config
+    if cfg["prefill"]:
+        m.fill_kv_normal(KV_SEED, cfg["prefill"])
+    toks = prompt_tokens(spec, cfg["prompt"] + 1)
+    for pos in range(cfg["prompt"]):
+        m.forward_no_logits(toks[pos], pos)
+    p0 = cfg["prefill"] + cfg["prompt"]
+    t0 = toks[-1]
+    window = cfg["window"]
+    stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
+
+    def steps(n):
+        # n greedy steps cycling over the window's positions
+        done, off = 0, 0
+        m.start(t0, p0)
+        while done < n:
+            k = min(n - done, window - off)
+            m.decode_async(k)
+            done += k
+            off += k
+            if off == window and done < n:
+                m.start(t0, p0)
+                off = 0
+
+    # warm-up
+    barrier(world)
+    steps(args.warmup)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = ClockSampler(list(range(world))) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.mark()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    steps(args.steps)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop() if clocks else None
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    toks_out = m.read_tokens(p0, min(args.steps, window))
+    tok_s = args.steps / (ms / 1e3)
+
+    # end to end through gb_model_forward: H2D token+position, D2H logits, host argmax
+    barrier(world)
+    n_e2e = max(8, min(args.steps, 2 * window))
+    logits = np.empty(c.vocab, np.float32)
+    tok = t0
+    m.forward(tok, p0) if rank == 0 else m.forward_no_logits(tok, p0)  # warm
+    barrier(world)
+    w0 = time.perf_counter()
+    for i in range(n_e2e):
+        pos = p0 + (i % window)
+        if rank == 0:
+            m.forward(tok, pos, out=logits)
+            tok = gb.argmax(logits)
+        else:
+            m.forward_no_logits(tok, pos)
+    wall = max_over_ranks(time.perf_counter() - w0, world)
+    e2e = {"value": n_e2e / wall, "unit": "tok/s", "h2d_bytes_per_step": 8,
+           "d2h_bytes_per_step": 4 * c.vocab + 4, "steps": n_e2e,
+           "how": "wall clock around gb_model_forward (pinned staging) + host model.Argmax per step"}
+
+    # roofline of the dominant kernel (gate/up GEMV with the SwiGLU epilogue), device events
+    prof = []
+    for i in range(5):
+        prof.append(m.profile_step(t0, p0 + i))
+    gu_ms = statistics.median(p["gate_up"][0] / max(1, p["gate_up"][1]) for p in prof)
+    bytes_tok, gu_bytes = m.step_bytes(p0 + window // 2)
+    peak, peak_src = peaks()
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    breakdown = {k: round(statistics.median(p[k][0] for p in prof), 4) for k in prof[0]}
+    result = {
+        "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q4_k/q6_k/q4_0 weights x int8-limb activations (dp4a), f32 accumulate",
+        "data": "synthetic: seeded random-init weights" + (", KV prefilled with seeded N(0,1) fp16" if cfg["prefill"] else ""),
+        "config": {"workload": cfg["workload"], "model": f"preset {cfg['preset']} (dim {c.dim}, {c.layers} layers, "
+                   f"{c.heads}/{c.kv_heads} heads, ffn {c.ffn}, vocab {c.vocab})", "global_batch": 1,
+                   "seq_len": c.max_len, "parallelism": f"tp{world}",
+                   "l2": f"inputs larger than L2: {bytes_tok / 1e9:.2f} GB read per token vs 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": ncu_traffic(args.config) if world == 1 else None,
+                     "kernel": "gemv_kernel, gate/up + SwiGLU (one launch per layer)",
+                     "bytes_per_launch": gu_bytes, "avg_launch_ms": round(gu_ms, 5), "peak_source": peak_src},
+        "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": round(bytes_tok * tok_s / 1e9, 1),
+                          "frac": round(bytes_tok * tok_s / 1e9 / peak, 4),
+                          "roofline_tok_s": round(peak * 1e9 / bytes_tok, 1)},
+        "kernel_ms_per_step": breakdown,
+        "e2e": e2e,
+        "gpu_launches": m.launches_per_step() * args.steps,
+        "clocks": clk,
+        "first_tokens": [int(t) for t in toks_out[:8]],
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(src, spec, cfg, p0, t0)
+    m.close()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def oracle_model(img_or_path, spec, cfg, p0, t0):
+    """The C restatement of the reference's backend/cpu forward over the same image."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as orc
+
+    import gollama_b200 as gb
+
+    if isinstance(img_or_path, str):
+        raw = np.fromfile(img_or_path, np.uint8)
+    else:
+        raw = img_or_path.view()
+    om = orc.OracleModel(raw, cfg["max_len"], bool(cfg["kv_f16"]))
+    kv_dim = spec.kv_heads * spec.head_dim
+    if cfg["prefill"]:
+        for layer in range(spec.layers):
+            k, v = gb.synth_kv_normal(KV_SEED, layer, 0, cfg["prefill"], kv_dim, bool(cfg["kv_f16"]))
+            om.set_kv(layer, 0, k, v)
+    toks = prompt_tokens(spec, cfg["prompt"] + 1)
+    for pos in range(cfg["prompt"]):
+        om.forward(toks[pos], pos, spec.vocab)
+    return om, raw
+
+
+def cpu_baseline(src, spec, cfg, p0, t0):
+    om, raw = oracle_model(src, spec, cfg, p0, t0)
+    cores = os.cpu_count() or 1
+    t = time.perf_counter()
+    om.forward(t0, p0, spec.vocab, threads=1)
+    t1 = time.perf_counter() - t
+    t = time.perf_counter()
+    om.forward(t0, p0, spec.vocab, threads=cores)
+    tn = time.perf_counter() - t
+    om.close()
+    return {"value": round(1 / t1, 4), "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": f"1 decode token at position {p0} of the bench workload, C restatement of backend/cpu "
+                      "+ cpuForward, single thread (the reference's Go path is single-threaded)",
+            "all_cores": {"value": round(1 / tn, 3), "cores": cores}}
+
+
+def run_reference(args, cfg, world, rank):
+    """The reference's CPU path (backend/cpu + cpuForward restated in C: Go is not on this image),
+    all host threads, rank 0 only. Each step is one decode token of the same workload."""
+    if rank != 0:
+        return
+    import gollama_b200 as gb
+
+    spec = gb.synth_preset(cfg["preset"], seed=SEED)
+    img = gb.SynthImage(spec)
+    p0 = cfg["prefill"] + cfg["prompt"]
+    toks = prompt_tokens(spec, cfg["prompt"] + 1)
+    om, _ = oracle_model(img, spec, cfg, p0, toks[-1])
+    cores = os.cpu_count() or 1
+    window = cfg["window"]
+    tok = toks[-1]
+    for i in range(args.warmup):
+        tok = gb.argmax(om.forward(tok, p0 + i % window, spec.vocab, threads=cores))
+    t = time.perf_counter()
+    tok = toks[-1]
+    for i in range(args.steps):
+        logits = om.forward(tok, p0 + i % window, spec.vocab, threads=cores)
+        tok = gb.argmax(logits)
+    wall = time.perf_counter() - t
+    om.close()
+    v = args.steps / wall
+    sample = (f"{args.steps} decode tokens of the bench workload ({cfg['workload']}), C restatement of "
+              f"backend/cpu + cpuForward, {cores} threads")
+    print(json.dumps({"metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 3),
+                      "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "impl": "reference",
+                      "dtype": "f32 weights dequantized per token, f64 accumulate",
+                      "data": "synthetic: seeded random-init weights",
+                      "config": {"workload": cfg["workload"], "global_batch": 1, "seq_len": cfg["max_len"],
+                                 "parallelism": "host threads"},
+                      "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+                                       "sample": sample},
+                      "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="truncate the model to this many layers (small ncu captures only; not a bench line)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    cfg = dict(CONFIGS[args.config])
+    if args.layers:
+        cfg["layers"] = args.layers
+        cfg["workload"] += f" [truncated to {args.layers} layers for profiling]"
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, cfg, world, rank)
+        else:
+            run_ours(args, cfg, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -831,6 +831,32 @@ int gb_model_generate(gb_model *m, int32_t token, int pos, int n, int32_t *out_t
   return check_err(m);
 }
 
+int gb_model_start(gb_model *m, int32_t token, int pos) {
+  gb_clear_error();
+  if (!m) return gb_fail(GB_ERR_INVALID, "model: null model");
+  return set_token_pos(m, token, pos);
+}
+
+int gb_model_decode_async(gb_model *m, int n) {
+  gb_clear_error();
+  if (!m || n < 0) return gb_fail(GB_ERR_INVALID, "model: bad decode arguments");
+  for (int i = 0; i < n; i++) {
+    int rc = run_step(m);
+    if (rc) return rc;
+  }
+  return GB_OK;
+}
+
+int gb_model_read_tokens(gb_model *m, int pos0, int n, int32_t *out_tokens) {
+  gb_clear_error();
+  if (!m || pos0 < 0 || n < 0 || pos0 + n > m->c.max_len || (n > 0 && !out_tokens))
+    return gb_fail(GB_ERR_INVALID, "model: bad token range");
+  if (n > 0)
+    GB_CUDA(cudaMemcpyAsync(out_tokens, m->gen + pos0, sizeof(int32_t) * (size_t)n, cudaMemcpyDeviceToHost, m->st),
+            "model: tokens");
+  return check_err(m);
+}
+
 int gb_model_fill_kv_normal(gb_model *m, uint64_t seed, int n_pos) {
   gb_clear_error();
   if (!m || n_pos < 0 || n_pos > m->c.max_len) return gb_fail(GB_ERR_INVALID, "model: bad KV fill");

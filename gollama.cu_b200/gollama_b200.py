@@ -80,6 +80,8 @@ _SIGS = {
     "gb_model_load_mem": (I, [P, S, P, C.POINTER(P)]), "gb_model_config": (I, [P, P]),
     "gb_model_forward": (I, [P, C.c_int32, I, P]), "gb_model_next": (I, [P, C.c_int32, I, P]),
     "gb_model_generate": (I, [P, C.c_int32, I, I, P]), "gb_model_fill_kv_normal": (I, [P, U64, I]),
+    "gb_model_start": (I, [P, C.c_int32, I]), "gb_model_decode_async": (I, [P, I]),
+    "gb_model_read_tokens": (I, [P, I, I, P]),
     "gb_model_read_kv": (I, [P, I, I, I, P, P]), "gb_model_stream": (P, [P]),
     "gb_model_profile_step": (I, [P, C.c_int32, I, P, P]),
     "gb_model_step_bytes": (I, [P, I, C.POINTER(D), C.POINTER(D)]),
@@ -284,6 +286,17 @@ class Model:
     def generate(self, token: int, pos: int, n: int) -> np.ndarray:
         out = np.empty(max(n, 1), dtype=np.int32)
         _check(lib().gb_model_generate(self.h, token, pos, n, out.ctypes.data))
+        return out[:n]
+
+    def start(self, token: int, pos: int) -> None:
+        _check(lib().gb_model_start(self.h, token, pos))
+
+    def decode_async(self, n: int) -> None:
+        _check(lib().gb_model_decode_async(self.h, n))
+
+    def read_tokens(self, pos0: int, n: int) -> np.ndarray:
+        out = np.empty(max(n, 1), dtype=np.int32)
+        _check(lib().gb_model_read_tokens(self.h, pos0, n, out.ctypes.data))
         return out[:n]
 
     def fill_kv_normal(self, seed: int, n_pos: int) -> None:

@@ -160,6 +160,14 @@ int gb_model_next(gb_model *m, int32_t token, int pos, int32_t *next);
 /* Added: n greedy steps from (token, pos) with no host round trip between
  * them; out_tokens[n] receives the generated ids. */
 int gb_model_generate(gb_model *m, int32_t token, int pos, int n, int32_t *out_tokens);
+/* Added, the three parts of gb_model_generate for callers that time or
+ * overlap the device work: stage (token, pos) on the device (stream-ordered,
+ * no host wait); run n greedy steps from the device-resident token and
+ * position (graph replays, no host wait); wait and copy the ids generated at
+ * positions [pos0, pos0+n) (checks the device status word). */
+int gb_model_start(gb_model *m, int32_t token, int pos);
+int gb_model_decode_async(gb_model *m, int n);
+int gb_model_read_tokens(gb_model *m, int pos0, int n, int32_t *out_tokens);
 /* Added: fill KV positions [0, n_pos) of every layer with the seeded N(0,1)
  * values of gb_synth_kv_normal (rounded to the cache type). */
 int gb_model_fill_kv_normal(gb_model *m, uint64_t seed, int n_pos);

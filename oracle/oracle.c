@@ -343,12 +343,12 @@ int or_matvec_q(int typ, const uint8_t *w, int64_t len, const float *x, float *y
   return err;
 }
 
-/* backend/cpu/cpu.go:143 AttnDecode. */
-void or_attn_decode(const float *q, const float *kcache, const float *vcache, float *out,
-                    int kv_len, int n_heads, int n_kv, int head_dim, float scale) {
+/* backend/cpu/cpu.go:143 AttnDecode, heads [h0, h1). */
+static void attn_heads(const float *q, const float *kcache, const float *vcache, float *out,
+                       int kv_len, int n_heads, int n_kv, int head_dim, float scale, int h0, int h1) {
   int group = n_heads / n_kv, kv_dim = n_kv * head_dim;
   float *scores = (float *)malloc(sizeof(float) * (size_t)(kv_len > 0 ? kv_len : 1));
-  for (int h = 0; h < n_heads; h++) {
+  for (int h = h0; h < h1; h++) {
     const float *qh = q + (int64_t)h * head_dim;
     int kvh = h / group;
     for (int t = 0; t < kv_len; t++) {
@@ -367,6 +367,43 @@ void or_attn_decode(const float *q, const float *kcache, const float *vcache, fl
     }
   }
   free(scores);
+}
+
+void or_attn_decode(const float *q, const float *kcache, const float *vcache, float *out,
+                    int kv_len, int n_heads, int n_kv, int head_dim, float scale) {
+  attn_heads(q, kcache, vcache, out, kv_len, n_heads, n_kv, head_dim, scale, 0, n_heads);
+}
+
+/* Heads are independent, so splitting them across threads changes no bit. */
+typedef struct {
+  const float *q, *k, *v; float *out;
+  int kv_len, n_heads, n_kv, head_dim; float scale; int h0, h1;
+} attn_job;
+
+static void *attn_run(void *arg) {
+  attn_job *j = (attn_job *)arg;
+  attn_heads(j->q, j->k, j->v, j->out, j->kv_len, j->n_heads, j->n_kv, j->head_dim, j->scale,
+             j->h0, j->h1);
+  return NULL;
+}
+
+static void attn_parallel(const float *q, const float *kcache, const float *vcache, float *out,
+                          int kv_len, int n_heads, int n_kv, int head_dim, float scale, int threads) {
+  if (threads > n_heads) threads = n_heads;
+  if (threads > 256) threads = 256;
+  if (threads <= 1) {
+    or_attn_decode(q, kcache, vcache, out, kv_len, n_heads, n_kv, head_dim, scale);
+    return;
+  }
+  attn_job jobs[256];
+  pthread_t th[256];
+  for (int t = 0; t < threads; t++) {
+    attn_job j = {q, kcache, vcache, out, kv_len, n_heads, n_kv, head_dim, scale,
+                  n_heads * t / threads, n_heads * (t + 1) / threads};
+    jobs[t] = j;
+    pthread_create(&th[t], NULL, attn_run, &jobs[t]);
+  }
+  for (int t = 0; t < threads; t++) pthread_join(th[t], NULL);
 }
 
 /* model/model.go:376 Argmax. */
@@ -757,7 +794,8 @@ int or_model_forward(or_model *m, int32_t token, int pos, float *logits, int thr
       kr[j] = m->kv_f16 ? or_f16_to_f32(or_f16_from(k[j])) : k[j];
       vr[j] = m->kv_f16 ? or_f16_to_f32(or_f16_from(v[j])) : v[j];
     }
-    or_attn_decode(q, m->kc[i], m->vc[i], attn, pos + 1, c.heads, c.kv_heads, c.head_dim, scale);
+    attn_parallel(q, m->kc[i], m->vc[i], attn, pos + 1, c.heads, c.kv_heads, c.head_dim, scale,
+                  threads);
     snprintf(name, sizeof name, "blk.%d.attn_output.weight", i);
     rc |= matvec(f, name, attn, o, c.dim, qdim, threads);
     if (rc) break;
