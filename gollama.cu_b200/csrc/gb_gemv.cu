@@ -8,63 +8,72 @@
 //    of the persistent grid takes one contiguous range of units (stream-K),
 //    so all SMs stay busy whatever the matrix shape and no wave is partial.
 //  * Each unit's sb-block (4608 or 6720 contiguous bytes) is brought into a
-//    per-warp shared-memory ring by one 1-D TMA bulk copy completing on an
-//    mbarrier; the copies of the next units are in flight while the warp
+//    per-warp shared-memory slot by a 1-D TMA bulk copy completing on an
+//    mbarrier; with two slots the next unit's copy is in flight while the warp
 //    decodes the current one. Lane l of the warp owns row l of the tile.
-//  * The activation arrives as a limb pack (gb_device.cuh): three int8
-//    limbs per element, so the 4-bit / 6-bit quants meet the activation in
-//    dp4a (4 products per instruction, exact int32 sums), and float math is
-//    only needed once per 16- or 32-element sub-block for the ggml scales.
+//  * The activation arrives as a limb pack (gb_device.cuh): three int8 limbs
+//    per element, so the 4-bit / 6-bit quants meet the activation in dp4a
+//    (4 products per instruction, exact int32 sums); float math is needed once
+//    per 16- or 32-element sub-block for the ggml scales. A CTA stages only the
+//    pack of the super-blocks its warps touch.
 //  * A row-block split between warps is finished by the warp whose atomic
 //    count completes it; it sums the partials in warp order (deterministic)
-//    and runs the epilogue. Counters are reset by that warp, so the kernel
-//    can be replayed from a CUDA graph.
+//    and runs the epilogue. Counters are reset by that warp, so the kernel can
+//    be replayed from a CUDA graph.
+//  * One instantiation per (weight types, epilogue) keeps each kernel's code
+//    small; unit cursors are 32-bit and advance without divisions.
 #include <math.h>
+#include <stdlib.h>
+
+#include <algorithm>
 
 #include "gb_device.cuh"
 #include "gb_internal.h"
 
 namespace {
 
-constexpr float kL1 = 1.f / 254.f;
-constexpr float kL2 = 1.f / 64516.f;
+constexpr float kL2 = 1.f / 64516.f;  // 1/254^2: limbs b, c are combined as 254*b + c
 
 GB_DEV float byte_f(uint32_t w, int i) { return (float)((w >> (8 * i)) & 0xFFu); }
 
 // ---- per-super-block decode + dot products. `st` is the sb-block in shared
 // memory; xa/xb/xc are the limb planes (as 32-bit words) of the block's 256
 // activation elements, xs the 8 group scales and xsum the 16 half-group sums.
+template <int T>
+GB_DEV float sb_dot(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                    const uint32_t *xc, const float *xs, const float *xsum);
 
 // Q4_K: quant/quant.go:97 layout; kernels/quantmv.go:66 factorisation
 // sum = d*sum_j sc_j*(q.x)_j - dmin*sum_j m_j*(sum x)_j.
-GB_DEV float sb_q4k(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                    const uint32_t *xc, const float *xs, const float *xsum) {
+template <>
+GB_DEV float sb_dot<GB_T_Q4_K>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xs, const float *xsum) {
   const uint4 *u = (const uint4 *)st;
-  uint4 h = u[lane];
-  float d = gb_half_to_float((uint16_t)(h.x & 0xFFFFu));
-  float dmin = gb_half_to_float((uint16_t)(h.x >> 16));
-  uint32_t sc03 = h.y & 0x3F3F3F3Fu, m03 = h.z & 0x3F3F3F3Fu;
-  uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-  uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+  const uint4 h = u[lane];
+  const float d = gb_half_to_float((uint16_t)(h.x & 0xFFFFu));
+  const float dmin = gb_half_to_float((uint16_t)(h.x >> 16));
+  const uint32_t sc03 = h.y & 0x3F3F3F3Fu, m03 = h.z & 0x3F3F3F3Fu;
+  const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+  const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
   float tq = 0.f, tm = 0.f;
 #pragma unroll
   for (int c = 0; c < 4; c++) {
-    uint4 q0 = u[(1 + 2 * c) * 32 + lane], q1 = u[(2 + 2 * c) * 32 + lane];
-    uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint4 q0 = u[(1 + 2 * c) * 32 + lane], q1 = u[(2 + 2 * c) * 32 + lane];
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const uint4 *pa = (const uint4 *)(xa + 16 * c), *pb = (const uint4 *)(xb + 16 * c),
                 *pc = (const uint4 *)(xc + 16 * c);
     int A0 = 0, B0 = 0, C0 = 0, A1 = 0, B1 = 0, C1 = 0;
 #pragma unroll
     for (int v = 0; v < 2; v++) {
-      uint4 la = pa[v], lb = pb[v], lc = pc[v], ha = pa[2 + v], hb = pb[2 + v], hc = pc[2 + v];
-      uint32_t a4[4] = {la.x, la.y, la.z, la.w}, b4[4] = {lb.x, lb.y, lb.z, lb.w},
-               c4[4] = {lc.x, lc.y, lc.z, lc.w};
-      uint32_t A4[4] = {ha.x, ha.y, ha.z, ha.w}, B4[4] = {hb.x, hb.y, hb.z, hb.w},
-               C4[4] = {hc.x, hc.y, hc.z, hc.w};
+      const uint4 la = pa[v], lb = pb[v], lc = pc[v], ha = pa[2 + v], hb = pb[2 + v], hc = pc[2 + v];
+      const uint32_t a4[4] = {la.x, la.y, la.z, la.w}, b4[4] = {lb.x, lb.y, lb.z, lb.w},
+                     c4[4] = {lc.x, lc.y, lc.z, lc.w};
+      const uint32_t A4[4] = {ha.x, ha.y, ha.z, ha.w}, B4[4] = {hb.x, hb.y, hb.z, hb.w},
+                     C4[4] = {hc.x, hc.y, hc.z, hc.w};
 #pragma unroll
       for (int k = 0; k < 4; k++) {
-        uint32_t w = qw[4 * v + k];
-        uint32_t lo = w & 0x0F0F0F0Fu, hi = w & 0xF0F0F0F0u;
+        const uint32_t w = qw[4 * v + k];
+        const uint32_t lo = w & 0x0F0F0F0Fu, hi = w & 0xF0F0F0F0u;
         A0 = gb_dp4a_us(lo, a4[k], A0);
         B0 = gb_dp4a_us(lo, b4[k], B0);
         C0 = gb_dp4a_us(lo, c4[k], C0);
@@ -73,58 +82,66 @@ GB_DEV float sb_q4k(const uint8_t *st, int lane, const uint32_t *xa, const uint3
         C1 = gb_dp4a_us(hi, C4[k], C1);
       }
     }
-    float S0 = (float)A0 + (float)B0 * kL1 + (float)C0 * kL2;
-    float S1 = ((float)A1 + (float)B1 * kL1 + (float)C1 * kL2) * 0.0625f;
+    // sum q*x / s_g = A + (254 B + C)/254^2  (254 B + C < 2^24: exact in float)
+    const float S0 = (float)A0 + (float)(254 * B0 + C0) * kL2;
+    const float S1 = ((float)A1 + (float)(254 * B1 + C1) * kL2) * 0.0625f;
     const int j0 = 2 * c, j1 = 2 * c + 1;
-    float sc0 = byte_f(j0 < 4 ? sc03 : sc47, j0 & 3), sc1 = byte_f(j1 < 4 ? sc03 : sc47, j1 & 3);
-    float m0 = byte_f(j0 < 4 ? m03 : m47, j0 & 3), m1 = byte_f(j1 < 4 ? m03 : m47, j1 & 3);
-    tq += sc0 * (xs[j0] * S0) + sc1 * (xs[j1] * S1);
-    tm += m0 * (xsum[2 * j0] + xsum[2 * j0 + 1]) + m1 * (xsum[2 * j1] + xsum[2 * j1 + 1]);
+    const float sc0 = byte_f(j0 < 4 ? sc03 : sc47, j0 & 3), sc1 = byte_f(j1 < 4 ? sc03 : sc47, j1 & 3);
+    const float m0 = byte_f(j0 < 4 ? m03 : m47, j0 & 3), m1 = byte_f(j1 < 4 ? m03 : m47, j1 & 3);
+    tq = fmaf(sc0, xs[j0] * S0, tq);
+    tq = fmaf(sc1, xs[j1] * S1, tq);
+    tm = fmaf(m0, xsum[2 * j0] + xsum[2 * j0 + 1], tm);
+    tm = fmaf(m1, xsum[2 * j1] + xsum[2 * j1 + 1], tm);
   }
   return d * tq - dmin * tm;
 }
 
 // Q6_K: quant/quant.go:114 layout; y = d*sc*(q-32) over 16-element sub-blocks.
-GB_DEV float sb_q6k(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                    const uint32_t *xc, const float *xs, const float *xsum) {
+template <>
+GB_DEV float sb_dot<GB_T_Q6_K>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xs, const float *xsum) {
   const uint4 *u = (const uint4 *)st;
-  uint4 scv = u[12 * 32 + lane];
-  const int8_t *sc8 = (const int8_t *)&scv;
-  float d = gb_half_to_float(((const uint16_t *)(st + 13 * 512))[lane]);
+  const uint4 scv = u[12 * 32 + lane];
+  const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+  const float d = gb_half_to_float(((const uint16_t *)(st + 13 * 512))[lane]);
   float acc = 0.f;
 #pragma unroll
   for (int c = 0; c < 2; c++) {
-    uint4 l0 = u[(4 * c + 0) * 32 + lane], l1 = u[(4 * c + 1) * 32 + lane];
-    uint4 l2 = u[(4 * c + 2) * 32 + lane], l3 = u[(4 * c + 3) * 32 + lane];
-    uint4 h0 = u[(8 + 2 * c) * 32 + lane], h1 = u[(9 + 2 * c) * 32 + lane];
-    uint32_t ql[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
-                       l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
-    uint32_t qh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    const uint4 l0 = u[(4 * c + 0) * 32 + lane], l1 = u[(4 * c + 1) * 32 + lane];
+    const uint4 l2 = u[(4 * c + 2) * 32 + lane], l3 = u[(4 * c + 3) * 32 + lane];
+    const uint4 h0 = u[(8 + 2 * c) * 32 + lane], h1 = u[(9 + 2 * c) * 32 + lane];
+    const uint32_t ql[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
+                             l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
+    const uint32_t qh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
 #pragma unroll
     for (int is = 0; is < 2; is++) {
-      int A[4] = {0, 0, 0, 0}, B[4] = {0, 0, 0, 0}, C[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int kk = 0; kk < 4; kk++) {
-        const int k = 4 * is + kk;
-        uint32_t L1 = ql[k], L2 = ql[8 + k], H = qh[k];
-        uint32_t q[4];
-        q[0] = (L1 & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
-        q[1] = (L2 & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
-        q[2] = ((L1 >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
-        q[3] = ((L2 >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int wi = 32 * c + 8 * i + k;  // limb word of elements 128c+32i+4k..+3
-          A[i] = gb_dp4a_us(q[i], xa[wi], A[i]);
-          B[i] = gb_dp4a_us(q[i], xb[wi], B[i]);
-          C[i] = gb_dp4a_us(q[i], xc[wi], C[i]);
-        }
-      }
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        float S = (float)A[i] + (float)B[i] * kL1 + (float)C[i] * kL2;
-        float sc = (float)sc8[8 * c + is + 2 * i];
-        acc += sc * (xs[4 * c + i] * S - 32.f * xsum[8 * c + 2 * i + is]);
+        // elements 128c + 32i + 16is .. +15: limb words 32c + 8i + 4is .. +3
+        const uint4 la = ((const uint4 *)xa)[8 * c + 2 * i + is];
+        const uint4 lb = ((const uint4 *)xb)[8 * c + 2 * i + is];
+        const uint4 lc = ((const uint4 *)xc)[8 * c + 2 * i + is];
+        const uint32_t a4[4] = {la.x, la.y, la.z, la.w}, b4[4] = {lb.x, lb.y, lb.z, lb.w},
+                       c4[4] = {lc.x, lc.y, lc.z, lc.w};
+        int A = 0, B = 0, C = 0;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+          const int k = 4 * is + kk;
+          const uint32_t L = i & 1 ? ql[8 + k] : ql[k];
+          const uint32_t H = qh[k];
+          uint32_t q;
+          if (i == 0) q = (L & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
+          else if (i == 1) q = (L & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
+          else if (i == 2) q = ((L >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
+          else q = ((L >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
+          A = gb_dp4a_us(q, a4[kk], A);
+          B = gb_dp4a_us(q, b4[kk], B);
+          C = gb_dp4a_us(q, c4[kk], C);
+        }
+        const float S = (float)A + (float)(254 * B + C) * kL2;
+        const int si = 8 * c + is + 2 * i;  // scale of this 16-element sub-block
+        const float sc = (float)(int8_t)((scw[si >> 2] >> (8 * (si & 3))) & 0xFFu);
+        acc = fmaf(sc, fmaf(xs[4 * c + i], S, -32.f * xsum[8 * c + 2 * i + is]), acc);
       }
     }
   }
@@ -132,27 +149,28 @@ GB_DEV float sb_q6k(const uint8_t *st, int lane, const uint32_t *xa, const uint3
 }
 
 // Q4_0: eight 32-element blocks per super-block, y = d*(q-8).
-GB_DEV float sb_q40(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                    const uint32_t *xc, const float *xs, const float *xsum) {
+template <>
+GB_DEV float sb_dot<GB_T_Q4_0>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xs, const float *xsum) {
   const uint4 *u = (const uint4 *)st;
-  uint4 h = u[lane];
-  uint32_t dw[4] = {h.x, h.y, h.z, h.w};
+  const uint4 h = u[lane];
+  const uint32_t dw[4] = {h.x, h.y, h.z, h.w};
   float acc = 0.f;
 #pragma unroll
   for (int k = 0; k < 8; k++) {
-    uint4 q = u[(1 + k) * 32 + lane];
-    uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-    uint4 la = ((const uint4 *)xa)[2 * k], ha = ((const uint4 *)xa)[2 * k + 1];
-    uint4 lb = ((const uint4 *)xb)[2 * k], hb = ((const uint4 *)xb)[2 * k + 1];
-    uint4 lc = ((const uint4 *)xc)[2 * k], hc = ((const uint4 *)xc)[2 * k + 1];
-    uint32_t a4[4] = {la.x, la.y, la.z, la.w}, b4[4] = {lb.x, lb.y, lb.z, lb.w},
-             c4[4] = {lc.x, lc.y, lc.z, lc.w};
-    uint32_t A4[4] = {ha.x, ha.y, ha.z, ha.w}, B4[4] = {hb.x, hb.y, hb.z, hb.w},
-             C4[4] = {hc.x, hc.y, hc.z, hc.w};
+    const uint4 q = u[(1 + k) * 32 + lane];
+    const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+    const uint4 la = ((const uint4 *)xa)[2 * k], ha = ((const uint4 *)xa)[2 * k + 1];
+    const uint4 lb = ((const uint4 *)xb)[2 * k], hb = ((const uint4 *)xb)[2 * k + 1];
+    const uint4 lc = ((const uint4 *)xc)[2 * k], hc = ((const uint4 *)xc)[2 * k + 1];
+    const uint32_t a4[4] = {la.x, la.y, la.z, la.w}, b4[4] = {lb.x, lb.y, lb.z, lb.w},
+                   c4[4] = {lc.x, lc.y, lc.z, lc.w};
+    const uint32_t A4[4] = {ha.x, ha.y, ha.z, ha.w}, B4[4] = {hb.x, hb.y, hb.z, hb.w},
+                   C4[4] = {hc.x, hc.y, hc.z, hc.w};
     int Al = 0, Bl = 0, Cl = 0, Ah = 0, Bh = 0, Ch = 0;
 #pragma unroll
     for (int kk = 0; kk < 4; kk++) {
-      uint32_t lo = qw[kk] & 0x0F0F0F0Fu, hi = qw[kk] & 0xF0F0F0F0u;
+      const uint32_t lo = qw[kk] & 0x0F0F0F0Fu, hi = qw[kk] & 0xF0F0F0F0u;
       Al = gb_dp4a_us(lo, a4[kk], Al);
       Bl = gb_dp4a_us(lo, b4[kk], Bl);
       Cl = gb_dp4a_us(lo, c4[kk], Cl);
@@ -160,15 +178,15 @@ GB_DEV float sb_q40(const uint8_t *st, int lane, const uint32_t *xa, const uint3
       Bh = gb_dp4a_us(hi, B4[kk], Bh);
       Ch = gb_dp4a_us(hi, C4[kk], Ch);
     }
-    int A = 16 * Al + Ah, B = 16 * Bl + Bh, C = 16 * Cl + Ch;
-    float S = ((float)A + (float)B * kL1 + (float)C * kL2) * 0.0625f;
-    float d = gb_half_to_float((uint16_t)((dw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu));
-    acc += d * (xs[k] * S - 8.f * (xsum[2 * k] + xsum[2 * k + 1]));
+    const int A = 16 * Al + Ah, B = 16 * Bl + Bh, C = 16 * Cl + Ch;
+    const float S = ((float)A + (float)(254 * B + C) * kL2) * 0.0625f;
+    const float dk = gb_half_to_float((uint16_t)((dw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu));
+    acc = fmaf(dk, fmaf(xs[k], S, -8.f * (xsum[2 * k] + xsum[2 * k + 1])), acc);
   }
   return acc;
 }
 
-// ---- epilogues (one warp, lane l = row 32*tile + l) -----------------------
+// ---- epilogues (one warp, lane l = row 32*rowblock + l) ---------------------
 
 GB_DEV uint64_t argmax_key(float v, uint32_t idx) {
   // larger value wins, then the lower index (model.Argmax, model/model.go:376)
@@ -179,197 +197,244 @@ GB_DEV uint64_t argmax_key(float v, uint32_t idx) {
 
 struct Kp {  // kernel parameters
   GbGemvArgs a;
-  int rb, nrb, stages, sbb_max;
-  unsigned long long units;
+  int rb, nrb, nslot, slot_bytes, xs_max;
+  unsigned units;
 };
 
+template <int EPI>
 GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1) {
   const GbGemvArgs &a = p.a;
   const GbEpiArgs &e = a.e;
   const int lane = threadIdx.x & 31;
-  switch (a.epi) {
-    case GB_EPI_PLAIN: {
-      int r = rbk * 32 + lane;
-      if (r < a.rows) e.y[r] = y0;
-      break;
+  if constexpr (EPI == GB_EPI_PLAIN) {
+    int r = rbk * 32 + lane;
+    if (r < a.rows) e.y[r] = y0;
+  } else if constexpr (EPI == GB_EPI_RESID) {
+    int r = rbk * 32 + lane;
+    float xn = e.x[r] + y0;  // cpu.Add, backend/cpu/cpu.go:60
+    e.x[r] = xn;
+    GbXPack pk{e.out_pack.a, e.out_pack.b, e.out_pack.c, e.out_pack.s, e.out_pack.sum16, e.out_pack.ssq};
+    gb_pack_group(pk, rbk, xn * e.wnorm[r]);
+    float ss = gb_warp_sum(xn * xn);
+    if (lane == 0) pk.ssq[rbk] = ss;
+  } else if constexpr (EPI == GB_EPI_SWIGLU) {  // cpu.SiluMul, backend/cpu/cpu.go:53
+    float g = y0, u = y1;
+    float ex = (float)exp(-(double)g);
+    float act = g / (1.f + ex) * u;
+    GbXPack pk{e.out_pack.a, e.out_pack.b, e.out_pack.c, e.out_pack.s, e.out_pack.sum16, nullptr};
+    gb_pack_group(pk, rbk, act);
+  } else if constexpr (EPI == GB_EPI_QKV) {
+    int r = rbk * 32 + lane;
+    int pos = *e.pos;
+    bool ok = pos >= 0 && pos < e.max_len;
+    if (!ok) {
+      if (lane == 0 && e.err) atomicOr(e.err, GB_DEVERR_POS);
+      return;
     }
-    case GB_EPI_RESID: {
-      int r = rbk * 32 + lane;
-      float xn = e.x[r] + y0;  // cpu.Add, backend/cpu/cpu.go:60
-      e.x[r] = xn;
-      GbXPack pk{e.out_pack.a, e.out_pack.b, e.out_pack.c, e.out_pack.s, e.out_pack.sum16,
-                 e.out_pack.ssq};
-      gb_pack_group(pk, rbk, xn * e.wnorm[r]);
-      float ss = gb_warp_sum(xn * xn);
-      if (lane == 0) pk.ssq[rbk] = ss;
-      break;
+    const int hd = e.head_dim;
+    float partner = __shfl_xor_sync(0xffffffffu, y0, 1);
+    float out = y0;
+    if (r < e.q_rows + e.kv_rows) {  // cpu.RoPE, backend/cpu/cpu.go:69 (float64 math)
+      int rr = r < e.q_rows ? r : r - e.q_rows;
+      int j = (rr % hd) >> 1;
+      const double *cs = e.rope_cs + ((size_t)pos * (hd / 2) + j) * 2;
+      double c = cs[0], s = cs[1];
+      double x0 = (lane & 1) ? (double)partner : (double)y0;
+      double x1 = (lane & 1) ? (double)y0 : (double)partner;
+      out = (lane & 1) ? (float)__dadd_rn(__dmul_rn(x0, s), __dmul_rn(x1, c))
+                       : (float)__dsub_rn(__dmul_rn(x0, c), __dmul_rn(x1, s));
     }
-    case GB_EPI_SWIGLU: {  // cpu.SiluMul, backend/cpu/cpu.go:53
-      float g = y0, u = y1;
-      float ex = (float)exp(-(double)g);
-      float act = g / (1.f + ex) * u;
-      GbXPack pk{e.out_pack.a, e.out_pack.b, e.out_pack.c, e.out_pack.s, e.out_pack.sum16,
-                 nullptr};
-      gb_pack_group(pk, rbk, act);
-      break;
+    if (r < e.q_rows) {
+      e.q_out[r] = out;
+    } else if (r < e.q_rows + e.kv_rows) {
+      int rr = r - e.q_rows, h = rr / hd, dd = rr % hd;
+      if (e.kv_f16) {
+        size_t idx = (((size_t)h * (hd / 8) + dd / 8) * e.max_len + pos) * 8 + (dd & 7);
+        ((uint16_t *)e.kcache)[idx] = gb_float_to_half_rn(out);
+      } else {
+        size_t idx = (((size_t)h * (hd / 4) + dd / 4) * e.max_len + pos) * 4 + (dd & 3);
+        ((float *)e.kcache)[idx] = out;
+      }
+    } else if (r < e.q_rows + 2 * e.kv_rows) {
+      int rr = r - e.q_rows - e.kv_rows, h = rr / hd, dd = rr % hd;
+      size_t idx = ((size_t)h * e.max_len + pos) * hd + dd;
+      if (e.kv_f16)
+        ((uint16_t *)e.vcache)[idx] = gb_float_to_half_rn(out);
+      else
+        ((float *)e.vcache)[idx] = out;
     }
-    case GB_EPI_QKV: {
-      int r = rbk * 32 + lane;
-      int pos = *e.pos;
-      bool ok = pos >= 0 && pos < e.max_len;
-      if (!ok) {
-        if (lane == 0 && e.err) atomicOr(e.err, GB_DEVERR_POS);
-        break;
-      }
-      const int hd = e.head_dim;
-      float partner = __shfl_xor_sync(0xffffffffu, y0, 1);
-      float out = y0;
-      if (r < e.q_rows + e.kv_rows) {  // cpu.RoPE, backend/cpu/cpu.go:69 (float64 math)
-        int rr = r < e.q_rows ? r : r - e.q_rows;
-        int j = (rr % hd) >> 1;
-        const double *cs = e.rope_cs + ((size_t)pos * (hd / 2) + j) * 2;
-        double c = cs[0], s = cs[1];
-        double x0 = (lane & 1) ? (double)partner : (double)y0;
-        double x1 = (lane & 1) ? (double)y0 : (double)partner;
-        out = (lane & 1) ? (float)__dadd_rn(__dmul_rn(x0, s), __dmul_rn(x1, c))
-                         : (float)__dsub_rn(__dmul_rn(x0, c), __dmul_rn(x1, s));
-      }
-      if (r < e.q_rows) {
-        e.q_out[r] = out;
-      } else if (r < e.q_rows + e.kv_rows) {
-        int rr = r - e.q_rows, h = rr / hd, dd = rr % hd;
-        if (e.kv_f16) {
-          size_t idx = (((size_t)h * (hd / 8) + dd / 8) * e.max_len + pos) * 8 + (dd & 7);
-          ((uint16_t *)e.kcache)[idx] = gb_float_to_half_rn(out);
-        } else {
-          size_t idx = (((size_t)h * (hd / 4) + dd / 4) * e.max_len + pos) * 4 + (dd & 3);
-          ((float *)e.kcache)[idx] = out;
-        }
-      } else if (r < e.q_rows + 2 * e.kv_rows) {
-        int rr = r - e.q_rows - e.kv_rows, h = rr / hd, dd = rr % hd;
-        size_t idx = ((size_t)h * e.max_len + pos) * hd + dd;
-        if (e.kv_f16)
-          ((uint16_t *)e.vcache)[idx] = gb_float_to_half_rn(out);
-        else
-          ((float *)e.vcache)[idx] = out;
-      }
-      break;
+  } else if constexpr (EPI == GB_EPI_LOGITS) {
+    int r = rbk * 32 + lane;
+    uint32_t gidx = (uint32_t)(e.row_offset + r);
+    uint64_t key = 0;
+    if (r < a.rows) {
+      e.y[r] = y0;
+      float v = y0;
+      // NaN never wins, except at index 0 where model.Argmax keeps it.
+      if (isnan(v)) v = gidx == 0 ? INFINITY : -INFINITY;
+      key = argmax_key(v, gidx);
     }
-    case GB_EPI_LOGITS: {
-      int r = rbk * 32 + lane;
-      uint32_t gidx = (uint32_t)(e.row_offset + r);
-      uint64_t key = 0;
-      if (r < a.rows) {
-        e.y[r] = y0;
-        float v = y0;
-        // NaN never wins, except at index 0 where model.Argmax keeps it.
-        if (isnan(v)) v = gidx == 0 ? INFINITY : -INFINITY;
-        key = argmax_key(v, gidx);
-      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        uint64_t k2 = __shfl_xor_sync(0xffffffffu, key, o);
-        key = k2 > key ? k2 : key;
-      }
-      if (lane == 0) {
-        unsigned long long *best = e.best;
-        atomicMax(best, (unsigned long long)key);
+    for (int o = 16; o > 0; o >>= 1) {
+      uint64_t k2 = __shfl_xor_sync(0xffffffffu, key, o);
+      key = k2 > key ? k2 : key;
+    }
+    if (lane == 0) {
+      atomicMax(e.best, (unsigned long long)key);
+      __threadfence();
+      unsigned done = atomicAdd(e.counter, 1u);
+      if (done + 1 == (unsigned)p.nrb) {
         __threadfence();
-        unsigned done = atomicAdd(e.counter, 1u);
-        if (done + 1 == (unsigned)p.nrb) {
-          __threadfence();
-          unsigned long long k = atomicAdd(best, 0ull);
-          int32_t tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
-          if (e.token_out) *e.token_out = tok;
-          if (e.key_out) *e.key_out = k;  // tensor parallel: reduced across ranks next
-          if (e.token_hist) {
-            int pos = *e.pos;
-            if (pos >= 0 && pos < e.max_len) e.token_hist[pos] = tok;
-          }
-          *best = 0ull;
-          *e.counter = 0u;
+        unsigned long long k = atomicAdd(e.best, 0ull);
+        int32_t tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+        if (e.token_out) *e.token_out = tok;
+        if (e.key_out) *e.key_out = k;  // tensor parallel: reduced across ranks next
+        if (e.token_hist) {
+          int pos = *e.pos;
+          if (pos >= 0 && pos < e.max_len) e.token_hist[pos] = tok;
         }
+        *e.best = 0ull;
+        *e.counter = 0u;
       }
-      break;
     }
   }
 }
 
-// Warp `w` of the grid owns units [U*w/Wt, U*(w+1)/Wt).
-GB_DEV unsigned long long unit_begin(unsigned long long U, unsigned long long Wt,
-                                     unsigned long long w) {
-  return U * w / Wt;
+// CTA b of G owns units [U*b/G, U*(b+1)/G) (the product fits 64 bits).
+GB_DEV unsigned ubeg(unsigned U, unsigned G, unsigned b) {
+  return (unsigned)(((unsigned long long)U * b) / G);
+}
+// CTA whose range contains unit u.
+GB_DEV unsigned cta_of_unit(unsigned U, unsigned G, unsigned u) {
+  unsigned b = (unsigned)(((unsigned long long)u * G) / U);
+  while (b > 0 && ubeg(U, G, b) > u) b--;
+  while (b + 1 < G && ubeg(U, G, b + 1) <= u) b++;
+  return b;
 }
 
-// Warp (of Wt) whose range contains unit u.
-GB_DEV unsigned long long warp_of_unit(unsigned long long U, unsigned long long Wt,
-                                       unsigned long long u) {
-  unsigned long long w = (u * Wt) / U;
-  while (w > 0 && unit_begin(U, Wt, w) > u) w--;
-  while (w + 1 < Wt && unit_begin(U, Wt, w + 1) <= u) w++;
-  return w;
+template <int T>
+__device__ __noinline__ float sb_dot_outlined(const uint8_t *st, int lane, const uint32_t *xa,
+                                              const uint32_t *xb, const uint32_t *xc, const float *xs,
+                                              const float *xsum) {
+  return sb_dot<T>(st, lane, xa, xb, xc, xs, xsum);
 }
 
-__global__ void __launch_bounds__(512) gemv_kernel(const Kp p) {
+template <int TA, int TB>
+GB_DEV float decode(int ty, const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                    const uint32_t *xc, const float *xs, const float *xsum) {
+  if (TA == TB || ty == TA) return sb_dot<TA>(st, lane, xa, xb, xc, xs, xsum);
+  return sb_dot<TB>(st, lane, xa, xb, xc, xs, xsum);
+}
+
+// The CTA's unit range is cut into segments, one per row-block it touches.
+// Warp w takes units seg_begin + w, seg_begin + w + W, ... of every segment,
+// so a segment's partial sums end up in shared memory and are added in warp
+// order by one reducer warp; only a segment that continues in another CTA
+// goes through global memory.
+template <int TA, int TB, int EPI>
+__global__ void __launch_bounds__(512, 1) gemv_kernel(const Kp p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const GbGemvArgs &a = p.a;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-  const int rb = p.rb, nsb = a.nsb, stages = p.stages, sbb_max = p.sbb_max;
-  const unsigned long long U = p.units, Wt = (unsigned long long)gridDim.x * W;
-  const unsigned long long gw = (unsigned long long)blockIdx.x * W + warp;
-  const unsigned long long u0 = unit_begin(U, Wt, gw), u1 = unit_begin(U, Wt, gw + 1);
-  const int n = (int)(u1 - u0);
+  const int rb = p.rb, nsb = a.nsb, nslot = p.nslot, slot_bytes = p.slot_bytes;
+  const unsigned U = p.units, G = gridDim.x, b = blockIdx.x;
+  const unsigned cu0 = ubeg(U, G, b), cu1 = ubeg(U, G, b + 1);
 
-  // shared memory: [stages rings][mbarriers][x pack planes][x scales][x sums][reduce]
-  uint8_t *ring = smem + (size_t)warp * stages * rb * sbb_max;
-  uint64_t *bars = (uint64_t *)(smem + (size_t)W * stages * rb * sbb_max) + warp * stages;
-  const int K = nsb * 256;
-  // barrier region rounded to 128 bytes: the pack planes below take 16-byte vector accesses
-  uint8_t *xbase = smem + (size_t)W * stages * rb * sbb_max + (((size_t)W * stages * 8 + 127) & ~(size_t)127);
+  // shared memory: [W][nslot] unit slots | mbarriers | pack planes a,b,c |
+  // scales | sums | 2 x [W][64] segment partials | misc
+  uint8_t *ring = smem + (size_t)warp * nslot * slot_bytes;
+  uint64_t *bars = (uint64_t *)(smem + (size_t)W * nslot * slot_bytes) + warp * nslot;
+  const int XS = p.xs_max;
+  uint8_t *xbase = smem + (size_t)W * nslot * slot_bytes + (((size_t)W * nslot * 8 + 127) & ~(size_t)127);
   uint32_t *xa_s = (uint32_t *)xbase;
-  uint32_t *xb_s = xa_s + K / 4;
-  uint32_t *xc_s = xb_s + K / 4;
-  float *xs_s = (float *)(xc_s + K / 4);
-  float *xsum_s = xs_s + K / 32;
-  float *misc = xsum_s + K / 16;  // [0] = RMSNorm inverse
+  uint32_t *xb_s = xa_s + XS * 64;
+  uint32_t *xc_s = xb_s + XS * 64;
+  float *xs_s = (float *)(xc_s + XS * 64);
+  float *xsum_s = xs_s + XS * 8;
+  float *psum = xsum_s + XS * 16;  // [2][W][64]
+  __shared__ double red[16];
+  __shared__ float inv_s;
 
-  const size_t sbb_a = (size_t)gb_tiled_sb_bytes(a.type_a), sbb_b = (size_t)gb_tiled_sb_bytes(a.type_b);
-  auto tile_type = [&](int tile) { return tile < a.split_tile ? a.type_a : a.type_b; };
+  const size_t sbb_a = (size_t)gb_tiled_sb_bytes(TA), sbb_b = (size_t)gb_tiled_sb_bytes(TB);
   auto tile_ptr = [&](int tile, int sb) -> const uint8_t * {
-    if (tile < a.split_tile) return a.w + ((size_t)tile * nsb + sb) * sbb_a;
+    if (TA == TB || tile < a.split_tile) return a.w + ((size_t)tile * nsb + sb) * sbb_a;
     return a.w + (size_t)a.split_tile * nsb * sbb_a + ((size_t)(tile - a.split_tile) * nsb + sb) * sbb_b;
   };
-  auto issue = [&](int i) {  // bring unit u0+i into ring slot i % stages (lane 0 only)
-    unsigned long long u = u0 + i;
-    int rbk = (int)(u / nsb), sb = (int)(u % nsb), s = i % stages;
+  auto tile_bytes = [&](int tile) -> uint32_t {
+    return (TA == TB || tile < a.split_tile) ? (uint32_t)sbb_a : (uint32_t)sbb_b;
+  };
+  auto issue = [&](unsigned u, int s) {  // unit u into slot s (lane 0 only)
+    const int irbk = (int)(u / (unsigned)nsb), isb = (int)(u % (unsigned)nsb);
     uint32_t bytes = 0;
-    for (int t = 0; t < rb; t++) bytes += (uint32_t)gb_tiled_sb_bytes(tile_type(rbk * rb + t));
+    for (int t = 0; t < rb; t++) bytes += tile_bytes(irbk * rb + t);
     gb_mbar_expect_tx(&bars[s], bytes);
+    uint32_t off = 0;
     for (int t = 0; t < rb; t++) {
-      int tile = rbk * rb + t;
-      gb_bulk_g2s(ring + ((size_t)s * rb + t) * sbb_max, tile_ptr(tile, sb),
-                  (uint32_t)gb_tiled_sb_bytes(tile_type(tile)), &bars[s]);
+      const int tile = irbk * rb + t;
+      gb_bulk_g2s(ring + (size_t)s * slot_bytes + off, tile_ptr(tile, isb), tile_bytes(tile), &bars[s]);
+      off += tile_bytes(tile);
     }
   };
+  // this warp's units in order: in each segment [start, end), the units
+  // start + warp, start + warp + W, ... (none when the segment is shorter)
+  auto unit_at = [&](unsigned seg_start) -> unsigned {  // first unit at or after a segment start
+    while (seg_start < cu1) {
+      const unsigned seg_end = min(cu1, (seg_start / (unsigned)nsb + 1) * (unsigned)nsb);
+      if (seg_start + (unsigned)warp < seg_end) return seg_start + (unsigned)warp;
+      seg_start = seg_end;
+    }
+    return cu1;
+  };
+  auto next_unit = [&](unsigned u) -> unsigned {  // the warp's unit after u (or cu1)
+    const unsigned seg_end = min(cu1, (u / (unsigned)nsb + 1) * (unsigned)nsb);
+    if (u + (unsigned)W < seg_end) return u + (unsigned)W;
+    return unit_at(seg_end);
+  };
+  const unsigned first = unit_at(cu0);
 
+  // 0. let the next kernel's CTAs start (they stream their weights meanwhile)
+  gb_grid_dep_launch();
   // 1. weights do not depend on the previous kernel: start their copies first
   if (lane == 0) {
-    for (int s = 0; s < stages; s++) gb_mbar_init(&bars[s], 1);
+    for (int s = 0; s < nslot; s++) gb_mbar_init(&bars[s], 1);
     gb_mbar_fence_init();
   }
   __syncwarp();
-  if (lane == 0)
-    for (int i = 0; i < n && i < stages; i++) issue(i);
+  unsigned iu = first;  // next unit to issue
+  int issued = 0;
+  for (; iu < cu1 && issued < nslot; issued++) {
+    if (lane == 0) issue(iu, issued);
+    iu = next_unit(iu);
+  }
 
-  // 2. the activation pack is produced by the preceding kernel
+  // 2. the activation pack (and the norm's sums of squares) come from the
+  // preceding kernel: one round trip for all of it
   gb_grid_dep_wait();
+  const int nsbs = (cu1 - cu0) >= (unsigned)nsb ? nsb : (int)(cu1 - cu0);
+  const int sbf = (int)(cu0 % (unsigned)nsb);
   {
-    // RMSNorm inverse from the per-group sums of squares (cpu.RMSNorm,
-    // backend/cpu/cpu.go:17: inv = 1/sqrt(sum/n + eps) in float64)
-    if (a.in_ssq) {
-      __shared__ double red[16];
-      double ss = 0;
-      for (int g = threadIdx.x; g < K / 32; g += blockDim.x) ss += (double)a.in_ssq[g];
+    double ss = 0;
+    if (a.in_ssq)
+      for (int g = threadIdx.x; g < nsb * 8; g += blockDim.x) ss += (double)__ldcg(a.in_ssq + g);
+    for (int i = threadIdx.x; i < nsbs * 48; i += blockDim.x) {  // 3 planes x 16 uint4 per sb
+      const int plane = i / (nsbs * 16), rest = i - plane * (nsbs * 16);
+      const int ls = rest >> 4, v = rest & 15;
+      int sb = sbf + ls;
+      if (sb >= nsb) sb -= nsb;
+      const int8_t *src = plane == 0 ? a.in.a : plane == 1 ? a.in.b : a.in.c;
+      uint32_t *dst = plane == 0 ? xa_s : plane == 1 ? xb_s : xc_s;
+      ((uint4 *)(dst + ls * 64))[v] = __ldcg((const uint4 *)(src + sb * 256) + v);
+    }
+    for (int i = threadIdx.x; i < nsbs * 24; i += blockDim.x) {
+      const int ls = i / 24, v = i - ls * 24;
+      int sb = sbf + ls;
+      if (sb >= nsb) sb -= nsb;
+      if (v < 8)
+        xs_s[ls * 8 + v] = __ldcg(a.in.s + sb * 8 + v);
+      else
+        xsum_s[ls * 16 + v - 8] = __ldcg(a.in.sum16 + sb * 16 + v - 8);
+    }
+    if (a.in_ssq) {  // cpu.RMSNorm, backend/cpu/cpu.go:17: inv = 1/sqrt(sum/n + eps), float64
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       if (lane == 0) red[warp] = ss;
@@ -377,117 +442,111 @@ __global__ void __launch_bounds__(512) gemv_kernel(const Kp p) {
       if (threadIdx.x == 0) {
         double t = 0;
         for (int w2 = 0; w2 < W; w2++) t += red[w2];
-        misc[0] = (float)(1.0 / sqrt(t / (double)K + (double)a.eps));
+        inv_s = (float)(1.0 / sqrt(t / (double)(nsb * 256) + (double)a.eps));
       }
       __syncthreads();
-    }
-    const float inv = a.in_ssq ? misc[0] : 1.f;
-    // Stage the pack for the super-blocks this CTA touches.
-    const unsigned long long cu0 = unit_begin(U, Wt, (unsigned long long)blockIdx.x * W);
-    const unsigned long long cu1 = unit_begin(U, Wt, (unsigned long long)(blockIdx.x + 1) * W);
-    int nsbs = (cu1 - cu0) >= (unsigned long long)nsb ? nsb : (int)(cu1 - cu0);
-    int sbf = (int)(cu0 % nsb);
-    for (int i = threadIdx.x; i < nsbs * 16 * 3; i += blockDim.x) {
-      int plane = i / (nsbs * 16), rest = i % (nsbs * 16);
-      int sb = (sbf + rest / 16) % nsb, v = rest % 16;
-      const int8_t *src = plane == 0 ? a.in.a : plane == 1 ? a.in.b : a.in.c;
-      uint32_t *dst = plane == 0 ? xa_s : plane == 1 ? xb_s : xc_s;
-      ((uint4 *)(dst + sb * 64))[v] = __ldcg((const uint4 *)(src + sb * 256) + v);
-    }
-    for (int i = threadIdx.x; i < nsbs * 24; i += blockDim.x) {
-      int sb = (sbf + i / 24) % nsb, v = i % 24;
-      if (v < 8)
-        xs_s[sb * 8 + v] = __ldcg(a.in.s + sb * 8 + v) * inv;
-      else
-        xsum_s[sb * 16 + v - 8] = __ldcg(a.in.sum16 + sb * 16 + v - 8) * inv;
+      const float inv = inv_s;
+      for (int i = threadIdx.x; i < nsbs * 24; i += blockDim.x) {
+        const int ls = i / 24, v = i - ls * 24;
+        if (v < 8) xs_s[ls * 8 + v] *= inv;
+        else xsum_s[ls * 16 + v - 8] *= inv;
+      }
     }
   }
   __syncthreads();
-  gb_grid_dep_launch();
 
-  // 3. stream the units
-  float acc0 = 0.f, acc1 = 0.f;
+  // 3. stream the units segment by segment
   bool timeout = false;
-  int cur = n > 0 ? (int)(u0 / nsb) : 0;
-  unsigned long long seg = u0;
-  auto flush = [&](int rbk, unsigned long long s_begin, unsigned long long s_end) {
-    const unsigned long long R0 = (unsigned long long)rbk * nsb, R1 = R0 + nsb;
-    if (s_begin == R0 && s_end == R1) {
-      epilogue(p, rbk, acc0, acc1);
-      return;
-    }
-    const int which = u0 >= R0 ? 0 : 1;
-    float *slot = a.e.part + (gw * 2 + which) * 64;
-    slot[lane] = acc0;
-    slot[32 + lane] = acc1;
-    __threadfence();
-    __syncwarp();
-    unsigned done = 0;
-    if (lane == 0) done = atomicAdd(a.e.tile_counter + rbk, (unsigned)(s_end - s_begin)) + (unsigned)(s_end - s_begin);
-    done = __shfl_sync(0xffffffffu, done, 0);
-    if (done != (unsigned)nsb) return;
-    __threadfence();
-    const unsigned long long wf = warp_of_unit(U, Wt, R0), wl = warp_of_unit(U, Wt, R1 - 1);
-    float y0 = 0.f, y1 = 0.f;
-    for (unsigned long long w2 = wf; w2 <= wl; w2++) {
-      unsigned long long b2 = unit_begin(U, Wt, w2), e2 = unit_begin(U, Wt, w2 + 1);
-      if (b2 == e2) continue;
-      const float *sl = a.e.part + (w2 * 2 + (b2 >= R0 ? 0 : 1)) * 64;
-      y0 += __ldcg(sl + lane);
-      y1 += __ldcg(sl + 32 + lane);
-    }
-    if (lane == 0) a.e.tile_counter[rbk] = 0u;
-    epilogue(p, rbk, y0, y1);
-  };
-
-  int issued = n < stages ? n : stages;
-  int i = 0;
-  for (; i < n; i++) {
-    const unsigned long long u = u0 + i;
-    const int rbk = (int)(u / nsb), sb = (int)(u % nsb), s = i % stages;
-    if (rbk != cur) {
-      flush(cur, seg, u);
-      acc0 = acc1 = 0.f;
-      cur = rbk;
-      seg = u;
-    }
-    if (!gb_mbar_wait(&bars[s], (uint32_t)((i / stages) & 1))) {
-      timeout = true;
-      break;
-    }
-    const uint32_t *xa = xa_s + sb * 64, *xb = xb_s + sb * 64, *xc = xc_s + sb * 64;
-    const float *xs = xs_s + sb * 8, *xsum = xsum_s + sb * 16;
-#pragma unroll 1
-    for (int t = 0; t < rb; t++) {
-      const uint8_t *st = ring + ((size_t)s * rb + t) * sbb_max;
-      int ty = tile_type(rbk * rb + t);
-      float v = ty == GB_T_Q4_K ? sb_q4k(st, lane, xa, xb, xc, xs, xsum)
-              : ty == GB_T_Q6_K ? sb_q6k(st, lane, xa, xb, xc, xs, xsum)
-                                : sb_q40(st, lane, xa, xb, xc, xs, xsum);
-      if (t == 0) acc0 += v; else acc1 += v;
-    }
-    __syncwarp();
-    if (i + stages < n) {
-      if (lane == 0) {
-        gb_fence_proxy_async();
-        issue(i + stages);
+  int consumed = 0;
+  unsigned cu = first;  // next unit to consume
+  int nseg = 0;
+  for (unsigned s0 = cu0; s0 < cu1; nseg++) {
+    const int rbk = (int)(s0 / (unsigned)nsb);
+    const unsigned s1 = min(cu1, (unsigned)(rbk + 1) * (unsigned)nsb);
+    float acc0 = 0.f, acc1 = 0.f;
+    while (cu < s1) {
+      const int s = consumed % nslot;
+      if (!timeout && !gb_mbar_wait(&bars[s], (uint32_t)((consumed / nslot) & 1))) timeout = true;
+      if (!timeout) {
+        int ls = (int)(cu % (unsigned)nsb) - sbf;
+        if (ls < 0) ls += nsb;
+        const uint32_t *xa = xa_s + ls * 64, *xb = xb_s + ls * 64, *xc = xc_s + ls * 64;
+        const float *xs = xs_s + ls * 8, *xsum = xsum_s + ls * 16;
+        const uint8_t *st = ring + (size_t)s * slot_bytes;
+        if constexpr (EPI == GB_EPI_SWIGLU) {
+          // gate then up (the up tile follows the gate tile in the slot); one
+          // decode at a time keeps the register footprint of a single tile
+          acc0 += sb_dot_outlined<TA>(st, lane, xa, xb, xc, xs, xsum);
+          acc1 += sb_dot_outlined<TA>(st + sbb_a, lane, xa, xb, xc, xs, xsum);
+        } else {
+          acc0 += decode<TA, TB>(rbk * rb < a.split_tile ? TA : TB, st, lane, xa, xb, xc, xs, xsum);
+        }
       }
-      issued++;
+      __syncwarp();
+      consumed++;
+      if (iu < cu1) {
+        if (lane == 0 && !timeout) {
+          gb_fence_proxy_async();
+          issue(iu, s);
+        }
+        iu = next_unit(iu);
+        issued++;
+      }
+      cu = next_unit(cu);
     }
+    float *ps = psum + (size_t)(nseg & 1) * W * 64;
+    ps[warp * 64 + lane] = acc0;
+    ps[warp * 64 + 32 + lane] = acc1;
+    __syncthreads();
+    if (warp == nseg % W) {  // reducer of this segment (sum in warp order)
+      float y0 = 0.f, y1 = 0.f;
+      const int wmax = min(W, (int)(s1 - s0));
+      for (int w2 = 0; w2 < wmax; w2++) {
+        y0 += ps[w2 * 64 + lane];
+        y1 += ps[w2 * 64 + 32 + lane];
+      }
+      const unsigned R0 = (unsigned)rbk * nsb, R1 = R0 + nsb;
+      if (s0 == R0 && s1 == R1) {
+        epilogue<EPI>(p, rbk, y0, y1);
+      } else {
+        // the row-block continues in another CTA: global partial per CTA
+        const int which = cu0 >= R0 ? 0 : 1;
+        float *slot = a.e.part + ((size_t)b * 2 + which) * 64;
+        slot[lane] = y0;
+        slot[32 + lane] = y1;
+        __threadfence();
+        __syncwarp();
+        unsigned done = 0;
+        if (lane == 0) done = atomicAdd(a.e.tile_counter + rbk, s1 - s0) + (s1 - s0);
+        done = __shfl_sync(0xffffffffu, done, 0);
+        if (done == (unsigned)nsb) {
+          __threadfence();
+          const unsigned bf = cta_of_unit(U, G, R0), bl = cta_of_unit(U, G, R1 - 1);
+          float z0 = 0.f, z1 = 0.f;
+          for (unsigned b2 = bf; b2 <= bl; b2++) {
+            const unsigned c0 = ubeg(U, G, b2), c1 = ubeg(U, G, b2 + 1);
+            if (c0 == c1) continue;
+            const float *sl = a.e.part + ((size_t)b2 * 2 + (c0 >= R0 ? 0 : 1)) * 64;
+            z0 += __ldcg(sl + lane);
+            z1 += __ldcg(sl + 32 + lane);
+          }
+          if (lane == 0) a.e.tile_counter[rbk] = 0u;
+          epilogue<EPI>(p, rbk, z0, z1);
+        }
+      }
+    }
+    s0 = s1;
   }
   if (timeout) {
     if (lane == 0 && a.e.err) atomicOr(a.e.err, GB_DEVERR_TIMEOUT);
     // let the copies still in flight land (bounded) before the CTA exits
-    for (int j = i + 1; j < issued; j++) (void)gb_mbar_wait(&bars[j % stages], (uint32_t)((j / stages) & 1));
-    return;
+    for (int j = consumed; j < issued; j++) (void)gb_mbar_wait(&bars[j % nslot], (uint32_t)((j / nslot) & 1));
   }
-  if (n > 0) flush(cur, seg, u1);
 }
 
 // ---- repack raw ggml rows into the tiled layout (load time) ---------------
 __global__ void repack_kernel(int typ, const uint8_t *raw, int rows, int nsb, int ntiles,
                               uint8_t *out) {
-  const int units = gb_tiled_units(typ);
   const long long sbb = gb_tiled_sb_bytes(typ);
   const long long rawsb = gb_sb_raw_bytes(typ);
   const long long rowbytes = rawsb * nsb;
@@ -501,7 +560,6 @@ __global__ void repack_kernel(int typ, const uint8_t *raw, int rows, int nsb, in
     uint8_t *dst = out + ((long long)tile * nsb + sb) * sbb;
     const uint8_t *src = raw + (long long)row * rowbytes + (long long)sb * rawsb;
     for (int b = 0; b < rawsb; b++) dst[gb_tiled_offset(typ, lane, b)] = row < rows ? src[b] : 0;
-    (void)units;
   }
 }
 
@@ -524,9 +582,47 @@ int sms() {
   return g_sms;
 }
 
-size_t gemv_smem(int warps, int stages, int rb, int sbb_max, int K) {
-  return (size_t)warps * stages * rb * sbb_max + (((size_t)warps * stages * 8 + 127) & ~(size_t)127) + 3 * (size_t)K +
-         4 * (size_t)(K / 32 + K / 16) + 64;
+size_t gemv_smem(int warps, int nslot, int slot_bytes, int xs_max) {
+  return (size_t)warps * nslot * slot_bytes + (((size_t)warps * nslot * 8 + 127) & ~(size_t)127) +
+         (size_t)xs_max * (3 * 256 + 4 * 24) + (size_t)2 * warps * 64 * 4 + 64;
+}
+
+using KernelFn = void (*)(Kp);
+
+template <int TA, int TB>
+KernelFn pick_epi(int epi) {
+  switch (epi) {
+    case GB_EPI_PLAIN: return gemv_kernel<TA, TB, GB_EPI_PLAIN>;
+    case GB_EPI_QKV: return gemv_kernel<TA, TB, GB_EPI_QKV>;
+    case GB_EPI_RESID: return gemv_kernel<TA, TB, GB_EPI_RESID>;
+    case GB_EPI_SWIGLU: return gemv_kernel<TA, TB, GB_EPI_SWIGLU>;
+    case GB_EPI_LOGITS: return gemv_kernel<TA, TB, GB_EPI_LOGITS>;
+  }
+  return nullptr;
+}
+
+KernelFn pick(int ta, int tb, int epi) {
+  if (ta == tb) {
+    if (ta == GB_T_Q4_K) return pick_epi<GB_T_Q4_K, GB_T_Q4_K>(epi);
+    if (ta == GB_T_Q6_K) return pick_epi<GB_T_Q6_K, GB_T_Q6_K>(epi);
+    if (ta == GB_T_Q4_0) return pick_epi<GB_T_Q4_0, GB_T_Q4_0>(epi);
+  } else if (ta == GB_T_Q4_K && tb == GB_T_Q6_K && epi == GB_EPI_QKV) {
+    return gemv_kernel<GB_T_Q4_K, GB_T_Q6_K, GB_EPI_QKV>;
+  } else if (ta == GB_T_Q6_K && tb == GB_T_Q4_K && epi == GB_EPI_QKV) {
+    return gemv_kernel<GB_T_Q6_K, GB_T_Q4_K, GB_EPI_QKV>;
+  }
+  return nullptr;
+}
+
+int smem_optin() {
+  static int v = 0;
+  if (!v) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (v <= 0) v = 227 * 1024;
+  }
+  return v;
 }
 
 }  // namespace
@@ -542,9 +638,9 @@ int gb_repack_launch(int typ, const uint8_t *raw, int rows, int cols, uint8_t *t
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: repack: %d columns of type %d", cols, typ);
   int ntiles = (rows + 31) / 32, nsb = cols / 256;
   long long total = (long long)ntiles * nsb * 32;
-  int blocks = (int)((total + 255) / 256);
-  if (blocks > 65535 * 8) blocks = 65535 * 8;
-  repack_kernel<<<blocks, 256, 0, st>>>(typ, raw, rows, nsb, ntiles, tiled);
+  long long blocks = (total + 255) / 256;
+  if (blocks > 65535LL * 8) blocks = 65535LL * 8;
+  repack_kernel<<<(unsigned)blocks, 256, 0, st>>>(typ, raw, rows, nsb, ntiles, tiled);
   GB_CUDA(cudaGetLastError(), "gpu: repack");
   return GB_OK;
 }
@@ -561,7 +657,7 @@ GbGemvPlan gb_gemv_plan(int ntiles, int nsb, int epi, int nsm) {
   GbGemvPlan p;
   p.rb = epi == GB_EPI_SWIGLU ? 2 : 1;
   p.warps = 8;
-  p.stages = p.rb == 2 ? 2 : 3;
+  p.stages = 2;
   p.ks = 1;
   (void)ntiles;
   (void)nsb;
@@ -571,8 +667,9 @@ GbGemvPlan gb_gemv_plan(int ntiles, int nsb, int epi, int nsm) {
 
 int gb_gemv_scratch_floats(int ntiles, const GbGemvPlan &p) {
   (void)ntiles;
-  // two 64-float partial slots per warp of the persistent grid
-  return sms() * 2 * p.warps * 2 * 64;
+  (void)p;
+  // two 64-float partial slots per warp of the persistent grid (<= 8 CTAs of 8 warps per SM)
+  return sms() * 8 * 8 * 2 * 64;
 }
 
 int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st, bool pdl) {
@@ -581,40 +678,104 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   p.a = a;
   p.rb = plan.rb;
   if (a.ntiles % p.rb) return gb_fail(GB_ERR_INVALID, "gpu: gemv: tiles not paired");
+  const int ta = a.type_a, tb = a.split_tile < a.ntiles ? a.type_b : a.type_a;
+  p.a.type_b = tb;
+  KernelFn fn = pick(ta, tb, a.epi);
+  if (!fn) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: types %d/%d with epilogue %d", ta, tb, a.epi);
+  if (p.rb == 2 && ta != tb) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: gate/up types differ");
   p.nrb = a.ntiles / p.rb;
-  p.units = (unsigned long long)p.nrb * a.nsb;
-  bool q6 = a.type_a == GB_T_Q6_K || (a.split_tile < a.ntiles && a.type_b == GB_T_Q6_K);
-  p.sbb_max = q6 ? 6720 : 4608;
-  int warps = plan.warps, stages = plan.stages;
-  const int K = a.nsb * 256;
-  // fit the shared memory budget (227 KB per CTA)
-  size_t smem = gemv_smem(warps, stages, p.rb, p.sbb_max, K);
-  while (smem > 220 * 1024 && stages > 1) smem = gemv_smem(warps, --stages, p.rb, p.sbb_max, K);
-  while (smem > 220 * 1024 && warps > 1) smem = gemv_smem(--warps, stages, p.rb, p.sbb_max, K);
-  if (smem > 220 * 1024) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: K=%d too large", K);
-  p.stages = stages;
-  int per_sm = (int)((227 * 1024) / (smem + 1024));
-  if (per_sm < 1) per_sm = 1;
-  if (per_sm > 2) per_sm = 2;
-  long long grid = (long long)sms() * per_sm;
-  long long need = (long long)((p.units + warps - 1) / warps);
-  if (grid > need) grid = need;
-  if (grid < 1) grid = 1;
-  if (grid * warps > (long long)gb_gemv_scratch_floats(a.ntiles, plan) / 128)
-    grid = gb_gemv_scratch_floats(a.ntiles, plan) / 128 / warps;
-  static int smem_cap = 0;
-  if (!smem_cap) {
-    int dev = 0, optin = 0;
+  p.units = (unsigned)p.nrb * (unsigned)a.nsb;
+  const int sbb_max = std::max(gb_tiled_sb_bytes(ta), gb_tiled_sb_bytes(tb));
+  p.slot_bytes = p.rb * sbb_max;
+  const int nsm = sms();
+  const long long cap = smem_optin();
+  // opt in to the shared memory and learn the register count (once per kernel)
+  static KernelFn seen[64];
+  static int seen_regs[64];
+  static int nseen = 0;
+  int regs = -1;
+  for (int i = 0; i < nseen; i++)
+    if (seen[i] == fn) regs = seen_regs[i];
+  if (regs < 0) {
     cudaFuncAttributes fa;
-    GB_CUDA(cudaGetDevice(&dev), "gpu: gemv");
-    GB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev), "gpu: gemv");
-    GB_CUDA(cudaFuncGetAttributes(&fa, gemv_kernel), "gpu: gemv");
-    int cap = optin - (int)fa.sharedSizeBytes;
-    GB_CUDA(cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cap),
+    GB_CUDA(cudaFuncGetAttributes(&fa, fn), "gpu: gemv");
+    GB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(cap - (long long)fa.sharedSizeBytes)),
             "gpu: gemv: shared memory attribute");
-    smem_cap = cap;
+    regs = fa.numRegs;
+    if (nseen < 64) {
+      seen[nseen] = fn;
+      seen_regs[nseen++] = regs;
+    }
   }
-  if (smem > (size_t)smem_cap) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: %zu bytes of shared memory", smem);
+  // Launch shape: (warps per CTA, slots per warp, CTAs per SM) that fits the
+  // SM's shared memory, threads and registers and maximises the copies a
+  // warp keeps in flight (slots - 1) times the resident warps.
+  // GB_GEMV_SHAPE_<PLAIN|QKV|RESID|SWIGLU|LOGITS> or GB_GEMV_SHAPE = "w,s,c"
+  // force a shape when it fits (sweeps); otherwise the choice is automatic.
+  static const char *epi_names[] = {"PLAIN", "QKV", "RESID", "SWIGLU", "LOGITS"};
+  int fw = 0, fs = 0, fc = 0;
+  {
+    char key[64];
+    snprintf(key, sizeof key, "GB_GEMV_SHAPE_%s", epi_names[a.epi]);
+    const char *e = getenv(key);
+    if (!e) e = getenv("GB_GEMV_SHAPE");
+    if (e && sscanf(e, "%d,%d,%d", &fw, &fs, &fc) != 3) fw = fs = fc = 0;
+  }
+  const long long regs_per_warp = ((long long)regs * 32 + 255) / 256 * 256;
+  double best = -1;
+  size_t smem = 0;
+  long long grid = 0;
+  int nslot = 0, warps = 0;
+  // Automatic shape. Grid: one row-block per CTA when there are at most two
+  // per SM (no partial sums leave the CTA), else one persistent CTA per SM
+  // walking a contiguous range of units. CTA: at most as many warps as a row
+  // has super-blocks; the most warps, then two slots over one, within a
+  // shared-memory budget (GB_SMEM_BUDGET; default: half an SM when two CTAs
+  // must share it, the whole SM otherwise).
+  const bool per_rb = p.nrb <= 2 * nsm;
+  const int ctas_per_sm = per_rb && p.nrb > nsm ? 2 : 1;
+  long long budget = ctas_per_sm == 2 ? 110 * 1024 : 220 * 1024;
+  if (const char *e = getenv("GB_SMEM_BUDGET")) budget = atoll(e);
+  for (int pass = fw ? 0 : 1; pass < 2 && !nslot; pass++)
+  for (int w : {16, 12, 8, 4}) {  // the kernel is built for at most 512 threads
+    if (pass == 0 && w != fw) continue;
+    if (pass == 1 && w > a.nsb && w > 4) continue;
+    for (int s = 1; s <= 8; s++) {
+      if (pass == 0 && s != fs) continue;
+      if (pass == 1 && s > 3) continue;
+      for (int c = 1; c <= 8; c++) {
+        if (pass == 0 && c != fc) continue;
+        if (pass == 1 && c != ctas_per_sm) continue;
+        if (w * c > 64 || regs_per_warp * w * c > 65536) continue;
+        long long g = per_rb ? p.nrb : (long long)nsm * c;
+        if (!per_rb && g > (long long)p.units) g = p.units;
+        if (g < 1) g = 1;
+        if (g * 128 > (long long)gb_gemv_scratch_floats(a.ntiles, plan)) continue;
+        int xs = (int)std::min<long long>(a.nsb, ((long long)p.units + g - 1) / g + 1);
+        size_t sm = gemv_smem(w, s, p.slot_bytes, xs);
+        if ((long long)(sm + 1024) * c > 228LL * 1024 || (long long)sm > cap - 256) continue;
+        if (pass == 1 && (long long)sm > budget) continue;
+        // slots beyond the units a warp sees per segment are not used
+        int per_warp = (a.nsb + w - 1) / w;
+        // warps that are busy in every round of a segment: nsb / (W * rounds)
+        const double busy = (double)a.nsb / ((double)w * per_warp);
+        double score = pass == 0 ? 1.0 : (double)w * busy * (s >= 2 && per_warp >= 2 ? 1.5 + 0.1 * (s - 2) : 1.0);
+        if (score > best) {
+          best = score;
+          smem = sm;
+          grid = g;
+          nslot = s;
+          warps = w;
+          p.xs_max = xs;
+        }
+      }
+    }
+  }
+  if (!nslot) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: no launch shape fits shared memory");
+  p.nslot = nslot;
+  if (getenv("GB_GEMV_VERBOSE"))
+    fprintf(stderr, "gemv epi=%s types=%d/%d units=%u rb=%d: warps=%d slots=%d grid=%lld smem=%zu regs=%d forced=%d,%d,%d\n",
+            epi_names[a.epi], ta, tb, p.units, p.rb, warps, nslot, grid, smem, regs, fw, fs, fc);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3((unsigned)(warps * 32));
@@ -625,6 +786,14 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  GB_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel, p), "gpu: gemv launch");
+  cudaError_t le = cudaLaunchKernelEx(&cfg, fn, p);
+  if (le != cudaSuccess) {
+    (void)cudaGetLastError();
+    cudaFuncAttributes fa;
+    cudaFuncGetAttributes(&fa, fn);
+    return gb_fail(GB_ERR_CUDA, "gpu: gemv launch: %s (grid %lld, %d warps, %d slots, %zu B shared, max %d B, static %zu B)",
+                   cudaGetErrorString(le), grid, warps, nslot, smem, fa.maxDynamicSharedSizeBytes,
+                   (size_t)fa.sharedSizeBytes);
+  }
   return GB_OK;
 }

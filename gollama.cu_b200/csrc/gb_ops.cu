@@ -237,6 +237,7 @@ __global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, co
                              int vocab, float *x, const float *wnorm, GbXPackBuf pk,
                              unsigned *err) {
   __shared__ __align__(16) uint8_t blk[8][224];
+  gb_grid_dep_launch();
   gb_grid_dep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x * (blockDim.x >> 5) + warp;
@@ -266,6 +267,7 @@ __global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, co
 // x += y, then pack x*wnorm (+ per-group sums of squares): the residual
 // epilogue when the projection's sum arrives from a collective.
 __global__ void resid_pack_kernel(float *x, const float *y, const float *wnorm, int n, GbXPackBuf pk) {
+  gb_grid_dep_launch();
   gb_grid_dep_wait();
   const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (g >= n / 32) return;
