@@ -9,12 +9,14 @@
 // with float32 accumulators (the reference's cpu.AttnDecode accumulates in
 // float64; tolerances cover the difference).
 //
-// Cache layouts are described by strides so that the same kernel reads the
-// reference's [kv_len][n_kv*head_dim] float32 caches (per-op API) and the
-// model's head-major caches: K as [head][head_dim/V][max_len][V] (V = 16
-// bytes of elements, so one thread reads one position's 16-byte chunk and a
-// warp reads 512 contiguous bytes), V as [head][max_len][head_dim].
+// Cache layouts are described by strides. The per-op API reads the
+// reference's [kv_len][n_kv*head_dim] float32 caches. The model's caches are
+// head-major: K as [head][head_dim/V][max_len][V] (V = 16 bytes of elements,
+// so a position's 16-byte chunks of one dim range are contiguous across
+// positions); V as [head][max_len][head_dim] for float32 caches and in the
+// K layout for fp16 caches (the tensor-core kernel reads both as 8x8 tiles).
 #include <math.h>
+#include <stdlib.h>
 
 #include "gb_device.cuh"
 #include "gb_internal.h"
@@ -61,6 +63,86 @@ template <bool F16>
 GB_DEV float vload(const void *base, long long off) {
   if (F16) return gb_half_to_float(((const uint16_t *)base)[off]);
   return ((const float *)base)[off];
+}
+
+// ---- slice partials and their merge -----------------------------------------
+// A slice partial per (KV head, slice, group head g) is a row of HD + 4
+// floats: the unnormalised output o[HD], the running max m, the sum l and two
+// pad floats that keep rows 16-byte aligned for float4 loads.
+constexpr int part_stride(int hd) { return hd + 4; }
+
+// Shared-memory floats merge_slices needs: weights [S][8], 1/L [8], one
+// float4 per thread, and the merged outputs for packing.
+__host__ __device__ constexpr int merge_floats(int S, int nthr, int G, int HD) {
+  return ((8 * S + 8 + 3) & ~3) + 4 * nthr + G * HD;
+}
+
+// Merge the S slice partials of KV head h into out (and its pack) with the
+// log-sum-exp rule: out = sum_j exp(m_j - M) o_j / sum_j exp(m_j - M) l_j.
+// Called by every thread of the head's last CTA. The slice weights come from
+// one warp per group head (lanes over slices); the weighted sums are spread
+// over all threads as float4 columns x slice groups and added in a fixed
+// order, so the result is deterministic.
+template <int HD>
+GB_DEV void merge_slices(const GbAttnArgs &a, int h, int S, int G, float *ms, int nthr) {
+  constexpr int PS = part_stride(HD);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float *wgt = ms, *linv = ms + 8 * S;
+  float4 *red4 = (float4 *)(ms + ((8 * S + 8 + 3) & ~3));
+  float *ov = (float *)(red4 + nthr);
+  const float *pb = a.part + (size_t)h * S * G * PS;
+  if (warp < G) {
+    float M = -INFINITY;
+    for (int j = lane; j < S; j += 32) M = fmaxf(M, __ldcg(pb + ((size_t)j * G + warp) * PS + HD));
+    M = gb_warp_max(M);
+    float L = 0.f;
+    for (int j = lane; j < S; j += 32) {
+      const float *pj = pb + ((size_t)j * G + warp) * PS;
+      const float m = __ldcg(pj + HD);
+      const float w = m == -INFINITY ? 0.f : expf(m - M);
+      wgt[j * 8 + warp] = w;
+      L += __ldcg(pj + HD + 1) * w;
+    }
+    L = gb_warp_sum(L);
+    if (lane == 0) linv[warp] = 1.f / L;
+  }
+  __syncthreads();
+  const int NV = G * HD / 4, ngrp = nthr / NV;  // NV <= 256 <= nthr
+  if (tid < ngrp * NV) {
+    const int v = tid % NV, grp = tid / NV, g = v / (HD / 4), d = (v % (HD / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int j = grp; j < S; j += ngrp) {
+      const float4 x = __ldcg((const float4 *)(pb + ((size_t)j * G + g) * PS + d));
+      const float w = wgt[j * 8 + g];
+      acc.x = fmaf(x.x, w, acc.x);
+      acc.y = fmaf(x.y, w, acc.y);
+      acc.z = fmaf(x.z, w, acc.z);
+      acc.w = fmaf(x.w, w, acc.w);
+    }
+    red4[tid] = acc;
+  }
+  __syncthreads();
+  if (tid < NV) {
+    float4 o = red4[tid];
+    for (int grp = 1; grp < ngrp; grp++) {
+      const float4 x = red4[grp * NV + tid];
+      o.x += x.x;
+      o.y += x.y;
+      o.z += x.z;
+      o.w += x.w;
+    }
+    const float li = linv[tid / (HD / 4)];
+    o = make_float4(o.x * li, o.y * li, o.z * li, o.w * li);
+    *(float4 *)(a.out + (size_t)h * G * HD + (size_t)tid * 4) = o;
+    ((float4 *)ov)[tid] = o;
+  }
+  if (a.out_pack.a) {
+    __syncthreads();
+    GbXPack pk{a.out_pack.a, a.out_pack.b, a.out_pack.c, a.out_pack.s, a.out_pack.sum16, nullptr};
+    // G*HD and nthr are multiples of 32: a warp packs one whole 32-group
+    for (int i = tid; i < G * HD; i += nthr) gb_pack_group(pk, (h * G * HD + i) / 32, ov[i]);
+  }
 }
 
 template <int GM, int HD, bool F16>
@@ -186,17 +268,17 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const GbAttnArgs a, int 
   __syncthreads();
 
   // this slice's partial: o[g][d] (unnormalised), m_g, l_g
-  const int stride = HD + 2;
-  float *part = a.part + ((size_t)h * S + s) * G * stride;
+  constexpr int PS = part_stride(HD);
+  float *part = a.part + ((size_t)h * S + s) * G * PS;
   for (int i = tid; i < G * HD; i += kThreads) {
     int g = i / HD, d = i % HD;
     float o = 0.f;
     for (int w = 0; w < kWarps; w++) o += red[(w * GM + g) * HD + d];
-    part[g * stride + d] = o;
+    part[g * PS + d] = o;
   }
   if (tid < G) {
-    part[tid * stride + HD] = mx[tid];
-    part[tid * stride + HD + 1] = sum[tid];
+    part[tid * PS + HD] = mx[tid];
+    part[tid * PS + HD + 1] = sum[tid];
   }
   __threadfence();
   __syncthreads();
@@ -204,30 +286,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const GbAttnArgs a, int 
   __syncthreads();
   if (!last) return;
   __threadfence();
-
-  // merge the S slices of this KV head (fixed order: deterministic)
-  const float *pbase = a.part + (size_t)h * S * G * stride;
-  const int ngroups = G * HD / 32;
-  for (int grp = warp; grp < ngroups; grp += kWarps) {
-    int g = (grp * 32) / HD, d = (grp * 32) % HD + lane;
-    float M = -INFINITY;
-    for (int j = 0; j < S; j++) M = fmaxf(M, __ldcg(pbase + ((size_t)j * G + g) * stride + HD));
-    float L = 0.f, O = 0.f;
-    for (int j = 0; j < S; j++) {
-      const float *pj = pbase + ((size_t)j * G + g) * stride;
-      float m = __ldcg(pj + HD);
-      float w = m == -INFINITY ? 0.f : expf(m - M);
-      L += __ldcg(pj + HD + 1) * w;
-      O += __ldcg(pj + d) * w;
-    }
-    float out = O / L;
-    int oi = (h * G + g) * HD + d;
-    a.out[oi] = out;
-    if (a.out_pack.a) {
-      GbXPack pk{a.out_pack.a, a.out_pack.b, a.out_pack.c, a.out_pack.s, a.out_pack.sum16, nullptr};
-      gb_pack_group(pk, oi / 32, out);
-    }
-  }
+  merge_slices<HD>(a, h, S, G, sm, kThreads);  // the dynamic buffer is free now
   if (tid == 0) a.counter[h] = 0u;
   gb_grid_dep_launch();
 }
@@ -425,15 +484,15 @@ __global__ void __launch_bounds__(kThreads) attn_flash_kernel(const GbAttnArgs a
   if (!ok && tid == 0 && a.err) atomicOr(a.err, GB_DEVERR_TIMEOUT);
 
   // this slice's partial: o[g][d] (unnormalised), m_g, l_g
-  const int stride = HD + 2;
-  float *part = a.part + ((size_t)h * S + s) * G * stride;
+  constexpr int PS = part_stride(HD);
+  float *part = a.part + ((size_t)h * S + s) * G * PS;
   if (pv_g < G) {
 #pragma unroll
-    for (int j = 0; j < DPT; j++) part[pv_g * stride + pv_d + j] = acc[j];
+    for (int j = 0; j < DPT; j++) part[pv_g * PS + pv_d + j] = acc[j];
   }
   if (tid < G) {
-    part[tid * stride + HD] = m_run[tid];
-    part[tid * stride + HD + 1] = l_run[tid];
+    part[tid * PS + HD] = m_run[tid];
+    part[tid * PS + HD + 1] = l_run[tid];
   }
   __threadfence();
   __syncthreads();
@@ -441,44 +500,17 @@ __global__ void __launch_bounds__(kThreads) attn_flash_kernel(const GbAttnArgs a
   __syncthreads();
   if (!last) return;
   __threadfence();
-
-  // merge the S slices of this KV head (fixed order: deterministic)
-  const float *pbase = a.part + (size_t)h * S * G * stride;
-  __shared__ float wgt[64 * 8], linv[GM];
-  if (tid < G) {
-    float M = -INFINITY;
-    for (int j = 0; j < S; j++) M = fmaxf(M, __ldcg(pbase + ((size_t)j * G + tid) * stride + HD));
-    float L = 0.f;
-    for (int j = 0; j < S; j++) {
-      const float m = __ldcg(pbase + ((size_t)j * G + tid) * stride + HD);
-      const float w = m == -INFINITY ? 0.f : expf(m - M);
-      wgt[j * GM + tid] = w;
-      L += __ldcg(pbase + ((size_t)j * G + tid) * stride + HD + 1) * w;
-    }
-    linv[tid] = 1.f / L;
-  }
-  __syncthreads();
-  for (int o = tid; o < G * HD; o += kThreads) {
-    const int g = o / HD, d = o % HD;
-    float O = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < S; j++) O = fmaf(__ldcg(pbase + ((size_t)j * G + g) * stride + d), wgt[j * GM + g], O);
-    const float out = O * linv[g];
-    const int oi = (h * G + g) * HD + d;
-    a.out[oi] = out;
-    if (a.out_pack.a) {
-      GbXPack pk{a.out_pack.a, a.out_pack.b, a.out_pack.c, a.out_pack.s, a.out_pack.sum16, nullptr};
-      gb_pack_group(pk, oi / 32, out);
-    }
-  }
+  // every issued stage has been waited on: the ring is free for the merge
+  merge_slices<HD>(a, h, S, G, (float *)smb, kThreads);
   if (tid == 0) a.counter[h] = 0u;
 }
 
 template <int GM, int HD, bool F16>
 int launch_flash(const GbAttnArgs &a, cudaStream_t st, bool pdl) {
   using FL = Flash<GM, HD, F16>;
-  if (a.splits > 64) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: %d slices (64 at most)", a.splits);
+  if (a.splits > 128) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: %d slices (128 at most)", a.splits);
   const size_t smem = FL::smem();
+  static_assert(merge_floats(128, kThreads, GM, HD) * 4 <= kStages * FL::STAGE, "merge scratch exceeds the ring");
   static bool attr = false;
   if (!attr) {
     GB_CUDA(cudaFuncSetAttribute(attn_flash_kernel<GM, HD, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
@@ -499,13 +531,309 @@ int launch_flash(const GbAttnArgs &a, cudaStream_t st, bool pdl) {
   return GB_OK;
 }
 
+// ---- flash decoding on tensor cores (fp16 caches) ---------------------------
+// K and V are both cached as [head][HD/8][max_len][8] halves: a run of
+// positions is HD/8 contiguous runs of 16 bytes per position for each of K
+// and V. A producer warp streams sub-chunks of SUB = 16 * kMW positions
+// through a ring of kMStages shared-memory stages with 1-D TMA bulk copies;
+// each of the kMW consumer warps owns 16 positions of every sub-chunk and
+// carries its own online softmax (running max and sum per head), so no block
+// barrier runs inside the loop: a stage returns to the producer once its
+// `empty` mbarrier has counted every consumer warp. After the loop the
+// warps' states are combined in shared memory into the CTA's slice partial.
+//
+// Products on mma.sync m16n8k16 (fp16 inputs, fp32 accumulation), per warp
+// and 16 positions:
+//   S[16 x 16 pos]  = Qs[16 x HD] . K^T   (B fragments: K rows by ldmatrix)
+//   O[16 x HD]     += Ps[16 x 16 pos] . V (B fragments: V rows by ldmatrix.trans)
+// Rows 0..7 of Qs hold the group's query heads rounded to fp16 and rows 8..15
+// the rounding residues, so rows g and g+8 of S add up to the score of head g
+// with about 22 bits of q (fp16 x fp16 products are exact in fp32); rows 0..7
+// of Ps hold p rounded to fp16 and rows 8..15 the residues. The accumulator
+// layout of S is the A-operand layout of Ps, so p never leaves registers.
+// The 16-byte rows of one 8x8 ldmatrix tile are contiguous in shared memory,
+// so neither ldmatrix form has bank conflicts. GQA groups of up to 8 heads;
+// smaller groups leave rows unused.
+GB_DEV uint32_t h2pack(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+// fp16 rounding of (x0, x1) and of the residues
+GB_DEV void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+  hi = h2pack(h0, h1);
+  lo = h2pack(__float2half_rn(x0 - __half2float(h0)), __float2half_rn(x1 - __half2float(h1)));
+}
+GB_DEV void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+GB_DEV void ldsm_x4(uint32_t r[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(gb_smem_u32(p)));
+}
+GB_DEV void ldsm_x4_t(uint32_t r[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(gb_smem_u32(p)));
+}
+
+constexpr int kMW = 8;                     // consumer warps
+constexpr int kMThreads = 32 * (kMW + 1);  // plus one producer warp
+constexpr int kMStages = 3;
+
+template <int HD>
+struct MmaAttn {
+  static constexpr int SUB = 16 * kMW;        // positions per sub-chunk
+  static constexpr int HALF = SUB * HD * 2;   // K (or V) bytes of a full sub-chunk
+  static constexpr int STAGE = 2 * HALF;
+  static constexpr size_t smem() { return (size_t)kMStages * STAGE; }
+  // after the loop: warp combine buffer [kMW][8][PS] in stage 0, merge scratch in stage 1
+  static_assert(kMW * 8 * (HD + 4) * 4 <= STAGE, "combine buffer exceeds a stage");
+  static_assert(merge_floats(128, kMThreads, 8, HD) * 4 <= STAGE, "merge scratch exceeds a stage");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kMThreads, 1) attn_mma_kernel(const GbAttnArgs a) {
+  using MA = MmaAttn<HD>;
+  constexpr int SUB = MA::SUB, KS = HD / 16, NT = HD / 8, PS = part_stride(HD);
+  extern __shared__ __align__(128) uint8_t smb[];
+  __shared__ __align__(8) uint64_t full[kMStages], empty[kMStages];
+  __shared__ float wm[kMW][8], wl[kMW][8];
+  __shared__ int last;
+  const int h = blockIdx.x, s = blockIdx.y, S = gridDim.y;
+  const int G = a.n_heads / a.n_kv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+
+  gb_grid_dep_launch();
+  // The position is written by the previous step's last kernel, which has
+  // completed: only q and the new K/V row need the preceding kernel.
+  int kv_len = *a.kv_len_pos + 1;
+  const bool bad = kv_len < 1 || kv_len > a.max_len;
+  if (bad) kv_len = kv_len < 1 ? 1 : a.max_len;
+  const int t0 = (int)((long long)kv_len * s / S), t1 = (int)((long long)kv_len * (s + 1) / S);
+  const int nsub = (t1 - t0 + SUB - 1) / SUB;
+  if (tid == 0) {
+    for (int i = 0; i < kMStages; i++) {
+      gb_mbar_init(&full[i], 1);
+      gb_mbar_init(&empty[i], kMW);
+    }
+    gb_mbar_fence_init();
+  }
+  __syncthreads();
+
+  bool ok = true;
+  float m_run = -INFINITY, l_run = 0.f;
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  if (warp == kMW) {
+    // producer: one lane issues every copy
+    if (lane == 0) {
+      if (bad && a.err) atomicOr(a.err, GB_DEVERR_POS);
+      const uint8_t *kg = (const uint8_t *)a.k + (size_t)h * a.k_sh * 2;
+      const uint8_t *vg = (const uint8_t *)a.v + (size_t)h * a.v_sh * 2;
+      bool waited = false;
+      for (int k = 0; k < nsub; k++) {
+        const int st = k % kMStages;
+        if (k >= kMStages) {
+          if (!gb_mbar_wait(&empty[st], (uint32_t)((k / kMStages - 1) & 1))) {
+            ok = false;
+            break;
+          }
+          gb_fence_proxy_async();
+        }
+        // the sub-chunk holding position kv_len-1 is written by the preceding kernel
+        if (!waited && t0 + (k + 1) * SUB >= kv_len) {
+          gb_grid_dep_wait();
+          waited = true;
+        }
+        const int p0 = t0 + k * SUB, nk = min(SUB, t1 - p0);
+        uint8_t *sk = smb + (size_t)st * MA::STAGE, *sv = sk + MA::HALF;
+        gb_mbar_expect_tx(&full[st], (uint32_t)(2 * NT * nk * 16));
+        for (int dc = 0; dc < NT; dc++) {
+          gb_bulk_g2s(sk + (size_t)dc * SUB * 16, kg + ((size_t)dc * a.k_sd + (size_t)p0 * 8) * 2,
+                      (uint32_t)(nk * 16), &full[st]);
+          gb_bulk_g2s(sv + (size_t)dc * SUB * 16, vg + ((size_t)dc * a.v_sd + (size_t)p0 * 8) * 2,
+                      (uint32_t)(nk * 16), &full[st]);
+        }
+      }
+    }
+  } else {
+    gb_grid_dep_wait();  // q comes from the preceding kernel
+    // Qs rows gid (hi) and gid+8 (lo) as A fragments
+    uint32_t qa[KS][4];
+    {
+      const float *qh = a.q + ((size_t)h * G + gid) * HD;
+#pragma unroll
+      for (int ks = 0; ks < KS; ks++) {
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+          const int d = ks * 16 + 8 * r + 2 * tig;
+          const float x0 = gid < G ? qh[d] : 0.f, x1 = gid < G ? qh[d + 1] : 0.f;
+          split2(x0, x1, qa[ks][2 * r], qa[ks][2 * r + 1]);
+        }
+      }
+    }
+    const int wp0 = warp * 16, mi = lane >> 3, lr = lane & 7;
+    for (int k = 0; k < nsub; k++) {
+      const int st = k % kMStages;
+      const int p0 = t0 + k * SUB, nv = min(SUB, t1 - p0) - wp0;  // valid positions of this warp
+      ok = gb_mbar_wait(&full[st], (uint32_t)((k / kMStages) & 1)) && ok;
+      const uint8_t *sk = smb + (size_t)st * MA::STAGE;
+      uint8_t *sv = smb + (size_t)st * MA::STAGE + MA::HALF;
+      if (ok && nv > 0) {
+        if (nv < 16) {  // rows past the slice hold stale bytes: zero V there (p is 0, 0*NaN is not)
+          const int nz = 16 - nv;
+          for (int i = lane; i < nz * NT; i += 32)
+            *(uint4 *)(sv + ((size_t)(i / nz) * SUB + wp0 + nv + i % nz) * 16) = make_uint4(0u, 0u, 0u, 0u);
+          __syncwarp();
+        }
+        float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < KS; ks++) {
+          uint32_t b[4];
+          ldsm_x4(b, sk + ((size_t)(2 * ks + (mi & 1)) * SUB + wp0 + (mi >> 1) * 8 + lr) * 16);
+          mma16816(c0, qa[ks], b[0], b[1]);
+          mma16816(c1, qa[ks], b[2], b[3]);
+        }
+        // this thread: head gid at local positions 2tig, 2tig+1, 8+2tig, 9+2tig
+        float sc[4] = {c0[0] + c0[2], c0[1] + c0[3], c1[0] + c1[2], c1[1] + c1[3]};
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int lp = 2 * tig + (i & 1) + 8 * (i >> 1);
+          sc[i] = lp < nv ? sc[i] * a.scale : -INFINITY;
+          mx = fmaxf(mx, sc[i]);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m_run, mx);
+        const float al = m_run == -INFINITY ? 0.f : expf(m_run - mn);
+        float p[4], psum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          p[i] = sc[i] == -INFINITY ? 0.f : expf(sc[i] - mn);
+          psum += p[i];
+        }
+        l_run = l_run * al + psum;
+        m_run = mn;
+        uint32_t pa[4];
+        split2(p[0], p[1], pa[0], pa[1]);
+        split2(p[2], p[3], pa[2], pa[3]);
+#pragma unroll
+        for (int n2 = 0; n2 < NT / 2; n2++) {
+          uint32_t b[4];
+          ldsm_x4_t(b, sv + ((size_t)(2 * n2 + (mi >> 1)) * SUB + wp0 + (mi & 1) * 8 + lr) * 16);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            o[2 * n2][j] *= al;
+            o[2 * n2 + 1][j] *= al;
+          }
+          mma16816(o[2 * n2], pa, b[0], b[1]);
+          mma16816(o[2 * n2 + 1], pa, b[2], b[3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) gb_mbar_arrive(&empty[st]);
+    }
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  }
+  if (!ok && a.err) atomicOr(a.err, GB_DEVERR_TIMEOUT);
+
+  // combine the warps' states into this slice's partial
+  __syncthreads();  // every issued stage has been waited on: the ring is free
+  if (warp < kMW && tig == 0) {
+    wm[warp][gid] = m_run;
+    wl[warp][gid] = l_run;
+  }
+  __syncthreads();
+  float *red = (float *)smb;  // [kMW][8][PS]
+  if (warp < kMW && gid < G) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kMW; w++) M = fmaxf(M, wm[w][gid]);
+    const float f = m_run == -INFINITY ? 0.f : expf(m_run - M);
+    float *r = red + ((size_t)warp * 8 + gid) * PS;
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+      *(float2 *)(r + n * 8 + 2 * tig) = make_float2((o[n][0] + o[n][2]) * f, (o[n][1] + o[n][3]) * f);
+  }
+  __syncthreads();
+  float *part = a.part + ((size_t)h * S + s) * G * PS;
+  for (int i = tid; i < G * HD; i += kMThreads) {
+    const int g = i / HD, d = i % HD;
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMW; w++) acc += red[((size_t)w * 8 + g) * PS + d];
+    part[g * PS + d] = acc;
+  }
+  if (tid < G) {
+    float M = -INFINITY, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMW; w++) M = fmaxf(M, wm[w][tid]);
+#pragma unroll
+    for (int w = 0; w < kMW; w++)
+      if (wm[w][tid] != -INFINITY) L += wl[w][tid] * expf(wm[w][tid] - M);
+    part[tid * PS + HD] = M;
+    part[tid * PS + HD + 1] = L;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(&a.counter[h], 1u) == (unsigned)(S - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  merge_slices<HD>(a, h, S, G, (float *)(smb + MA::STAGE), kMThreads);
+  if (tid == 0) a.counter[h] = 0u;
+}
+
+template <int HD>
+int launch_mma(const GbAttnArgs &a, cudaStream_t st, bool pdl) {
+  using MA = MmaAttn<HD>;
+  if (a.splits > 128) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: %d slices (128 at most)", a.splits);
+  const size_t smem = MA::smem();
+  static bool attr = false;
+  if (!attr) {
+    GB_CUDA(cudaFuncSetAttribute(attn_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+            "gpu: AttnDecode: shared memory attribute");
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.n_kv, (unsigned)a.splits);
+  cfg.blockDim = dim3(kMThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr1[1];
+  attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr1[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr1;
+  cfg.numAttrs = pdl ? 1 : 0;
+  GB_CUDA(cudaLaunchKernelEx(&cfg, attn_mma_kernel<HD>, a), "gpu: AttnDecode");
+  return GB_OK;
+}
+
 template <int GM, int HD, bool F16>
 int launch_t(const GbAttnArgs &a, cudaStream_t st, bool pdl) {
-  if (a.kv_len_pos && a.max_len > 0 && a.k_st == Chunk<F16>::V && a.v_st == HD)
-    return launch_flash<GM, HD, F16>(a, st, pdl);
+  if (a.kv_len_pos && a.max_len > 0) {  // the model's head-major caches
+    if constexpr (F16) {
+      if (a.k_st != 8 || a.v_st != 8) return gb_fail(GB_ERR_INVALID, "gpu: AttnDecode: fp16 cache layout");
+      return launch_mma<HD>(a, st, pdl);
+    } else {
+      if (a.k_st != 4 || a.v_st != HD) return gb_fail(GB_ERR_INVALID, "gpu: AttnDecode: fp32 cache layout");
+      return launch_flash<GM, HD, false>(a, st, pdl);
+    }
+  }
   int cap_len = a.max_len > 0 ? a.max_len : a.kv_len;
   int chunk_cap = (cap_len + a.splits - 1) / a.splits + 1;
   size_t smem = sizeof(float) * ((size_t)GM * HD + (size_t)GM * chunk_cap + (size_t)kWarps * GM * HD);
+  const size_t msmem = sizeof(float) * (size_t)merge_floats(a.splits, kThreads, GM, HD);
+  if (smem < msmem) smem = msmem;
+  if (a.splits > 128) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: %d slices (128 at most)", a.splits);
   if (smem > 200 * 1024) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: %d positions per slice", chunk_cap);
   static bool attr = false;
   if (!attr) {
@@ -529,19 +857,20 @@ int launch_t(const GbAttnArgs &a, cudaStream_t st, bool pdl) {
 
 }  // namespace
 
-// Slices per KV head for a cache of max_len positions: two CTAs per SM (each
-// streams its slice through a TMA ring), at most 64 slices (the merge reads
-// all of them) and at least 64 positions per slice at full length.
+// Slices per KV head for the model's caches of max_len positions: one CTA
+// per SM (each streams its slice through a TMA ring that fills most of the
+// SM's shared memory), at most 128 slices (the merge reads all of them) and
+// at least 128 positions per slice at full length.
 int gb_attn_splits(int n_kv, int max_len, int nsm) {
-  int s = 2 * nsm / n_kv;
-  if (s > 64) s = 64;
-  int by_len = (max_len + 63) / 64;
+  int s = nsm / n_kv;
+  if (s > 128) s = 128;
+  int by_len = (max_len + 127) / 128;
   if (s > by_len) s = by_len;
   return s < 1 ? 1 : s;
 }
 
 size_t gb_attn_part_floats(int n_kv, int splits, int group, int head_dim) {
-  return (size_t)n_kv * splits * group * (head_dim + 2);
+  return (size_t)n_kv * splits * group * part_stride(head_dim);
 }
 
 int gb_attn_launch(const GbAttnArgs &a, cudaStream_t st, bool pdl) {

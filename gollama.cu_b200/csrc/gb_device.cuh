@@ -125,6 +125,9 @@ GB_DEV void gb_bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *ba
       "l"(src), "r"(bytes), "r"(gb_smem_u32(bar))
       : "memory");
 }
+GB_DEV void gb_mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(gb_smem_u32(bar)) : "memory");
+}
 GB_DEV bool gb_mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -4,24 +4,29 @@
 // Replaces kernels.MatVecQ4_0 / MatVecQ4K / MatVecQ6K (kernels/quantmv.go:18-136)
 // on the model path. Design:
 //  * Work is the list of units (row-block, super-block); a row-block is one
-//    32-row tile, or a gate/up tile pair for the SwiGLU epilogue. Every warp
-//    of the persistent grid takes one contiguous range of units (stream-K),
-//    so all SMs stay busy whatever the matrix shape and no wave is partial.
-//  * Each unit's sb-block (4608 or 6720 contiguous bytes) is brought into a
-//    per-warp shared-memory slot by a 1-D TMA bulk copy completing on an
-//    mbarrier; with two slots the next unit's copy is in flight while the warp
-//    decodes the current one. Lane l of the warp owns row l of the tile.
+//    32-row tile, or a gate/up tile pair for the SwiGLU epilogue. Every CTA
+//    takes one contiguous range of units (stream-K over a persistent grid,
+//    or one row-block per CTA for small matrices), so all SMs stay busy
+//    whatever the matrix shape and no wave is partial.
+//  * Units are contiguous in memory in that order, so a CTA's range is one
+//    byte range. A producer warp streams it through a ring of shared-memory
+//    stages of K units (tens of KB) with one 1-D TMA bulk copy per stage;
+//    eight consumer warps decode the units round-robin and give each stage
+//    back through an mbarrier. Lane l of a warp owns row l of the tile.
 //  * The activation arrives as a limb pack (gb_device.cuh): three int8 limbs
 //    per element, so the 4-bit / 6-bit quants meet the activation in dp4a
 //    (4 products per instruction, exact int32 sums); float math is needed once
 //    per 16- or 32-element sub-block for the ggml scales. A CTA stages only the
-//    pack of the super-blocks its warps touch.
-//  * A row-block split between warps is finished by the warp whose atomic
-//    count completes it; it sums the partials in warp order (deterministic)
-//    and runs the epilogue. Counters are reset by that warp, so the kernel can
+//    pack of the super-blocks its units touch.
+//  * A row-block split between CTAs is finished by the CTA whose atomic
+//    count completes it; it sums the partials in CTA order (deterministic)
+//    and runs the epilogue. Counters are reset by that CTA, so the kernel can
 //    be replayed from a CUDA graph.
+//  * A CTA uses about half an SM, so under programmatic dependent launch the
+//    next kernel's CTA fits beside it and streams its own weights during
+//    this kernel's tail.
 //  * One instantiation per (weight types, epilogue) keeps each kernel's code
-//    small; unit cursors are 32-bit and advance without divisions.
+//    small.
 #include <math.h>
 #include <stdlib.h>
 
@@ -197,9 +202,15 @@ GB_DEV uint64_t argmax_key(float v, uint32_t idx) {
 
 struct Kp {  // kernel parameters
   GbGemvArgs a;
-  int rb, nrb, nslot, slot_bytes, xs_max;
+  int rb, nrb;
+  int K;            // units per ring stage
+  int nstage;       // ring stages (at most kMaxStages)
+  int stage_bytes;  // bytes of one stage buffer (K units of the larger type)
+  int xs_max;       // super-blocks of activation staged per CTA
   unsigned units;
 };
+
+constexpr int kMaxStages = 8;
 
 template <int EPI>
 GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1) {
@@ -257,11 +268,12 @@ GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1) {
       }
     } else if (r < e.q_rows + 2 * e.kv_rows) {
       int rr = r - e.q_rows - e.kv_rows, h = rr / hd, dd = rr % hd;
-      size_t idx = ((size_t)h * e.max_len + pos) * hd + dd;
-      if (e.kv_f16)
+      if (e.kv_f16) {  // fp16 V: the K layout
+        size_t idx = (((size_t)h * (hd / 8) + dd / 8) * e.max_len + pos) * 8 + (dd & 7);
         ((uint16_t *)e.vcache)[idx] = gb_float_to_half_rn(out);
-      else
-        ((float *)e.vcache)[idx] = out;
+      } else {
+        ((float *)e.vcache)[((size_t)h * e.max_len + pos) * hd + dd] = out;
+      }
     }
   } else if constexpr (EPI == GB_EPI_LOGITS) {
     int r = rbk * 32 + lane;
@@ -326,97 +338,107 @@ GB_DEV float decode(int ty, const uint8_t *st, int lane, const uint32_t *xa, con
   return sb_dot<TB>(st, lane, xa, xb, xc, xs, xsum);
 }
 
-// The CTA's unit range is cut into segments, one per row-block it touches.
-// Warp w takes units seg_begin + w, seg_begin + w + W, ... of every segment,
-// so a segment's partial sums end up in shared memory and are added in warp
-// order by one reducer warp; only a segment that continues in another CTA
-// goes through global memory.
-template <int TA, int TB, int EPI>
-__global__ void __launch_bounds__(512, 1) gemv_kernel(const Kp p) {
+// Byte offset of unit u (row-block u / nsb, super-block u % nsb) in the tiled
+// weights. Units are contiguous in this order: 32-row tiles are tile-major
+// and super-block-minor, the type-B tiles follow the type-A ones, and a
+// gate/up row-block holds the gate and up sb-blocks of each super-block side
+// by side. So any run of units is one contiguous byte range.
+template <int TA, int TB>
+GB_DEV size_t unit_off(const Kp &p, unsigned u) {
+  const size_t ua = (size_t)p.rb * gb_tiled_sb_bytes(TA);
+  if (TA == TB) return (size_t)u * ua;
+  const unsigned split_u = (unsigned)p.a.split_tile * (unsigned)p.a.nsb;  // rb is 1 here
+  return u < split_u ? (size_t)u * ua : (size_t)split_u * ua + (size_t)(u - split_u) * gb_tiled_sb_bytes(TB);
+}
+
+// Named barrier over the W consumer warps (the producer warp never joins).
+template <int W>
+GB_DEV void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory"); }
+
+// One CTA owns the contiguous unit range [cu0, cu1) (stream-K over the
+// persistent grid, or one row-block per CTA). A producer warp streams the
+// range through a ring of shared-memory stages, each stage K consecutive
+// units moved by ONE 1-D TMA bulk copy (tens of KB: few copies and few
+// mbarrier phases keep the copy engine at HBM speed). Consumer warps take
+// the units round-robin (unit j of the CTA goes to warp j mod W), decode them
+// against the activation pack and release each unit's slot through the
+// stage's `empty` mbarrier, which completes after K releases. The CTA's
+// range is cut into segments, one per row-block it touches; at a segment's
+// end the warps' partial sums are added in warp order by one reducer warp
+// (deterministic), and only a segment that continues in another CTA goes
+// through global memory.
+template <int TA, int TB, int EPI, int W>
+__global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(const Kp p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const GbGemvArgs &a = p.a;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-  const int rb = p.rb, nsb = a.nsb, nslot = p.nslot, slot_bytes = p.slot_bytes;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nsb = a.nsb, K = p.K, NS = p.nstage;
   const unsigned U = p.units, G = gridDim.x, b = blockIdx.x;
   const unsigned cu0 = ubeg(U, G, b), cu1 = ubeg(U, G, b + 1);
+  const unsigned nst = (cu1 - cu0 + (unsigned)K - 1) / (unsigned)K;  // stages of this CTA
 
-  // shared memory: [W][nslot] unit slots | mbarriers | pack planes a,b,c |
-  // scales | sums | 2 x [W][64] segment partials | misc
-  uint8_t *ring = smem + (size_t)warp * nslot * slot_bytes;
-  uint64_t *bars = (uint64_t *)(smem + (size_t)W * nslot * slot_bytes) + warp * nslot;
+  // shared memory: [NS] stages | pack planes a,b,c | scales | sums | 2 x [W][64] segment partials
+  uint8_t *ring = smem;
   const int XS = p.xs_max;
-  uint8_t *xbase = smem + (size_t)W * nslot * slot_bytes + (((size_t)W * nslot * 8 + 127) & ~(size_t)127);
+  uint8_t *xbase = smem + (size_t)NS * p.stage_bytes;
   uint32_t *xa_s = (uint32_t *)xbase;
   uint32_t *xb_s = xa_s + XS * 64;
   uint32_t *xc_s = xb_s + XS * 64;
   float *xs_s = (float *)(xc_s + XS * 64);
   float *xsum_s = xs_s + XS * 8;
   float *psum = xsum_s + XS * 16;  // [2][W][64]
-  __shared__ double red[16];
+  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+  __shared__ double red[W];
   __shared__ float inv_s;
-
-  const size_t sbb_a = (size_t)gb_tiled_sb_bytes(TA), sbb_b = (size_t)gb_tiled_sb_bytes(TB);
-  auto tile_ptr = [&](int tile, int sb) -> const uint8_t * {
-    if (TA == TB || tile < a.split_tile) return a.w + ((size_t)tile * nsb + sb) * sbb_a;
-    return a.w + (size_t)a.split_tile * nsb * sbb_a + ((size_t)(tile - a.split_tile) * nsb + sb) * sbb_b;
-  };
-  auto tile_bytes = [&](int tile) -> uint32_t {
-    return (TA == TB || tile < a.split_tile) ? (uint32_t)sbb_a : (uint32_t)sbb_b;
-  };
-  auto issue = [&](unsigned u, int s) {  // unit u into slot s (lane 0 only)
-    const int irbk = (int)(u / (unsigned)nsb), isb = (int)(u % (unsigned)nsb);
-    uint32_t bytes = 0;
-    for (int t = 0; t < rb; t++) bytes += tile_bytes(irbk * rb + t);
-    gb_mbar_expect_tx(&bars[s], bytes);
-    uint32_t off = 0;
-    for (int t = 0; t < rb; t++) {
-      const int tile = irbk * rb + t;
-      gb_bulk_g2s(ring + (size_t)s * slot_bytes + off, tile_ptr(tile, isb), tile_bytes(tile), &bars[s]);
-      off += tile_bytes(tile);
-    }
-  };
-  // this warp's units in order: in each segment [start, end), the units
-  // start + warp, start + warp + W, ... (none when the segment is shorter)
-  auto unit_at = [&](unsigned seg_start) -> unsigned {  // first unit at or after a segment start
-    while (seg_start < cu1) {
-      const unsigned seg_end = min(cu1, (seg_start / (unsigned)nsb + 1) * (unsigned)nsb);
-      if (seg_start + (unsigned)warp < seg_end) return seg_start + (unsigned)warp;
-      seg_start = seg_end;
-    }
-    return cu1;
-  };
-  auto next_unit = [&](unsigned u) -> unsigned {  // the warp's unit after u (or cu1)
-    const unsigned seg_end = min(cu1, (u / (unsigned)nsb + 1) * (unsigned)nsb);
-    if (u + (unsigned)W < seg_end) return u + (unsigned)W;
-    return unit_at(seg_end);
-  };
-  const unsigned first = unit_at(cu0);
 
   // 0. let the next kernel's CTAs start (they stream their weights meanwhile)
   gb_grid_dep_launch();
-  // 1. weights do not depend on the previous kernel: start their copies first
-  if (lane == 0) {
-    for (int s = 0; s < nslot; s++) gb_mbar_init(&bars[s], 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; s++) {
+      gb_mbar_init(&full[s], 1);
+      gb_mbar_init(&empty[s], (uint32_t)K);
+    }
     gb_mbar_fence_init();
   }
-  __syncwarp();
-  unsigned iu = first;  // next unit to issue
-  int issued = 0;
-  for (; iu < cu1 && issued < nslot; issued++) {
-    if (lane == 0) issue(iu, issued);
-    iu = next_unit(iu);
+  __syncthreads();
+
+  if (warp == W) {
+    // 1. producer: weights do not depend on the previous kernel
+    if (lane == 0) {
+      unsigned k = 0;
+      for (; k < nst; k++) {
+        const int s = (int)(k % (unsigned)NS);
+        if (k >= (unsigned)NS) {
+          if (!gb_mbar_wait(&empty[s], (k / NS - 1) & 1)) {
+            if (a.e.err) atomicOr(a.e.err, GB_DEVERR_TIMEOUT);
+            break;
+          }
+          gb_fence_proxy_async();
+        }
+        const unsigned j0 = cu0 + k * (unsigned)K, j1 = min(cu1, j0 + (unsigned)K);
+        const size_t o0 = unit_off<TA, TB>(p, j0), o1 = unit_off<TA, TB>(p, j1);
+        gb_mbar_expect_tx(&full[s], (uint32_t)(o1 - o0));
+        gb_bulk_g2s(ring + (size_t)s * p.stage_bytes, a.w + o0, (uint32_t)(o1 - o0), &full[s]);
+      }
+      // the copies still in flight land (bounded) before the CTA exits
+      for (unsigned j = k > (unsigned)NS ? k - NS : 0; j < k; j++)
+        (void)gb_mbar_wait(&full[j % NS], (j / NS) & 1);
+    }
+    return;
   }
 
   // 2. the activation pack (and the norm's sums of squares) come from the
   // preceding kernel: one round trip for all of it
+  constexpr int CT = W * 32;
+  const int tid = threadIdx.x;
   gb_grid_dep_wait();
   const int nsbs = (cu1 - cu0) >= (unsigned)nsb ? nsb : (int)(cu1 - cu0);
   const int sbf = (int)(cu0 % (unsigned)nsb);
   {
     double ss = 0;
     if (a.in_ssq)
-      for (int g = threadIdx.x; g < nsb * 8; g += blockDim.x) ss += (double)__ldcg(a.in_ssq + g);
-    for (int i = threadIdx.x; i < nsbs * 48; i += blockDim.x) {  // 3 planes x 16 uint4 per sb
+      for (int g = tid; g < nsb * 8; g += CT) ss += (double)__ldcg(a.in_ssq + g);
+    for (int i = tid; i < nsbs * 48; i += CT) {  // 3 planes x 16 uint4 per sb
       const int plane = i / (nsbs * 16), rest = i - plane * (nsbs * 16);
       const int ls = rest >> 4, v = rest & 15;
       int sb = sbf + ls;
@@ -425,7 +447,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const Kp p) {
       uint32_t *dst = plane == 0 ? xa_s : plane == 1 ? xb_s : xc_s;
       ((uint4 *)(dst + ls * 64))[v] = __ldcg((const uint4 *)(src + sb * 256) + v);
     }
-    for (int i = threadIdx.x; i < nsbs * 24; i += blockDim.x) {
+    for (int i = tid; i < nsbs * 24; i += CT) {
       const int ls = i / 24, v = i - ls * 24;
       int sb = sbf + ls;
       if (sb >= nsb) sb -= nsb;
@@ -438,70 +460,62 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const Kp p) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       if (lane == 0) red[warp] = ss;
-      __syncthreads();
-      if (threadIdx.x == 0) {
+      consumers_sync<W>();
+      if (tid == 0) {
         double t = 0;
         for (int w2 = 0; w2 < W; w2++) t += red[w2];
         inv_s = (float)(1.0 / sqrt(t / (double)(nsb * 256) + (double)a.eps));
       }
-      __syncthreads();
+      consumers_sync<W>();
       const float inv = inv_s;
-      for (int i = threadIdx.x; i < nsbs * 24; i += blockDim.x) {
+      for (int i = tid; i < nsbs * 24; i += CT) {
         const int ls = i / 24, v = i - ls * 24;
         if (v < 8) xs_s[ls * 8 + v] *= inv;
         else xsum_s[ls * 16 + v - 8] *= inv;
       }
     }
   }
-  __syncthreads();
+  consumers_sync<W>();
 
-  // 3. stream the units segment by segment
+  // 3. units round-robin over the warps, segment by segment
+  const size_t sbb_a = (size_t)gb_tiled_sb_bytes(TA);
   bool timeout = false;
-  int consumed = 0;
-  unsigned cu = first;  // next unit to consume
+  unsigned j = (unsigned)warp;  // this warp's next unit (CTA-relative)
   int nseg = 0;
   for (unsigned s0 = cu0; s0 < cu1; nseg++) {
     const int rbk = (int)(s0 / (unsigned)nsb);
     const unsigned s1 = min(cu1, (unsigned)(rbk + 1) * (unsigned)nsb);
     float acc0 = 0.f, acc1 = 0.f;
-    while (cu < s1) {
-      const int s = consumed % nslot;
-      if (!timeout && !gb_mbar_wait(&bars[s], (uint32_t)((consumed / nslot) & 1))) timeout = true;
+    for (; cu0 + j < s1; j += W) {
+      const unsigned u = cu0 + j, k = j / (unsigned)K;
+      const int s = (int)(k % (unsigned)NS);
+      if (!timeout && !gb_mbar_wait(&full[s], (k / NS) & 1)) timeout = true;
       if (!timeout) {
-        int ls = (int)(cu % (unsigned)nsb) - sbf;
+        int ls = (int)(u % (unsigned)nsb) - sbf;
         if (ls < 0) ls += nsb;
         const uint32_t *xa = xa_s + ls * 64, *xb = xb_s + ls * 64, *xc = xc_s + ls * 64;
         const float *xs = xs_s + ls * 8, *xsum = xsum_s + ls * 16;
-        const uint8_t *st = ring + (size_t)s * slot_bytes;
+        const uint8_t *st = ring + (size_t)s * p.stage_bytes +
+                            (unit_off<TA, TB>(p, u) - unit_off<TA, TB>(p, cu0 + k * (unsigned)K));
         if constexpr (EPI == GB_EPI_SWIGLU) {
-          // gate then up (the up tile follows the gate tile in the slot); one
-          // decode at a time keeps the register footprint of a single tile
+          // gate then up sb-block; one decode at a time keeps the register
+          // footprint of a single tile
           acc0 += sb_dot_outlined<TA>(st, lane, xa, xb, xc, xs, xsum);
           acc1 += sb_dot_outlined<TA>(st + sbb_a, lane, xa, xb, xc, xs, xsum);
         } else {
-          acc0 += decode<TA, TB>(rbk * rb < a.split_tile ? TA : TB, st, lane, xa, xb, xc, xs, xsum);
+          acc0 += decode<TA, TB>(rbk < a.split_tile ? TA : TB, st, lane, xa, xb, xc, xs, xsum);
         }
       }
       __syncwarp();
-      consumed++;
-      if (iu < cu1) {
-        if (lane == 0 && !timeout) {
-          gb_fence_proxy_async();
-          issue(iu, s);
-        }
-        iu = next_unit(iu);
-        issued++;
-      }
-      cu = next_unit(cu);
+      if (lane == 0) gb_mbar_arrive(&empty[s]);
     }
     float *ps = psum + (size_t)(nseg & 1) * W * 64;
     ps[warp * 64 + lane] = acc0;
     ps[warp * 64 + 32 + lane] = acc1;
-    __syncthreads();
+    consumers_sync<W>();
     if (warp == nseg % W) {  // reducer of this segment (sum in warp order)
       float y0 = 0.f, y1 = 0.f;
-      const int wmax = min(W, (int)(s1 - s0));
-      for (int w2 = 0; w2 < wmax; w2++) {
+      for (int w2 = 0; w2 < W; w2++) {
         y0 += ps[w2 * 64 + lane];
         y1 += ps[w2 * 64 + 32 + lane];
       }
@@ -537,11 +551,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const Kp p) {
     }
     s0 = s1;
   }
-  if (timeout) {
-    if (lane == 0 && a.e.err) atomicOr(a.e.err, GB_DEVERR_TIMEOUT);
-    // let the copies still in flight land (bounded) before the CTA exits
-    for (int j = consumed; j < issued; j++) (void)gb_mbar_wait(&bars[j % nslot], (uint32_t)((j / nslot) & 1));
-  }
+  if (timeout && lane == 0 && a.e.err) atomicOr(a.e.err, GB_DEVERR_TIMEOUT);
 }
 
 // ---- repack raw ggml rows into the tiled layout (load time) ---------------
@@ -582,36 +592,40 @@ int sms() {
   return g_sms;
 }
 
-size_t gemv_smem(int warps, int nslot, int slot_bytes, int xs_max) {
-  return (size_t)warps * nslot * slot_bytes + (((size_t)warps * nslot * 8 + 127) & ~(size_t)127) +
-         (size_t)xs_max * (3 * 256 + 4 * 24) + (size_t)2 * warps * 64 * 4 + 64;
+size_t gemv_smem(int warps, int nstage, int stage_bytes, int xs_max) {
+  return (size_t)nstage * stage_bytes + (size_t)xs_max * (3 * 256 + 4 * 24) + (size_t)2 * warps * 64 * 4;
 }
 
 using KernelFn = void (*)(Kp);
 
-template <int TA, int TB>
+template <int TA, int TB, int W>
 KernelFn pick_epi(int epi) {
   switch (epi) {
-    case GB_EPI_PLAIN: return gemv_kernel<TA, TB, GB_EPI_PLAIN>;
-    case GB_EPI_QKV: return gemv_kernel<TA, TB, GB_EPI_QKV>;
-    case GB_EPI_RESID: return gemv_kernel<TA, TB, GB_EPI_RESID>;
-    case GB_EPI_SWIGLU: return gemv_kernel<TA, TB, GB_EPI_SWIGLU>;
-    case GB_EPI_LOGITS: return gemv_kernel<TA, TB, GB_EPI_LOGITS>;
+    case GB_EPI_PLAIN: return gemv_kernel<TA, TB, GB_EPI_PLAIN, W>;
+    case GB_EPI_QKV: return gemv_kernel<TA, TB, GB_EPI_QKV, W>;
+    case GB_EPI_RESID: return gemv_kernel<TA, TB, GB_EPI_RESID, W>;
+    case GB_EPI_SWIGLU: return gemv_kernel<TA, TB, GB_EPI_SWIGLU, W>;
+    case GB_EPI_LOGITS: return gemv_kernel<TA, TB, GB_EPI_LOGITS, W>;
   }
   return nullptr;
 }
 
-KernelFn pick(int ta, int tb, int epi) {
+template <int W>
+KernelFn pick_w(int ta, int tb, int epi) {
   if (ta == tb) {
-    if (ta == GB_T_Q4_K) return pick_epi<GB_T_Q4_K, GB_T_Q4_K>(epi);
-    if (ta == GB_T_Q6_K) return pick_epi<GB_T_Q6_K, GB_T_Q6_K>(epi);
-    if (ta == GB_T_Q4_0) return pick_epi<GB_T_Q4_0, GB_T_Q4_0>(epi);
+    if (ta == GB_T_Q4_K) return pick_epi<GB_T_Q4_K, GB_T_Q4_K, W>(epi);
+    if (ta == GB_T_Q6_K) return pick_epi<GB_T_Q6_K, GB_T_Q6_K, W>(epi);
+    if (ta == GB_T_Q4_0) return pick_epi<GB_T_Q4_0, GB_T_Q4_0, W>(epi);
   } else if (ta == GB_T_Q4_K && tb == GB_T_Q6_K && epi == GB_EPI_QKV) {
-    return gemv_kernel<GB_T_Q4_K, GB_T_Q6_K, GB_EPI_QKV>;
+    return gemv_kernel<GB_T_Q4_K, GB_T_Q6_K, GB_EPI_QKV, W>;
   } else if (ta == GB_T_Q6_K && tb == GB_T_Q4_K && epi == GB_EPI_QKV) {
-    return gemv_kernel<GB_T_Q6_K, GB_T_Q4_K, GB_EPI_QKV>;
+    return gemv_kernel<GB_T_Q6_K, GB_T_Q4_K, GB_EPI_QKV, W>;
   }
   return nullptr;
+}
+
+KernelFn pick(int ta, int tb, int epi, int warps) {
+  return warps == 16 ? pick_w<16>(ta, tb, epi) : pick_w<8>(ta, tb, epi);
 }
 
 int smem_optin() {
@@ -680,105 +694,86 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   if (a.ntiles % p.rb) return gb_fail(GB_ERR_INVALID, "gpu: gemv: tiles not paired");
   const int ta = a.type_a, tb = a.split_tile < a.ntiles ? a.type_b : a.type_a;
   p.a.type_b = tb;
-  KernelFn fn = pick(ta, tb, a.epi);
+  // consumer warps per CTA: 16 (a whole SM) or 8 (half an SM); GB_GEMV_WARPS overrides
+  int warps = 16;
+  if (const char *e = getenv("GB_GEMV_WARPS")) warps = atoi(e) == 8 ? 8 : 16;
+  KernelFn fn = pick(ta, tb, a.epi, warps);
   if (!fn) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: types %d/%d with epilogue %d", ta, tb, a.epi);
   if (p.rb == 2 && ta != tb) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: gate/up types differ");
   p.nrb = a.ntiles / p.rb;
   p.units = (unsigned)p.nrb * (unsigned)a.nsb;
-  const int sbb_max = std::max(gb_tiled_sb_bytes(ta), gb_tiled_sb_bytes(tb));
-  p.slot_bytes = p.rb * sbb_max;
+  const int ub = p.rb * std::max(gb_tiled_sb_bytes(ta), gb_tiled_sb_bytes(tb));  // largest unit
   const int nsm = sms();
   const long long cap = smem_optin();
   // opt in to the shared memory and learn the register count (once per kernel)
   static KernelFn seen[64];
-  static int seen_regs[64];
+  static int seen_static[64];
   static int nseen = 0;
-  int regs = -1;
+  int static_smem = -1;
   for (int i = 0; i < nseen; i++)
-    if (seen[i] == fn) regs = seen_regs[i];
-  if (regs < 0) {
+    if (seen[i] == fn) static_smem = seen_static[i];
+  if (static_smem < 0) {
     cudaFuncAttributes fa;
     GB_CUDA(cudaFuncGetAttributes(&fa, fn), "gpu: gemv");
-    GB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(cap - (long long)fa.sharedSizeBytes)),
+    static_smem = (int)fa.sharedSizeBytes;
+    GB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(cap - static_smem)),
             "gpu: gemv: shared memory attribute");
-    regs = fa.numRegs;
     if (nseen < 64) {
       seen[nseen] = fn;
-      seen_regs[nseen++] = regs;
+      seen_static[nseen++] = static_smem;
     }
   }
-  // Launch shape: (warps per CTA, slots per warp, CTAs per SM) that fits the
-  // SM's shared memory, threads and registers and maximises the copies a
-  // warp keeps in flight (slots - 1) times the resident warps.
-  // GB_GEMV_SHAPE_<PLAIN|QKV|RESID|SWIGLU|LOGITS> or GB_GEMV_SHAPE = "w,s,c"
-  // force a shape when it fits (sweeps); otherwise the choice is automatic.
+  // Launch shape. Grid: one row-block per CTA when there are at most as many
+  // row-blocks as SMs (no partial sums leave the CTA), else one persistent CTA
+  // per SM over a contiguous range of units. Either way a CTA uses about half
+  // an SM (GB_SMEM_BUDGET bytes of shared memory, 288 threads of at most 112
+  // registers), so the next kernel's CTA fits beside it and starts streaming
+  // its own weights during this kernel's tail. Ring: stages of K units of
+  // about 36 KB, as many stages as the budget holds (2 to 8).
+  // GB_GEMV_RING_<PLAIN|QKV|RESID|SWIGLU|LOGITS> or GB_GEMV_RING = "K,stages"
+  // force the ring (sweeps) when it fits.
   static const char *epi_names[] = {"PLAIN", "QKV", "RESID", "SWIGLU", "LOGITS"};
-  int fw = 0, fs = 0, fc = 0;
+  int fk = 0, fs = 0;
   {
     char key[64];
-    snprintf(key, sizeof key, "GB_GEMV_SHAPE_%s", epi_names[a.epi]);
+    snprintf(key, sizeof key, "GB_GEMV_RING_%s", epi_names[a.epi]);
     const char *e = getenv(key);
-    if (!e) e = getenv("GB_GEMV_SHAPE");
-    if (e && sscanf(e, "%d,%d,%d", &fw, &fs, &fc) != 3) fw = fs = fc = 0;
+    if (!e) e = getenv("GB_GEMV_RING");
+    if (e && sscanf(e, "%d,%d", &fk, &fs) != 2) fk = fs = 0;
   }
-  const long long regs_per_warp = ((long long)regs * 32 + 255) / 256 * 256;
-  double best = -1;
-  size_t smem = 0;
-  long long grid = 0;
-  int nslot = 0, warps = 0;
-  // Automatic shape. Grid: one row-block per CTA when there are at most two
-  // per SM (no partial sums leave the CTA), else one persistent CTA per SM
-  // walking a contiguous range of units. CTA: at most as many warps as a row
-  // has super-blocks; the most warps, then two slots over one, within a
-  // shared-memory budget (GB_SMEM_BUDGET; default: half an SM when two CTAs
-  // must share it, the whole SM otherwise).
-  const bool per_rb = p.nrb <= 2 * nsm;
-  const int ctas_per_sm = per_rb && p.nrb > nsm ? 2 : 1;
-  long long budget = ctas_per_sm == 2 ? 110 * 1024 : 220 * 1024;
+  long long grid = p.nrb <= nsm ? p.nrb : std::min<long long>(nsm, p.units);
+  if (grid * 128 > (long long)gb_gemv_scratch_floats(a.ntiles, plan)) grid = gb_gemv_scratch_floats(a.ntiles, plan) / 128;
+  const int upc = (int)((p.units + grid - 1) / grid);  // units per CTA (at most)
+  const int xs = std::min(a.nsb, upc + 1);
+  long long budget = warps == 8 ? 113 * 1024 : 220 * 1024;
   if (const char *e = getenv("GB_SMEM_BUDGET")) budget = atoll(e);
-  for (int pass = fw ? 0 : 1; pass < 2 && !nslot; pass++)
-  for (int w : {16, 12, 8, 4}) {  // the kernel is built for at most 512 threads
-    if (pass == 0 && w != fw) continue;
-    if (pass == 1 && w > a.nsb && w > 4) continue;
-    for (int s = 1; s <= 8; s++) {
-      if (pass == 0 && s != fs) continue;
-      if (pass == 1 && s > 3) continue;
-      for (int c = 1; c <= 8; c++) {
-        if (pass == 0 && c != fc) continue;
-        if (pass == 1 && c != ctas_per_sm) continue;
-        if (w * c > 64 || regs_per_warp * w * c > 65536) continue;
-        long long g = per_rb ? p.nrb : (long long)nsm * c;
-        if (!per_rb && g > (long long)p.units) g = p.units;
-        if (g < 1) g = 1;
-        if (g * 128 > (long long)gb_gemv_scratch_floats(a.ntiles, plan)) continue;
-        int xs = (int)std::min<long long>(a.nsb, ((long long)p.units + g - 1) / g + 1);
-        size_t sm = gemv_smem(w, s, p.slot_bytes, xs);
-        if ((long long)(sm + 1024) * c > 228LL * 1024 || (long long)sm > cap - 256) continue;
-        if (pass == 1 && (long long)sm > budget) continue;
-        // slots beyond the units a warp sees per segment are not used
-        int per_warp = (a.nsb + w - 1) / w;
-        // warps that are busy in every round of a segment: nsb / (W * rounds)
-        const double busy = (double)a.nsb / ((double)w * per_warp);
-        double score = pass == 0 ? 1.0 : (double)w * busy * (s >= 2 && per_warp >= 2 ? 1.5 + 0.1 * (s - 2) : 1.0);
-        if (score > best) {
-          best = score;
-          smem = sm;
-          grid = g;
-          nslot = s;
-          warps = w;
-          p.xs_max = xs;
-        }
-      }
+  const long long room = cap - static_smem;
+  const long long fixed = (long long)gemv_smem(warps, 0, 0, xs);
+  int K = std::max(1, std::min(16, (36 * 1024 + ub / 2) / ub)), ns = 0;
+  K = std::min(K, upc);
+  if (fk > 0 && fs >= 2 && fs <= kMaxStages && fixed + (long long)fs * fk * ub <= room) {
+    K = fk;
+    ns = fs;
+  } else {
+    for (;; K--) {
+      ns = (int)std::min<long long>(kMaxStages, (budget - fixed) / ((long long)K * ub));
+      if (ns >= 2 || K == 1) break;
     }
+    if (ns < 2) ns = 2;
   }
-  if (!nslot) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: no launch shape fits shared memory");
-  p.nslot = nslot;
+  p.K = K;
+  p.nstage = ns;
+  p.stage_bytes = (K * ub + 127) / 128 * 128;
+  p.xs_max = xs;
+  const size_t smem = gemv_smem(warps, ns, p.stage_bytes, xs);
+  if ((long long)smem > room)
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: %zu B of shared memory for %d stages of %d units", smem, ns, K);
   if (getenv("GB_GEMV_VERBOSE"))
-    fprintf(stderr, "gemv epi=%s types=%d/%d units=%u rb=%d: warps=%d slots=%d grid=%lld smem=%zu regs=%d forced=%d,%d,%d\n",
-            epi_names[a.epi], ta, tb, p.units, p.rb, warps, nslot, grid, smem, regs, fw, fs, fc);
+    fprintf(stderr, "gemv epi=%s types=%d/%d units=%u rb=%d: grid=%lld warps=%d K=%d stages=%d stage=%d smem=%zu forced=%d,%d\n",
+            epi_names[a.epi], ta, tb, p.units, p.rb, grid, warps, K, ns, p.stage_bytes, smem, fk, fs);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3((unsigned)(warps * 32));
+  cfg.blockDim = dim3((unsigned)(32 * (warps + 1)));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -791,8 +786,8 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
     (void)cudaGetLastError();
     cudaFuncAttributes fa;
     cudaFuncGetAttributes(&fa, fn);
-    return gb_fail(GB_ERR_CUDA, "gpu: gemv launch: %s (grid %lld, %d warps, %d slots, %zu B shared, max %d B, static %zu B)",
-                   cudaGetErrorString(le), grid, warps, nslot, smem, fa.maxDynamicSharedSizeBytes,
+    return gb_fail(GB_ERR_CUDA, "gpu: gemv launch: %s (grid %lld, %d stages of %d units, %zu B shared, max %d B, static %zu B)",
+                   cudaGetErrorString(le), grid, ns, K, smem, fa.maxDynamicSharedSizeBytes,
                    (size_t)fa.sharedSizeBytes);
   }
   return GB_OK;

@@ -104,6 +104,7 @@ struct GbAttnArgs {
   // element strides (in elements of the cache type)
   long long k_sh = 0, k_sd = 0, k_st = 0;  // head, 16-byte dim chunk, position
   long long v_sh = 0, v_st = 0;            // head, position (dims contiguous)
+  long long v_sd = 0;                      // 16-byte dim chunk (fp16 model cache only)
   int n_heads = 0, n_kv = 0, head_dim = 0;
   float scale = 1.f;
   int kv_len = 0;                // used when kv_len_pos is null

@@ -245,17 +245,17 @@ int upload_tiles(const GbTensor *t, int r0, int nr, int c0, int nc, uint8_t *dst
     if (rc) return rc;
   } else {
     // interleaved destination (gate/up pairs): repack into a scratch region
-    // after the raw bytes, then place each tile
+    // after the raw bytes, then place each sb-block at slot dst_tile0 of its
+    // (row-block, super-block) pair, so that a gate/up unit is contiguous
     uint8_t *tmp = staging + ((need + 255) / 256) * 256;
     size_t tb = (size_t)ntiles * nsb * sbb;
     if (((need + 255) / 256) * 256 + tb > staging_bytes)
       return gb_fail(GB_ERR_INVALID, "model: staging buffer too small");
     int rc = gb_repack_launch(typ, staging, nr, nc, tmp, st);
     if (rc) return rc;
-    for (int i = 0; i < ntiles; i++)
-      GB_CUDA(cudaMemcpyAsync(dst_base + (size_t)(dst_tile0 + i * dst_tile_mul) * nsb * sbb,
-                              tmp + (size_t)i * nsb * sbb, (size_t)nsb * sbb, cudaMemcpyDeviceToDevice, st),
-              "model: place tiles");
+    GB_CUDA(cudaMemcpy2DAsync(dst_base + (size_t)dst_tile0 * sbb, (size_t)dst_tile_mul * sbb, tmp, sbb, sbb,
+                              (size_t)ntiles * nsb, cudaMemcpyDeviceToDevice, st),
+            "model: place sb-blocks");
   }
   GB_CUDA(cudaStreamSynchronize(st), "model: upload");
   return GB_OK;
@@ -367,7 +367,8 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
     at.k_sd = (long long)c.max_len * V;
     at.k_st = V;
     at.v_sh = (long long)c.max_len * c.head_dim;
-    at.v_st = c.head_dim;
+    at.v_st = c.kv_f16 ? V : c.head_dim;  // fp16 V is stored in the K layout
+    at.v_sd = c.kv_f16 ? (long long)c.max_len * V : 0;
     at.n_heads = m->q_local / c.head_dim;
     at.n_kv = m->kv_local / c.head_dim;
     at.head_dim = c.head_dim;
@@ -635,7 +636,7 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
     if ((rc = alloc_tiled(m, &L.wo, wo->type, wo->type, 1 << 30, c.dim / 32, m->q_local / 256, c.dim, m->q_local)) ||
         (rc = upload_tiles(wo, 0, c.dim, R * m->q_local, m->q_local, L.wo.w, 0, 1, m->st, staging, staging_bytes)))
       return fail(rc);
-    // gate/up: this rank's FFN rows, tiles interleaved gate0 up0 gate1 up1 ...
+    // gate/up: this rank's FFN rows; per (row-block, super-block) the gate then the up sb-block
     const int tf = m->ffn_local / 32;
     if ((rc = alloc_tiled(m, &L.gu, wg->type, wg->type, 1 << 30, 2 * tf, c.dim / 256, 2 * m->ffn_local, c.dim)) ||
         (rc = upload_tiles(wg, R * m->ffn_local, m->ffn_local, 0, c.dim, L.gu.w, 0, 2, m->st, staging, staging_bytes)) ||
@@ -874,7 +875,7 @@ int gb_model_fill_kv_normal(gb_model *m, uint64_t seed, int n_pos) {
         int h = j / hd, d = j % hd;
         float kx = k[(size_t)t * kv_dim + h0 + j], vx = v[(size_t)t * kv_dim + h0 + j];
         size_t ki = (((size_t)h * (hd / V) + d / V) * c.max_len + t) * V + d % V;
-        size_t vi = ((size_t)h * c.max_len + t) * hd + d;
+        size_t vi = c.kv_f16 ? ki : ((size_t)h * c.max_len + t) * hd + d;
         if (c.kv_f16) {
           ((uint16_t *)kd.data())[ki] = host_f16(kx);
           ((uint16_t *)vd.data())[vi] = host_f16(vx);
@@ -904,7 +905,7 @@ int gb_model_read_kv(gb_model *m, int layer, int pos0, int n, float *k_out, floa
     for (int j = 0; j < kvl; j++) {
       int h = j / hd, d = j % hd, p = pos0 + t;
       size_t ki = (((size_t)h * (hd / V) + d / V) * c.max_len + p) * V + d % V;
-      size_t vi = ((size_t)h * c.max_len + p) * hd + d;
+      size_t vi = c.kv_f16 ? ki : ((size_t)h * c.max_len + p) * hd + d;
       k_out[(size_t)t * kvl + j] = c.kv_f16 ? host_half(((uint16_t *)kd.data())[ki]) : ((float *)kd.data())[ki];
       v_out[(size_t)t * kvl + j] = c.kv_f16 ? host_half(((uint16_t *)vd.data())[vi]) : ((float *)vd.data())[vi];
     }

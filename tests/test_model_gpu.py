@@ -14,6 +14,9 @@ MODELS = {
     "q40_tied": dict(layers=2, dim=256, ffn=512, heads=4, kv_heads=2, head_dim=64, vocab=512, ctx_len=96, mix=0, seed=12),
     "q4km_hd128": dict(layers=3, dim=512, ffn=768, heads=4, kv_heads=2, head_dim=128, vocab=777, ctx_len=96, mix=1, seed=13),
     "q4k_all": dict(layers=2, dim=512, ffn=512, heads=4, kv_heads=4, head_dim=128, vocab=600, ctx_len=96, mix=2, seed=14),
+    # GQA groups of 3 and 8 query heads per KV head
+    "gqa3_hd64": dict(layers=2, dim=768, ffn=512, heads=12, kv_heads=4, head_dim=64, vocab=500, ctx_len=96, mix=1, seed=15),
+    "gqa8_hd128": dict(layers=2, dim=1024, ffn=512, heads=8, kv_heads=1, head_dim=128, vocab=500, ctx_len=96, mix=1, seed=16),
 }
 
 
@@ -167,6 +170,24 @@ def test_prefilled_kv_long_context(gb, orc, cuda):
         got = m.forward(tok, n_pos + i).copy()
         want = om.forward(tok, n_pos + i, cfg["vocab"])
         check_logits(f"long pos {n_pos + i}", got, want)
+    m.close()
+    om.close()
+
+
+@pytest.mark.parametrize("kv_f16", [0, 1])
+def test_early_positions_many_slices(gb, orc, cuda, kv_f16):
+    # a long cache split into more slices than there are positions yet:
+    # the empty slices must drop out of the merge
+    cfg = dict(MODELS["gqa3_hd64"], ctx_len=2500)
+    spec = gb.synth_spec(**cfg)
+    img = gb.SynthImage(spec)
+    raw = np.array(img.view(), copy=True)
+    m = gb.Model(img, max_len=2500, kv_f16=kv_f16)
+    om = orc.OracleModel(raw, 2500, bool(kv_f16))
+    for pos, tok in enumerate([3, 1, 4, 1, 5]):
+        got = m.forward(tok, pos).copy()
+        want = om.forward(tok, pos, cfg["vocab"])
+        check_logits(f"early pos {pos}", got, want)
     m.close()
     om.close()
 
