@@ -11,6 +11,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
 #include <string>
 
 #include "gb_device.cuh"
@@ -526,6 +527,99 @@ int gb_gpu_attn_decode(gb_kernels *k, void *stream, const float *q, const float 
   a.out = out;
   a.part = k->ws;
   a.counter = k->ws_counter;
+  return gb_attn_launch(a, (cudaStream_t)stream, false);
+}
+
+// ---- AttnDecode without allocation ------------------------------------------
+namespace {
+// The slice partials and per-KV-head counters of gb_gpu_attn_decode_noalloc
+// live in file-scope device arrays of fixed size (4 MiB of partials, 256
+// counters), one copy per device, shared by every call on that device.
+constexpr size_t kNoAllocPartFloats = (size_t)1 << 20;
+constexpr int kNoAllocHeads = 256;
+constexpr int kNoAllocDevices = 64;
+__device__ __align__(256) float g_noalloc_part[kNoAllocPartFloats];
+__device__ __align__(256) unsigned g_noalloc_counter[kNoAllocHeads];
+
+struct NoAllocScratch {
+  float *part = nullptr;
+  unsigned *counter = nullptr;
+};
+NoAllocScratch g_noalloc[kNoAllocDevices];
+std::mutex g_noalloc_mu;
+
+// Addresses of the arrays on `device`, resolved once per device with that
+// device current.
+int noalloc_scratch(int device, NoAllocScratch *out) {
+  if (device < 0 || device >= kNoAllocDevices)
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode (no-alloc): device %d (0..%d)", device, kNoAllocDevices - 1);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocScratch &s = g_noalloc[device];
+  if (!s.part) {
+    int cur = 0;
+    GB_CUDA(cudaGetDevice(&cur), "gpu: AttnDecode (no-alloc): current device");
+    if (cur != device) GB_CUDA(cudaSetDevice(device), "gpu: AttnDecode (no-alloc): set device");
+    void *part = nullptr, *counter = nullptr;
+    cudaError_t e1 = cudaGetSymbolAddress(&part, g_noalloc_part);
+    cudaError_t e2 = e1 == cudaSuccess ? cudaGetSymbolAddress(&counter, g_noalloc_counter) : e1;
+    if (cur != device) cudaSetDevice(cur);
+    GB_CUDA(e2, "gpu: AttnDecode (no-alloc): scratch address");
+    s.part = (float *)part;
+    s.counter = (unsigned *)counter;
+  }
+  *out = s;
+  return GB_OK;
+}
+
+}  // namespace
+
+int gb_gpu_attn_decode_noalloc(gb_kernels *k, void *stream, const float *q, const float *kcache,
+                               const float *vcache, float *out, int kv_len, int n_heads, int n_kv,
+                               int head_dim, float scale) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (kv_len <= 0) return gb_fail(GB_ERR_INVALID, "gpu: AttnDecode: kv_len %d", kv_len);
+  if (n_kv <= 0 || n_heads % n_kv)
+    return gb_fail(GB_ERR_INVALID, "gpu: AttnDecode: %d heads is not a multiple of %d KV heads", n_heads, n_kv);
+  if (n_kv > kNoAllocHeads)
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode (no-alloc): %d KV heads, at most %d", n_kv, kNoAllocHeads);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, k->device);
+  int splits = (2 * sms + n_kv - 1) / n_kv;
+  if (splits > 128) splits = 128;
+  if (splits > kv_len) splits = kv_len;
+  while ((kv_len + splits - 1) / splits > 2048) splits++;
+  const int G = n_heads / n_kv;
+  const size_t need = gb_attn_part_floats(n_kv, splits, G, head_dim);
+  if (need > kNoAllocPartFloats)
+    return gb_fail(GB_ERR_UNSUPPORTED,
+                   "gpu: AttnDecode (no-alloc): %zu floats of slice partials needed, the static scratch holds %zu",
+                   need, kNoAllocPartFloats);
+  NoAllocScratch s;
+  if (int rc = noalloc_scratch(k->device, &s)) return rc;
+  // the counters must start at zero (each launch also leaves them at zero)
+  GB_CUDA(cudaMemsetAsync(s.counter, 0, sizeof(unsigned) * (size_t)n_kv, (cudaStream_t)stream),
+          "gpu: AttnDecode (no-alloc): clear counters");
+  GbAttnArgs a;
+  a.q = q;
+  a.k = kcache;
+  a.v = vcache;
+  a.kv_f16 = 0;
+  const long long kv_dim = (long long)n_kv * head_dim;
+  a.k_sh = head_dim;
+  a.k_sd = 4;
+  a.k_st = kv_dim;
+  a.v_sh = head_dim;
+  a.v_st = kv_dim;
+  a.n_heads = n_heads;
+  a.n_kv = n_kv;
+  a.head_dim = head_dim;
+  a.scale = scale;
+  a.kv_len = kv_len;
+  a.splits = splits;
+  a.out = out;
+  a.part = s.part;
+  a.counter = s.counter;
   return gb_attn_launch(a, (cudaStream_t)stream, false);
 }
 

@@ -69,6 +69,7 @@ _SIGS = {
     "gb_gpu_silu_mul": (I, [P, P, P, P, P, I]), "gb_gpu_add": (I, [P, P, P, P, P, I]),
     "gb_gpu_rope": (I, [P, P, P, P, P, I, I, I, F]),
     "gb_gpu_attn_decode": (I, [P, P, P, P, P, P, I, I, I, I, F]),
+    "gb_gpu_attn_decode_noalloc": (I, [P, P, P, P, P, P, I, I, I, I, F]),
     "gb_gpu_matvec_f16": (I, [P, P, P, P, P, I, I, I]), "gb_gpu_matvec_f32": (I, [P, P, P, P, P, I, I, I]),
     "gb_gpu_matvec_q": (I, [P, P, I, P, P, P, I, I, I]), "gb_gpu_ones": (I, [I, C.POINTER(P)]),
     "gb_free": (I, [P]), "gb_gpu_dequant_rows": (I, [P, P, I, P, I, I, I, I, P]),
@@ -196,6 +197,11 @@ class Kernels:
     def attn_decode(self, q, kc, vc, out, kv_len, n_heads, n_kv, head_dim, scale, stream=None):
         _check(lib().gb_gpu_attn_decode(self.h, _stream(stream), _ptr(q), _ptr(kc), _ptr(vc), _ptr(out),
                                         kv_len, n_heads, n_kv, head_dim, scale))
+
+    def attn_decode_noalloc(self, q, kc, vc, out, kv_len, n_heads, n_kv, head_dim, scale, stream=None):
+        """gb_gpu_attn_decode_noalloc: scratch in fixed device arrays (no allocation)."""
+        _check(lib().gb_gpu_attn_decode_noalloc(self.h, _stream(stream), _ptr(q), _ptr(kc), _ptr(vc),
+                                                _ptr(out), kv_len, n_heads, n_kv, head_dim, scale))
 
     def matvec_f16(self, w, x, y, rows, cols, batch, stream=None):
         _check(lib().gb_gpu_matvec_f16(self.h, _stream(stream), _ptr(w), _ptr(x), _ptr(y), rows, cols, batch))

@@ -80,6 +80,19 @@ int gb_gpu_rope(gb_kernels *k, void *stream, float *x, const int32_t *pos, const
 int gb_gpu_attn_decode(gb_kernels *k, void *stream, const float *q, const float *kcache,
                        const float *vcache, float *out, int kv_len, int n_heads, int n_kv,
                        int head_dim, float scale);
+/* AttnDecode with no allocation: no counterpart in the reference. The same
+ * arguments and results as gb_gpu_attn_decode, but the slice partials and
+ * counters live in fixed device arrays of this library (at most 2^20 floats
+ * of partials, i.e. n_kv * slices * (n_heads/n_kv) * (head_dim + 4), and at
+ * most 256 KV heads); larger requests fail with GB_ERR_UNSUPPORTED and a
+ * message naming the limit. It calls no cudaMalloc or cudaFree. The first
+ * call on a device resolves the arrays' addresses for that device, so make
+ * it before any stream capture. Every call on a device shares the arrays:
+ * calls whose work overlaps on the GPU (other streams, other threads) race
+ * and must be serialized by the caller. */
+int gb_gpu_attn_decode_noalloc(gb_kernels *k, void *stream, const float *q, const float *kcache,
+                               const float *vcache, float *out, int kv_len, int n_heads, int n_kv,
+                               int head_dim, float scale);
 /* (*Kernels).MatVecF16, backend/gpu/gpu.go:126: y[b] = W x[b]. */
 int gb_gpu_matvec_f16(gb_kernels *k, void *stream, const uint16_t *w, const float *x, float *y,
                       int rows, int cols, int batch);
