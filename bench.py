@@ -23,6 +23,7 @@ import argparse
 import datetime
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -62,14 +63,19 @@ def peaks():
 
 
 def ncu_traffic(config):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    """DRAM bytes per launch of the dominant kernel (gate/up + SwiGLU GEMV) from the
+    committed ncu summary profiles/step_kernels_8b_traffic.md (line
+    `dram_bytes_per_launch[<config>] = N`); None when no capture covers the config."""
+    p = os.path.join(ROOT, "profiles", "step_kernels_8b_traffic.md")
     try:
         with open(p) as f:
-            d = json.load(f)
-        return d.get(config, {}).get("gateup_dram_bytes_per_launch")
-    except Exception:
-        return None
+            for line in f:
+                m = re.match(r"dram_bytes_per_launch\[(\w+)\]\s*=\s*(\d+)", line.strip())
+                if m and m.group(1) == config:
+                    return int(m.group(2))
+    except OSError:
+        pass
+    return None
 
 
 class ClockSampler:
