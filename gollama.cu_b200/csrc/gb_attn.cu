@@ -72,12 +72,10 @@ GB_DEV float vload(const void *base, long long off) {
 constexpr int part_stride(int hd) { return hd + 4; }
 
 // Shared-memory floats merge_slices needs: weights [S][8], 1/L [8], one
-// float4 per thread, and the merged outputs for packing.
-__host__ __device__ constexpr int merge_floats(int S, int nthr, int G, int HD) {
-  return ((8 * S + 8 + 3) & ~3) + 4 * nthr + G * HD;
-}
+// float4 per thread.
+__host__ __device__ constexpr int merge_floats(int S, int nthr) { return ((8 * S + 8 + 3) & ~3) + 4 * nthr; }
 
-// Merge the S slice partials of KV head h into out (and its pack) with the
+// Merge the S slice partials of KV head h into out with the
 // log-sum-exp rule: out = sum_j exp(m_j - M) o_j / sum_j exp(m_j - M) l_j.
 // Called by every thread of the head's last CTA. The slice weights come from
 // one warp per group head (lanes over slices); the weighted sums are spread
@@ -89,7 +87,6 @@ GB_DEV void merge_slices(const GbAttnArgs &a, int h, int S, int G, float *ms, in
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float *wgt = ms, *linv = ms + 8 * S;
   float4 *red4 = (float4 *)(ms + ((8 * S + 8 + 3) & ~3));
-  float *ov = (float *)(red4 + nthr);
   const float *pb = a.part + (size_t)h * S * G * PS;
   if (warp < G) {
     float M = -INFINITY;
@@ -135,13 +132,6 @@ GB_DEV void merge_slices(const GbAttnArgs &a, int h, int S, int G, float *ms, in
     const float li = linv[tid / (HD / 4)];
     o = make_float4(o.x * li, o.y * li, o.z * li, o.w * li);
     *(float4 *)(a.out + (size_t)h * G * HD + (size_t)tid * 4) = o;
-    ((float4 *)ov)[tid] = o;
-  }
-  if (a.out_pack.a) {
-    __syncthreads();
-    GbXPack pk{a.out_pack.a, a.out_pack.b, a.out_pack.c, a.out_pack.s, a.out_pack.sum16, nullptr};
-    // G*HD and nthr are multiples of 32: a warp packs one whole 32-group
-    for (int i = tid; i < G * HD; i += nthr) gb_pack_group(pk, (h * G * HD + i) / 32, ov[i]);
   }
 }
 
@@ -510,7 +500,7 @@ int launch_flash(const GbAttnArgs &a, cudaStream_t st, bool pdl) {
   using FL = Flash<GM, HD, F16>;
   if (a.splits > 128) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: %d slices (128 at most)", a.splits);
   const size_t smem = FL::smem();
-  static_assert(merge_floats(128, kThreads, GM, HD) * 4 <= kStages * FL::STAGE, "merge scratch exceeds the ring");
+  static_assert(merge_floats(128, kThreads) * 4 <= kStages * FL::STAGE, "merge scratch exceeds the ring");
   static bool attr = false;
   if (!attr) {
     GB_CUDA(cudaFuncSetAttribute(attn_flash_kernel<GM, HD, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
@@ -592,7 +582,7 @@ struct MmaAttn {
   static constexpr size_t smem() { return (size_t)kMStages * STAGE; }
   // after the loop: warp combine buffer [kMW][8][PS] in stage 0, merge scratch in stage 1
   static_assert(kMW * 8 * (HD + 4) * 4 <= STAGE, "combine buffer exceeds a stage");
-  static_assert(merge_floats(128, kMThreads, 8, HD) * 4 <= STAGE, "merge scratch exceeds a stage");
+  static_assert(merge_floats(128, kMThreads) * 4 <= STAGE, "merge scratch exceeds a stage");
 };
 
 template <int HD>
@@ -831,7 +821,7 @@ int launch_t(const GbAttnArgs &a, cudaStream_t st, bool pdl) {
   int cap_len = a.max_len > 0 ? a.max_len : a.kv_len;
   int chunk_cap = (cap_len + a.splits - 1) / a.splits + 1;
   size_t smem = sizeof(float) * ((size_t)GM * HD + (size_t)GM * chunk_cap + (size_t)kWarps * GM * HD);
-  const size_t msmem = sizeof(float) * (size_t)merge_floats(a.splits, kThreads, GM, HD);
+  const size_t msmem = sizeof(float) * (size_t)merge_floats(a.splits, kThreads);
   if (smem < msmem) smem = msmem;
   if (a.splits > 128) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: %d slices (128 at most)", a.splits);
   if (smem > 200 * 1024) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: %d positions per slice", chunk_cap);

@@ -159,41 +159,10 @@ GB_DEV uint4 gb_ld_stream16(const void *p) {
   return v;
 }
 
-// ---- the limb pack of an activation vector ---------------------------------
-// Every group of 32 consecutive elements x[32g..32g+31] is stored as a
-// scale s_g = max|x|/127 and three signed-byte limbs per element with
-//   x ~= s_g * (a + b/254 + c/254^2),  a,b,c in [-127,127],
-// which represents x to within s_g/2/254^2 (about 6e-8 of the group's
-// largest magnitude, the float32 rounding level). Quantized matrix-vector
-// products then run on dp4a with exact int32 sums; `sum16` holds the sum
-// of x over each 16-element half-group (for the ggml offsets and mins) and
-// `ssq` the sum of squares of the residual stream per group (for a
-// following RMSNorm).
-struct GbXPack {
-  int8_t *a, *b, *c;
-  float *s;      // [n/32]
-  float *sum16;  // [n/16]
-  float *ssq;    // [n/32], written only by norm-producing epilogues
-};
-
-// Pack one group from a full warp: lane i holds element 32g+i.
-GB_DEV void gb_pack_group(const GbXPack &p, int g, float v) {
-  const int lane = threadIdx.x & 31;
-  float amax = gb_warp_max(fabsf(v));
-  float inv = amax > 0.f ? 127.f / amax : 0.f;
-  float t = v * inv;
-  float a = rintf(t);
-  float r1 = (t - a) * 254.f;
-  float b = rintf(r1);
-  float r2 = (r1 - b) * 254.f;
-  float c = rintf(r2);
-  int idx = g * 32 + lane;
-  p.a[idx] = (int8_t)(int)a;
-  p.b[idx] = (int8_t)(int)b;
-  p.c[idx] = (int8_t)(int)c;
-  float h = v;
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) h += __shfl_xor_sync(0xffffffffu, h, o);
-  if ((lane & 15) == 0) p.sum16[2 * g + (lane >> 4)] = h;
-  if (lane == 0) p.s[g] = amax / 127.f;
-}
+// ---- the limb form of an activation block ---------------------------------
+// A GEMV stages each 256-element super-block of its input as a scale
+// s = max|x|/127 and three signed-byte limbs per element with
+//   x ~= s * (a + b/254 + c/254^2),  a,b,c in [-127,127],
+// which represents x to within s/2/254^2 (about 6e-8 of the block's largest
+// magnitude, the float32 rounding level). Quantized matrix-vector products
+// then run on dp4a with exact int32 sums (gb_gemv.cu).

@@ -39,20 +39,29 @@ namespace {
 
 constexpr float kL2 = 1.f / 64516.f;  // 1/254^2: limbs b, c are combined as 254*b + c
 
-GB_DEV float byte_f(uint32_t w, int i) { return (float)((w >> (8 * i)) & 0xFFu); }
 
 // ---- per-super-block decode + dot products. `st` is the sb-block in shared
 // memory; xa/xb/xc are the limb planes (as 32-bit words) of the block's 256
-// activation elements, xs the 8 group scales and xsum the 16 half-group sums.
+// activation elements (one scale xs for all 256: x ~ xs*(a + b/254 + c/254^2)),
+// xsum the 16 sums of 16 activation values and sl the 16 per-16 limb sums
+// (int16 a, b, c sums packed in a uint2). The integer dot products of every
+// sub-block are weighted by its integer scale in int32 and converted to float
+// once per super-block.
 template <int T>
 GB_DEV float sb_dot(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                    const uint32_t *xc, const float *xs, const float *xsum);
+                    const uint32_t *xc, const float *xsum, const uint2 *sl, float xs);
+
+GB_DEV int lo16(uint32_t w) { return (int)(int16_t)(w & 0xFFFFu); }
+GB_DEV int hi16(uint32_t w) { return (int)(int16_t)(w >> 16); }
+GB_DEV int byte_i(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xFFu); }
 
 // Q4_K: quant/quant.go:97 layout; kernels/quantmv.go:66 factorisation
-// sum = d*sum_j sc_j*(q.x)_j - dmin*sum_j m_j*(sum x)_j.
+// sum = d*sum_j sc_j*(q.x)_j - dmin*sum_j m_j*(sum x)_j. The high nibbles are
+// used in place (16*q), so their family of sums carries a factor 16.
 template <>
 GB_DEV float sb_dot<GB_T_Q4_K>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                               const uint32_t *xc, const float *xs, const float *xsum) {
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)sl;
   const uint4 *u = (const uint4 *)st;
   const uint4 h = u[lane];
   const float d = gb_half_to_float((uint16_t)(h.x & 0xFFFFu));
@@ -60,7 +69,8 @@ GB_DEV float sb_dot<GB_T_Q4_K>(const uint8_t *st, int lane, const uint32_t *xa, 
   const uint32_t sc03 = h.y & 0x3F3F3F3Fu, m03 = h.z & 0x3F3F3F3Fu;
   const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
   const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-  float tq = 0.f, tm = 0.f;
+  int IA0 = 0, IB0 = 0, IC0 = 0, IA1 = 0, IB1 = 0, IC1 = 0;
+  float tm = 0.f;
 #pragma unroll
   for (int c = 0; c < 4; c++) {
     const uint4 q0 = u[(1 + 2 * c) * 32 + lane], q1 = u[(2 + 2 * c) * 32 + lane];
@@ -87,29 +97,35 @@ GB_DEV float sb_dot<GB_T_Q4_K>(const uint8_t *st, int lane, const uint32_t *xa, 
         C1 = gb_dp4a_us(hi, C4[k], C1);
       }
     }
-    // sum q*x / s_g = A + (254 B + C)/254^2  (254 B + C < 2^24: exact in float)
-    const float S0 = (float)A0 + (float)(254 * B0 + C0) * kL2;
-    const float S1 = ((float)A1 + (float)(254 * B1 + C1) * kL2) * 0.0625f;
     const int j0 = 2 * c, j1 = 2 * c + 1;
-    const float sc0 = byte_f(j0 < 4 ? sc03 : sc47, j0 & 3), sc1 = byte_f(j1 < 4 ? sc03 : sc47, j1 & 3);
-    const float m0 = byte_f(j0 < 4 ? m03 : m47, j0 & 3), m1 = byte_f(j1 < 4 ? m03 : m47, j1 & 3);
-    tq = fmaf(sc0, xs[j0] * S0, tq);
-    tq = fmaf(sc1, xs[j1] * S1, tq);
-    tm = fmaf(m0, xsum[2 * j0] + xsum[2 * j0 + 1], tm);
-    tm = fmaf(m1, xsum[2 * j1] + xsum[2 * j1 + 1], tm);
+    const int sc0 = byte_i(j0 < 4 ? sc03 : sc47, j0 & 3), sc1 = byte_i(j1 < 4 ? sc03 : sc47, j1 & 3);
+    IA0 += sc0 * A0;
+    IB0 += sc0 * B0;
+    IC0 += sc0 * C0;
+    IA1 += sc1 * A1;
+    IB1 += sc1 * B1;
+    IC1 += sc1 * C1;
+    const float m0 = (float)byte_i(j0 < 4 ? m03 : m47, j0 & 3), m1 = (float)byte_i(j1 < 4 ? m03 : m47, j1 & 3);
+    tm = fmaf(m0, xsum[4 * c] + xsum[4 * c + 1], tm);
+    tm = fmaf(m1, xsum[4 * c + 2] + xsum[4 * c + 3], tm);
   }
-  return d * tq - dmin * tm;
+  // sum sc*q*x / xs = A + (254 B + C)/254^2 per family; |I| < 2^28, float error 2^-24
+  const float A = (float)IA0 + (float)IA1 * 0.0625f, B = (float)IB0 + (float)IB1 * 0.0625f,
+              C = (float)IC0 + (float)IC1 * 0.0625f;
+  return d * (xs * (A + (254.f * B + C) * kL2)) - dmin * tm;
 }
 
 // Q6_K: quant/quant.go:114 layout; y = d*sc*(q-32) over 16-element sub-blocks.
+// The -32 enters the dp4a sums as their starting value -32*(limb sums).
 template <>
 GB_DEV float sb_dot<GB_T_Q6_K>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                               const uint32_t *xc, const float *xs, const float *xsum) {
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)xsum;
   const uint4 *u = (const uint4 *)st;
   const uint4 scv = u[12 * 32 + lane];
   const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
   const float d = gb_half_to_float(((const uint16_t *)(st + 13 * 512))[lane]);
-  float acc = 0.f;
+  int IA = 0, IB = 0, IC = 0;
 #pragma unroll
   for (int c = 0; c < 2; c++) {
     const uint4 l0 = u[(4 * c + 0) * 32 + lane], l1 = u[(4 * c + 1) * 32 + lane];
@@ -122,13 +138,15 @@ GB_DEV float sb_dot<GB_T_Q6_K>(const uint8_t *st, int lane, const uint32_t *xa, 
     for (int is = 0; is < 2; is++) {
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        // elements 128c + 32i + 16is .. +15: limb words 32c + 8i + 4is .. +3
-        const uint4 la = ((const uint4 *)xa)[8 * c + 2 * i + is];
-        const uint4 lb = ((const uint4 *)xb)[8 * c + 2 * i + is];
-        const uint4 lc = ((const uint4 *)xc)[8 * c + 2 * i + is];
+        // elements 128c + 32i + 16is .. +15: limb words 32c + 8i + 4is .. +3, 16-group g
+        const int g = 8 * c + 2 * i + is;
+        const uint4 la = ((const uint4 *)xa)[g];
+        const uint4 lb = ((const uint4 *)xb)[g];
+        const uint4 lc = ((const uint4 *)xc)[g];
+        const uint2 o = sl[g];
         const uint32_t a4[4] = {la.x, la.y, la.z, la.w}, b4[4] = {lb.x, lb.y, lb.z, lb.w},
                        c4[4] = {lc.x, lc.y, lc.z, lc.w};
-        int A = 0, B = 0, C = 0;
+        int A = -32 * lo16(o.x), B = -32 * hi16(o.x), C = -32 * lo16(o.y);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
           const int k = 4 * is + kk;
@@ -143,20 +161,22 @@ GB_DEV float sb_dot<GB_T_Q6_K>(const uint8_t *st, int lane, const uint32_t *xa, 
           B = gb_dp4a_us(q, b4[kk], B);
           C = gb_dp4a_us(q, c4[kk], C);
         }
-        const float S = (float)A + (float)(254 * B + C) * kL2;
-        const int si = 8 * c + is + 2 * i;  // scale of this 16-element sub-block
-        const float sc = (float)(int8_t)((scw[si >> 2] >> (8 * (si & 3))) & 0xFFu);
-        acc = fmaf(sc, fmaf(xs[4 * c + i], S, -32.f * xsum[8 * c + 2 * i + is]), acc);
+        const int sc = (int)(int8_t)((scw[g >> 2] >> (8 * (g & 3))) & 0xFFu);  // scale of sub-block g
+        IA += sc * A;
+        IB += sc * B;
+        IC += sc * C;
       }
     }
   }
-  return d * acc;
+  return d * (xs * ((float)IA + (254.f * (float)IB + (float)IC) * kL2));
 }
 
-// Q4_0: eight 32-element blocks per super-block, y = d*(q-8).
+// Q4_0: eight 32-element blocks per super-block, y = d*(q-8); the -8 enters
+// the dp4a sums as their starting value (x16 for the high nibbles, used in place).
 template <>
 GB_DEV float sb_dot<GB_T_Q4_0>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                               const uint32_t *xc, const float *xs, const float *xsum) {
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)xsum;
   const uint4 *u = (const uint4 *)st;
   const uint4 h = u[lane];
   const uint32_t dw[4] = {h.x, h.y, h.z, h.w};
@@ -168,11 +188,13 @@ GB_DEV float sb_dot<GB_T_Q4_0>(const uint8_t *st, int lane, const uint32_t *xa, 
     const uint4 la = ((const uint4 *)xa)[2 * k], ha = ((const uint4 *)xa)[2 * k + 1];
     const uint4 lb = ((const uint4 *)xb)[2 * k], hb = ((const uint4 *)xb)[2 * k + 1];
     const uint4 lc = ((const uint4 *)xc)[2 * k], hc = ((const uint4 *)xc)[2 * k + 1];
+    const uint2 ol = sl[2 * k], oh = sl[2 * k + 1];
     const uint32_t a4[4] = {la.x, la.y, la.z, la.w}, b4[4] = {lb.x, lb.y, lb.z, lb.w},
                    c4[4] = {lc.x, lc.y, lc.z, lc.w};
     const uint32_t A4[4] = {ha.x, ha.y, ha.z, ha.w}, B4[4] = {hb.x, hb.y, hb.z, hb.w},
                    C4[4] = {hc.x, hc.y, hc.z, hc.w};
-    int Al = 0, Bl = 0, Cl = 0, Ah = 0, Bh = 0, Ch = 0;
+    int Al = -8 * lo16(ol.x), Bl = -8 * hi16(ol.x), Cl = -8 * lo16(ol.y);
+    int Ah = -128 * lo16(oh.x), Bh = -128 * hi16(oh.x), Ch = -128 * lo16(oh.y);
 #pragma unroll
     for (int kk = 0; kk < 4; kk++) {
       const uint32_t lo = qw[kk] & 0x0F0F0F0Fu, hi = qw[kk] & 0xF0F0F0F0u;
@@ -186,9 +208,9 @@ GB_DEV float sb_dot<GB_T_Q4_0>(const uint8_t *st, int lane, const uint32_t *xa, 
     const int A = 16 * Al + Ah, B = 16 * Bl + Bh, C = 16 * Cl + Ch;
     const float S = ((float)A + (float)(254 * B + C) * kL2) * 0.0625f;
     const float dk = gb_half_to_float((uint16_t)((dw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu));
-    acc = fmaf(dk, fmaf(xs[k], S, -8.f * (xsum[2 * k] + xsum[2 * k + 1])), acc);
+    acc = fmaf(dk, S, acc);
   }
-  return acc;
+  return xs * acc;
 }
 
 // ---- epilogues (one warp, lane l = row 32*rowblock + l) ---------------------
@@ -203,7 +225,7 @@ GB_DEV uint64_t argmax_key(float v, uint32_t idx) {
 struct Kp {  // kernel parameters
   GbGemvArgs a;
   int rb, nrb;
-  int K;            // units per ring stage
+  int lk;           // log2 of the units per ring stage (K = 1 << lk, K <= consumer warps)
   int nstage;       // ring stages (at most kMaxStages)
   int stage_bytes;  // bytes of one stage buffer (K units of the larger type)
   int xs_max;       // super-blocks of activation staged per CTA
@@ -221,19 +243,16 @@ GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1) {
     int r = rbk * 32 + lane;
     if (r < a.rows) e.y[r] = y0;
   } else if constexpr (EPI == GB_EPI_RESID) {
+    // cpu.Add, backend/cpu/cpu.go:60; the sums of squares feed the next RMSNorm
     int r = rbk * 32 + lane;
-    float xn = e.x[r] + y0;  // cpu.Add, backend/cpu/cpu.go:60
+    float xn = e.x[r] + y0;
     e.x[r] = xn;
-    GbXPack pk{e.out_pack.a, e.out_pack.b, e.out_pack.c, e.out_pack.s, e.out_pack.sum16, e.out_pack.ssq};
-    gb_pack_group(pk, rbk, xn * e.wnorm[r]);
     float ss = gb_warp_sum(xn * xn);
-    if (lane == 0) pk.ssq[rbk] = ss;
+    if (lane == 0) e.ssq[rbk] = ss;
   } else if constexpr (EPI == GB_EPI_SWIGLU) {  // cpu.SiluMul, backend/cpu/cpu.go:53
     float g = y0, u = y1;
     float ex = (float)exp(-(double)g);
-    float act = g / (1.f + ex) * u;
-    GbXPack pk{e.out_pack.a, e.out_pack.b, e.out_pack.c, e.out_pack.s, e.out_pack.sum16, nullptr};
-    gb_pack_group(pk, rbk, act);
+    e.y[rbk * 32 + lane] = g / (1.f + ex) * u;
   } else if constexpr (EPI == GB_EPI_QKV) {
     int r = rbk * 32 + lane;
     int pos = *e.pos;
@@ -326,16 +345,16 @@ GB_DEV unsigned cta_of_unit(unsigned U, unsigned G, unsigned u) {
 
 template <int T>
 __device__ __noinline__ float sb_dot_outlined(const uint8_t *st, int lane, const uint32_t *xa,
-                                              const uint32_t *xb, const uint32_t *xc, const float *xs,
-                                              const float *xsum) {
-  return sb_dot<T>(st, lane, xa, xb, xc, xs, xsum);
+                                              const uint32_t *xb, const uint32_t *xc, const float *xsum,
+                                              const uint2 *sl, float xs) {
+  return sb_dot<T>(st, lane, xa, xb, xc, xsum, sl, xs);
 }
 
 template <int TA, int TB>
 GB_DEV float decode(int ty, const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                    const uint32_t *xc, const float *xs, const float *xsum) {
-  if (TA == TB || ty == TA) return sb_dot<TA>(st, lane, xa, xb, xc, xs, xsum);
-  return sb_dot<TB>(st, lane, xa, xb, xc, xs, xsum);
+                    const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  if (TA == TB || ty == TA) return sb_dot<TA>(st, lane, xa, xb, xc, xsum, sl, xs);
+  return sb_dot<TB>(st, lane, xa, xb, xc, xsum, sl, xs);
 }
 
 // Byte offset of unit u (row-block u / nsb, super-block u % nsb) in the tiled
@@ -361,7 +380,7 @@ GB_DEV void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "m
 // units moved by ONE 1-D TMA bulk copy (tens of KB: few copies and few
 // mbarrier phases keep the copy engine at HBM speed). Consumer warps take
 // the units round-robin (unit j of the CTA goes to warp j mod W), decode them
-// against the activation pack and release each unit's slot through the
+// against the staged activation and release each unit's slot through the
 // stage's `empty` mbarrier, which completes after K releases. The CTA's
 // range is cut into segments, one per row-block it touches; at a segment's
 // end the warps' partial sums are added in warp order by one reducer warp
@@ -372,21 +391,22 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   extern __shared__ __align__(128) uint8_t smem[];
   const GbGemvArgs &a = p.a;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nsb = a.nsb, K = p.K, NS = p.nstage;
+  const int nsb = a.nsb, LK = p.lk, K = 1 << LK, NS = p.nstage;
   const unsigned U = p.units, G = gridDim.x, b = blockIdx.x;
   const unsigned cu0 = ubeg(U, G, b), cu1 = ubeg(U, G, b + 1);
-  const unsigned nst = (cu1 - cu0 + (unsigned)K - 1) / (unsigned)K;  // stages of this CTA
+  const unsigned nst = (cu1 - cu0 + (unsigned)K - 1) >> LK;  // stages of this CTA
 
-  // shared memory: [NS] stages | pack planes a,b,c | scales | sums | 2 x [W][64] segment partials
+  // shared memory: [NS] stages | staged activation [XS] | 2 x [W][64] segment partials
   uint8_t *ring = smem;
   const int XS = p.xs_max;
   uint8_t *xbase = smem + (size_t)NS * p.stage_bytes;
   uint32_t *xa_s = (uint32_t *)xbase;
   uint32_t *xb_s = xa_s + XS * 64;
   uint32_t *xc_s = xb_s + XS * 64;
-  float *xs_s = (float *)(xc_s + XS * 64);
-  float *xsum_s = xs_s + XS * 8;
-  float *psum = xsum_s + XS * 16;  // [2][W][64]
+  float *xsum_s = (float *)(xc_s + XS * 64);
+  uint2 *sl_s = (uint2 *)(xsum_s + XS * 16);
+  float *xs_s = (float *)(sl_s + XS * 16);
+  float *psum = xs_s + ((XS + 3) & ~3);  // [2][W][64]
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
   __shared__ double red[W];
   __shared__ float inv_s;
@@ -415,7 +435,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
           }
           gb_fence_proxy_async();
         }
-        const unsigned j0 = cu0 + k * (unsigned)K, j1 = min(cu1, j0 + (unsigned)K);
+        const unsigned j0 = cu0 + (k << LK), j1 = min(cu1, j0 + (unsigned)K);
         const size_t o0 = unit_off<TA, TB>(p, j0), o1 = unit_off<TA, TB>(p, j1);
         gb_mbar_expect_tx(&full[s], (uint32_t)(o1 - o0));
         gb_bulk_g2s(ring + (size_t)s * p.stage_bytes, a.w + o0, (uint32_t)(o1 - o0), &full[s]);
@@ -427,87 +447,138 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
     return;
   }
 
-  // 2. the activation pack (and the norm's sums of squares) come from the
-  // preceding kernel: one round trip for all of it
+  // 2. stage the activation of the super-blocks this CTA touches. The input
+  // is a float vector from the preceding kernel; an RMS-normalised input is
+  // z = (x * inv) * w with inv = 1/sqrt(sum x^2 / n + eps) from per-32 sums of
+  // squares (cpu.RMSNorm, backend/cpu/cpu.go:17: float64 sum, float32 products).
+  // Per super-block: s = max|z| / 127 and three int8 limbs per element,
+  // z ~ s*(a + b/254 + c/254^2) (error below 2^-21 of the block maximum).
   constexpr int CT = W * 32;
   const int tid = threadIdx.x;
   gb_grid_dep_wait();
   const int nsbs = (cu1 - cu0) >= (unsigned)nsb ? nsb : (int)(cu1 - cu0);
   const int sbf = (int)(cu0 % (unsigned)nsb);
-  {
+  float inv = 1.f;
+  if (a.in_ssq) {
     double ss = 0;
-    if (a.in_ssq)
-      for (int g = tid; g < nsb * 8; g += CT) ss += (double)__ldcg(a.in_ssq + g);
-    for (int i = tid; i < nsbs * 48; i += CT) {  // 3 planes x 16 uint4 per sb
-      const int plane = i / (nsbs * 16), rest = i - plane * (nsbs * 16);
-      const int ls = rest >> 4, v = rest & 15;
-      int sb = sbf + ls;
-      if (sb >= nsb) sb -= nsb;
-      const int8_t *src = plane == 0 ? a.in.a : plane == 1 ? a.in.b : a.in.c;
-      uint32_t *dst = plane == 0 ? xa_s : plane == 1 ? xb_s : xc_s;
-      ((uint4 *)(dst + ls * 64))[v] = __ldcg((const uint4 *)(src + sb * 256) + v);
-    }
-    for (int i = tid; i < nsbs * 24; i += CT) {
-      const int ls = i / 24, v = i - ls * 24;
-      int sb = sbf + ls;
-      if (sb >= nsb) sb -= nsb;
-      if (v < 8)
-        xs_s[ls * 8 + v] = __ldcg(a.in.s + sb * 8 + v);
-      else
-        xsum_s[ls * 16 + v - 8] = __ldcg(a.in.sum16 + sb * 16 + v - 8);
-    }
-    if (a.in_ssq) {  // cpu.RMSNorm, backend/cpu/cpu.go:17: inv = 1/sqrt(sum/n + eps), float64
+    for (int g = tid; g < nsb * 8; g += CT) ss += (double)__ldcg(a.in_ssq + g);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) red[warp] = ss;
-      consumers_sync<W>();
-      if (tid == 0) {
-        double t = 0;
-        for (int w2 = 0; w2 < W; w2++) t += red[w2];
-        inv_s = (float)(1.0 / sqrt(t / (double)(nsb * 256) + (double)a.eps));
-      }
-      consumers_sync<W>();
-      const float inv = inv_s;
-      for (int i = tid; i < nsbs * 24; i += CT) {
-        const int ls = i / 24, v = i - ls * 24;
-        if (v < 8) xs_s[ls * 8 + v] *= inv;
-        else xsum_s[ls * 16 + v - 8] *= inv;
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    consumers_sync<W>();
+    if (tid == 0) {
+      double t = 0;
+      for (int w2 = 0; w2 < W; w2++) t += red[w2];
+      inv_s = (float)(1.0 / sqrt(t / (double)(nsb * 256) + (double)a.eps));
+    }
+    consumers_sync<W>();
+    inv = inv_s;
+  }
+  for (int ls = warp; ls < nsbs; ls += W) {
+    int sb = sbf + ls;
+    if (sb >= nsb) sb -= nsb;
+    const int e0 = sb * 256 + lane * 8;
+    float z[8];
+    {
+      const float4 x0 = __ldcg((const float4 *)(a.in_x + e0)), x1 = __ldcg((const float4 *)(a.in_x + e0 + 4));
+      z[0] = x0.x; z[1] = x0.y; z[2] = x0.z; z[3] = x0.w;
+      z[4] = x1.x; z[5] = x1.y; z[6] = x1.z; z[7] = x1.w;
+      if (a.in_w) {
+        const float4 w0 = __ldg((const float4 *)(a.in_w + e0)), w1 = __ldg((const float4 *)(a.in_w + e0 + 4));
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) z[i] = __fmul_rn(__fmul_rn(z[i], inv), wv[i]);
       }
     }
+    float m = 0.f, zs = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      m = fmaxf(m, fabsf(z[i]));
+      zs += z[i];
+    }
+    m = gb_warp_max(m);
+    const float r = m > 0.f ? 127.f / m : 0.f;
+    uint32_t wa[2] = {0u, 0u}, wb[2] = {0u, 0u}, wc[2] = {0u, 0u};
+    int sa = 0, sbs = 0, sc = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float t = z[i] * r;
+      const float fa = rintf(t), r1 = (t - fa) * 254.f, fb = rintf(r1), fc = rintf((r1 - fb) * 254.f);
+      const int ia = (int)fa, ib = (int)fb, ic = (int)fc;
+      sa += ia;
+      sbs += ib;
+      sc += ic;
+      wa[i >> 2] |= (uint32_t)(ia & 0xFF) << (8 * (i & 3));
+      wb[i >> 2] |= (uint32_t)(ib & 0xFF) << (8 * (i & 3));
+      wc[i >> 2] |= (uint32_t)(ic & 0xFF) << (8 * (i & 3));
+    }
+    ((uint2 *)(xa_s + ls * 64))[lane] = make_uint2(wa[0], wa[1]);
+    ((uint2 *)(xb_s + ls * 64))[lane] = make_uint2(wb[0], wb[1]);
+    ((uint2 *)(xc_s + ls * 64))[lane] = make_uint2(wc[0], wc[1]);
+    // lanes 2i and 2i+1 hold 16-group i
+    zs += __shfl_xor_sync(0xffffffffu, zs, 1);
+    sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+    sbs += __shfl_xor_sync(0xffffffffu, sbs, 1);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+    if ((lane & 1) == 0) {
+      xsum_s[ls * 16 + (lane >> 1)] = zs;
+      sl_s[ls * 16 + (lane >> 1)] =
+          make_uint2(((uint32_t)sa & 0xFFFFu) | ((uint32_t)sbs << 16), (uint32_t)sc & 0xFFFFu);
+    }
+    if (lane == 0) xs_s[ls] = m / 127.f;
   }
   consumers_sync<W>();
 
-  // 3. units round-robin over the warps, segment by segment
+  // 3. units round-robin over the warps, segment by segment. Cursors advance
+  // by W units per step: stage k = j >> LK (K is a power of two), ring slot
+  // s = k mod NS with the phase parity ph, super-block usb = u mod nsb.
   const size_t sbb_a = (size_t)gb_tiled_sb_bytes(TA);
+  const unsigned dk = (unsigned)W >> LK;  // stages per step (K <= W)
   bool timeout = false;
   unsigned j = (unsigned)warp;  // this warp's next unit (CTA-relative)
+  unsigned k = j >> LK;
+  int s = (int)(k % (unsigned)NS);
+  uint32_t ph = (k / (unsigned)NS) & 1u;
+  unsigned usb = (cu0 + j) % (unsigned)nsb;
   int nseg = 0;
   for (unsigned s0 = cu0; s0 < cu1; nseg++) {
     const int rbk = (int)(s0 / (unsigned)nsb);
     const unsigned s1 = min(cu1, (unsigned)(rbk + 1) * (unsigned)nsb);
+    const int ty = rbk < a.split_tile ? TA : TB;
     float acc0 = 0.f, acc1 = 0.f;
-    for (; cu0 + j < s1; j += W) {
-      const unsigned u = cu0 + j, k = j / (unsigned)K;
-      const int s = (int)(k % (unsigned)NS);
-      if (!timeout && !gb_mbar_wait(&full[s], (k / NS) & 1)) timeout = true;
+    for (; cu0 + j < s1;) {
+      const unsigned u = cu0 + j;
+      if (!timeout && !gb_mbar_wait(&full[s], ph)) timeout = true;
       if (!timeout) {
-        int ls = (int)(u % (unsigned)nsb) - sbf;
+        int ls = (int)usb - sbf;
         if (ls < 0) ls += nsb;
         const uint32_t *xa = xa_s + ls * 64, *xb = xb_s + ls * 64, *xc = xc_s + ls * 64;
-        const float *xs = xs_s + ls * 8, *xsum = xsum_s + ls * 16;
-        const uint8_t *st = ring + (size_t)s * p.stage_bytes +
-                            (unit_off<TA, TB>(p, u) - unit_off<TA, TB>(p, cu0 + k * (unsigned)K));
+        const float *xsum = xsum_s + ls * 16;
+        const uint2 *sl = sl_s + ls * 16;
+        const float xs = xs_s[ls];
+        const size_t off = TA == TB ? (size_t)(j & (unsigned)(K - 1)) * (size_t)p.rb * sbb_a
+                                    : unit_off<TA, TB>(p, u) - unit_off<TA, TB>(p, cu0 + (k << LK));
+        const uint8_t *st = ring + (size_t)s * p.stage_bytes + off;
         if constexpr (EPI == GB_EPI_SWIGLU) {
           // gate then up sb-block; one decode at a time keeps the register
           // footprint of a single tile
-          acc0 += sb_dot_outlined<TA>(st, lane, xa, xb, xc, xs, xsum);
-          acc1 += sb_dot_outlined<TA>(st + sbb_a, lane, xa, xb, xc, xs, xsum);
+          acc0 += sb_dot_outlined<TA>(st, lane, xa, xb, xc, xsum, sl, xs);
+          acc1 += sb_dot_outlined<TA>(st + sbb_a, lane, xa, xb, xc, xsum, sl, xs);
         } else {
-          acc0 += decode<TA, TB>(rbk < a.split_tile ? TA : TB, st, lane, xa, xb, xc, xs, xsum);
+          acc0 += decode<TA, TB>(ty, st, lane, xa, xb, xc, xsum, sl, xs);
         }
       }
       __syncwarp();
       if (lane == 0) gb_mbar_arrive(&empty[s]);
+      j += W;
+      k += dk;
+      s += (int)dk;
+      while (s >= NS) {
+        s -= NS;
+        ph ^= 1u;
+      }
+      usb += W;
+      while (usb >= (unsigned)nsb) usb -= nsb;
     }
     float *ps = psum + (size_t)(nseg & 1) * W * 64;
     ps[warp * 64 + lane] = acc0;
@@ -540,9 +611,9 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
           for (unsigned b2 = bf; b2 <= bl; b2++) {
             const unsigned c0 = ubeg(U, G, b2), c1 = ubeg(U, G, b2 + 1);
             if (c0 == c1) continue;
-            const float *sl = a.e.part + ((size_t)b2 * 2 + (c0 >= R0 ? 0 : 1)) * 64;
-            z0 += __ldcg(sl + lane);
-            z1 += __ldcg(sl + 32 + lane);
+            const float *sl2 = a.e.part + ((size_t)b2 * 2 + (c0 >= R0 ? 0 : 1)) * 64;
+            z0 += __ldcg(sl2 + lane);
+            z1 += __ldcg(sl2 + 32 + lane);
           }
           if (lane == 0) a.e.tile_counter[rbk] = 0u;
           epilogue<EPI>(p, rbk, z0, z1);
@@ -573,14 +644,6 @@ __global__ void repack_kernel(int typ, const uint8_t *raw, int rows, int nsb, in
   }
 }
 
-// ---- standalone limb pack of a float vector (one warp per group) ---------
-__global__ void pack_kernel(const float *x, int n, GbXPackBuf p) {
-  int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (g >= n / 32) return;
-  GbXPack pk{p.a, p.b, p.c, p.s, p.sum16, nullptr};
-  gb_pack_group(pk, g, x[g * 32 + (threadIdx.x & 31)]);
-}
-
 int g_sms = 0;
 int sms() {
   if (!g_sms) {
@@ -592,8 +655,12 @@ int sms() {
   return g_sms;
 }
 
+// Dynamic shared memory: ring stages, then per staged super-block the limb
+// planes (3 x 256 B), 16 sums (64 B) and 16 packed limb sums (128 B), the
+// scales (padded to 4 floats), then 2 x [warps][64] segment partials.
 size_t gemv_smem(int warps, int nstage, int stage_bytes, int xs_max) {
-  return (size_t)nstage * stage_bytes + (size_t)xs_max * (3 * 256 + 4 * 24) + (size_t)2 * warps * 64 * 4;
+  return (size_t)nstage * stage_bytes + (size_t)xs_max * (3 * 256 + 64 + 128) +
+         (size_t)((xs_max + 3) & ~3) * 4 + (size_t)2 * warps * 64 * 4;
 }
 
 using KernelFn = void (*)(Kp);
@@ -656,14 +723,6 @@ int gb_repack_launch(int typ, const uint8_t *raw, int rows, int cols, uint8_t *t
   if (blocks > 65535LL * 8) blocks = 65535LL * 8;
   repack_kernel<<<(unsigned)blocks, 256, 0, st>>>(typ, raw, rows, nsb, ntiles, tiled);
   GB_CUDA(cudaGetLastError(), "gpu: repack");
-  return GB_OK;
-}
-
-int gb_pack_launch(const float *x, int n, const GbXPackBuf &p, cudaStream_t st) {
-  if (n % 32) return gb_fail(GB_ERR_INVALID, "gpu: pack: %d is not a multiple of 32", n);
-  int groups = n / 32;
-  pack_kernel<<<(groups + 7) / 8, 256, 0, st>>>(x, n, p);
-  GB_CUDA(cudaGetLastError(), "gpu: pack");
   return GB_OK;
 }
 
@@ -749,19 +808,31 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   if (const char *e = getenv("GB_SMEM_BUDGET")) budget = atoll(e);
   const long long room = cap - static_smem;
   const long long fixed = (long long)gemv_smem(warps, 0, 0, xs);
-  int K = std::max(1, std::min(16, (36 * 1024 + ub / 2) / ub)), ns = 0;
-  K = std::min(K, upc);
-  if (fk > 0 && fs >= 2 && fs <= kMaxStages && fixed + (long long)fs * fk * ub <= room) {
+  // K: a power of two, at most the consumer warps (each warp then takes one
+  // unit every warps/K stages), about 36 KB per stage, at most the units a
+  // CTA owns
+  auto pow2_floor = [](int v) {
+    int r = 1;
+    while (r * 2 <= v) r *= 2;
+    return r;
+  };
+  int K = pow2_floor(std::max(1, std::min(warps, (36 * 1024 + ub / 2) / ub)));
+  K = std::min(K, pow2_floor(std::max(1, upc)));
+  int ns = 0;
+  if (fk > 0 && fk <= warps && (fk & (fk - 1)) == 0 && fs >= 2 && fs <= kMaxStages &&
+      fixed + (long long)fs * fk * ub <= room) {
     K = fk;
     ns = fs;
   } else {
-    for (;; K--) {
+    for (;; K /= 2) {
       ns = (int)std::min<long long>(kMaxStages, (budget - fixed) / ((long long)K * ub));
       if (ns >= 2 || K == 1) break;
     }
     if (ns < 2) ns = 2;
   }
-  p.K = K;
+  int lk = 0;
+  while ((1 << lk) < K) lk++;
+  p.lk = lk;
   p.nstage = ns;
   p.stage_bytes = (K * ub + 127) / 128 * 128;
   p.xs_max = xs;

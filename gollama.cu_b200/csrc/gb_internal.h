@@ -25,21 +25,12 @@ void gb_clear_error();
     if (e_ != cudaSuccess) return gb_cuda_fail(e_, what); \
   } while (0)
 
-// ---- the limb pack of a device vector (see gb_device.cuh)
-struct GbXPackBuf {
-  int n = 0;
-  int8_t *a = nullptr, *b = nullptr, *c = nullptr;
-  float *s = nullptr, *sum16 = nullptr, *ssq = nullptr;
-};
-int gb_xpack_alloc(GbXPackBuf *p, int n);
-void gb_xpack_free(GbXPackBuf *p);
-
 // ---- tiled GEMV (gb_gemv.cu)
 enum GbEpi {
   GB_EPI_PLAIN = 0,   // y[r] = W x
   GB_EPI_QKV = 1,     // RoPE q,k; q -> qbuf, k,v -> KV cache at *pos
-  GB_EPI_RESID = 2,   // x[r] += y; pack x*wnorm (+ssq) for the next layer
-  GB_EPI_SWIGLU = 3,  // gate/up tile pairs -> act = silu(g)*u, packed
+  GB_EPI_RESID = 2,   // x[r] += y; per-32 sums of squares for the next RMSNorm
+  GB_EPI_SWIGLU = 3,  // gate/up pairs -> act = silu(g)*u
   GB_EPI_LOGITS = 4,  // logits[r] = y; argmax candidates; last CTA -> token
 };
 
@@ -57,11 +48,10 @@ struct GbEpiArgs {
   int q_rows = 0, kv_rows = 0, head_dim = 0, max_len = 0, kv_f16 = 1;
   const double *rope_cs = nullptr;  // [max_len][head_dim/2][2] (cos, sin)
   const int32_t *pos = nullptr;
-  // RESID
+  // RESID: x += y and per-row-block sums of squares of the new x
   float *x = nullptr;
-  const float *wnorm = nullptr;
-  GbXPackBuf out_pack;
-  // LOGITS / PLAIN
+  float *ssq = nullptr;
+  // LOGITS / PLAIN / SWIGLU output
   float *y = nullptr;
   unsigned long long *best = nullptr;     // running argmax key (zero between launches)
   unsigned long long *key_out = nullptr;  // tensor parallel: final local key
@@ -81,8 +71,9 @@ struct GbGemvArgs {
   int type_a = GB_T_Q4_K, type_b = GB_T_Q4_K;
   int split_tile = 1 << 30;    // tiles >= split_tile use type_b
   int rows = 0, ntiles = 0, nsb = 0;
-  GbXPackBuf in;               // input pack
-  const float *in_ssq = nullptr;  // non-null: the input is RMS-normalised (ssq partials)
+  const float *in_x = nullptr;    // input vector [nsb*256] (float, from the preceding kernel)
+  const float *in_w = nullptr;    // RMSNorm weights when the input is normalised in the prologue
+  const float *in_ssq = nullptr;  // per-32 sums of squares of in_x (with in_w)
   float eps = 1e-5f;
   int epi = GB_EPI_PLAIN;
   GbEpiArgs e;
@@ -93,7 +84,6 @@ GbGemvPlan gb_gemv_plan(int ntiles, int nsb, int epi, int sms);
 size_t gb_tiled_bytes(int typ, int rows, int cols);
 int gb_repack_launch(int typ, const uint8_t *raw, int rows, int cols, uint8_t *tiled,
                      cudaStream_t st);
-int gb_pack_launch(const float *x, int n, const GbXPackBuf &p, cudaStream_t st);
 int gb_gemv_scratch_floats(int ntiles, const GbGemvPlan &p);
 
 // ---- attention (gb_attn.cu)
@@ -112,8 +102,7 @@ struct GbAttnArgs {
   int max_len = 0;
   int splits = 1;
   float *out = nullptr;          // [n_heads*head_dim]
-  GbXPackBuf out_pack;           // optional pack of out (model path)
-  float *part = nullptr;         // [n_kv][splits][group*(head_dim+2)]
+  float *part = nullptr;         // [n_kv][splits][group][head_dim+4]
   unsigned *counter = nullptr;   // [n_kv], zero between launches
   unsigned *err = nullptr;
 };
@@ -122,11 +111,11 @@ int gb_attn_splits(int n_kv, int max_len, int sms);
 size_t gb_attn_part_floats(int n_kv, int splits, int group, int head_dim);
 
 // ---- misc kernels (gb_ops.cu)
+// Embedding row of *token into x, with per-32 sums of squares (first RMSNorm).
 int gb_embed_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
-                    int vocab, float *x, const float *wnorm, const GbXPackBuf &pk,
-                    unsigned *err, cudaStream_t st, bool pdl);
-int gb_resid_pack_launch(float *x, const float *y, const float *wnorm, int n,
-                         const GbXPackBuf &pk, cudaStream_t st, bool pdl);
+                    int vocab, float *x, float *ssq, unsigned *err, cudaStream_t st, bool pdl);
+// x += y with per-32 sums of squares: the residual after a collective.
+int gb_resid_launch(float *x, const float *y, int n, float *ssq, cudaStream_t st, bool pdl);
 // Reduce n per-rank argmax keys (tensor-parallel lm_head) to the token.
 int gb_argmax_keys_launch(const unsigned long long *keys, int n, int32_t *token, int32_t *hist,
                           const int32_t *pos, int max_len, cudaStream_t st);

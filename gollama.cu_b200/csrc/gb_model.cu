@@ -140,7 +140,6 @@ enum { K_QKV = 0, K_ATTN, K_O, K_GU, K_DOWN, K_HEAD, K_OTHER, K_CLASSES };
 struct gb_linear {
   int device = 0;
   Tiled t;
-  GbXPackBuf pack;
   float *part = nullptr;
   unsigned *tile_counter = nullptr;
 };
@@ -162,7 +161,8 @@ struct gb_model {
   // work
   float *x = nullptr, *q = nullptr, *attn = nullptr, *logits = nullptr, *logits_full = nullptr,
         *ypart = nullptr;
-  GbXPackBuf pack_dim, pack_q, pack_ffn;
+  float *act = nullptr;  // SwiGLU output [ffn_local]
+  float *ssq = nullptr;  // per-32 sums of squares of x [dim/32] (RMSNorm input)
   int32_t *token = nullptr, *pos = nullptr, *gen = nullptr;
   unsigned *err = nullptr;
   float *gemv_part = nullptr;
@@ -298,8 +298,9 @@ struct Hook {
   int n = 0;
 };
 
-GbGemvArgs gemv_args(const Tiled &t, const GbXPackBuf &in, const float *in_ssq, float eps, int epi,
-                     gb_model *m) {
+// GEMV arguments; the input is x (float), RMS-normalised with `norm` in the
+// GEMV's prologue when norm is non-null (per-32 sums of squares in m->ssq).
+GbGemvArgs gemv_args(const Tiled &t, const float *x, const float *norm, float eps, int epi, gb_model *m) {
   GbGemvArgs a;
   a.w = t.w;
   a.type_a = t.type_a;
@@ -308,8 +309,9 @@ GbGemvArgs gemv_args(const Tiled &t, const GbXPackBuf &in, const float *in_ssq, 
   a.rows = t.rows;
   a.ntiles = t.ntiles;
   a.nsb = t.nsb;
-  a.in = in;
-  a.in_ssq = in_ssq;
+  a.in_x = x;
+  a.in_w = norm;
+  a.in_ssq = norm ? m->ssq : nullptr;
   a.eps = eps;
   a.epi = epi;
   a.e.err = m->err;
@@ -339,14 +341,13 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
     hook->cls[hook->n] = -1;
     GB_CUDA(cudaEventRecord(hook->ev[hook->n++], st), "model: profile event");
   }
-  rc = gb_embed_launch(m->embd_type, m->embd.w, m->embd_nsb, c.dim, m->token, c.vocab, m->x,
-                       m->layers[0].attn_norm, m->pack_dim, m->err, st, pdl);
+  rc = gb_embed_launch(m->embd_type, m->embd.w, m->embd_nsb, c.dim, m->token, c.vocab, m->x, m->ssq,
+                       m->err, st, pdl);
   if (rc || (rc = mark(K_OTHER))) return rc;
   for (int l = 0; l < c.layers; l++) {
     gb_model::Layer &L = m->layers[l];
-    const float *next_norm = l + 1 < c.layers ? m->layers[l + 1].attn_norm : m->out_norm;
-    // q, k, v with RoPE and the KV-cache store fused in the epilogue
-    GbGemvArgs a = gemv_args(L.qkv, m->pack_dim, m->pack_dim.ssq, c.eps, GB_EPI_QKV, m);
+    // attn RMSNorm in the prologue; q, k, v with RoPE and the KV-cache store in the epilogue
+    GbGemvArgs a = gemv_args(L.qkv, m->x, L.attn_norm, c.eps, GB_EPI_QKV, m);
     a.e.q_out = m->q;
     a.e.kcache = L.kc;
     a.e.vcache = L.vc;
@@ -356,7 +357,7 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
     a.e.kv_f16 = c.kv_f16;
     a.e.rope_cs = m->rope_cs;
     if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_QKV))) return rc;
-    // attention over the cache, output packed for the o projection
+    // attention over the cache
     GbAttnArgs at;
     at.q = m->q;
     at.k = L.kc;
@@ -377,52 +378,45 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
     at.max_len = c.max_len;
     at.splits = m->attn_splits;
     at.out = m->attn;
-    at.out_pack = m->pack_q;
     at.part = m->attn_part;
     at.counter = m->attn_counter;
     at.err = m->err;
     if ((rc = gb_attn_launch(at, st, pdl)) || (rc = mark(K_ATTN))) return rc;
-    // o projection + residual (+ pack for the FFN norm)
+    // o projection + residual (+ sums of squares for the FFN norm)
     if (!tp) {
-      a = gemv_args(L.wo, m->pack_q, nullptr, c.eps, GB_EPI_RESID, m);
+      a = gemv_args(L.wo, m->attn, nullptr, c.eps, GB_EPI_RESID, m);
       a.e.x = m->x;
-      a.e.wnorm = L.ffn_norm;
-      a.e.out_pack = m->pack_dim;
+      a.e.ssq = m->ssq;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_O))) return rc;
     } else {
-      a = gemv_args(L.wo, m->pack_q, nullptr, c.eps, GB_EPI_PLAIN, m);
+      a = gemv_args(L.wo, m->attn, nullptr, c.eps, GB_EPI_PLAIN, m);
       a.e.y = m->ypart;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_O))) return rc;
       GB_NCCL(nccl()->allReduce(m->ypart, m->ypart, (size_t)c.dim, ncclFloat, ncclSum, m->comm, st),
               "model: all-reduce");
-      if ((rc = gb_resid_pack_launch(m->x, m->ypart, L.ffn_norm, c.dim, m->pack_dim, st, false)) ||
-          (rc = mark(K_OTHER)))
-        return rc;
+      if ((rc = gb_resid_launch(m->x, m->ypart, c.dim, m->ssq, st, false)) || (rc = mark(K_OTHER))) return rc;
     }
-    // gate/up + SwiGLU
-    a = gemv_args(L.gu, m->pack_dim, m->pack_dim.ssq, c.eps, GB_EPI_SWIGLU, m);
-    a.e.out_pack = m->pack_ffn;
+    // FFN RMSNorm in the prologue; gate/up + SwiGLU
+    a = gemv_args(L.gu, m->x, L.ffn_norm, c.eps, GB_EPI_SWIGLU, m);
+    a.e.y = m->act;
     if ((rc = gb_gemv_launch(a, m->plan_gu, st, pdl)) || (rc = mark(K_GU))) return rc;
-    // down + residual (+ pack for the next layer's norm)
+    // down + residual (+ sums of squares for the next norm)
     if (!tp) {
-      a = gemv_args(L.down, m->pack_ffn, nullptr, c.eps, GB_EPI_RESID, m);
+      a = gemv_args(L.down, m->act, nullptr, c.eps, GB_EPI_RESID, m);
       a.e.x = m->x;
-      a.e.wnorm = next_norm;
-      a.e.out_pack = m->pack_dim;
+      a.e.ssq = m->ssq;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_DOWN))) return rc;
     } else {
-      a = gemv_args(L.down, m->pack_ffn, nullptr, c.eps, GB_EPI_PLAIN, m);
+      a = gemv_args(L.down, m->act, nullptr, c.eps, GB_EPI_PLAIN, m);
       a.e.y = m->ypart;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_DOWN))) return rc;
       GB_NCCL(nccl()->allReduce(m->ypart, m->ypart, (size_t)c.dim, ncclFloat, ncclSum, m->comm, st),
               "model: all-reduce");
-      if ((rc = gb_resid_pack_launch(m->x, m->ypart, next_norm, c.dim, m->pack_dim, st, false)) ||
-          (rc = mark(K_OTHER)))
-        return rc;
+      if ((rc = gb_resid_launch(m->x, m->ypart, c.dim, m->ssq, st, false)) || (rc = mark(K_OTHER))) return rc;
     }
   }
-  // lm_head + argmax (model.Argmax on the device)
-  GbGemvArgs a = gemv_args(m->head, m->pack_dim, m->pack_dim.ssq, c.eps, GB_EPI_LOGITS, m);
+  // output RMSNorm in the prologue; lm_head + argmax (model.Argmax on the device)
+  GbGemvArgs a = gemv_args(m->head, m->x, m->out_norm, c.eps, GB_EPI_LOGITS, m);
   a.e.y = m->logits;
   a.e.best = m->best;
   a.e.counter = m->done;
@@ -503,9 +497,6 @@ void free_model(gb_model *m) {
   if (m->graph) cudaGraphExecDestroy(m->graph);
   if (m->comm && nccl() && nccl()->commDestroy) nccl()->commDestroy(m->comm);
   for (void *p : m->allocs) cudaFree(p);
-  gb_xpack_free(&m->pack_dim);
-  gb_xpack_free(&m->pack_q);
-  gb_xpack_free(&m->pack_ffn);
   if (m->h_stage) cudaFreeHost(m->h_stage);
   if (m->h_logits) cudaFreeHost(m->h_logits);
   if (m->st) cudaStreamDestroy(m->st);
@@ -662,7 +653,8 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
   const GbTensor *head = f->tensor("output.weight");
   if (head) {
     const GbTensor *h2;
-    if ((rc = check_matrix(f, "output.weight", c.vocab, c.dim, &h2))) return fail(rc);
+    rc = check_matrix(f, "output.weight", c.vocab, c.dim, &h2);
+    if (rc) return fail(rc);
     if ((rc = alloc_tiled(m, &m->head, head->type, head->type, 1 << 30, (m->vocab_local + 31) / 32, c.dim / 256,
                           m->vocab_local, c.dim)))
       return fail(rc);
@@ -713,8 +705,8 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
       (rc = dalloc(m, &m->best, 1, "model: work")) || (rc = dalloc(m, &m->key_local, 1, "model: work")) ||
       (rc = dalloc(m, &m->keys, (size_t)N, "model: work")) || (rc = dalloc(m, &m->done, 1, "model: work")))
     return fail(rc);
-  if ((rc = gb_xpack_alloc(&m->pack_dim, c.dim)) || (rc = gb_xpack_alloc(&m->pack_q, m->q_local)) ||
-      (rc = gb_xpack_alloc(&m->pack_ffn, m->ffn_local)))
+  if ((rc = dalloc(m, &m->act, (size_t)m->ffn_local, "model: work")) ||
+      (rc = dalloc(m, &m->ssq, (size_t)c.dim / 32, "model: work")))
     return fail(rc);
   m->plan_plain = gb_gemv_plan(0, 0, GB_EPI_PLAIN, m->sms);
   m->plan_gu = gb_gemv_plan(0, 0, GB_EPI_SWIGLU, m->sms);
@@ -983,7 +975,6 @@ int gb_tp_unique_id(uint8_t out[128]) {
 static void free_linear(gb_linear *l) {
   if (!l) return;
   if (l->t.w) cudaFree(l->t.w);
-  gb_xpack_free(&l->pack);
   if (l->part) cudaFree(l->part);
   if (l->tile_counter) cudaFree(l->tile_counter);
   delete l;
@@ -1017,7 +1008,6 @@ int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes,
     if (e != cudaSuccess) rc = gb_cuda_fail(e, "model: linear repack");
   }
   if (raw) cudaFree(raw);
-  if (!rc) rc = gb_xpack_alloc(&l->pack, cols);
   GbGemvPlan plan = gb_gemv_plan(t.ntiles, t.nsb, GB_EPI_PLAIN, 148);
   if (!rc && cudaMalloc(&l->part, sizeof(float) * (size_t)gb_gemv_scratch_floats(t.ntiles, plan) * 2) != cudaSuccess)
     rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
@@ -1036,16 +1026,15 @@ int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes,
 int gb_linear_matvec(gb_linear *l, void *stream, const float *x, float *y) {
   gb_clear_error();
   if (!l) return gb_fail(GB_ERR_INVALID, "model: linear: null handle");
+  if ((uintptr_t)x % 16) return gb_fail(GB_ERR_INVALID, "model: linear: x must be 16-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
-  int rc = gb_pack_launch(x, l->t.cols, l->pack, st);
-  if (rc) return rc;
   GbGemvArgs a;
   a.w = l->t.w;
   a.type_a = a.type_b = l->t.type_a;
   a.rows = l->t.rows;
   a.ntiles = l->t.ntiles;
   a.nsb = l->t.nsb;
-  a.in = l->pack;
+  a.in_x = x;
   a.epi = GB_EPI_PLAIN;
   a.e.y = y;
   a.e.part = l->part;

@@ -232,11 +232,10 @@ __global__ void argmax_keys_kernel(const unsigned long long *keys, int n, int32_
 __global__ void advance_pos_kernel(int32_t *pos) { *pos += 1; }
 
 // Embedding lookup (model/model.go:326 quant.Row on the host, moved on the
-// device): row *token of the tiled token_embd, bit-exact, into x; packs
-// x*wnorm and the per-group sums of squares for the first RMSNorm.
+// device): row *token of the tiled token_embd, bit-exact, into x, with the
+// per-32 sums of squares the first RMSNorm needs.
 __global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
-                             int vocab, float *x, const float *wnorm, GbXPackBuf pk,
-                             unsigned *err) {
+                             int vocab, float *x, float *ssq, unsigned *err) {
   __shared__ __align__(16) uint8_t blk[8][224];
   gb_grid_dep_launch();
   gb_grid_dep_wait();
@@ -256,18 +255,14 @@ __global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, co
   int e = (g % 8) * 32 + lane;  // element within the super-block
   float v = typ == GB_T_Q4_0 ? gb_dequant_elem(typ, blk[warp] + 18 * (e / 32), e % 32)
                              : gb_dequant_elem(typ, blk[warp], e);
-  int c = g * 32 + lane;
-  x[c] = v;
-  GbXPack p{pk.a, pk.b, pk.c, pk.s, pk.sum16, pk.ssq};
-  gb_pack_group(p, g, v * wnorm[c]);
+  x[g * 32 + lane] = v;
   float ss = gb_warp_sum(v * v);
-  if (lane == 0) pk.ssq[g] = ss;
-  gb_grid_dep_launch();
+  if (lane == 0) ssq[g] = ss;
 }
 
-// x += y, then pack x*wnorm (+ per-group sums of squares): the residual
-// epilogue when the projection's sum arrives from a collective.
-__global__ void resid_pack_kernel(float *x, const float *y, const float *wnorm, int n, GbXPackBuf pk) {
+// x += y with per-32 sums of squares: the residual epilogue when the
+// projection's sum arrives from a collective.
+__global__ void resid_kernel(float *x, const float *y, int n, float *ssq) {
   gb_grid_dep_launch();
   gb_grid_dep_wait();
   const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -275,11 +270,8 @@ __global__ void resid_pack_kernel(float *x, const float *y, const float *wnorm, 
   int c = g * 32 + lane;
   float xn = x[c] + y[c];
   x[c] = xn;
-  GbXPack p{pk.a, pk.b, pk.c, pk.s, pk.sum16, pk.ssq};
-  gb_pack_group(p, g, xn * wnorm[c]);
   float ss = gb_warp_sum(xn * xn);
-  if (lane == 0) pk.ssq[g] = ss;
-  gb_grid_dep_launch();
+  if (lane == 0) ssq[g] = ss;
 }
 
 __global__ void fill_kernel(float *p, int n, float v) {
@@ -322,41 +314,21 @@ const char *type_name(int t) {
 
 // ---- internal launchers -----------------------------------------------------
 
-int gb_xpack_alloc(GbXPackBuf *p, int n) {
-  p->n = n;
-  GB_CUDA(cudaMalloc(&p->a, 3 * (size_t)n), "gpu: alloc pack");
-  p->b = p->a + n;
-  p->c = p->b + n;
-  GB_CUDA(cudaMalloc(&p->s, sizeof(float) * (size_t)(n / 32 + n / 16 + n / 32)), "gpu: alloc pack");
-  p->sum16 = p->s + n / 32;
-  p->ssq = p->sum16 + n / 16;
-  GB_CUDA(cudaMemset(p->a, 0, 3 * (size_t)n), "gpu: clear pack");
-  GB_CUDA(cudaMemset(p->s, 0, sizeof(float) * (size_t)(n / 32 + n / 16 + n / 32)), "gpu: clear pack");
-  return GB_OK;
-}
-void gb_xpack_free(GbXPackBuf *p) {
-  if (p->a) cudaFree(p->a);
-  if (p->s) cudaFree(p->s);
-  *p = GbXPackBuf();
-}
-
 int gb_embed_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
-                    int vocab, float *x, const float *wnorm, const GbXPackBuf &pk, unsigned *err,
-                    cudaStream_t st, bool pdl) {
+                    int vocab, float *x, float *ssq, unsigned *err, cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];
   int groups = dim / 32;
   cudaLaunchConfig_t cfg = make_cfg(dim3((groups + 7) / 8), dim3(256), st, attr, pdl);
-  GB_CUDA(cudaLaunchKernelEx(&cfg, embed_kernel, typ, tiled, nsb, dim, token, vocab, x, wnorm, pk, err),
+  GB_CUDA(cudaLaunchKernelEx(&cfg, embed_kernel, typ, tiled, nsb, dim, token, vocab, x, ssq, err),
           "gpu: embed");
   return GB_OK;
 }
 
-int gb_resid_pack_launch(float *x, const float *y, const float *wnorm, int n, const GbXPackBuf &pk,
-                         cudaStream_t st, bool pdl) {
+int gb_resid_launch(float *x, const float *y, int n, float *ssq, cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];
   int groups = n / 32;
   cudaLaunchConfig_t cfg = make_cfg(dim3((groups + 7) / 8), dim3(256), st, attr, pdl);
-  GB_CUDA(cudaLaunchKernelEx(&cfg, resid_pack_kernel, x, y, wnorm, n, pk), "gpu: residual");
+  GB_CUDA(cudaLaunchKernelEx(&cfg, resid_kernel, x, y, n, ssq), "gpu: residual");
   return GB_OK;
 }
 
