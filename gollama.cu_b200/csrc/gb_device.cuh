@@ -150,6 +150,16 @@ GB_DEV bool gb_mbar_wait(uint64_t *bar, uint32_t parity) {
 GB_DEV void gb_grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 GB_DEV void gb_grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// System-scope flag accesses for peer (NVLink) signalling.
+GB_DEV unsigned gb_ld_acquire_sys(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+GB_DEV void gb_st_release_sys(unsigned *p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Streaming 16-byte global load that does not allocate in L1.
 GB_DEV uint4 gb_ld_stream16(const void *p) {
   uint4 v;

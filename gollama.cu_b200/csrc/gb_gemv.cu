@@ -294,6 +294,22 @@ GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1) {
         ((float *)e.vcache)[((size_t)h * e.max_len + pos) * hd + dd] = out;
       }
     }
+  } else if constexpr (EPI == GB_EPI_PARTIAL) {
+    // this rank's partial of rows r into its own slot; the row-block that
+    // completes the vector publishes the step's flag (the other ranks read
+    // both over NVLink)
+    const GbPeer &P = e.peer;
+    P.my_buf[(size_t)e.peer_slot * P.dim + rbk * 32 + lane] = y0;
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) {
+      const unsigned done = atomicAdd(P.done + e.peer_slot, 1u) + 1u;
+      if (done == (unsigned)p.nrb) {
+        P.done[e.peer_slot] = 0u;
+        __threadfence();
+        gb_st_release_sys(P.my_flag + e.peer_slot, *P.epoch + 1u);
+      }
+    }
   } else if constexpr (EPI == GB_EPI_LOGITS) {
     int r = rbk * 32 + lane;
     uint32_t gidx = (uint32_t)(e.row_offset + r);
@@ -319,7 +335,12 @@ GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1) {
         unsigned long long k = atomicAdd(e.best, 0ull);
         int32_t tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         if (e.token_out) *e.token_out = tok;
-        if (e.key_out) *e.key_out = k;  // tensor parallel: reduced across ranks next
+        if (e.peer_slot >= 0) {
+          // tensor parallel: this rank's key into its own slot, then the flag
+          const GbPeer &P = e.peer;
+          *(unsigned long long *)(P.my_buf + (size_t)e.peer_slot * P.dim) = k;
+          gb_st_release_sys(P.my_flag + e.peer_slot, *P.epoch + 1u);
+        }
         if (e.token_hist) {
           int pos = *e.pos;
           if (pos >= 0 && pos < e.max_len) e.token_hist[pos] = tok;
@@ -673,6 +694,7 @@ KernelFn pick_epi(int epi) {
     case GB_EPI_RESID: return gemv_kernel<TA, TB, GB_EPI_RESID, W>;
     case GB_EPI_SWIGLU: return gemv_kernel<TA, TB, GB_EPI_SWIGLU, W>;
     case GB_EPI_LOGITS: return gemv_kernel<TA, TB, GB_EPI_LOGITS, W>;
+    case GB_EPI_PARTIAL: return gemv_kernel<TA, TB, GB_EPI_PARTIAL, W>;
   }
   return nullptr;
 }
@@ -791,7 +813,7 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   // about 36 KB, as many stages as the budget holds (2 to 8).
   // GB_GEMV_RING_<PLAIN|QKV|RESID|SWIGLU|LOGITS> or GB_GEMV_RING = "K,stages"
   // force the ring (sweeps) when it fits.
-  static const char *epi_names[] = {"PLAIN", "QKV", "RESID", "SWIGLU", "LOGITS"};
+  static const char *epi_names[] = {"PLAIN", "QKV", "RESID", "SWIGLU", "LOGITS", "PARTIAL"};
   int fk = 0, fs = 0;
   {
     char key[64];

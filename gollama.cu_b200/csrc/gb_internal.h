@@ -32,6 +32,23 @@ enum GbEpi {
   GB_EPI_RESID = 2,   // x[r] += y; per-32 sums of squares for the next RMSNorm
   GB_EPI_SWIGLU = 3,  // gate/up pairs -> act = silu(g)*u
   GB_EPI_LOGITS = 4,  // logits[r] = y; argmax candidates; last CTA -> token
+  GB_EPI_PARTIAL = 5, // tensor parallel: this rank's partial y into every rank's peer slot
+};
+
+// Tensor-parallel exchange over peer memory. Every rank owns a buffer
+// [slots][dim] floats for its own partials and flags [slots], mapped into the
+// other ranks' address spaces (CUDA IPC). A rank stores its partial of slot s
+// locally and publishes flag[s] = epoch+1 (system-scope release) once all its
+// row-blocks are stored; a reducer reads every rank's flag and partial over
+// NVLink. `epoch` counts decode steps and is the same on every rank.
+struct GbPeer {
+  int world = 1, rank = 0, dim = 0;
+  const float *const *bufs = nullptr;     // device array [world]: every rank's partials
+  const unsigned *const *flags = nullptr; // device array [world]: every rank's flags
+  float *my_buf = nullptr;                // this rank's partials [slots][dim]
+  unsigned *my_flag = nullptr;            // this rank's flags [slots]
+  unsigned *done = nullptr;               // [slots] local row-block counters (zero between launches)
+  const unsigned *epoch = nullptr;        // device step counter
 };
 
 struct GbGemvPlan {
@@ -54,7 +71,6 @@ struct GbEpiArgs {
   // LOGITS / PLAIN / SWIGLU output
   float *y = nullptr;
   unsigned long long *best = nullptr;     // running argmax key (zero between launches)
-  unsigned long long *key_out = nullptr;  // tensor parallel: final local key
   unsigned *counter = nullptr;            // finished row-blocks (zero between launches)
   int32_t *token_out = nullptr;   // argmax result (device)
   int32_t *token_hist = nullptr;  // optional history slot base ([max_len]); indexed by *pos
@@ -64,6 +80,9 @@ struct GbEpiArgs {
   // K-split scratch
   float *part = nullptr;          // [ntiles][ks][32]
   unsigned *tile_counter = nullptr;
+  // PARTIAL (and LOGITS under tensor parallelism): peer exchange slot
+  GbPeer peer;
+  int peer_slot = -1;
 };
 
 struct GbGemvArgs {
@@ -116,10 +135,17 @@ int gb_embed_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32
                     int vocab, float *x, float *ssq, unsigned *err, cudaStream_t st, bool pdl);
 // x += y with per-32 sums of squares: the residual after a collective.
 int gb_resid_launch(float *x, const float *y, int n, float *ssq, cudaStream_t st, bool pdl);
-// Reduce n per-rank argmax keys (tensor-parallel lm_head) to the token.
-int gb_argmax_keys_launch(const unsigned long long *keys, int n, int32_t *token, int32_t *hist,
-                          const int32_t *pos, int max_len, cudaStream_t st);
-int gb_advance_pos_launch(int32_t *pos, cudaStream_t st);
+// Tensor parallel: wait for every rank's partial in peer slot `slot`, then
+// x += sum of the partials (rank order, identical on every rank) with per-32
+// sums of squares.
+int gb_peer_resid_launch(const GbPeer &p, int slot, float *x, int n, float *ssq, unsigned *err,
+                         cudaStream_t st, bool pdl);
+// Tensor parallel: wait for every rank's argmax key in peer slot `slot` and
+// reduce them to the token.
+int gb_peer_argmax_launch(const GbPeer &p, int slot, int32_t *token, int32_t *hist, const int32_t *pos,
+                          int max_len, unsigned *err, cudaStream_t st, bool pdl);
+// Advance the position (and the tensor-parallel step counter when non-null).
+int gb_advance_pos_launch(int32_t *pos, unsigned *epoch, cudaStream_t st);
 
 // ---- GGUF (gb_gguf.cpp): reader restating gguf/gguf.go:62 Parse and
 // writer restating gguf/writer.go.

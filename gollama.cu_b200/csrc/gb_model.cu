@@ -159,8 +159,7 @@ struct gb_model {
   float *out_norm = nullptr;
   double *rope_cs = nullptr;
   // work
-  float *x = nullptr, *q = nullptr, *attn = nullptr, *logits = nullptr, *logits_full = nullptr,
-        *ypart = nullptr;
+  float *x = nullptr, *q = nullptr, *attn = nullptr, *logits = nullptr, *logits_full = nullptr;
   float *act = nullptr;  // SwiGLU output [ffn_local]
   float *ssq = nullptr;  // per-32 sums of squares of x [dim/32] (RMSNorm input)
   int32_t *token = nullptr, *pos = nullptr, *gen = nullptr;
@@ -169,7 +168,10 @@ struct gb_model {
   unsigned *tile_counter = nullptr;
   float *attn_part = nullptr;
   unsigned *attn_counter = nullptr;
-  unsigned long long *best = nullptr, *key_local = nullptr, *keys = nullptr;
+  unsigned long long *best = nullptr;
+  // tensor parallel: peer exchange (receive buffers mapped by every rank)
+  GbPeer peer;
+  std::vector<void *> ipc_opened;  // peers' buffers and flags mapped into this process
   unsigned *done = nullptr;
   int attn_splits = 1;
   GbGemvPlan plan_plain, plan_gu;
@@ -258,6 +260,75 @@ int upload_tiles(const GbTensor *t, int r0, int nr, int c0, int nc, uint8_t *dst
             "model: place sb-blocks");
   }
   GB_CUDA(cudaStreamSynchronize(st), "model: upload");
+  return GB_OK;
+}
+
+// Tensor parallel: every rank allocates a buffer [slots][dim] floats for its
+// partials and flags [slots] (slots: o and down of every layer, plus the
+// lm_head's argmax key), exports them with CUDA IPC, gathers every rank's
+// handles over NCCL (once, at load) and maps the peers' buffers, so that the
+// step's kernels exchange partial sums with loads over NVLink and
+// system-scope flags instead of collectives.
+int setup_peers(gb_model *m) {
+  const gb_config &c = m->c;
+  const int N = c.tp_world, R = c.tp_rank, slots = 2 * c.layers + 1;
+  const int dim = std::max(c.dim, 2);
+  float *buf = nullptr;
+  unsigned *flag = nullptr, *done = nullptr, *epoch = nullptr;
+  int rc;
+  if ((rc = dalloc(m, &buf, (size_t)slots * dim, "model: peer buffers")) ||
+      (rc = dalloc(m, &flag, (size_t)slots, "model: peer flags")) ||
+      (rc = dalloc(m, &done, (size_t)slots, "model: peer counters")) || (rc = dalloc(m, &epoch, 1, "model: step counter")))
+    return rc;
+  struct Handles {
+    cudaIpcMemHandle_t buf, flag;
+  } mine;
+  GB_CUDA(cudaIpcGetMemHandle(&mine.buf, buf), "model: IPC handle");
+  GB_CUDA(cudaIpcGetMemHandle(&mine.flag, flag), "model: IPC handle");
+  uint8_t *dh = nullptr;
+  GB_CUDA(cudaMalloc(&dh, sizeof(Handles) * (size_t)(N + 1)), "model: IPC exchange");
+  std::vector<Handles> all((size_t)N);
+  cudaError_t e = cudaMemcpy(dh + sizeof(Handles) * N, &mine, sizeof mine, cudaMemcpyHostToDevice);
+  ncclResult_t nr = e == cudaSuccess ? nccl()->allGather(dh + sizeof(Handles) * N, dh, sizeof(Handles), ncclUint8,
+                                                         m->comm, m->st)
+                                     : ncclSuccess;
+  if (e == cudaSuccess && nr == ncclSuccess) e = cudaStreamSynchronize(m->st);
+  if (e == cudaSuccess && nr == ncclSuccess) e = cudaMemcpy(all.data(), dh, sizeof(Handles) * N, cudaMemcpyDeviceToHost);
+  cudaFree(dh);
+  if (nr != ncclSuccess) return gb_fail(GB_ERR_NCCL, "model: IPC exchange: %s", nccl()->getErrorString(nr));
+  GB_CUDA(e, "model: IPC exchange");
+  std::vector<float *> bufs((size_t)N);
+  std::vector<unsigned *> flags((size_t)N);
+  for (int q = 0; q < N; q++) {
+    if (q == R) {
+      bufs[q] = buf;
+      flags[q] = flag;
+      continue;
+    }
+    void *pb = nullptr, *pf = nullptr;
+    GB_CUDA(cudaIpcOpenMemHandle(&pb, all[q].buf, cudaIpcMemLazyEnablePeerAccess), "model: map peer buffer");
+    m->ipc_opened.push_back(pb);
+    GB_CUDA(cudaIpcOpenMemHandle(&pf, all[q].flag, cudaIpcMemLazyEnablePeerAccess), "model: map peer flags");
+    m->ipc_opened.push_back(pf);
+    bufs[q] = (float *)pb;
+    flags[q] = (unsigned *)pf;
+  }
+  float **dbufs = nullptr;
+  unsigned **dflags = nullptr;
+  if ((rc = dalloc(m, &dbufs, (size_t)N, "model: peer table")) || (rc = dalloc(m, &dflags, (size_t)N, "model: peer table")))
+    return rc;
+  GB_CUDA(cudaMemcpy(dbufs, bufs.data(), sizeof(float *) * N, cudaMemcpyHostToDevice), "model: peer table");
+  GB_CUDA(cudaMemcpy(dflags, flags.data(), sizeof(unsigned *) * N, cudaMemcpyHostToDevice), "model: peer table");
+  GbPeer &P = m->peer;
+  P.world = N;
+  P.rank = R;
+  P.dim = dim;
+  P.bufs = dbufs;
+  P.flags = dflags;
+  P.my_buf = buf;
+  P.my_flag = flag;
+  P.done = done;
+  P.epoch = epoch;
   return GB_OK;
 }
 
@@ -389,12 +460,13 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
       a.e.ssq = m->ssq;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_O))) return rc;
     } else {
-      a = gemv_args(L.wo, m->attn, nullptr, c.eps, GB_EPI_PLAIN, m);
-      a.e.y = m->ypart;
+      // partials to every rank's peer slot 2l; sum + residual once all arrived
+      a = gemv_args(L.wo, m->attn, nullptr, c.eps, GB_EPI_PARTIAL, m);
+      a.e.peer = m->peer;
+      a.e.peer_slot = 2 * l;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_O))) return rc;
-      GB_NCCL(nccl()->allReduce(m->ypart, m->ypart, (size_t)c.dim, ncclFloat, ncclSum, m->comm, st),
-              "model: all-reduce");
-      if ((rc = gb_resid_launch(m->x, m->ypart, c.dim, m->ssq, st, false)) || (rc = mark(K_OTHER))) return rc;
+      if ((rc = gb_peer_resid_launch(m->peer, 2 * l, m->x, c.dim, m->ssq, m->err, st, pdl)) || (rc = mark(K_OTHER)))
+        return rc;
     }
     // FFN RMSNorm in the prologue; gate/up + SwiGLU
     a = gemv_args(L.gu, m->x, L.ffn_norm, c.eps, GB_EPI_SWIGLU, m);
@@ -407,12 +479,13 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
       a.e.ssq = m->ssq;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_DOWN))) return rc;
     } else {
-      a = gemv_args(L.down, m->act, nullptr, c.eps, GB_EPI_PLAIN, m);
-      a.e.y = m->ypart;
+      a = gemv_args(L.down, m->act, nullptr, c.eps, GB_EPI_PARTIAL, m);
+      a.e.peer = m->peer;
+      a.e.peer_slot = 2 * l + 1;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_DOWN))) return rc;
-      GB_NCCL(nccl()->allReduce(m->ypart, m->ypart, (size_t)c.dim, ncclFloat, ncclSum, m->comm, st),
-              "model: all-reduce");
-      if ((rc = gb_resid_launch(m->x, m->ypart, c.dim, m->ssq, st, false)) || (rc = mark(K_OTHER))) return rc;
+      if ((rc = gb_peer_resid_launch(m->peer, 2 * l + 1, m->x, c.dim, m->ssq, m->err, st, pdl)) ||
+          (rc = mark(K_OTHER)))
+        return rc;
     }
   }
   // output RMSNorm in the prologue; lm_head + argmax (model.Argmax on the device)
@@ -426,16 +499,16 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
     a.e.token_out = m->token;
     a.e.token_hist = m->gen;
   } else {
-    a.e.key_out = m->key_local;
+    a.e.peer = m->peer;  // the local argmax key goes to every rank's slot 2L
+    a.e.peer_slot = 2 * c.layers;
   }
   if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_HEAD))) return rc;
-  if (tp) {
-    GB_NCCL(nccl()->allGather(m->key_local, m->keys, 1, ncclUint64, m->comm, st), "model: all-gather");
-    if ((rc = gb_argmax_keys_launch(m->keys, c.tp_world, m->token, m->gen, m->pos, c.max_len, st)) ||
-        (rc = mark(K_OTHER)))
-      return rc;
-  }
-  if ((rc = gb_advance_pos_launch(m->pos, st)) || (rc = mark(K_OTHER))) return rc;
+  if (tp && ((rc = gb_peer_argmax_launch(m->peer, 2 * c.layers, m->token, m->gen, m->pos, c.max_len, m->err, st,
+                                         pdl)) ||
+             (rc = mark(K_OTHER))))
+    return rc;
+  if ((rc = gb_advance_pos_launch(m->pos, tp ? (unsigned *)m->peer.epoch : nullptr, st)) || (rc = mark(K_OTHER)))
+    return rc;
   m->launches = n;
   return GB_OK;
 }
@@ -495,6 +568,7 @@ int set_token_pos(gb_model *m, int32_t token, int pos) {
 void free_model(gb_model *m) {
   if (!m) return;
   if (m->graph) cudaGraphExecDestroy(m->graph);
+  for (void *p : m->ipc_opened) cudaIpcCloseMemHandle(p);
   if (m->comm && nccl() && nccl()->commDestroy) nccl()->commDestroy(m->comm);
   for (void *p : m->allocs) cudaFree(p);
   if (m->h_stage) cudaFreeHost(m->h_stage);
@@ -699,11 +773,9 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
       (rc = dalloc(m, &m->attn, (size_t)m->q_local, "model: work")) ||
       (rc = dalloc(m, &m->logits, (size_t)m->vocab_local, "model: work")) ||
       (rc = dalloc(m, &m->logits_full, (size_t)c.vocab, "model: work")) ||
-      (rc = dalloc(m, &m->ypart, (size_t)c.dim, "model: work")) ||
       (rc = dalloc(m, &m->token, 4, "model: work")) || (rc = dalloc(m, &m->pos, 4, "model: work")) ||
       (rc = dalloc(m, &m->gen, (size_t)c.max_len, "model: work")) || (rc = dalloc(m, &m->err, 4, "model: work")) ||
-      (rc = dalloc(m, &m->best, 1, "model: work")) || (rc = dalloc(m, &m->key_local, 1, "model: work")) ||
-      (rc = dalloc(m, &m->keys, (size_t)N, "model: work")) || (rc = dalloc(m, &m->done, 1, "model: work")))
+      (rc = dalloc(m, &m->best, 1, "model: work")) || (rc = dalloc(m, &m->done, 1, "model: work")))
     return fail(rc);
   if ((rc = dalloc(m, &m->act, (size_t)m->ffn_local, "model: work")) ||
       (rc = dalloc(m, &m->ssq, (size_t)c.dim / 32, "model: work")))
@@ -731,6 +803,7 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
     memcpy(&id, o.nccl_id, sizeof id);
     ncclResult_t r = nccl()->commInitRank(&m->comm, N, id, R);
     if (r != ncclSuccess) return fail(gb_fail(GB_ERR_NCCL, "model: NCCL init: %s", nccl()->getErrorString(r)));
+    if ((rc = setup_peers(m))) return fail(rc);
   }
   if (cudaDeviceSynchronize() != cudaSuccess) return fail(gb_fail(GB_ERR_CUDA, "model: load"));
   // embedding, 5 per layer (+2 per layer for the collectives' residual

@@ -217,19 +217,77 @@ __global__ void argmax_kernel(const float *x, int n, int32_t *out) {
 }
 
 // Reduce per-rank argmax keys (tensor-parallel lm_head) to the token.
-__global__ void argmax_keys_kernel(const unsigned long long *keys, int n, int32_t *token,
-                                   int32_t *hist, const int32_t *pos, int max_len) {
+// Iterations of a peer-flag wait (each sleeps ~100 ns): about half a second.
+constexpr unsigned kPeerWaitLimit = 1u << 22;
+
+// Wait (bounded) until rank q's flag of peer slot `slot` carries this step's
+// value (read over NVLink for another rank); false on timeout.
+GB_DEV bool peer_wait(const GbPeer &p, int slot, int q) {
+  const unsigned ep = *p.epoch + 1u;
+  const unsigned *f = p.flags[q] + slot;
+  for (unsigned i = 0; i < kPeerWaitLimit; i++) {
+    if (gb_ld_acquire_sys(f) == ep) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
+
+// x += sum over ranks of the partials in peer slot `slot` (rank order, so
+// every rank computes the same x), with per-32 sums of squares.
+__global__ void peer_resid_kernel(GbPeer p, int slot, float *x, int n, float *ssq, unsigned *err) {
+  gb_grid_dep_launch();
+  gb_grid_dep_wait();
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if ((int)threadIdx.x < p.world && !peer_wait(p, slot, threadIdx.x)) {
+    ok = 0;
+    if (err) atomicOr(err, GB_DEVERR_TIMEOUT);
+  }
+  __syncthreads();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x, lane = threadIdx.x & 31;
+  if (c >= n) return;  // n is a multiple of 32: whole warps leave together
+  float sum = 0.f;
+  if (ok)
+    for (int q = 0; q < p.world; q++) sum += __ldcv(p.bufs[q] + (size_t)slot * p.dim + c);
+  const float xn = x[c] + sum;
+  x[c] = xn;
+  const float ss = gb_warp_sum(xn * xn);
+  if (lane == 0) ssq[c / 32] = ss;
+}
+
+// The token from every rank's argmax key in peer slot `slot` (the largest
+// key: larger value, then lower index, as model.Argmax).
+__global__ void peer_argmax_kernel(GbPeer p, int slot, int32_t *token, int32_t *hist, const int32_t *pos,
+                                   int max_len, unsigned *err) {
+  gb_grid_dep_launch();
+  gb_grid_dep_wait();
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if ((int)threadIdx.x < p.world && !peer_wait(p, slot, threadIdx.x)) {
+    ok = 0;
+    if (err) atomicOr(err, GB_DEVERR_TIMEOUT);
+  }
+  __syncthreads();
+  if (threadIdx.x != 0 || !ok) return;
   unsigned long long t = 0;
-  for (int i = 0; i < n; i++) t = keys[i] > t ? keys[i] : t;
-  int32_t tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(t & 0xFFFFFFFFull));
+  for (int q = 0; q < p.world; q++) {
+    const unsigned long long k = __ldcv((const unsigned long long *)(p.bufs[q] + (size_t)slot * p.dim));
+    t = k > t ? k : t;
+  }
+  const int32_t tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(t & 0xFFFFFFFFull));
   *token = tok;
   if (hist) {
-    int p = *pos;
-    if (p >= 0 && p < max_len) hist[p] = tok;
+    const int ps = *pos;
+    if (ps >= 0 && ps < max_len) hist[ps] = tok;
   }
 }
 
-__global__ void advance_pos_kernel(int32_t *pos) { *pos += 1; }
+__global__ void advance_pos_kernel(int32_t *pos, unsigned *epoch) {
+  *pos += 1;
+  if (epoch) *epoch += 1u;
+}
 
 // Embedding lookup (model/model.go:326 quant.Row on the host, moved on the
 // device): row *token of the tiled token_embd, bit-exact, into x, with the
@@ -332,15 +390,25 @@ int gb_resid_launch(float *x, const float *y, int n, float *ssq, cudaStream_t st
   return GB_OK;
 }
 
-int gb_argmax_keys_launch(const unsigned long long *keys, int n, int32_t *token, int32_t *hist,
-                          const int32_t *pos, int max_len, cudaStream_t st) {
-  argmax_keys_kernel<<<1, 1, 0, st>>>(keys, n, token, hist, pos, max_len);
-  GB_CUDA(cudaGetLastError(), "gpu: argmax reduce");
+int gb_peer_resid_launch(const GbPeer &p, int slot, float *x, int n, float *ssq, unsigned *err,
+                         cudaStream_t st, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_cfg(dim3((n + 255) / 256), dim3(256), st, attr, pdl);
+  GB_CUDA(cudaLaunchKernelEx(&cfg, peer_resid_kernel, p, slot, x, n, ssq, err), "gpu: peer residual");
   return GB_OK;
 }
 
-int gb_advance_pos_launch(int32_t *pos, cudaStream_t st) {
-  advance_pos_kernel<<<1, 1, 0, st>>>(pos);
+int gb_peer_argmax_launch(const GbPeer &p, int slot, int32_t *token, int32_t *hist, const int32_t *pos,
+                          int max_len, unsigned *err, cudaStream_t st, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(32), st, attr, pdl);
+  GB_CUDA(cudaLaunchKernelEx(&cfg, peer_argmax_kernel, p, slot, token, hist, pos, max_len, err),
+          "gpu: peer argmax");
+  return GB_OK;
+}
+
+int gb_advance_pos_launch(int32_t *pos, unsigned *epoch, cudaStream_t st) {
+  advance_pos_kernel<<<1, 1, 0, st>>>(pos, epoch);
   GB_CUDA(cudaGetLastError(), "gpu: advance position");
   return GB_OK;
 }
