@@ -187,11 +187,15 @@ struct gb_model {
 
 namespace {
 
+// Every transfer and memset of a model goes on its own stream m->st: that
+// stream is non-blocking, so work on the legacy default stream (a plain
+// cudaMemset, which returns before a device-memory memset is done) would not
+// be ordered before the uploads and kernels that follow on m->st.
 template <class T>
 int dalloc(gb_model *m, T **p, size_t n, const char *what) {
   void *q = nullptr;
   GB_CUDA(cudaMalloc(&q, n * sizeof(T) > 0 ? n * sizeof(T) : 16), what);
-  GB_CUDA(cudaMemset(q, 0, n * sizeof(T) > 0 ? n * sizeof(T) : 16), what);
+  GB_CUDA(cudaMemsetAsync(q, 0, n * sizeof(T) > 0 ? n * sizeof(T) : 16, m->st), what);
   m->allocs.push_back(q);
   *p = (T *)q;
   return GB_OK;
@@ -223,7 +227,8 @@ int host_vector(const GbTensor *t, int n, std::vector<float> &out, const char *n
 int upload_vec(gb_model *m, const std::vector<float> &v, float **dst, const char *what) {
   int rc = dalloc(m, dst, v.size(), what);
   if (rc) return rc;
-  GB_CUDA(cudaMemcpy(*dst, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice), what);
+  GB_CUDA(cudaMemcpyAsync(*dst, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice, m->st), what);
+  GB_CUDA(cudaStreamSynchronize(m->st), what);  // v is the caller's scratch
   return GB_OK;
 }
 
@@ -288,12 +293,14 @@ int setup_peers(gb_model *m) {
   uint8_t *dh = nullptr;
   GB_CUDA(cudaMalloc(&dh, sizeof(Handles) * (size_t)(N + 1)), "model: IPC exchange");
   std::vector<Handles> all((size_t)N);
-  cudaError_t e = cudaMemcpy(dh + sizeof(Handles) * N, &mine, sizeof mine, cudaMemcpyHostToDevice);
+  cudaError_t e = cudaMemcpyAsync(dh + sizeof(Handles) * N, &mine, sizeof mine, cudaMemcpyHostToDevice, m->st);
   ncclResult_t nr = e == cudaSuccess ? nccl()->allGather(dh + sizeof(Handles) * N, dh, sizeof(Handles), ncclUint8,
                                                          m->comm, m->st)
                                      : ncclSuccess;
   if (e == cudaSuccess && nr == ncclSuccess) e = cudaStreamSynchronize(m->st);
-  if (e == cudaSuccess && nr == ncclSuccess) e = cudaMemcpy(all.data(), dh, sizeof(Handles) * N, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && nr == ncclSuccess)
+    e = cudaMemcpyAsync(all.data(), dh, sizeof(Handles) * N, cudaMemcpyDeviceToHost, m->st);
+  if (e == cudaSuccess && nr == ncclSuccess) e = cudaStreamSynchronize(m->st);
   cudaFree(dh);
   if (nr != ncclSuccess) return gb_fail(GB_ERR_NCCL, "model: IPC exchange: %s", nccl()->getErrorString(nr));
   GB_CUDA(e, "model: IPC exchange");
@@ -317,8 +324,10 @@ int setup_peers(gb_model *m) {
   unsigned **dflags = nullptr;
   if ((rc = dalloc(m, &dbufs, (size_t)N, "model: peer table")) || (rc = dalloc(m, &dflags, (size_t)N, "model: peer table")))
     return rc;
-  GB_CUDA(cudaMemcpy(dbufs, bufs.data(), sizeof(float *) * N, cudaMemcpyHostToDevice), "model: peer table");
-  GB_CUDA(cudaMemcpy(dflags, flags.data(), sizeof(unsigned *) * N, cudaMemcpyHostToDevice), "model: peer table");
+  GB_CUDA(cudaMemcpyAsync(dbufs, bufs.data(), sizeof(float *) * N, cudaMemcpyHostToDevice, m->st), "model: peer table");
+  GB_CUDA(cudaMemcpyAsync(dflags, flags.data(), sizeof(unsigned *) * N, cudaMemcpyHostToDevice, m->st),
+          "model: peer table");
+  GB_CUDA(cudaStreamSynchronize(m->st), "model: peer table");
   GbPeer &P = m->peer;
   P.world = N;
   P.rank = R;
@@ -765,7 +774,9 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
         cs[((size_t)p * (hd / 2) + j) * 2 + 1] = sin(theta);
       }
     if ((rc = dalloc(m, &m->rope_cs, cs.size(), "model: rope table"))) return fail(rc);
-    if (cudaMemcpy(m->rope_cs, cs.data(), cs.size() * sizeof(double), cudaMemcpyHostToDevice) != cudaSuccess)
+    if (cudaMemcpyAsync(m->rope_cs, cs.data(), cs.size() * sizeof(double), cudaMemcpyHostToDevice, m->st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(m->st) != cudaSuccess)
       return fail(gb_fail(GB_ERR_CUDA, "model: rope table upload"));
   }
   // work buffers
@@ -949,8 +960,11 @@ int gb_model_fill_kv_normal(gb_model *m, uint64_t seed, int n_pos) {
           ((float *)vd.data())[vi] = vx;
         }
       }
-    GB_CUDA(cudaMemcpy(m->layers[(size_t)l].kc, kd.data(), kd.size(), cudaMemcpyHostToDevice), "model: KV fill");
-    GB_CUDA(cudaMemcpy(m->layers[(size_t)l].vc, vd.data(), vd.size(), cudaMemcpyHostToDevice), "model: KV fill");
+    GB_CUDA(cudaMemcpyAsync(m->layers[(size_t)l].kc, kd.data(), kd.size(), cudaMemcpyHostToDevice, m->st),
+            "model: KV fill");
+    GB_CUDA(cudaMemcpyAsync(m->layers[(size_t)l].vc, vd.data(), vd.size(), cudaMemcpyHostToDevice, m->st),
+            "model: KV fill");
+    GB_CUDA(cudaStreamSynchronize(m->st), "model: KV fill");  // kd, vd are reused per layer
   }
   return GB_OK;
 }
@@ -963,9 +977,11 @@ int gb_model_read_kv(gb_model *m, int layer, int pos0, int n, float *k_out, floa
   const int hd = c.head_dim, kvl = m->kv_local, V = c.kv_f16 ? 8 : 4;
   const size_t esz = c.kv_f16 ? 2 : 4, elems = (size_t)kvl * c.max_len;
   std::vector<uint8_t> kd(elems * esz), vd(elems * esz);
+  GB_CUDA(cudaMemcpyAsync(kd.data(), m->layers[(size_t)layer].kc, kd.size(), cudaMemcpyDeviceToHost, m->st),
+          "model: KV read");
+  GB_CUDA(cudaMemcpyAsync(vd.data(), m->layers[(size_t)layer].vc, vd.size(), cudaMemcpyDeviceToHost, m->st),
+          "model: KV read");
   GB_CUDA(cudaStreamSynchronize(m->st), "model: KV read");
-  GB_CUDA(cudaMemcpy(kd.data(), m->layers[(size_t)layer].kc, kd.size(), cudaMemcpyDeviceToHost), "model: KV read");
-  GB_CUDA(cudaMemcpy(vd.data(), m->layers[(size_t)layer].vc, vd.size(), cudaMemcpyDeviceToHost), "model: KV read");
   for (int t = 0; t < n; t++)
     for (int j = 0; j < kvl; j++) {
       int h = j / hd, d = j % hd, p = pos0 + t;
@@ -1086,7 +1102,10 @@ int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes,
     rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
   if (!rc && cudaMalloc(&l->tile_counter, sizeof(unsigned) * (size_t)(t.ntiles + 64)) != cudaSuccess)
     rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
-  if (!rc && cudaMemset(l->tile_counter, 0, sizeof(unsigned) * (size_t)(t.ntiles + 64)) != cudaSuccess)
+  // a plain cudaMemset returns before a device-memory memset is done, and the
+  // caller's stream may be non-blocking: finish it before the first product
+  if (!rc && (cudaMemset(l->tile_counter, 0, sizeof(unsigned) * (size_t)(t.ntiles + 64)) != cudaSuccess ||
+              cudaDeviceSynchronize() != cudaSuccess))
     rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
   if (rc) {
     free_linear(l);  // keeps the error message of the failed step

@@ -543,7 +543,9 @@ int gb_gpu_attn_decode(gb_kernels *k, void *stream, const float *q, const float 
     k->ws_nkv = 0;
     GB_CUDA(cudaMalloc(&k->ws, need * sizeof(float)), "gpu: AttnDecode: workspace");
     GB_CUDA(cudaMalloc(&k->ws_counter, sizeof(unsigned) * (size_t)n_kv), "gpu: AttnDecode: workspace");
-    GB_CUDA(cudaMemset(k->ws_counter, 0, sizeof(unsigned) * (size_t)n_kv), "gpu: AttnDecode: workspace");
+    // on the call's stream: ordered before this launch whatever kind of stream it is
+    GB_CUDA(cudaMemsetAsync(k->ws_counter, 0, sizeof(unsigned) * (size_t)n_kv, (cudaStream_t)stream),
+            "gpu: AttnDecode: workspace");
     k->ws_floats = need;
     k->ws_nkv = n_kv;
   }

@@ -26,10 +26,37 @@ def make(gb, name):
     return img, np.array(img.view(), copy=True)
 
 
-def check_logits(name, got, want):
+def kv_report(m, om, orc, cfg, n_pos, kv_f16):
+    """Where the KV caches first differ from cpuForward's: localises a logits mismatch."""
+    import ctypes as C
+
+    kv_dim = cfg["kv_heads"] * cfg["head_dim"]
+    tol = 4e-3 if kv_f16 else 1e-4
+    out = []
+    for layer in range(cfg["layers"]):
+        k, v = m.read_kv(layer, 0, n_pos)
+        kp = orc.lib().or_model_kcache(om.h, layer)
+        vp = orc.lib().or_model_vcache(om.h, layer)
+        kw = np.ctypeslib.as_array((C.c_float * (n_pos * kv_dim)).from_address(kp)).reshape(n_pos, kv_dim)
+        vw = np.ctypeslib.as_array((C.c_float * (n_pos * kv_dim)).from_address(vp)).reshape(n_pos, kv_dim)
+        for nm, g, w in (("K", k, kw), ("V", v, vw)):
+            bad = np.abs(g - w) > tol * (1 + np.abs(w))
+            if bad.any():
+                p, j = np.argwhere(bad)[0]
+                out.append(f"layer {layer} {nm}: {int(bad.sum())} bad, first at pos {p} dim {j}")
+    return "; ".join(out) if out else "KV caches match"
+
+
+def check_logits(name, got, want, report=None):
     d = np.abs(got.astype(np.float64) - want.astype(np.float64))
     bad = d > ATOL + RTOL * np.abs(want)
-    assert not bad.any(), f"{name}: max abs diff {d.max():.3g} at {int(np.argmax(d))}"
+    if bad.any():
+        tiles = sorted({int(i) // 32 for i in np.flatnonzero(bad)})
+        msg = (f"{name}: max abs diff {d.max():.3g} at {int(np.argmax(d))}; {int(bad.sum())} of {bad.size} "
+               f"logits bad, 32-row tiles {tiles[:16]}")
+        if report is not None:
+            msg += "; " + report()
+        raise AssertionError(msg)
     return float(d.max())
 
 
@@ -50,7 +77,8 @@ def test_forward_vs_cpu(gb, orc, cuda, name, kv_f16):
     for pos, tok in enumerate(rng.integers(0, cfg["vocab"], 8)):
         got = m.forward(int(tok), pos).copy()
         want = om.forward(int(tok), pos, cfg["vocab"])
-        worst = max(worst, check_logits(f"{name} pos {pos}", got, want))
+        rep = lambda: kv_report(m, om, orc, cfg, pos + 1, kv_f16)
+        worst = max(worst, check_logits(f"{name} kv_f16={kv_f16} pos {pos}", got, want, rep))
         if not near_tie(want):
             assert gb.argmax(got) == orc.argmax(want)
     m.close()
