@@ -346,6 +346,7 @@ __global__ void __launch_bounds__(kThreads) attn_flash_kernel(const GbAttnArgs a
   gb_grid_dep_wait();  // q and the new K/V row come from the preceding kernel
   if (tid == 0) {
     if (bad && a.err) atomicOr(a.err, GB_DEVERR_POS);
+    gb_fence_proxy_async_global();  // the new row was written by generic stores
     while (issued < nsub && issued < kStages) issue(issued++);
   }
   if (tid < GM) {
@@ -639,6 +640,7 @@ __global__ void __launch_bounds__(kMThreads, 1) attn_mma_kernel(const GbAttnArgs
         // the sub-chunk holding position kv_len-1 is written by the preceding kernel
         if (!waited && t0 + (k + 1) * SUB >= kv_len) {
           gb_grid_dep_wait();
+          gb_fence_proxy_async_global();  // the new row was written by generic stores
           waited = true;
         }
         const int p0 = t0 + k * SUB, nk = min(SUB, t1 - p0);

@@ -111,6 +111,9 @@ GB_DEV void gb_mbar_fence_init() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 GB_DEV void gb_fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Order this thread's later async-proxy (TMA) reads of global memory after
+// what the generic proxy wrote there (the preceding kernel's stores).
+GB_DEV void gb_fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 GB_DEV void gb_mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(gb_smem_u32(bar)),
                "r"(bytes)

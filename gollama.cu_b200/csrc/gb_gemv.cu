@@ -233,6 +233,7 @@ struct Kp {  // kernel parameters
 };
 
 constexpr int kMaxStages = 8;
+constexpr int kPend = 4;  // segments reduced per barrier
 
 template <int EPI>
 GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1) {
@@ -427,7 +428,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   float *xsum_s = (float *)(xc_s + XS * 64);
   uint2 *sl_s = (uint2 *)(xsum_s + XS * 16);
   float *xs_s = (float *)(sl_s + XS * 16);
-  float *psum = xs_s + ((XS + 3) & ~3);  // [2][W][64]
+  float *psum = xs_s + ((XS + 3) & ~3);  // [2][kPend][W][64]
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
   __shared__ double red[W];
   __shared__ float inv_s;
@@ -555,6 +556,18 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   // s = k mod NS with the phase parity ph, super-block usb = u mod nsb.
   const size_t sbb_a = (size_t)gb_tiled_sb_bytes(TA);
   const unsigned dk = (unsigned)W >> LK;  // stages per step (K <= W)
+  // A warp takes every dk-th stage. When dk does not divide NS, the stage
+  // that last used slot s (k - NS) was other warps', and may still be in
+  // flight when this warp gets to stage k: a parity wait on full[s] for k
+  // alone would then see the completed phase before k - NS (same parity)
+  // and read early. So such a warp first waits until slot s was released
+  // after stage k - NS: phase (k - NS) of empty[s], parity ph ^ 1. Its
+  // consumers arrive there only after full[s] completed k - NS, and the
+  // next phase of empty[s] cannot complete before this warp arrives, so the
+  // parity is unambiguous. That needs stage k - NS to have been issued: the
+  // launcher keeps dk <= NS, so this warp's own stage k - dk >= k - NS has
+  // landed, and stages are issued in order.
+  const bool prewait = (unsigned)NS % dk != 0u;
   bool timeout = false;
   unsigned j = (unsigned)warp;  // this warp's next unit (CTA-relative)
   unsigned k = j >> LK;
@@ -562,6 +575,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   uint32_t ph = (k / (unsigned)NS) & 1u;
   unsigned usb = (cu0 + j) % (unsigned)nsb;
   int nseg = 0;
+  unsigned batch_s0 = cu0;  // first unit of the current batch of segments
   for (unsigned s0 = cu0; s0 < cu1; nseg++) {
     const int rbk = (int)(s0 / (unsigned)nsb);
     const unsigned s1 = min(cu1, (unsigned)(rbk + 1) * (unsigned)nsb);
@@ -569,6 +583,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
     float acc0 = 0.f, acc1 = 0.f;
     for (; cu0 + j < s1;) {
       const unsigned u = cu0 + j;
+      if (prewait && k >= (unsigned)NS && !timeout && !gb_mbar_wait(&empty[s], ph ^ 1u)) timeout = true;
       if (!timeout && !gb_mbar_wait(&full[s], ph)) timeout = true;
       if (!timeout) {
         int ls = (int)usb - sbf;
@@ -601,47 +616,63 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
       usb += W;
       while (usb >= (unsigned)nsb) usb -= nsb;
     }
-    float *ps = psum + (size_t)(nseg & 1) * W * 64;
+    // this warp's partials of segment nseg go to slot nseg % kPend of the
+    // batch's half of psum; a batch (kPend segments, or the end of the range)
+    // ends with one barrier, after which each pending segment is reduced by
+    // its own warp. A half is written again only after the next batch's
+    // barrier, which the reducers of this batch pass first.
+    const int slot = nseg % kPend, half = (nseg / kPend) & 1;
+    if (slot == 0) batch_s0 = s0;
+    float *ps = psum + (size_t)(half * kPend + slot) * W * 64;
     ps[warp * 64 + lane] = acc0;
     ps[warp * 64 + 32 + lane] = acc1;
-    consumers_sync<W>();
-    if (warp == nseg % W) {  // reducer of this segment (sum in warp order)
-      float y0 = 0.f, y1 = 0.f;
-      for (int w2 = 0; w2 < W; w2++) {
-        y0 += ps[w2 * 64 + lane];
-        y1 += ps[w2 * 64 + 32 + lane];
-      }
-      const unsigned R0 = (unsigned)rbk * nsb, R1 = R0 + nsb;
-      if (s0 == R0 && s1 == R1) {
-        epilogue<EPI>(p, rbk, y0, y1);
-      } else {
-        // the row-block continues in another CTA: global partial per CTA
-        const int which = cu0 >= R0 ? 0 : 1;
-        float *slot = a.e.part + ((size_t)b * 2 + which) * 64;
-        slot[lane] = y0;
-        slot[32 + lane] = y1;
-        __threadfence();
-        __syncwarp();
-        unsigned done = 0;
-        if (lane == 0) done = atomicAdd(a.e.tile_counter + rbk, s1 - s0) + (s1 - s0);
-        done = __shfl_sync(0xffffffffu, done, 0);
-        if (done == (unsigned)nsb) {
+    s0 = s1;
+    if (slot == kPend - 1 || s0 >= cu1) {
+      consumers_sync<W>();
+      for (int q = 0; q <= slot; q++) {
+        const int seg = nseg - slot + q;
+        if (warp != seg % W) continue;  // reducer of segment seg (sum in warp order)
+        // segments after the batch's first start on row-block boundaries
+        const unsigned t0 = q == 0 ? batch_s0 : (batch_s0 / (unsigned)nsb + (unsigned)q) * (unsigned)nsb;
+        const int rbq = (int)(t0 / (unsigned)nsb);
+        const unsigned t1 = min(cu1, (unsigned)(rbq + 1) * (unsigned)nsb);
+        const float *pq = psum + (size_t)(half * kPend + q) * W * 64;
+        float y0 = 0.f, y1 = 0.f;
+        for (int w2 = 0; w2 < W; w2++) {
+          y0 += pq[w2 * 64 + lane];
+          y1 += pq[w2 * 64 + 32 + lane];
+        }
+        const unsigned R0 = (unsigned)rbq * nsb, R1 = R0 + nsb;
+        if (t0 == R0 && t1 == R1) {
+          epilogue<EPI>(p, rbq, y0, y1);
+        } else {
+          // the row-block continues in another CTA: global partial per CTA
+          const int which = cu0 >= R0 ? 0 : 1;
+          float *gslot = a.e.part + ((size_t)b * 2 + which) * 64;
+          gslot[lane] = y0;
+          gslot[32 + lane] = y1;
           __threadfence();
-          const unsigned bf = cta_of_unit(U, G, R0), bl = cta_of_unit(U, G, R1 - 1);
-          float z0 = 0.f, z1 = 0.f;
-          for (unsigned b2 = bf; b2 <= bl; b2++) {
-            const unsigned c0 = ubeg(U, G, b2), c1 = ubeg(U, G, b2 + 1);
-            if (c0 == c1) continue;
-            const float *sl2 = a.e.part + ((size_t)b2 * 2 + (c0 >= R0 ? 0 : 1)) * 64;
-            z0 += __ldcg(sl2 + lane);
-            z1 += __ldcg(sl2 + 32 + lane);
+          __syncwarp();
+          unsigned done = 0;
+          if (lane == 0) done = atomicAdd(a.e.tile_counter + rbq, t1 - t0) + (t1 - t0);
+          done = __shfl_sync(0xffffffffu, done, 0);
+          if (done == (unsigned)nsb) {
+            __threadfence();
+            const unsigned bf = cta_of_unit(U, G, R0), bl = cta_of_unit(U, G, R1 - 1);
+            float z0 = 0.f, z1 = 0.f;
+            for (unsigned b2 = bf; b2 <= bl; b2++) {
+              const unsigned c0 = ubeg(U, G, b2), c1 = ubeg(U, G, b2 + 1);
+              if (c0 == c1) continue;
+              const float *sl2 = a.e.part + ((size_t)b2 * 2 + (c0 >= R0 ? 0 : 1)) * 64;
+              z0 += __ldcg(sl2 + lane);
+              z1 += __ldcg(sl2 + 32 + lane);
+            }
+            if (lane == 0) a.e.tile_counter[rbq] = 0u;
+            epilogue<EPI>(p, rbq, z0, z1);
           }
-          if (lane == 0) a.e.tile_counter[rbk] = 0u;
-          epilogue<EPI>(p, rbk, z0, z1);
         }
       }
     }
-    s0 = s1;
   }
   if (timeout && lane == 0 && a.e.err) atomicOr(a.e.err, GB_DEVERR_TIMEOUT);
 }
@@ -678,10 +709,10 @@ int sms() {
 
 // Dynamic shared memory: ring stages, then per staged super-block the limb
 // planes (3 x 256 B), 16 sums (64 B) and 16 packed limb sums (128 B), the
-// scales (padded to 4 floats), then 2 x [warps][64] segment partials.
+// scales (padded to 4 floats), then 2 x kPend x [warps][64] segment partials.
 size_t gemv_smem(int warps, int nstage, int stage_bytes, int xs_max) {
   return (size_t)nstage * stage_bytes + (size_t)xs_max * (3 * 256 + 64 + 128) +
-         (size_t)((xs_max + 3) & ~3) * 4 + (size_t)2 * warps * 64 * 4;
+         (size_t)((xs_max + 3) & ~3) * 4 + (size_t)2 * kPend * warps * 64 * 4;
 }
 
 using KernelFn = void (*)(Kp);
@@ -841,7 +872,10 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   int K = pow2_floor(std::max(1, std::min(warps, (36 * 1024 + ub / 2) / ub)));
   K = std::min(K, pow2_floor(std::max(1, upc)));
   int ns = 0;
-  if (fk > 0 && fk <= warps && (fk & (fk - 1)) == 0 && fs >= 2 && fs <= kMaxStages &&
+  // A consumer warp takes every (warps/K)-th stage, so the ring must hold at
+  // least warps/K stages: then a warp's own previous stage bounds the phase
+  // of the slot it waits on next (gemv_kernel, step 3).
+  if (fk > 0 && fk <= warps && (fk & (fk - 1)) == 0 && fs >= 2 && fs <= kMaxStages && warps / fk <= fs &&
       fixed + (long long)fs * fk * ub <= room) {
     K = fk;
     ns = fs;
@@ -851,6 +885,10 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
       if (ns >= 2 || K == 1) break;
     }
     if (ns < 2) ns = 2;
+    while (warps / K > ns && (upc + K - 1) / K > ns && K < warps) {
+      K *= 2;
+      ns = (int)std::max<long long>(2, std::min<long long>(kMaxStages, (budget - fixed) / ((long long)K * ub)));
+    }
   }
   int lk = 0;
   while ((1 << lk) < K) lk++;
