@@ -167,7 +167,9 @@ def max_over_ranks(x, world):
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    # a CPU tensor under gloo (the CPU tests), a device tensor under NCCL
+    dev = "cpu" if dist.get_backend() == "gloo" else "cuda"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
