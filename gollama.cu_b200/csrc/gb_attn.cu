@@ -80,7 +80,12 @@ __host__ __device__ constexpr int merge_floats(int S, int nthr) { return ((8 * S
 // Called by every thread of the head's last CTA. The slice weights come from
 // one warp per group head (lanes over slices); the weighted sums are spread
 // over all threads as float4 columns x slice groups and added in a fixed
-// order, so the result is deterministic.
+// order, so the result is deterministic. The partials were written by other
+// CTAs and are read from L2, where each dependent access costs a round trip
+// of about a microsecond: every thread issues its loads -- the (m, l) pairs
+// and up to kMergeBatch of its o columns -- before any arithmetic needs them.
+constexpr int kMergeBatch = 16;
+
 template <int HD>
 GB_DEV void merge_slices(const GbAttnArgs &a, int h, int S, int G, float *ms, int nthr) {
   constexpr int PS = part_stride(HD);
@@ -88,42 +93,90 @@ GB_DEV void merge_slices(const GbAttnArgs &a, int h, int S, int G, float *ms, in
   float *wgt = ms, *linv = ms + 8 * S;
   float4 *red4 = (float4 *)(ms + ((8 * S + 8 + 3) & ~3));
   const float *pb = a.part + (size_t)h * S * G * PS;
-  if (warp < G) {
+  const int NV = G * HD / 4, ngrp = nthr / NV;  // NV <= 256 <= nthr
+  const bool mine = tid < ngrp * NV;
+  const int v = tid % NV, grp = tid / NV, g = v / (HD / 4), d = (v % (HD / 4)) * 4;
+  // 1. loads: this thread's first batch of o columns, and (m, l) of the slices
+  float4 xb[kMergeBatch];
+  int nb = 0;
+  if (mine) {
+#pragma unroll
+    for (int q = 0; q < kMergeBatch; q++) {
+      const int j = grp + q * ngrp;
+      if (j < S) {
+        xb[q] = __ldcg((const float4 *)(pb + ((size_t)j * G + g) * PS + d));
+        nb = q + 1;
+      }
+    }
+  }
+  if (warp < G && S > 128) {  // more slices than the fast path holds: two passes over L2
     float M = -INFINITY;
     for (int j = lane; j < S; j += 32) M = fmaxf(M, __ldcg(pb + ((size_t)j * G + warp) * PS + HD));
     M = gb_warp_max(M);
     float L = 0.f;
     for (int j = lane; j < S; j += 32) {
-      const float *pj = pb + ((size_t)j * G + warp) * PS;
-      const float m = __ldcg(pj + HD);
-      const float w = m == -INFINITY ? 0.f : expf(m - M);
+      const float2 ml = __ldcg((const float2 *)(pb + ((size_t)j * G + warp) * PS + HD));
+      const float w = ml.x == -INFINITY ? 0.f : expf(ml.x - M);
       wgt[j * 8 + warp] = w;
-      L += __ldcg(pj + HD + 1) * w;
+      L += ml.y * w;
+    }
+    L = gb_warp_sum(L);
+    if (lane == 0) linv[warp] = 1.f / L;
+  } else if (warp < G) {
+    float2 ml[4];  // S <= 128 slices: at most 4 per lane
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int j = lane + 32 * q;
+      ml[q] = j < S ? __ldcg((const float2 *)(pb + ((size_t)j * G + warp) * PS + HD)) : make_float2(-INFINITY, 0.f);
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 4; q++) M = fmaxf(M, ml[q].x);
+    M = gb_warp_max(M);
+    float L = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int j = lane + 32 * q;
+      const float w = ml[q].x == -INFINITY ? 0.f : expf(ml[q].x - M);
+      if (j < S) wgt[j * 8 + warp] = w;
+      L += ml[q].y * w;
     }
     L = gb_warp_sum(L);
     if (lane == 0) linv[warp] = 1.f / L;
   }
   __syncthreads();
-  const int NV = G * HD / 4, ngrp = nthr / NV;  // NV <= 256 <= nthr
-  if (tid < ngrp * NV) {
-    const int v = tid % NV, grp = tid / NV, g = v / (HD / 4), d = (v % (HD / 4)) * 4;
+  // 2. weighted sums in slice order: the loaded batch, then any further batches
+  if (mine) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int j = grp; j < S; j += ngrp) {
-      const float4 x = __ldcg((const float4 *)(pb + ((size_t)j * G + g) * PS + d));
-      const float w = wgt[j * 8 + g];
-      acc.x = fmaf(x.x, w, acc.x);
-      acc.y = fmaf(x.y, w, acc.y);
-      acc.z = fmaf(x.z, w, acc.z);
-      acc.w = fmaf(x.w, w, acc.w);
+    for (int base = 0;; base += kMergeBatch) {
+#pragma unroll
+      for (int q = 0; q < kMergeBatch; q++) {
+        if (q < nb) {
+          const float w = wgt[(grp + (base + q) * ngrp) * 8 + g];
+          acc.x = fmaf(xb[q].x, w, acc.x);
+          acc.y = fmaf(xb[q].y, w, acc.y);
+          acc.z = fmaf(xb[q].z, w, acc.z);
+          acc.w = fmaf(xb[q].w, w, acc.w);
+        }
+      }
+      if (grp + (base + kMergeBatch) * ngrp >= S) break;
+      nb = 0;
+#pragma unroll
+      for (int q = 0; q < kMergeBatch; q++) {
+        const int j = grp + (base + kMergeBatch + q) * ngrp;
+        if (j < S) {
+          xb[q] = __ldcg((const float4 *)(pb + ((size_t)j * G + g) * PS + d));
+          nb = q + 1;
+        }
+      }
     }
     red4[tid] = acc;
   }
   __syncthreads();
   if (tid < NV) {
     float4 o = red4[tid];
-    for (int grp = 1; grp < ngrp; grp++) {
-      const float4 x = red4[grp * NV + tid];
+    for (int gi = 1; gi < ngrp; gi++) {
+      const float4 x = red4[gi * NV + tid];
       o.x += x.x;
       o.y += x.y;
       o.z += x.z;
