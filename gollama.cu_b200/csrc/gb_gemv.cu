@@ -3,28 +3,30 @@
 //
 // Replaces kernels.MatVecQ4_0 / MatVecQ4K / MatVecQ6K (kernels/quantmv.go:18-136)
 // on the model path. Design:
-//  * Work is the list of units (row-block, super-block); a row-block is one
-//    32-row tile, or a gate/up tile pair for the SwiGLU epilogue. Every CTA
-//    takes one contiguous range of units (stream-K over a persistent grid,
-//    or one row-block per CTA for small matrices), so all SMs stay busy
-//    whatever the matrix shape and no wave is partial.
+//  * Work is the list of units: sb-blocks (32 rows x 256 columns) in
+//    (row-block, super-block) order. A row-block is one 32-row tile, or for
+//    the SwiGLU epilogue a gate/up tile pair whose gate and up sb-blocks are
+//    two units. Every CTA takes one contiguous range of units (stream-K over
+//    a persistent grid, or one row-block per CTA for small matrices), so all
+//    SMs stay busy whatever the matrix shape and no wave is partial.
 //  * Units are contiguous in memory in that order, so a CTA's range is one
 //    byte range. A producer warp streams it through a ring of shared-memory
 //    stages of K units (tens of KB) with one 1-D TMA bulk copy per stage;
-//    eight consumer warps decode the units round-robin and give each stage
-//    back through an mbarrier. Lane l of a warp owns row l of the tile.
-//  * The activation arrives as a limb pack (gb_device.cuh): three int8 limbs
-//    per element, so the 4-bit / 6-bit quants meet the activation in dp4a
-//    (4 products per instruction, exact int32 sums); float math is needed once
-//    per 16- or 32-element sub-block for the ggml scales. A CTA stages only the
-//    pack of the super-blocks its units touch.
+//    16 consumer warps decode the units round-robin and give each stage back
+//    through an mbarrier. Lane l of a warp owns row l of the tile; with an
+//    even warp count a warp sees only gate or only up units of a pair.
+//  * The activation is staged per CTA as three int8 limbs per element with
+//    one scale per 256-element super-block (RMSNorm applied first when the
+//    GEMV consumes a normalised input), so the 4-bit / 6-bit quants meet it
+//    in dp4a (4 products per instruction, exact int32 sums) and the ggml
+//    sub-block scales are applied in int32; float math once per super-block.
 //  * A row-block split between CTAs is finished by the CTA whose atomic
 //    count completes it; it sums the partials in CTA order (deterministic)
 //    and runs the epilogue. Counters are reset by that CTA, so the kernel can
 //    be replayed from a CUDA graph.
-//  * A CTA uses about half an SM, so under programmatic dependent launch the
-//    next kernel's CTA fits beside it and streams its own weights during
-//    this kernel's tail.
+//  * Under programmatic dependent launch the next kernel is launched at this
+//    kernel's start; its producer streams its own weights as soon as its CTAs
+//    find room.
 //  * One instantiation per (weight types, epilogue) keeps each kernel's code
 //    small.
 #include <math.h>
@@ -224,7 +226,9 @@ GB_DEV uint64_t argmax_key(float v, uint32_t idx) {
 
 struct Kp {  // kernel parameters
   GbGemvArgs a;
-  int rb, nrb;
+  int rb, nrb;      // rb: sb-blocks per unit (1); nrb: row-blocks
+  int half;         // gate/up row-block pairs: unit u is the gate (u even) or up (u odd) sb-block
+  int upr;          // units per row-block (nsb, or 2*nsb for gate/up pairs)
   int lk;           // log2 of the units per ring stage (K = 1 << lk, K <= consumer warps)
   int nstage;       // ring stages (at most kMaxStages)
   int stage_bytes;  // bytes of one stage buffer (K units of the larger type)
@@ -365,13 +369,6 @@ GB_DEV unsigned cta_of_unit(unsigned U, unsigned G, unsigned u) {
   return b;
 }
 
-template <int T>
-__device__ __noinline__ float sb_dot_outlined(const uint8_t *st, int lane, const uint32_t *xa,
-                                              const uint32_t *xb, const uint32_t *xc, const float *xsum,
-                                              const uint2 *sl, float xs) {
-  return sb_dot<T>(st, lane, xa, xb, xc, xsum, sl, xs);
-}
-
 template <int TA, int TB>
 GB_DEV float decode(int ty, const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
                     const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
@@ -478,8 +475,11 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   constexpr int CT = W * 32;
   const int tid = threadIdx.x;
   gb_grid_dep_wait();
-  const int nsbs = (cu1 - cu0) >= (unsigned)nsb ? nsb : (int)(cu1 - cu0);
-  const int sbf = (int)(cu0 % (unsigned)nsb);
+  const int half = p.half;
+  const unsigned upr = (unsigned)p.upr;
+  const unsigned su0 = half ? cu0 >> 1 : cu0, su1 = half ? ((cu1 - 1) >> 1) + 1 : cu1;  // super-block units
+  const int nsbs = (su1 - su0) >= (unsigned)nsb ? nsb : (int)(su1 - su0);
+  const int sbf = (int)(su0 % (unsigned)nsb);
   float inv = 1.f;
   if (a.in_ssq) {
     double ss = 0;
@@ -573,14 +573,16 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   unsigned k = j >> LK;
   int s = (int)(k % (unsigned)NS);
   uint32_t ph = (k / (unsigned)NS) & 1u;
-  unsigned usb = (cu0 + j) % (unsigned)nsb;
+  unsigned usb = ((cu0 + j) >> half) % (unsigned)nsb;
+  const unsigned dsb = (unsigned)W >> half;              // super-blocks per step
+  const int hw = half ? (int)((cu0 + j) & 1u) : 0;        // gate (0) or up (1) rows of this warp (W even)
   int nseg = 0;
   unsigned batch_s0 = cu0;  // first unit of the current batch of segments
   for (unsigned s0 = cu0; s0 < cu1; nseg++) {
-    const int rbk = (int)(s0 / (unsigned)nsb);
-    const unsigned s1 = min(cu1, (unsigned)(rbk + 1) * (unsigned)nsb);
+    const int rbk = (int)(s0 / upr);
+    const unsigned s1 = min(cu1, (unsigned)(rbk + 1) * upr);
     const int ty = rbk < a.split_tile ? TA : TB;
-    float acc0 = 0.f, acc1 = 0.f;
+    float acc0 = 0.f;
     for (; cu0 + j < s1;) {
       const unsigned u = cu0 + j;
       if (prewait && k >= (unsigned)NS && !timeout && !gb_mbar_wait(&empty[s], ph ^ 1u)) timeout = true;
@@ -595,14 +597,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
         const size_t off = TA == TB ? (size_t)(j & (unsigned)(K - 1)) * (size_t)p.rb * sbb_a
                                     : unit_off<TA, TB>(p, u) - unit_off<TA, TB>(p, cu0 + (k << LK));
         const uint8_t *st = ring + (size_t)s * p.stage_bytes + off;
-        if constexpr (EPI == GB_EPI_SWIGLU) {
-          // gate then up sb-block; one decode at a time keeps the register
-          // footprint of a single tile
-          acc0 += sb_dot_outlined<TA>(st, lane, xa, xb, xc, xsum, sl, xs);
-          acc1 += sb_dot_outlined<TA>(st + sbb_a, lane, xa, xb, xc, xsum, sl, xs);
-        } else {
-          acc0 += decode<TA, TB>(ty, st, lane, xa, xb, xc, xsum, sl, xs);
-        }
+        acc0 += decode<TA, TB>(ty, st, lane, xa, xb, xc, xsum, sl, xs);
       }
       __syncwarp();
       if (lane == 0) gb_mbar_arrive(&empty[s]);
@@ -613,7 +608,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
         s -= NS;
         ph ^= 1u;
       }
-      usb += W;
+      usb += dsb;
       while (usb >= (unsigned)nsb) usb -= nsb;
     }
     // this warp's partials of segment nseg go to slot nseg % kPend of the
@@ -624,8 +619,8 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
     const int slot = nseg % kPend, half = (nseg / kPend) & 1;
     if (slot == 0) batch_s0 = s0;
     float *ps = psum + (size_t)(half * kPend + slot) * W * 64;
-    ps[warp * 64 + lane] = acc0;
-    ps[warp * 64 + 32 + lane] = acc1;
+    ps[warp * 64 + hw * 32 + lane] = acc0;  // the other family's half stays zero
+    ps[warp * 64 + (1 - hw) * 32 + lane] = 0.f;
     s0 = s1;
     if (slot == kPend - 1 || s0 >= cu1) {
       consumers_sync<W>();
@@ -633,16 +628,16 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
         const int seg = nseg - slot + q;
         if (warp != seg % W) continue;  // reducer of segment seg (sum in warp order)
         // segments after the batch's first start on row-block boundaries
-        const unsigned t0 = q == 0 ? batch_s0 : (batch_s0 / (unsigned)nsb + (unsigned)q) * (unsigned)nsb;
-        const int rbq = (int)(t0 / (unsigned)nsb);
-        const unsigned t1 = min(cu1, (unsigned)(rbq + 1) * (unsigned)nsb);
+        const unsigned t0 = q == 0 ? batch_s0 : (batch_s0 / upr + (unsigned)q) * upr;
+        const int rbq = (int)(t0 / upr);
+        const unsigned t1 = min(cu1, (unsigned)(rbq + 1) * upr);
         const float *pq = psum + (size_t)(half * kPend + q) * W * 64;
         float y0 = 0.f, y1 = 0.f;
         for (int w2 = 0; w2 < W; w2++) {
           y0 += pq[w2 * 64 + lane];
           y1 += pq[w2 * 64 + 32 + lane];
         }
-        const unsigned R0 = (unsigned)rbq * nsb, R1 = R0 + nsb;
+        const unsigned R0 = (unsigned)rbq * upr, R1 = R0 + upr;
         if (t0 == R0 && t1 == R1) {
           epilogue<EPI>(p, rbq, y0, y1);
         } else {
@@ -656,7 +651,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
           unsigned done = 0;
           if (lane == 0) done = atomicAdd(a.e.tile_counter + rbq, t1 - t0) + (t1 - t0);
           done = __shfl_sync(0xffffffffu, done, 0);
-          if (done == (unsigned)nsb) {
+          if (done == upr) {
             __threadfence();
             const unsigned bf = cta_of_unit(U, G, R0), bl = cta_of_unit(U, G, R1 - 1);
             float z0 = 0.f, z1 = 0.f;
@@ -781,7 +776,7 @@ int gb_repack_launch(int typ, const uint8_t *raw, int rows, int cols, uint8_t *t
 
 GbGemvPlan gb_gemv_plan(int ntiles, int nsb, int epi, int nsm) {
   GbGemvPlan p;
-  p.rb = epi == GB_EPI_SWIGLU ? 2 : 1;
+  p.rb = 1;
   p.warps = 8;
   p.stages = 2;
   p.ks = 1;
@@ -802,8 +797,9 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   if (a.nsb <= 0 || a.ntiles <= 0) return gb_fail(GB_ERR_INVALID, "gpu: gemv: empty matrix");
   Kp p;
   p.a = a;
-  p.rb = plan.rb;
-  if (a.ntiles % p.rb) return gb_fail(GB_ERR_INVALID, "gpu: gemv: tiles not paired");
+  p.rb = 1;
+  p.half = a.epi == GB_EPI_SWIGLU ? 1 : 0;
+  if (p.half && a.ntiles % 2) return gb_fail(GB_ERR_INVALID, "gpu: gemv: tiles not paired");
   const int ta = a.type_a, tb = a.split_tile < a.ntiles ? a.type_b : a.type_a;
   p.a.type_b = tb;
   // consumer warps per CTA: 16 (a whole SM) or 8 (half an SM); GB_GEMV_WARPS overrides
@@ -811,9 +807,10 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   if (const char *e = getenv("GB_GEMV_WARPS")) warps = atoi(e) == 8 ? 8 : 16;
   KernelFn fn = pick(ta, tb, a.epi, warps);
   if (!fn) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: types %d/%d with epilogue %d", ta, tb, a.epi);
-  if (p.rb == 2 && ta != tb) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: gate/up types differ");
-  p.nrb = a.ntiles / p.rb;
-  p.units = (unsigned)p.nrb * (unsigned)a.nsb;
+  if (p.half && ta != tb) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: gate/up types differ");
+  p.nrb = p.half ? a.ntiles / 2 : a.ntiles;
+  p.upr = p.half ? 2 * a.nsb : a.nsb;
+  p.units = (unsigned)p.nrb * (unsigned)p.upr;
   const int ub = p.rb * std::max(gb_tiled_sb_bytes(ta), gb_tiled_sb_bytes(tb));  // largest unit
   const int nsm = sms();
   const long long cap = smem_optin();
@@ -856,7 +853,7 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   long long grid = p.nrb <= nsm ? p.nrb : std::min<long long>(nsm, p.units);
   if (grid * 128 > (long long)gb_gemv_scratch_floats(a.ntiles, plan)) grid = gb_gemv_scratch_floats(a.ntiles, plan) / 128;
   const int upc = (int)((p.units + grid - 1) / grid);  // units per CTA (at most)
-  const int xs = std::min(a.nsb, upc + 1);
+  const int xs = std::min(a.nsb, (p.half ? upc / 2 + 1 : upc) + 1);  // super-blocks a CTA touches
   long long budget = warps == 8 ? 113 * 1024 : 220 * 1024;
   if (const char *e = getenv("GB_SMEM_BUDGET")) budget = atoll(e);
   const long long room = cap - static_smem;
