@@ -640,9 +640,10 @@ struct MmaAttn {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(kMThreads, 1) attn_mma_kernel(const GbAttnArgs a) {
+__global__ void __launch_bounds__(kMThreads, 1) attn_mma_kernel(const __grid_constant__ GbAttnArgs a) {
   using MA = MmaAttn<HD>;
   constexpr int SUB = MA::SUB, KS = HD / 16, NT = HD / 8, PS = part_stride(HD);
+  static_assert(SUB == 128, "the tensor maps' box holds 128 positions");
   extern __shared__ __align__(128) uint8_t smb[];
   __shared__ __align__(8) uint64_t full[kMStages], empty[kMStages];
   __shared__ float wm[kMW][8], wl[kMW][8];
@@ -658,7 +659,9 @@ __global__ void __launch_bounds__(kMThreads, 1) attn_mma_kernel(const GbAttnArgs
   int kv_len = *a.kv_len_pos + 1;
   const bool bad = kv_len < 1 || kv_len > a.max_len;
   if (bad) kv_len = kv_len < 1 ? 1 : a.max_len;
-  const int t0 = (int)((long long)kv_len * s / S), t1 = (int)((long long)kv_len * (s + 1) / S);
+  // slice bounds on 32-position boundaries (the tensor maps address rows of 32 positions)
+  const int t0 = s == 0 ? 0 : (int)((long long)kv_len * s / S) & ~31;
+  const int t1 = s == S - 1 ? kv_len : (int)((long long)kv_len * (s + 1) / S) & ~31;
   const int nsub = (t1 - t0 + SUB - 1) / SUB;
   if (tid == 0) {
     for (int i = 0; i < kMStages; i++) {
@@ -699,6 +702,13 @@ __global__ void __launch_bounds__(kMThreads, 1) attn_mma_kernel(const GbAttnArgs
         const int p0 = t0 + k * SUB, nk = min(SUB, t1 - p0);
         uint8_t *sk = smb + (size_t)st * MA::STAGE, *sv = sk + MA::HALF;
         gb_mbar_expect_tx(&full[st], (uint32_t)(2 * NT * nk * 16));
+        if (a.tmap && nk == SUB) {
+          // a whole sub-chunk: one 4-D copy each of K and V lands as
+          // [dim chunk][position][16 B], the layout the consumers read
+          gb_tma_load_4d(sk, &a.tk, 0, p0 >> 5, 0, h, &full[st]);
+          gb_tma_load_4d(sv, &a.tv, 0, p0 >> 5, 0, h, &full[st]);
+          continue;
+        }
         for (int dc = 0; dc < NT; dc++) {
           gb_bulk_g2s(sk + (size_t)dc * SUB * 16, kg + ((size_t)dc * a.k_sd + (size_t)p0 * 8) * 2,
                       (uint32_t)(nk * 16), &full[st]);
@@ -837,6 +847,10 @@ __global__ void __launch_bounds__(kMThreads, 1) attn_mma_kernel(const GbAttnArgs
   if (tid == 0) a.counter[h] = 0u;
 }
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
 template <int HD>
 int launch_mma(const GbAttnArgs &a, cudaStream_t st, bool pdl) {
   using MA = MmaAttn<HD>;
@@ -933,4 +947,44 @@ int gb_attn_launch(const GbAttnArgs &a, cudaStream_t st, bool pdl) {
       return f16 ? launch_t<8, 128, true>(a, st, pdl) : launch_t<8, 128, false>(a, st, pdl);
   }
   return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: head_dim %d (64 or 128 supported)", a.head_dim);
+}
+
+// Tensor maps of one layer's fp16 K and V caches. The cache is
+// [kv_head][head_dim/8][max_len][8 halves]; as a 4-D tensor (innermost
+// first) {256 = 32 positions x 8 halves, max_len/32, head_dim/8, n_kv} with
+// byte strides {512, 16*max_len, 16*max_len*head_dim/8}. A box
+// {256, 4, head_dim/8, 1} is one head's 128 positions (from a multiple of
+// 32) of every 16-byte dim chunk, read as 512-byte rows, and lands in shared
+// memory as [chunk][position][16 B] -- the stage layout of attn_mma_kernel.
+// (A 16-byte innermost dimension would make the copy engine move 16-byte
+// rows, slower than per-chunk 1-D copies; 256 is the largest box side.) The
+// encoder comes from the driver
+// through the runtime's entry-point query, so the library does not link
+// libcuda.
+int gb_attn_tensor_maps(const void *k, const void *v, int n_kv, int head_dim, int max_len, CUtensorMap *tk,
+                        CUtensorMap *tv) {
+  static EncodeTiledFn encode = nullptr;
+  if (!encode) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return gb_fail(GB_ERR_CUDA, "gpu: AttnDecode: cuTensorMapEncodeTiled unavailable");
+    encode = (EncodeTiledFn)fn;
+  }
+  if (max_len < 128 || max_len % 32 || (head_dim != 64 && head_dim != 128))
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: AttnDecode: no tensor map for max_len %d, head_dim %d", max_len, head_dim);
+  const cuuint64_t dims[4] = {256, (cuuint64_t)(max_len / 32), (cuuint64_t)(head_dim / 8), (cuuint64_t)n_kv};
+  const cuuint64_t strides[3] = {512, (cuuint64_t)max_len * 16, (cuuint64_t)max_len * 16 * (head_dim / 8)};
+  const cuuint32_t box[4] = {256, 4, (cuuint32_t)(head_dim / 8), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const void *src[2] = {k, v};
+  CUtensorMap *dst[2] = {tk, tv};
+  for (int i = 0; i < 2; i++) {
+    CUresult r = encode(dst[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void *>(src[i]), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return gb_fail(GB_ERR_CUDA, "gpu: AttnDecode: tensor map encode failed (%d)", (int)r);
+  }
+  return GB_OK;
 }

@@ -128,6 +128,16 @@ GB_DEV void gb_bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *ba
       "l"(src), "r"(bytes), "r"(gb_smem_u32(bar))
       : "memory");
 }
+// Tiled 4-D TMA load of one box of the tensor map `tmap` (a __grid_constant__
+// kernel parameter) at coordinates (c0 innermost .. c3) into dst, completing
+// on bar. c0 * element size must be a multiple of 16 bytes; no multicast.
+GB_DEV void gb_tma_load_4d(void *dst, const void *tmap, int c0, int c1, int c2, int c3, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(gb_smem_u32(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(gb_smem_u32(bar))
+      : "memory");
+}
 GB_DEV void gb_mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(gb_smem_u32(bar)) : "memory");
 }

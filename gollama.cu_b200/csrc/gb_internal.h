@@ -2,6 +2,7 @@
 // units: error reporting, kernel launch entry points, GGUF reader/writer.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (the encoder is reached through cudaGetDriverEntryPoint)
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdint.h>
@@ -124,8 +125,15 @@ struct GbAttnArgs {
   float *part = nullptr;         // [n_kv][splits][group][head_dim+4]
   unsigned *counter = nullptr;   // [n_kv], zero between launches
   unsigned *err = nullptr;
+  // fp16 model caches: 4-D tensor maps of K and V ([head][dim chunk][position][8 halves]),
+  // box of one head x all chunks x 128 positions, for whole 128-position sub-chunks
+  int tmap = 0;
+  CUtensorMap tk, tv;
 };
 int gb_attn_launch(const GbAttnArgs &a, cudaStream_t st, bool pdl);
+// Encode the tensor maps of one layer's fp16 K and V caches (the model layout).
+int gb_attn_tensor_maps(const void *k, const void *v, int n_kv, int head_dim, int max_len, CUtensorMap *tk,
+                        CUtensorMap *tv);
 int gb_attn_splits(int n_kv, int max_len, int sms);
 size_t gb_attn_part_floats(int n_kv, int splits, int group, int head_dim);
 

@@ -153,6 +153,8 @@ struct gb_model {
     float *attn_norm = nullptr, *ffn_norm = nullptr;
     Tiled qkv, wo, gu, down;
     void *kc = nullptr, *vc = nullptr;
+    bool tmap = false;  // fp16 caches: tensor maps of K and V for the attention's TMA
+    CUtensorMap tk, tv;
   };
   std::vector<Layer> layers;
   Tiled embd, head;
@@ -461,6 +463,11 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
     at.part = m->attn_part;
     at.counter = m->attn_counter;
     at.err = m->err;
+    if (L.tmap) {
+      at.tmap = 1;
+      at.tk = L.tk;
+      at.tv = L.tv;
+    }
     if ((rc = gb_attn_launch(at, st, pdl)) || (rc = mark(K_ATTN))) return rc;
     // o projection + residual (+ sums of squares for the FFN norm)
     if (!tp) {
@@ -728,6 +735,10 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
       return fail(rc);
     L.kc = kc;
     L.vc = vc;
+    if (c.kv_f16) {  // whole 128-position sub-chunks then move with one TMA copy each
+      L.tmap = gb_attn_tensor_maps(kc, vc, m->kv_local / hd, hd, c.max_len, &L.tk, &L.tv) == GB_OK;
+      if (!L.tmap) gb_clear_error();
+    }
   }
   if ((rc = host_vector(f->tensor("output_norm.weight"), c.dim, hv, "output_norm.weight")) ||
       (rc = upload_vec(m, hv, &m->out_norm, "model: norm")))

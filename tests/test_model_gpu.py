@@ -202,6 +202,31 @@ def test_prefilled_kv_long_context(gb, orc, cuda):
     om.close()
 
 
+@pytest.mark.parametrize("name,max_len", [("q4km_hd128", 16384), ("q4km_hd64", 16384), ("q4km_hd128", 16376)])
+def test_long_context_tensor_map_attention(gb, orc, cuda, name, max_len):
+    # fp16 caches with max_len a multiple of 32 move whole 128-position
+    # sub-chunks of K and V with one TMA tensor copy each (16376: per-chunk
+    # copies only); ~200+ positions per slice so most sub-chunks are whole
+    cfg = dict(MODELS[name], ctx_len=max_len)
+    spec = gb.synth_spec(**cfg)
+    img = gb.SynthImage(spec)
+    raw = np.array(img.view(), copy=True)
+    n_pos = 16000
+    m = gb.Model(img, max_len=max_len, kv_f16=1)
+    m.fill_kv_normal(5, n_pos)
+    om = orc.OracleModel(raw, max_len, True)
+    kv_dim = cfg["kv_heads"] * cfg["head_dim"]
+    for layer in range(cfg["layers"]):
+        k, v = gb.synth_kv_normal(5, layer, 0, n_pos, kv_dim, True)
+        om.set_kv(layer, 0, k, v)
+    for i, tok in enumerate([11, 22, 33]):
+        got = m.forward(tok, n_pos + i).copy()
+        want = om.forward(tok, n_pos + i, cfg["vocab"])
+        check_logits(f"{name} max_len {max_len} pos {n_pos + i}", got, want)
+    m.close()
+    om.close()
+
+
 @pytest.mark.parametrize("kv_f16", [0, 1])
 def test_early_positions_many_slices(gb, orc, cuda, kv_f16):
     # a long cache split into more slices than there are positions yet:
