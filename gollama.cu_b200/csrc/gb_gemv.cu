@@ -228,6 +228,8 @@ struct Kp {  // kernel parameters
   GbGemvArgs a;
   int rb, nrb;      // rb: sb-blocks per unit (1); nrb: row-blocks
   int half;         // gate/up row-block pairs: unit u is the gate (u even) or up (u odd) sb-block
+  int aux_w;        // 1: the norm weights of the staged super-blocks are copied to shared memory
+  int aux_rope;     // doubles of the RoPE row copied to shared memory (QKV epilogue), else 0
   int upr;          // units per row-block (nsb, or 2*nsb for gate/up pairs)
   int lk;           // log2 of the units per ring stage (K = 1 << lk, K <= consumer warps)
   int nstage;       // ring stages (at most kMaxStages)
@@ -240,7 +242,7 @@ constexpr int kMaxStages = 8;
 constexpr int kPend = 4;  // segments reduced per barrier
 
 template <int EPI>
-GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1) {
+GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1, const double *rope_row) {
   const GbGemvArgs &a = p.a;
   const GbEpiArgs &e = a.e;
   const int lane = threadIdx.x & 31;
@@ -272,7 +274,7 @@ GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1) {
     if (r < e.q_rows + e.kv_rows) {  // cpu.RoPE, backend/cpu/cpu.go:69 (float64 math)
       int rr = r < e.q_rows ? r : r - e.q_rows;
       int j = (rr % hd) >> 1;
-      const double *cs = e.rope_cs + ((size_t)pos * (hd / 2) + j) * 2;
+      const double *cs = rope_row + (size_t)j * 2;  // row `pos` of the table, staged at kernel start
       double c = cs[0], s = cs[1];
       double x0 = (lane & 1) ? (double)partner : (double)y0;
       double x1 = (lane & 1) ? (double)y0 : (double)partner;
@@ -426,7 +428,10 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   uint2 *sl_s = (uint2 *)(xsum_s + XS * 16);
   float *xs_s = (float *)(sl_s + XS * 16);
   float *psum = xs_s + ((XS + 3) & ~3);  // [2][kPend][W][64]
+  float *wn_s = psum + 2 * kPend * W * 64;                    // [XS][256] norm weights (aux_w)
+  double *rope_s = (double *)(wn_s + (p.aux_w ? XS * 256 : 0));  // RoPE row (aux_rope doubles)
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
+  __shared__ __align__(8) uint64_t aux;  // norm weights and RoPE row landed
   __shared__ double red[W];
   __shared__ float inv_s;
 
@@ -437,13 +442,37 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
       gb_mbar_init(&full[s], 1);
       gb_mbar_init(&empty[s], (uint32_t)K);
     }
+    gb_mbar_init(&aux, 1);
     gb_mbar_fence_init();
   }
   __syncthreads();
+  // super-blocks of activation this CTA touches: [sbf, sbf + nsbs) mod nsb
+  const int half = p.half;
+  const unsigned upr = (unsigned)p.upr;
+  const unsigned su0 = half ? cu0 >> 1 : cu0, su1 = half ? ((cu1 - 1) >> 1) + 1 : cu1;  // super-block units
+  const int nsbs = (su1 - su0) >= (unsigned)nsb ? nsb : (int)(su1 - su0);
+  const int sbf = (int)(su0 % (unsigned)nsb);
+  const bool use_aux = p.aux_w || p.aux_rope;
 
   if (warp == W) {
-    // 1. producer: weights do not depend on the previous kernel
+    // 1. producer: weights do not depend on the previous kernel. First the
+    // norm weights of the staged super-blocks and the RoPE row of `pos`
+    // (constant tables that the weight stream evicts from L2 every token, so
+    // reading them in the prologue would be a DRAM round trip ahead of the
+    // activation's L2 loads); `pos` is set before the step starts.
     if (lane == 0) {
+      if (use_aux) {
+        const int n1 = min(nsbs, nsb - sbf);
+        int pos = 0;
+        if (p.aux_rope) pos = min(max(*a.e.pos, 0), a.e.max_len - 1);
+        gb_mbar_expect_tx(&aux, (uint32_t)((p.aux_w ? nsbs * 1024 : 0) + p.aux_rope * 8));
+        if (p.aux_w) {
+          gb_bulk_g2s(wn_s, a.in_w + (size_t)sbf * 256, (uint32_t)n1 * 1024u, &aux);
+          if (nsbs > n1) gb_bulk_g2s(wn_s + (size_t)n1 * 256, a.in_w, (uint32_t)(nsbs - n1) * 1024u, &aux);
+        }
+        if (p.aux_rope)
+          gb_bulk_g2s(rope_s, a.e.rope_cs + (size_t)pos * p.aux_rope, (uint32_t)p.aux_rope * 8u, &aux);
+      }
       unsigned k = 0;
       for (; k < nst; k++) {
         const int s = (int)(k % (unsigned)NS);
@@ -462,6 +491,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
       // the copies still in flight land (bounded) before the CTA exits
       for (unsigned j = k > (unsigned)NS ? k - NS : 0; j < k; j++)
         (void)gb_mbar_wait(&full[j % NS], (j / NS) & 1);
+      if (use_aux) (void)gb_mbar_wait(&aux, 0);
     }
     return;
   }
@@ -475,11 +505,15 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   constexpr int CT = W * 32;
   const int tid = threadIdx.x;
   gb_grid_dep_wait();
-  const int half = p.half;
-  const unsigned upr = (unsigned)p.upr;
-  const unsigned su0 = half ? cu0 >> 1 : cu0, su1 = half ? ((cu1 - 1) >> 1) + 1 : cu1;  // super-block units
-  const int nsbs = (su1 - su0) >= (unsigned)nsb ? nsb : (int)(su1 - su0);
-  const int sbf = (int)(su0 % (unsigned)nsb);
+  // this warp's first super-block of x is loaded with the sums of squares
+  // (it does not depend on them): one L2 round trip instead of two
+  float4 x0p = make_float4(0.f, 0.f, 0.f, 0.f), x1p = x0p;
+  if (warp < nsbs) {
+    int sb = sbf + warp;
+    if (sb >= nsb) sb -= nsb;
+    x0p = __ldcg((const float4 *)(a.in_x + sb * 256 + lane * 8));
+    x1p = __ldcg((const float4 *)(a.in_x + sb * 256 + lane * 8 + 4));
+  }
   float inv = 1.f;
   if (a.in_ssq) {
     double ss = 0;
@@ -496,17 +530,21 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
     consumers_sync<W>();
     inv = inv_s;
   }
+  bool timeout = use_aux && !gb_mbar_wait(&aux, 0);
   for (int ls = warp; ls < nsbs; ls += W) {
     int sb = sbf + ls;
     if (sb >= nsb) sb -= nsb;
     const int e0 = sb * 256 + lane * 8;
     float z[8];
     {
-      const float4 x0 = __ldcg((const float4 *)(a.in_x + e0)), x1 = __ldcg((const float4 *)(a.in_x + e0 + 4));
+      const bool first = ls == warp;
+      const float4 x0 = first ? x0p : __ldcg((const float4 *)(a.in_x + e0));
+      const float4 x1 = first ? x1p : __ldcg((const float4 *)(a.in_x + e0 + 4));
       z[0] = x0.x; z[1] = x0.y; z[2] = x0.z; z[3] = x0.w;
       z[4] = x1.x; z[5] = x1.y; z[6] = x1.z; z[7] = x1.w;
       if (a.in_w) {
-        const float4 w0 = __ldg((const float4 *)(a.in_w + e0)), w1 = __ldg((const float4 *)(a.in_w + e0 + 4));
+        const float4 *wq = (const float4 *)(wn_s + (size_t)ls * 256 + lane * 8);
+        const float4 w0 = wq[0], w1 = wq[1];
         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
         for (int i = 0; i < 8; i++) z[i] = __fmul_rn(__fmul_rn(z[i], inv), wv[i]);
@@ -568,7 +606,6 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   // launcher keeps dk <= NS, so this warp's own stage k - dk >= k - NS has
   // landed, and stages are issued in order.
   const bool prewait = (unsigned)NS % dk != 0u;
-  bool timeout = false;
   unsigned j = (unsigned)warp;  // this warp's next unit (CTA-relative)
   unsigned k = j >> LK;
   int s = (int)(k % (unsigned)NS);
@@ -639,7 +676,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
         }
         const unsigned R0 = (unsigned)rbq * upr, R1 = R0 + upr;
         if (t0 == R0 && t1 == R1) {
-          epilogue<EPI>(p, rbq, y0, y1);
+          epilogue<EPI>(p, rbq, y0, y1, rope_s);
         } else {
           // the row-block continues in another CTA: global partial per CTA
           const int which = cu0 >= R0 ? 0 : 1;
@@ -663,7 +700,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
               z1 += __ldcg(sl2 + 32 + lane);
             }
             if (lane == 0) a.e.tile_counter[rbq] = 0u;
-            epilogue<EPI>(p, rbq, z0, z1);
+            epilogue<EPI>(p, rbq, z0, z1, rope_s);
           }
         }
       }
@@ -705,9 +742,10 @@ int sms() {
 // Dynamic shared memory: ring stages, then per staged super-block the limb
 // planes (3 x 256 B), 16 sums (64 B) and 16 packed limb sums (128 B), the
 // scales (padded to 4 floats), then 2 x kPend x [warps][64] segment partials.
-size_t gemv_smem(int warps, int nstage, int stage_bytes, int xs_max) {
+size_t gemv_smem(int warps, int nstage, int stage_bytes, int xs_max, int aux_w, int aux_rope) {
   return (size_t)nstage * stage_bytes + (size_t)xs_max * (3 * 256 + 64 + 128) +
-         (size_t)((xs_max + 3) & ~3) * 4 + (size_t)2 * kPend * warps * 64 * 4;
+         (size_t)((xs_max + 3) & ~3) * 4 + (size_t)2 * kPend * warps * 64 * 4 + (aux_w ? (size_t)xs_max * 1024 : 0) +
+         (size_t)aux_rope * 8;
 }
 
 using KernelFn = void (*)(Kp);
@@ -799,6 +837,8 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   p.a = a;
   p.rb = 1;
   p.half = a.epi == GB_EPI_SWIGLU ? 1 : 0;
+  p.aux_w = a.in_w != nullptr ? 1 : 0;
+  p.aux_rope = a.epi == GB_EPI_QKV ? a.e.head_dim : 0;
   if (p.half && a.ntiles % 2) return gb_fail(GB_ERR_INVALID, "gpu: gemv: tiles not paired");
   const int ta = a.type_a, tb = a.split_tile < a.ntiles ? a.type_b : a.type_a;
   p.a.type_b = tb;
@@ -857,7 +897,7 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   long long budget = warps == 8 ? 113 * 1024 : 220 * 1024;
   if (const char *e = getenv("GB_SMEM_BUDGET")) budget = atoll(e);
   const long long room = cap - static_smem;
-  const long long fixed = (long long)gemv_smem(warps, 0, 0, xs);
+  const long long fixed = (long long)gemv_smem(warps, 0, 0, xs, p.aux_w, p.aux_rope);
   // K: a power of two, at most the consumer warps (each warp then takes one
   // unit every warps/K stages), about 36 KB per stage, at most the units a
   // CTA owns
@@ -893,7 +933,7 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   p.nstage = ns;
   p.stage_bytes = (K * ub + 127) / 128 * 128;
   p.xs_max = xs;
-  const size_t smem = gemv_smem(warps, ns, p.stage_bytes, xs);
+  const size_t smem = gemv_smem(warps, ns, p.stage_bytes, xs, p.aux_w, p.aux_rope);
   if ((long long)smem > room)
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: %zu B of shared memory for %d stages of %d units", smem, ns, K);
   if (getenv("GB_GEMV_VERBOSE"))
