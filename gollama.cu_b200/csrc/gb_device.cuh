@@ -87,6 +87,13 @@ GB_DEV int gb_dp4a_us(uint32_t a, uint32_t b, int c) {
   return d;
 }
 
+// 4 signed bytes x 4 signed bytes + c.
+GB_DEV int gb_dp4a_ss(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 // ---- warp reductions
 GB_DEV float gb_warp_sum(float v) {
 #pragma unroll

@@ -15,6 +15,9 @@
 //   Q4_0: the 8 raw 18-byte blocks of the super-block are regrouped:
 //         unit 0 = the eight binary16 d, unit 1+k = the 16 quant bytes of
 //         block k (sb-block 4608 bytes = 32*144).
+//   Q8_0: the 8 raw 34-byte blocks likewise: unit 0 = the eight binary16 d,
+//         units 1+2k, 2+2k = the 32 int8 quants of block k (17 units,
+//         sb-block 8704 bytes = 32*272).
 // The tiled buffer holds exactly the raw bytes (plus row padding), so a
 // decode step reads the algorithmic byte count.
 #pragma once
@@ -63,9 +66,9 @@ GB_HD int64_t gb_row_bytes(int t, int64_t n) {
   return bs ? n / bs * gb_type_size(t) : 0;
 }
 
-GB_HD bool gb_tiled_type(int t) { return t == GB_T_Q4_0 || t == GB_T_Q4_K || t == GB_T_Q6_K; }
-GB_HD int gb_tiled_units(int t) { return t == GB_T_Q6_K ? 13 : 9; }
-GB_HD int gb_tiled_sb_bytes(int t) { return t == GB_T_Q6_K ? 6720 : 4608; }
+GB_HD bool gb_tiled_type(int t) { return t == GB_T_Q4_0 || t == GB_T_Q8_0 || t == GB_T_Q4_K || t == GB_T_Q6_K; }
+GB_HD int gb_tiled_units(int t) { return t == GB_T_Q6_K ? 13 : t == GB_T_Q8_0 ? 17 : 9; }
+GB_HD int gb_tiled_sb_bytes(int t) { return t == GB_T_Q6_K ? 6720 : t == GB_T_Q8_0 ? 8704 : 4608; }
 
 // Where raw byte `b` (0 <= b < 32*typesize/... of one super-block of a row)
 // lives inside the sb-block, for lane `lane`.
@@ -75,8 +78,14 @@ GB_HD int gb_tiled_offset(int t, int lane, int b) {
     if (w < 2) return lane * 16 + 2 * k + w;
     return (1 + k) * 512 + lane * 16 + (w - 2);
   }
+  if (t == GB_T_Q8_0) {
+    int k = b / 34, w = b % 34;
+    if (w < 2) return lane * 16 + 2 * k + w;
+    int q = w - 2;
+    return (1 + 2 * k + q / 16) * 512 + lane * 16 + (q & 15);
+  }
   if (t == GB_T_Q6_K && b >= 208) return 13 * 512 + lane * 2 + (b - 208);
   return (b >> 4) * 512 + lane * 16 + (b & 15);
 }
 // Raw bytes per super-block of one row (256 elements).
-GB_HD int gb_sb_raw_bytes(int t) { return t == GB_T_Q6_K ? 210 : 144; }
+GB_HD int gb_sb_raw_bytes(int t) { return t == GB_T_Q6_K ? 210 : t == GB_T_Q8_0 ? 272 : 144; }

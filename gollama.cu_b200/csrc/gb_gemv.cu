@@ -215,6 +215,42 @@ GB_DEV float sb_dot<GB_T_Q4_0>(const uint8_t *st, int lane, const uint32_t *xa, 
   return xs * acc;
 }
 
+// Q8_0: eight 32-element blocks per super-block, y = d*q with int8 q
+// (quant/quant.go:44-55); signed x signed dp4a, one float FMA per block.
+template <>
+GB_DEV float sb_dot<GB_T_Q8_0>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)xsum;
+  (void)sl;
+  const uint4 *u = (const uint4 *)st;
+  const uint4 h = u[lane];
+  const uint32_t dw[4] = {h.x, h.y, h.z, h.w};
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const uint4 q0 = u[(1 + 2 * k) * 32 + lane], q1 = u[(2 + 2 * k) * 32 + lane];
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint4 la = ((const uint4 *)xa)[2 * k], ha = ((const uint4 *)xa)[2 * k + 1];
+    const uint4 lb = ((const uint4 *)xb)[2 * k], hb = ((const uint4 *)xb)[2 * k + 1];
+    const uint4 lc = ((const uint4 *)xc)[2 * k], hc = ((const uint4 *)xc)[2 * k + 1];
+    const uint32_t a8[8] = {la.x, la.y, la.z, la.w, ha.x, ha.y, ha.z, ha.w};
+    const uint32_t b8[8] = {lb.x, lb.y, lb.z, lb.w, hb.x, hb.y, hb.z, hb.w};
+    const uint32_t c8[8] = {lc.x, lc.y, lc.z, lc.w, hc.x, hc.y, hc.z, hc.w};
+    int A = 0, B = 0, C = 0;
+#pragma unroll
+    for (int kk = 0; kk < 8; kk++) {
+      A = gb_dp4a_ss(qw[kk], a8[kk], A);
+      B = gb_dp4a_ss(qw[kk], b8[kk], B);
+      C = gb_dp4a_ss(qw[kk], c8[kk], C);
+    }
+    // |A|, |B|, |C| < 32*127*128; 254*B + C fits int32
+    const float S = (float)A + (float)(254 * B + C) * kL2;
+    const float dk = gb_half_to_float((uint16_t)((dw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu));
+    acc = fmaf(dk, S, acc);
+  }
+  return xs * acc;
+}
+
 // ---- epilogues (one warp, lane l = row 32*rowblock + l) ---------------------
 
 GB_DEV uint64_t argmax_key(float v, uint32_t idx) {
@@ -769,6 +805,7 @@ KernelFn pick_w(int ta, int tb, int epi) {
     if (ta == GB_T_Q4_K) return pick_epi<GB_T_Q4_K, GB_T_Q4_K, W>(epi);
     if (ta == GB_T_Q6_K) return pick_epi<GB_T_Q6_K, GB_T_Q6_K, W>(epi);
     if (ta == GB_T_Q4_0) return pick_epi<GB_T_Q4_0, GB_T_Q4_0, W>(epi);
+    if (ta == GB_T_Q8_0) return pick_epi<GB_T_Q8_0, GB_T_Q8_0, W>(epi);
   } else if (ta == GB_T_Q4_K && tb == GB_T_Q6_K && epi == GB_EPI_QKV) {
     return gemv_kernel<GB_T_Q4_K, GB_T_Q6_K, GB_EPI_QKV, W>;
   } else if (ta == GB_T_Q6_K && tb == GB_T_Q4_K && epi == GB_EPI_QKV) {

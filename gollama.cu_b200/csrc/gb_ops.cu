@@ -294,7 +294,7 @@ __global__ void advance_pos_kernel(int32_t *pos, unsigned *epoch) {
 // per-32 sums of squares the first RMSNorm needs.
 __global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
                              int vocab, float *x, float *ssq, unsigned *err) {
-  __shared__ __align__(16) uint8_t blk[8][224];
+  __shared__ __align__(16) uint8_t blk[8][272];  // one super-block of one row (Q8_0: 272 B)
   gb_grid_dep_launch();
   gb_grid_dep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -311,8 +311,9 @@ __global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, co
   for (int b = lane; b < raw; b += 32) blk[warp][b] = base[gb_tiled_offset(typ, tl, b)];
   __syncwarp();
   int e = (g % 8) * 32 + lane;  // element within the super-block
-  float v = typ == GB_T_Q4_0 ? gb_dequant_elem(typ, blk[warp] + 18 * (e / 32), e % 32)
-                             : gb_dequant_elem(typ, blk[warp], e);
+  float v = typ == GB_T_Q4_0   ? gb_dequant_elem(typ, blk[warp] + 18 * (e / 32), e % 32)
+            : typ == GB_T_Q8_0 ? gb_dequant_elem(typ, blk[warp] + 34 * (e / 32), e % 32)
+                               : gb_dequant_elem(typ, blk[warp], e);
   x[g * 32 + lane] = v;
   float ss = gb_warp_sum(v * v);
   if (lane == 0) ssq[g] = ss;

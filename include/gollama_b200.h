@@ -247,7 +247,8 @@ typedef struct {
   int layers, dim, ffn, heads, kv_heads, head_dim, vocab, ctx_len;
   float rope_base, eps;
   int mix;        /* 0 = all Q4_0 with tied head; 1 = Q4_K_M mix (Q6_K attn_v,
-                     even-layer ffn_down and output); 2 = all Q4_K; 3 = all Q6_K */
+                     even-layer ffn_down and output); 2 = all Q4_K; 3 = all Q6_K;
+                     4 = all Q8_0 */
   uint64_t seed;
 } gb_synth_spec;
 /* Fills spec with a BASELINE preset: 1 = Llama-3.2-1B Q4_0, 3 = 3B Q4_K_M,

@@ -39,7 +39,7 @@ def host(t):
 
 def rand_quant(rng, typ, rows, cols):
     # backend/gpu/gpu_test.go:221 randQuant: random bytes, scale fields overwritten
-    ts, bs = {Q4_0: (18, 32), Q4_K: (144, 256), Q6_K: (210, 256)}[typ]
+    ts, bs = {Q4_0: (18, 32), Q8_0: (34, 32), Q4_K: (144, 256), Q6_K: (210, 256)}[typ]
     w = rng.integers(0, 256, rows * cols // bs * ts, dtype=np.uint8)
 
     def scale(off, mag):
@@ -50,6 +50,8 @@ def rand_quant(rng, typ, rows, cols):
 
     if typ == Q4_0:
         scale(0, 0.02)
+    elif typ == Q8_0:  # not in randQuant (the reference has no Q8_0 GPU kernel); same recipe
+        scale(0, 0.002)
     elif typ == Q4_K:
         scale(0, 0.002)
         scale(2, 0.002)
@@ -161,7 +163,7 @@ TILED_SHAPES = [(64, 256), (300, 1024), (300, 4096), (4096, 4096), (1000, 14336)
 
 
 @pytest.mark.parametrize("rows,cols", TILED_SHAPES)
-@pytest.mark.parametrize("typ", [Q4_0, Q4_K, Q6_K])
+@pytest.mark.parametrize("typ", [Q4_0, Q8_0, Q4_K, Q6_K])
 def test_linear_tiled_vs_oracle(gb, orc, cuda, typ, rows, cols):
     rng = np.random.default_rng(rows * 7 + cols + typ)
     w = rand_quant(rng, typ, rows, cols)

@@ -17,6 +17,8 @@ MODELS = {
     # GQA groups of 3 and 8 query heads per KV head
     "gqa3_hd64": dict(layers=2, dim=768, ffn=512, heads=12, kv_heads=4, head_dim=64, vocab=500, ctx_len=96, mix=1, seed=15),
     "gqa8_hd128": dict(layers=2, dim=1024, ffn=512, heads=8, kv_heads=1, head_dim=128, vocab=500, ctx_len=96, mix=1, seed=16),
+    # all Q8_0 (untied head)
+    "q80_all": dict(layers=2, dim=512, ffn=768, heads=8, kv_heads=2, head_dim=64, vocab=700, ctx_len=96, mix=4, seed=17),
 }
 
 
