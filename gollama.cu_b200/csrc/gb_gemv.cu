@@ -260,6 +260,9 @@ GB_DEV uint64_t argmax_key(float v, uint32_t idx) {
   return ((uint64_t)b << 32) | (uint64_t)(0xFFFFFFFFu - idx);
 }
 
+struct Kp;
+using KernelFnF = void (*)(Kp);
+
 struct Kp {  // kernel parameters
   GbGemvArgs a;
   int rb, nrb;      // rb: sb-blocks per unit (1); nrb: row-blocks
@@ -745,6 +748,108 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   if (timeout && lane == 0 && a.e.err) atomicOr(a.e.err, GB_DEVERR_TIMEOUT);
 }
 
+// ---- unquantized weights (F16 / F32 matrices) ------------------------------
+// model.Linear's MatVecF16 / MatVecF32 (model/model.go:108-117). One CTA of
+// 8 warps per row-block (or gate/up pair), so no row-block is split: the
+// input is staged in shared memory as floats (RMSNorm applied as in the
+// quantized path), warp w takes super-blocks w, w + 8, ... with lane = row
+// and several 16-byte streaming loads in flight, and the warps' sums are
+// added in warp order before the same fused epilogue.
+template <typename TW, int EPI>
+__global__ void __launch_bounds__(256) gemv_float_kernel(const Kp p) {
+  extern __shared__ __align__(16) float fz[];  // [nsb*256] input, then [8][64] partials
+  __shared__ double red[8];
+  __shared__ float inv_s;
+  const GbGemvArgs &a = p.a;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
+  const int nsb = a.nsb, n = nsb * 256, rbk = blockIdx.x, G = p.half ? 2 : 1;
+  gb_grid_dep_launch();
+  gb_grid_dep_wait();
+  float inv = 1.f;
+  if (a.in_ssq) {
+    double ss = 0;
+    for (int g = tid; g < nsb * 8; g += 256) ss += (double)__ldcg(a.in_ssq + g);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      double t = 0;
+      for (int w2 = 0; w2 < 8; w2++) t += red[w2];
+      inv_s = (float)(1.0 / sqrt(t / (double)n + (double)a.eps));
+    }
+    __syncthreads();
+    inv = inv_s;
+  }
+  for (int i = tid * 4; i < n; i += 256 * 4) {
+    float4 x = __ldcg((const float4 *)(a.in_x + i));
+    if (a.in_w) {
+      const float4 w = __ldg((const float4 *)(a.in_w + i));
+      x = make_float4(__fmul_rn(__fmul_rn(x.x, inv), w.x), __fmul_rn(__fmul_rn(x.y, inv), w.y),
+                      __fmul_rn(__fmul_rn(x.z, inv), w.z), __fmul_rn(__fmul_rn(x.w, inv), w.w));
+    }
+    *(float4 *)(fz + i) = x;
+  }
+  __syncthreads();
+  constexpr int EPU = 16 / (int)sizeof(TW);  // elements per 16-byte unit
+  constexpr int UPB = 256 / EPU;              // units per row and super-block
+  const size_t sbb = (size_t)32 * UPB * 16;
+  float acc[2] = {0.f, 0.f};
+  for (int sb = warp; sb < nsb; sb += 8) {
+    for (int g = 0; g < G; g++) {
+      const uint8_t *blk = a.w + (((size_t)rbk * nsb + sb) * G + g) * sbb + lane * 16;
+      const float *zs = fz + sb * 256;
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll 8
+      for (int u = 0; u < UPB; u++) {
+        const uint4 v = gb_ld_stream16(blk + (size_t)u * 512);
+        const float4 z0 = *(const float4 *)(zs + u * EPU);
+        if constexpr (EPU == 8) {
+          const float4 z1 = *(const float4 *)(zs + u * EPU + 4);
+          const float2 f0 = __half22float2(*(const __half2 *)&v.x), f1 = __half22float2(*(const __half2 *)&v.y);
+          const float2 f2 = __half22float2(*(const __half2 *)&v.z), f3 = __half22float2(*(const __half2 *)&v.w);
+          s0 = fmaf(f0.x, z0.x, fmaf(f0.y, z0.y, fmaf(f1.x, z0.z, fmaf(f1.y, z0.w, s0))));
+          s1 = fmaf(f2.x, z1.x, fmaf(f2.y, z1.y, fmaf(f3.x, z1.z, fmaf(f3.y, z1.w, s1))));
+        } else {
+          s0 = fmaf(__uint_as_float(v.x), z0.x, fmaf(__uint_as_float(v.y), z0.y, s0));
+          s1 = fmaf(__uint_as_float(v.z), z0.z, fmaf(__uint_as_float(v.w), z0.w, s1));
+        }
+      }
+      acc[g] += s0 + s1;
+    }
+  }
+  float *ps = fz + n;
+  ps[warp * 64 + lane] = acc[0];
+  ps[warp * 64 + 32 + lane] = acc[1];
+  __syncthreads();
+  if (warp == 0) {
+    float y0 = 0.f, y1 = 0.f;
+    for (int w2 = 0; w2 < 8; w2++) {
+      y0 += ps[w2 * 64 + lane];
+      y1 += ps[w2 * 64 + 32 + lane];
+    }
+    const double *rope_row = nullptr;
+    if constexpr (EPI == GB_EPI_QKV) {
+      const int pos = min(max(*a.e.pos, 0), a.e.max_len - 1);
+      rope_row = a.e.rope_cs + (size_t)pos * a.e.head_dim;
+    }
+    epilogue<EPI>(p, rbk, y0, y1, rope_row);
+  }
+}
+
+template <typename TW>
+KernelFnF pick_float(int epi) {
+  switch (epi) {
+    case GB_EPI_PLAIN: return gemv_float_kernel<TW, GB_EPI_PLAIN>;
+    case GB_EPI_QKV: return gemv_float_kernel<TW, GB_EPI_QKV>;
+    case GB_EPI_RESID: return gemv_float_kernel<TW, GB_EPI_RESID>;
+    case GB_EPI_SWIGLU: return gemv_float_kernel<TW, GB_EPI_SWIGLU>;
+    case GB_EPI_LOGITS: return gemv_float_kernel<TW, GB_EPI_LOGITS>;
+    case GB_EPI_PARTIAL: return gemv_float_kernel<TW, GB_EPI_PARTIAL>;
+  }
+  return nullptr;
+}
+
 // ---- repack raw ggml rows into the tiled layout (load time) ---------------
 __global__ void repack_kernel(int typ, const uint8_t *raw, int rows, int nsb, int ntiles,
                               uint8_t *out) {
@@ -868,8 +973,47 @@ int gb_gemv_scratch_floats(int ntiles, const GbGemvPlan &p) {
   return sms() * 8 * 8 * 2 * 64;
 }
 
+namespace {
+int gemv_float_launch(const GbGemvArgs &a, cudaStream_t st, bool pdl) {
+  Kp p;
+  p.a = a;
+  p.half = a.epi == GB_EPI_SWIGLU ? 1 : 0;
+  if (p.half && a.ntiles % 2) return gb_fail(GB_ERR_INVALID, "gpu: gemv: tiles not paired");
+  if (a.split_tile < a.ntiles && a.type_b != a.type_a)
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: unquantized and quantized rows in one matrix");
+  p.nrb = p.half ? a.ntiles / 2 : a.ntiles;
+  KernelFnF fn = a.type_a == GB_T_F16 ? pick_float<__half>(a.epi) : pick_float<float>(a.epi);
+  if (!fn) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: epilogue %d", a.epi);
+  const size_t smem = sizeof(float) * ((size_t)a.nsb * 256 + 8 * 64);
+  static KernelFnF opted[12];
+  static int nopted = 0;
+  bool seen = false;
+  for (int i = 0; i < nopted; i++) seen = seen || opted[i] == fn;
+  if (!seen) {
+    GB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin() - 4096),
+            "gpu: gemv: shared memory attribute");
+    if (nopted < 12) opted[nopted++] = fn;
+  }
+  if ((long long)smem > smem_optin() - 4096)
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: %d input columns exceed shared memory", a.nsb * 256);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.nrb);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  GB_CUDA(cudaLaunchKernelEx(&cfg, fn, p), "gpu: gemv launch (unquantized weights)");
+  return GB_OK;
+}
+}  // namespace
+
 int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st, bool pdl) {
   if (a.nsb <= 0 || a.ntiles <= 0) return gb_fail(GB_ERR_INVALID, "gpu: gemv: empty matrix");
+  if (gb_float_type(a.type_a)) return gemv_float_launch(a, st, pdl);
   Kp p;
   p.a = a;
   p.rb = 1;

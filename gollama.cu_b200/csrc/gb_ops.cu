@@ -294,7 +294,7 @@ __global__ void advance_pos_kernel(int32_t *pos, unsigned *epoch) {
 // per-32 sums of squares the first RMSNorm needs.
 __global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
                              int vocab, float *x, float *ssq, unsigned *err) {
-  __shared__ __align__(16) uint8_t blk[8][272];  // one super-block of one row (Q8_0: 272 B)
+  __shared__ __align__(16) uint8_t blk[8][1024];  // one super-block of one row (F32: 1024 B)
   gb_grid_dep_launch();
   gb_grid_dep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -124,6 +124,9 @@ void gen_block(int typ, uint64_t seed, uint32_t tensor, uint64_t block, float si
       put16(p, f16_from((float)(fabs(r.normal() * sigma) / 128.0)));
       r.bytes(p + 2, 32);
       break;
+    case GB_T_F16:  // one element per "block": N(0, sigma)
+      put16(p, f16_from((float)(r.normal() * sigma)));
+      break;
     case GB_T_Q4_K:
       put16(p, f16_from((float)fabs(r.normal() * sigma)));
       put16(p + 2, f16_from((float)fabs(r.normal() * sigma)));
@@ -168,6 +171,7 @@ float default_sigma(int typ) {
   switch (typ) {
     case GB_T_Q4_0: return 0.02f;
     case GB_T_Q8_0: return 0.02f;
+    case GB_T_F16: return 0.02f;
     case GB_T_Q4_K: return 0.01f;
     case GB_T_Q6_K: return 0.002f;
   }
@@ -189,10 +193,12 @@ std::vector<TensorSpec> model_tensors(const gb_synth_spec &s) {
     if (s.mix == 2) return (int)GB_T_Q4_K;
     if (s.mix == 3) return (int)GB_T_Q6_K;
     if (s.mix == 4) return (int)GB_T_Q8_0;
+    if (s.mix == 5) return (int)GB_T_F16;
     return six ? (int)GB_T_Q6_K : (int)GB_T_Q4_K;
   };
   auto sig = [&](int t) {
     if (t == GB_T_Q4_0 || t == GB_T_Q8_0) return 0.02f;
+    if (t == GB_T_F16) return 0.02f;
     if (t == GB_T_Q4_K) return 0.01f / 128.f;
     return 0.002f / 32.f;
   };

@@ -178,6 +178,23 @@ def test_linear_tiled_vs_oracle(gb, orc, cuda, typ, rows, cols):
     assert worst < 1e-3
 
 
+@pytest.mark.parametrize("rows,cols", [(64, 256), (300, 1024), (1000, 4096), (4096, 4096)])
+@pytest.mark.parametrize("typ", [F16, F32])
+def test_linear_unquantized_vs_oracle(gb, orc, cuda, typ, rows, cols):
+    # model.uploadLinear keeps F16 / F32 matrices (model/model.go:86-96); MatVecF16/F32
+    rng = np.random.default_rng(rows * 11 + cols + typ)
+    vals = rng.standard_normal(rows * cols) * 0.05
+    w = (vals.astype(np.float16) if typ == F16 else vals.astype(np.float32)).view(np.uint8)
+    x = rng.standard_normal(cols).astype(np.float32)
+    want = orc.matvec_q(typ, w, x, rows, cols)
+    lin = gb.Linear(typ, w, rows, cols)
+    dy = torch.zeros(rows, device="cuda")
+    for _ in range(2):
+        lin.matvec(dev(x), dy)
+    assert_close(f"Linear[{typ}] {rows}x{cols}", host(dy), want, 1e-4, 1e-4)
+    lin.close()
+
+
 @pytest.mark.parametrize("typ", [Q4_0, Q4_K, Q6_K])
 def test_linear_tiled_synthetic_recipe(gb, orc, cuda, typ):
     # the BASELINE GEMV-sweep block recipe, one of its shapes

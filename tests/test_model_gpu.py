@@ -19,6 +19,8 @@ MODELS = {
     "gqa8_hd128": dict(layers=2, dim=1024, ffn=512, heads=8, kv_heads=1, head_dim=128, vocab=500, ctx_len=96, mix=1, seed=16),
     # all Q8_0 (untied head)
     "q80_all": dict(layers=2, dim=512, ffn=768, heads=8, kv_heads=2, head_dim=64, vocab=700, ctx_len=96, mix=4, seed=17),
+    # all F16 matrices (model.uploadLinear's F16 case, MatVecF16)
+    "f16_all": dict(layers=2, dim=512, ffn=768, heads=8, kv_heads=2, head_dim=64, vocab=700, ctx_len=96, mix=5, seed=18),
 }
 
 
