@@ -18,8 +18,8 @@
 //   Q8_0: the 8 raw 34-byte blocks likewise: unit 0 = the eight binary16 d,
 //         units 1+2k, 2+2k = the 32 int8 quants of block k (17 units,
 //         sb-block 8704 bytes = 32*272).
-//   F16 / F32: the row's 256 elements in order, 8 or 4 per unit (32 or 64
-//         units, sb-block 16384 or 32768 bytes).
+//   F16 / BF16 / F32: the row's 256 elements in order, 8 or 4 per unit
+//         (32 or 64 units, sb-block 16384 or 32768 bytes).
 // The tiled buffer holds exactly the raw bytes (plus row padding), so a
 // decode step reads the algorithmic byte count.
 #pragma once
@@ -68,16 +68,21 @@ GB_HD int64_t gb_row_bytes(int t, int64_t n) {
   return bs ? n / bs * gb_type_size(t) : 0;
 }
 
-// Unquantized weight matrices (model.uploadLinear, model/model.go:86-96).
-GB_HD bool gb_float_type(int t) { return t == GB_T_F16 || t == GB_T_F32; }
+// Unquantized weight matrices (model.uploadLinear, model/model.go:86-96: F16
+// and F32; BF16 added, as the embedding accepts any known type).
+GB_HD bool gb_float_type(int t) { return t == GB_T_F16 || t == GB_T_BF16 || t == GB_T_F32; }
 GB_HD bool gb_tiled_type(int t) {
   return t == GB_T_Q4_0 || t == GB_T_Q8_0 || t == GB_T_Q4_K || t == GB_T_Q6_K || gb_float_type(t);
 }
 GB_HD int gb_tiled_units(int t) {
-  return t == GB_T_Q6_K ? 13 : t == GB_T_Q8_0 ? 17 : t == GB_T_F16 ? 32 : t == GB_T_F32 ? 64 : 9;
+  return t == GB_T_Q6_K ? 13 : t == GB_T_Q8_0 ? 17 : (t == GB_T_F16 || t == GB_T_BF16) ? 32 : t == GB_T_F32 ? 64 : 9;
 }
 GB_HD int gb_tiled_sb_bytes(int t) {
-  return t == GB_T_Q6_K ? 6720 : t == GB_T_Q8_0 ? 8704 : t == GB_T_F16 ? 16384 : t == GB_T_F32 ? 32768 : 4608;
+  return t == GB_T_Q6_K ? 6720
+         : t == GB_T_Q8_0 ? 8704
+         : (t == GB_T_F16 || t == GB_T_BF16) ? 16384
+         : t == GB_T_F32 ? 32768
+                          : 4608;
 }
 
 // Where raw byte `b` (0 <= b < 32*typesize/... of one super-block of a row)
@@ -99,5 +104,5 @@ GB_HD int gb_tiled_offset(int t, int lane, int b) {
 }
 // Raw bytes per super-block of one row (256 elements).
 GB_HD int gb_sb_raw_bytes(int t) {
-  return t == GB_T_Q6_K ? 210 : t == GB_T_Q8_0 ? 272 : t == GB_T_F16 ? 512 : t == GB_T_F32 ? 1024 : 144;
+  return t == GB_T_Q6_K ? 210 : t == GB_T_Q8_0 ? 272 : (t == GB_T_F16 || t == GB_T_BF16) ? 512 : t == GB_T_F32 ? 1024 : 144;
 }

@@ -755,6 +755,19 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
 // quantized path), warp w takes super-blocks w, w + 8, ... with lane = row
 // and several 16-byte streaming loads in flight, and the warps' sums are
 // added in warp order before the same fused epilogue.
+// Element tag for bfloat16 weights (16 bits, decoded by widening).
+struct Bf16 {
+  uint16_t bits;
+};
+template <typename T>
+struct TW_BF16 {
+  static constexpr bool value = false;
+};
+template <>
+struct TW_BF16<Bf16> {
+  static constexpr bool value = true;
+};
+
 template <typename TW, int EPI>
 __global__ void __launch_bounds__(256) gemv_float_kernel(const Kp p) {
   extern __shared__ __align__(16) float fz[];  // [nsb*256] input, then [8][64] partials
@@ -806,8 +819,18 @@ __global__ void __launch_bounds__(256) gemv_float_kernel(const Kp p) {
         const float4 z0 = *(const float4 *)(zs + u * EPU);
         if constexpr (EPU == 8) {
           const float4 z1 = *(const float4 *)(zs + u * EPU + 4);
-          const float2 f0 = __half22float2(*(const __half2 *)&v.x), f1 = __half22float2(*(const __half2 *)&v.y);
-          const float2 f2 = __half22float2(*(const __half2 *)&v.z), f3 = __half22float2(*(const __half2 *)&v.w);
+          float2 f0, f1, f2, f3;
+          if constexpr (sizeof(TW) == 2 && TW_BF16<TW>::value) {  // bf16: the high half of a float
+            f0 = make_float2(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u));
+            f1 = make_float2(__uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+            f2 = make_float2(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u));
+            f3 = make_float2(__uint_as_float(v.w << 16), __uint_as_float(v.w & 0xFFFF0000u));
+          } else {
+            f0 = __half22float2(*(const __half2 *)&v.x);
+            f1 = __half22float2(*(const __half2 *)&v.y);
+            f2 = __half22float2(*(const __half2 *)&v.z);
+            f3 = __half22float2(*(const __half2 *)&v.w);
+          }
           s0 = fmaf(f0.x, z0.x, fmaf(f0.y, z0.y, fmaf(f1.x, z0.z, fmaf(f1.y, z0.w, s0))));
           s1 = fmaf(f2.x, z1.x, fmaf(f2.y, z1.y, fmaf(f3.x, z1.z, fmaf(f3.y, z1.w, s1))));
         } else {
@@ -982,17 +1005,19 @@ int gemv_float_launch(const GbGemvArgs &a, cudaStream_t st, bool pdl) {
   if (a.split_tile < a.ntiles && a.type_b != a.type_a)
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: unquantized and quantized rows in one matrix");
   p.nrb = p.half ? a.ntiles / 2 : a.ntiles;
-  KernelFnF fn = a.type_a == GB_T_F16 ? pick_float<__half>(a.epi) : pick_float<float>(a.epi);
+  KernelFnF fn = a.type_a == GB_T_F16    ? pick_float<__half>(a.epi)
+                 : a.type_a == GB_T_BF16 ? pick_float<Bf16>(a.epi)
+                                         : pick_float<float>(a.epi);
   if (!fn) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: epilogue %d", a.epi);
   const size_t smem = sizeof(float) * ((size_t)a.nsb * 256 + 8 * 64);
-  static KernelFnF opted[12];
+  static KernelFnF opted[18];
   static int nopted = 0;
   bool seen = false;
   for (int i = 0; i < nopted; i++) seen = seen || opted[i] == fn;
   if (!seen) {
     GB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin() - 4096),
             "gpu: gemv: shared memory attribute");
-    if (nopted < 12) opted[nopted++] = fn;
+    if (nopted < 18) opted[nopted++] = fn;
   }
   if ((long long)smem > smem_optin() - 4096)
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: %d input columns exceed shared memory", a.nsb * 256);

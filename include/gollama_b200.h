@@ -122,7 +122,7 @@ int gb_gpu_argmax(gb_kernels *k, void *stream, const float *x, int n, int32_t *o
 typedef struct gb_linear gb_linear;
 /* uploadLinear, model/model.go:77: uploads a [rows][cols] matrix given as
  * raw ggml bytes on the host and repacks it on the device into 32-row
- * tiles. Supported: Q4_0, Q8_0, Q4_K, Q6_K, F16, F32 with cols a multiple of 256. */
+ * tiles. Supported: Q4_0, Q8_0, Q4_K, Q6_K, F16, BF16, F32 with cols a multiple of 256. */
 int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes, int rows,
                      int cols, gb_linear **out);
 /* (*Linear).MatVec, model/model.go:109 for batch 1: y[rows] = W x[cols]

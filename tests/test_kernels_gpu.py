@@ -9,7 +9,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-Q4_0, Q8_0, Q4_K, Q6_K, F32, F16 = 2, 8, 12, 14, 0, 1
+Q4_0, Q8_0, Q4_K, Q6_K, F32, F16, BF16 = 2, 8, 12, 14, 0, 1, 30
 
 
 def randf(rng, n, scale):
@@ -179,12 +179,16 @@ def test_linear_tiled_vs_oracle(gb, orc, cuda, typ, rows, cols):
 
 
 @pytest.mark.parametrize("rows,cols", [(64, 256), (300, 1024), (1000, 4096), (4096, 4096)])
-@pytest.mark.parametrize("typ", [F16, F32])
+@pytest.mark.parametrize("typ", [F16, BF16, F32])
 def test_linear_unquantized_vs_oracle(gb, orc, cuda, typ, rows, cols):
-    # model.uploadLinear keeps F16 / F32 matrices (model/model.go:86-96); MatVecF16/F32
+    # model.uploadLinear keeps F16 / F32 matrices (model/model.go:86-96); MatVecF16/F32.
+    # BF16 (added) is the top half of a float32.
     rng = np.random.default_rng(rows * 11 + cols + typ)
     vals = rng.standard_normal(rows * cols) * 0.05
-    w = (vals.astype(np.float16) if typ == F16 else vals.astype(np.float32)).view(np.uint8)
+    if typ == BF16:
+        w = (vals.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16).view(np.uint8)
+    else:
+        w = (vals.astype(np.float16) if typ == F16 else vals.astype(np.float32)).view(np.uint8)
     x = rng.standard_normal(cols).astype(np.float32)
     want = orc.matvec_q(typ, w, x, rows, cols)
     lin = gb.Linear(typ, w, rows, cols)
