@@ -140,7 +140,8 @@ size_t gb_attn_part_floats(int n_kv, int splits, int group, int head_dim);
 // ---- misc kernels (gb_ops.cu)
 // Embedding row of *token into x, with per-32 sums of squares (first RMSNorm).
 int gb_embed_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
-                    int vocab, float *x, float *ssq, unsigned *err, cudaStream_t st, bool pdl);
+                    int vocab, float *x, float *ssq, unsigned *err, int32_t *fed, const int32_t *pos, int max_len,
+                    cudaStream_t st, bool pdl);
 // x += y with per-32 sums of squares: the residual after a collective.
 int gb_resid_launch(float *x, const float *y, int n, float *ssq, cudaStream_t st, bool pdl);
 // Tensor parallel: wait for every rank's partial in peer slot `slot`, then
@@ -154,6 +155,16 @@ int gb_peer_argmax_launch(const GbPeer &p, int slot, int32_t *token, int32_t *hi
                           int max_len, unsigned *err, cudaStream_t st, bool pdl);
 // Advance the position (and the tensor-parallel step counter when non-null).
 int gb_advance_pos_launch(int32_t *pos, unsigned *epoch, cudaStream_t st);
+
+// gb_sample.cu: one token from logits[n]; parameters by value (p_host) or
+// from device memory (p_dev, for graph replays); the penalty window is
+// recent[n_recent] or, for the model, fed[pos-N+1..pos]; counter = *pos when
+// pos is given. Writes *out and, with gen, gen[*pos].
+typedef gb_sample_params GbSampleParams;
+constexpr int kSampleMaxVocab = GB_SAMPLE_MAX_VOCAB;
+int gb_sample_launch(const float *logits, int n, const GbSampleParams *p_host, const GbSampleParams *p_dev,
+                     const int32_t *recent, int n_recent, const int32_t *fed, const int32_t *pos, int max_len,
+                     unsigned long long counter, int32_t *out, int32_t *gen, unsigned *err, cudaStream_t st);
 
 // ---- GGUF (gb_gguf.cpp): reader restating gguf/gguf.go:62 Parse and
 // writer restating gguf/writer.go.

@@ -165,6 +165,10 @@ struct gb_model {
   float *act = nullptr;  // SwiGLU output [ffn_local]
   float *ssq = nullptr;  // per-32 sums of squares of x [dim/32] (RMSNorm input)
   int32_t *token = nullptr, *pos = nullptr, *gen = nullptr;
+  int32_t *fed = nullptr;             // token fed at each position [max_len]
+  GbSampleParams *sample_p = nullptr; // device copy of the sampler parameters
+  bool sampling = false;              // next/generate sample instead of argmax
+  cudaGraphExec_t graph_sample = nullptr;
   unsigned *err = nullptr;
   float *gemv_part = nullptr;
   unsigned *tile_counter = nullptr;
@@ -404,7 +408,7 @@ GbGemvArgs gemv_args(const Tiled &t, const float *x, const float *norm, float ep
   return a;
 }
 
-int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
+int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook, bool sample = false) {
   const gb_config &c = m->c;
   const bool pdl = true;
   const bool tp = c.tp_world > 1;
@@ -424,7 +428,7 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
     GB_CUDA(cudaEventRecord(hook->ev[hook->n++], st), "model: profile event");
   }
   rc = gb_embed_launch(m->embd_type, m->embd.w, m->embd_nsb, c.dim, m->token, c.vocab, m->x, m->ssq,
-                       m->err, st, pdl);
+                       m->err, m->fed, m->pos, c.max_len, st, pdl);
   if (rc || (rc = mark(K_OTHER))) return rc;
   for (int l = 0; l < c.layers; l++) {
     gb_model::Layer &L = m->layers[l];
@@ -523,34 +527,61 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook) {
                                          pdl)) ||
              (rc = mark(K_OTHER))))
     return rc;
+  // the sampler replaces the argmax token (and its history slot) of the head's epilogue
+  if (sample && ((rc = gb_sample_launch(m->logits, c.vocab, nullptr, m->sample_p, nullptr, 0, m->fed, m->pos,
+                                        c.max_len, 0, m->token, m->gen, m->err, st)) ||
+                 (rc = mark(K_OTHER))))
+    return rc;
   if ((rc = gb_advance_pos_launch(m->pos, tp ? (unsigned *)m->peer.epoch : nullptr, st)) || (rc = mark(K_OTHER)))
     return rc;
   m->launches = n;
   return GB_OK;
 }
 
-int capture(gb_model *m) {
+int capture(gb_model *m, bool sample = false) {
   cudaGraph_t g = nullptr;
   GB_CUDA(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal), "model: graph capture");
-  int rc = enqueue_step(m, m->st, nullptr);
+  const int launches = m->launches;
+  int rc = enqueue_step(m, m->st, nullptr, sample);
+  if (sample) m->launches = launches;  // the greedy step's count stays the model's figure
   cudaError_t e = cudaStreamEndCapture(m->st, &g);
   if (rc) {
     if (g) cudaGraphDestroy(g);
     return rc;
   }
   if (e != cudaSuccess) return gb_cuda_fail(e, "model: graph capture");
-  e = cudaGraphInstantiate(&m->graph, g, 0);
+  e = cudaGraphInstantiate(sample ? &m->graph_sample : &m->graph, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) return gb_cuda_fail(e, "model: graph instantiate");
   return GB_OK;
 }
 
+// One step with the model's token rule (argmax, or the sampler when set).
 int run_step(gb_model *m) {
+  if (m->sampling) {
+    if (m->graph_sample) {
+      GB_CUDA(cudaGraphLaunch(m->graph_sample, m->st), "model: graph launch");
+      return GB_OK;
+    }
+    const int launches = m->launches;
+    int rc = enqueue_step(m, m->st, nullptr, true);
+    m->launches = launches;
+    return rc;
+  }
   if (m->graph) {
     GB_CUDA(cudaGraphLaunch(m->graph, m->st), "model: graph launch");
     return GB_OK;
   }
   return enqueue_step(m, m->st, nullptr);
+}
+
+// forward() returns logits: the argmax step is enough (same logits).
+int run_logits_step(gb_model *m) {
+  const bool s = m->sampling;
+  m->sampling = false;
+  int rc = run_step(m);
+  m->sampling = s;
+  return rc;
 }
 
 int check_err(gb_model *m) {
@@ -584,6 +615,7 @@ int set_token_pos(gb_model *m, int32_t token, int pos) {
 void free_model(gb_model *m) {
   if (!m) return;
   if (m->graph) cudaGraphExecDestroy(m->graph);
+  if (m->graph_sample) cudaGraphExecDestroy(m->graph_sample);
   for (void *p : m->ipc_opened) cudaIpcCloseMemHandle(p);
   if (m->comm && nccl() && nccl()->commDestroy) nccl()->commDestroy(m->comm);
   for (void *p : m->allocs) cudaFree(p);
@@ -797,6 +829,8 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
       (rc = dalloc(m, &m->logits_full, (size_t)c.vocab, "model: work")) ||
       (rc = dalloc(m, &m->token, 4, "model: work")) || (rc = dalloc(m, &m->pos, 4, "model: work")) ||
       (rc = dalloc(m, &m->gen, (size_t)c.max_len, "model: work")) || (rc = dalloc(m, &m->err, 4, "model: work")) ||
+      (rc = dalloc(m, &m->fed, (size_t)c.max_len, "model: work")) ||
+      (rc = dalloc(m, &m->sample_p, 1, "model: work")) ||
       (rc = dalloc(m, &m->best, 1, "model: work")) || (rc = dalloc(m, &m->done, 1, "model: work")))
     return fail(rc);
   if ((rc = dalloc(m, &m->act, (size_t)m->ffn_local, "model: work")) ||
@@ -878,7 +912,7 @@ int gb_model_forward(gb_model *m, int32_t token, int pos, float *host_logits) {
   gb_clear_error();
   if (!m) return gb_fail(GB_ERR_INVALID, "model: null model");
   int rc = set_token_pos(m, token, pos);
-  if (rc || (rc = run_step(m))) return rc;
+  if (rc || (rc = run_logits_step(m))) return rc;
   const float *src = m->logits;
   if (m->c.tp_world > 1) {
     GB_NCCL(nccl()->allGather(m->logits, m->logits_full, (size_t)m->vocab_local, ncclFloat, m->comm, m->st),
@@ -917,6 +951,29 @@ int gb_model_generate(gb_model *m, int32_t token, int pos, int n, int32_t *out_t
     GB_CUDA(cudaMemcpyAsync(out_tokens, m->gen + pos, sizeof(int32_t) * (size_t)n, cudaMemcpyDeviceToHost, m->st),
             "model: tokens");
   return check_err(m);
+}
+
+int gb_model_set_sampler(gb_model *m, const gb_sample_params *p) {
+  gb_clear_error();
+  if (!m) return gb_fail(GB_ERR_INVALID, "model: null model");
+  if (!p) {
+    m->sampling = false;
+    return GB_OK;
+  }
+  if (m->c.tp_world > 1) return gb_fail(GB_ERR_UNSUPPORTED, "model: sampling under tensor parallelism");
+  if (m->c.vocab > kSampleMaxVocab) return gb_fail(GB_ERR_UNSUPPORTED, "model: vocabulary too large to sample");
+  if (p->top_p != p->top_p || p->temperature != p->temperature || p->repeat_penalty != p->repeat_penalty)
+    return gb_fail(GB_ERR_INVALID, "model: NaN sampler parameter");
+  // the graph reads the parameters from device memory: copy, then wait, so
+  // the host struct may go away
+  GB_CUDA(cudaMemcpyAsync(m->sample_p, p, sizeof *p, cudaMemcpyHostToDevice, m->st), "model: sampler");
+  GB_CUDA(cudaStreamSynchronize(m->st), "model: sampler");
+  if (m->o.use_graph && !m->graph_sample) {
+    int rc = capture(m, true);
+    if (rc) return rc;
+  }
+  m->sampling = true;
+  return GB_OK;
 }
 
 int gb_model_start(gb_model *m, int32_t token, int pos) {

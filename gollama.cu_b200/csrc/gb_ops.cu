@@ -293,7 +293,8 @@ __global__ void advance_pos_kernel(int32_t *pos, unsigned *epoch) {
 // device): row *token of the tiled token_embd, bit-exact, into x, with the
 // per-32 sums of squares the first RMSNorm needs.
 __global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
-                             int vocab, float *x, float *ssq, unsigned *err) {
+                             int vocab, float *x, float *ssq, unsigned *err, int32_t *fed, const int32_t *pos,
+                             int max_len) {
   __shared__ __align__(16) uint8_t blk[8][1024];  // one super-block of one row (F32: 1024 B)
   gb_grid_dep_launch();
   gb_grid_dep_wait();
@@ -301,6 +302,11 @@ __global__ void embed_kernel(int typ, const uint8_t *tiled, int nsb, int dim, co
   const int g = blockIdx.x * (blockDim.x >> 5) + warp;
   if (g >= dim / 32) return;
   int tok = *token;
+  if (fed && g == 0 && lane == 0) {
+    // the token fed at this position (the sampler's repetition window)
+    const int p = *pos;
+    if (p >= 0 && p < max_len) fed[p] = tok;
+  }
   if (tok < 0 || tok >= vocab) {
     if (g == 0 && lane == 0 && err) atomicOr(err, GB_DEVERR_TOKEN);
     tok = 0;
@@ -374,11 +380,13 @@ const char *type_name(int t) {
 // ---- internal launchers -----------------------------------------------------
 
 int gb_embed_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *token,
-                    int vocab, float *x, float *ssq, unsigned *err, cudaStream_t st, bool pdl) {
+                    int vocab, float *x, float *ssq, unsigned *err, int32_t *fed, const int32_t *pos, int max_len,
+                    cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];
   int groups = dim / 32;
   cudaLaunchConfig_t cfg = make_cfg(dim3((groups + 7) / 8), dim3(256), st, attr, pdl);
-  GB_CUDA(cudaLaunchKernelEx(&cfg, embed_kernel, typ, tiled, nsb, dim, token, vocab, x, ssq, err),
+  GB_CUDA(cudaLaunchKernelEx(&cfg, embed_kernel, typ, tiled, nsb, dim, token, vocab, x, ssq, err, fed, pos,
+                             max_len),
           "gpu: embed");
   return GB_OK;
 }
@@ -755,6 +763,16 @@ int gb_gpu_argmax(gb_kernels *k, void *stream, const float *x, int n, int32_t *o
   argmax_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, out);
   GB_CUDA(cudaGetLastError(), "gpu: argmax");
   return GB_OK;
+}
+
+int gb_gpu_sample(gb_kernels *k, void *stream, const float *logits, int n, const gb_sample_params *p,
+                  const int32_t *recent, int n_recent, uint64_t counter, int32_t *out) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (!logits || !p || !out || n <= 0 || n_recent < 0 || (n_recent > 0 && !recent))
+    return gb_fail(GB_ERR_INVALID, "gpu: sample: bad arguments");
+  return gb_sample_launch(logits, n, p, nullptr, recent, n_recent, nullptr, nullptr, 0, counter, out, nullptr,
+                          nullptr, (cudaStream_t)stream);
 }
 
 // model.Argmax, model/model.go:376.

@@ -60,6 +60,18 @@ class SynthSpec(C.Structure):
                 ("seed", C.c_uint64)]
 
 
+class SampleParams(C.Structure):
+    """gb_sample_params: the on-device sampler's rule (include/gollama_b200.h)."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float),
+                ("repeat_penalty", C.c_float), ("repeat_last_n", C.c_int), ("reserved", C.c_int),
+                ("seed", C.c_uint64)]
+
+
+def sample_params(temperature=0.8, top_k=40, top_p=0.95, repeat_penalty=1.0, repeat_last_n=64,
+                  seed=0) -> SampleParams:
+    return SampleParams(temperature, top_k, top_p, repeat_penalty, repeat_last_n, 0, seed)
+
+
 _lib = None
 P, I, U64, F, D, S = C.c_void_p, C.c_int, C.c_uint64, C.c_float, C.c_double, C.c_size_t
 _SIGS = {
@@ -73,7 +85,8 @@ _SIGS = {
     "gb_gpu_matvec_f16": (I, [P, P, P, P, P, I, I, I]), "gb_gpu_matvec_f32": (I, [P, P, P, P, P, I, I, I]),
     "gb_gpu_matvec_q": (I, [P, P, I, P, P, P, I, I, I]), "gb_gpu_ones": (I, [I, C.POINTER(P)]),
     "gb_free": (I, [P]), "gb_gpu_dequant_rows": (I, [P, P, I, P, I, I, I, I, P]),
-    "gb_gpu_argmax": (I, [P, P, P, I, P]),
+    "gb_gpu_argmax": (I, [P, P, P, I, P]), "gb_gpu_sample": (I, [P, P, P, I, P, P, I, U64, P]),
+    "gb_model_set_sampler": (I, [P, P]),
     "gb_linear_upload": (I, [I, I, P, S, I, I, C.POINTER(P)]), "gb_linear_matvec": (I, [P, P, P, P]),
     "gb_linear_info": (I, [P, C.POINTER(I), C.POINTER(I), C.POINTER(I), C.POINTER(S)]),
     "gb_linear_free": (I, [P]),
@@ -218,6 +231,10 @@ class Kernels:
     def argmax(self, x, n, out, stream=None):
         _check(lib().gb_gpu_argmax(self.h, _stream(stream), _ptr(x), n, _ptr(out)))
 
+    def sample(self, logits, n, params: SampleParams, recent, n_recent, counter, out, stream=None):
+        _check(lib().gb_gpu_sample(self.h, _stream(stream), _ptr(logits), n, C.byref(params),
+                                   _ptr(recent) if n_recent else None, n_recent, counter, _ptr(out)))
+
 
 class Linear:
     """model.Linear in the tiled layout: uploadLinear (model/model.go:77) + MatVec (:109)."""
@@ -293,6 +310,10 @@ class Model:
         out = np.empty(max(n, 1), dtype=np.int32)
         _check(lib().gb_model_generate(self.h, token, pos, n, out.ctypes.data))
         return out[:n]
+
+    def set_sampler(self, params: SampleParams | None) -> None:
+        """Token rule of next/generate/decode_async: None = greedy argmax."""
+        _check(lib().gb_model_set_sampler(self.h, C.byref(params) if params is not None else None))
 
     def start(self, token: int, pos: int) -> None:
         _check(lib().gb_model_start(self.h, token, pos))

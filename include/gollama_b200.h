@@ -118,6 +118,39 @@ int gb_gpu_dequant_rows(gb_kernels *k, void *stream, int typ, const uint8_t *w, 
  * with model.Argmax's tie rule (model/model.go:376: first maximum wins). */
 int gb_gpu_argmax(gb_kernels *k, void *stream, const float *x, int n, int32_t *out);
 
+/* ---- sampling (added; the reference's roadmap item, ROADMAP.md:42-45) ----
+ * One token from a logits vector on the device:
+ *  1. the logits of every distinct id among the last repeat_last_n context
+ *     tokens are penalised: v <= 0 ? v * repeat_penalty : v / repeat_penalty;
+ *  2. temperature <= 0 or top_k == 1: the first maximum (model.Argmax's rule);
+ *  3. otherwise s = v / temperature; top_k <= 0 with top_p >= 1 samples the
+ *     whole vocabulary in index order; else the candidates are the
+ *     min(top_k > 0 ? top_k : 1024, 1024) largest, sorted (value
+ *     descending, index ascending), cut to the shortest prefix whose
+ *     probability reaches top_p;
+ *  4. the draw u in [0,1) is splitmix64 of (seed, counter), 24 bits.
+ * The exact float32 operations (and the association of every sum) are
+ * fixed, so a host restatement picks the same token bit for bit. */
+typedef struct {
+  float temperature;     /* <= 0: greedy */
+  int top_k;             /* <= 0: no limit */
+  float top_p;           /* >= 1: no nucleus cut */
+  float repeat_penalty;  /* 1: none */
+  int repeat_last_n;     /* context tokens the penalty looks back over (<= 0: none) */
+  int reserved;          /* 0 */
+  uint64_t seed;
+} gb_sample_params;
+
+/* Largest vocabulary the sampler accepts. */
+#define GB_SAMPLE_MAX_VOCAB (1 << 20)
+
+/* Sample one token from logits[n] (device) into *out (device int32).
+ * recent[n_recent] (device, may be NULL when n_recent == 0) holds the context
+ * ids, oldest first; the penalty looks at the last repeat_last_n of them.
+ * counter selects the draw (use the position). */
+int gb_gpu_sample(gb_kernels *k, void *stream, const float *logits, int n, const gb_sample_params *p,
+                  const int32_t *recent, int n_recent, uint64_t counter, int32_t *out);
+
 /* ---- model.Linear with the B200 tiled layout ----------------------------- */
 typedef struct gb_linear gb_linear;
 /* uploadLinear, model/model.go:77: uploads a [rows][cols] matrix given as
@@ -181,6 +214,12 @@ int gb_model_generate(gb_model *m, int32_t token, int pos, int n, int32_t *out_t
 int gb_model_start(gb_model *m, int32_t token, int pos);
 int gb_model_decode_async(gb_model *m, int n);
 int gb_model_read_tokens(gb_model *m, int pos0, int n, int32_t *out_tokens);
+/* Added: the token rule of gb_model_next / generate / decode_async. NULL
+ * (the default) is greedy model.Argmax; otherwise the sampler above with
+ * counter = the position of the step and the penalty window = the tokens fed
+ * at the last repeat_last_n positions (prompt included). One GPU only
+ * (GB_ERR_UNSUPPORTED under tensor parallelism). */
+int gb_model_set_sampler(gb_model *m, const gb_sample_params *p);
 /* Added: fill KV positions [0, n_pos) of every layer with the seeded N(0,1)
  * values of gb_synth_kv_normal (rounded to the cache type). */
 int gb_model_fill_kv_normal(gb_model *m, uint64_t seed, int n_pos);

@@ -830,3 +830,151 @@ done:
   free(x); free(xn); free(q); free(k); free(v); free(attn); free(o); free(gate); free(up);
   return rc;
 }
+
+/* ---- sampler (the B200 build's rule, restated; see oracle.h) -------------- */
+
+enum { SMP_T = 1024, SMP_MAXK = 1024 };
+
+float or_exp_nonpos(float x) {
+  if (!(x >= -87.f)) return 0.f;
+  float n = rintf(x * 1.44269502f);
+  float r = fmaf(-n, 0.693359375f, x);
+  r = fmaf(-n, -2.12194440e-4f, r);
+  float p = 1.98412698e-4f;
+  p = fmaf(p, r, 1.38888889e-3f);
+  p = fmaf(p, r, 8.33333333e-3f);
+  p = fmaf(p, r, 4.16666667e-2f);
+  p = fmaf(p, r, 1.66666667e-1f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.f);
+  p = fmaf(p, r, 1.f);
+  uint32_t b = (uint32_t)((int)n + 127) << 23;
+  float s;
+  memcpy(&s, &b, 4);
+  return p * s;
+}
+
+float or_uniform24(uint64_t seed, uint64_t counter) {
+  uint64_t z = seed + (counter + 1ull) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(uint32_t)(z >> 40) * (1.f / 16777216.f);
+}
+
+static uint32_t smp_okey(float f) {
+  if (f != f) return 0u;
+  uint32_t b;
+  memcpy(&b, &f, 4);
+  if ((b << 1) == 0u) b = 0u;
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+static float smp_okey_value(uint32_t k) {
+  uint32_t b = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+  float f;
+  memcpy(&f, &b, 4);
+  return f;
+}
+
+static void smp_scan(float *a) { /* Hillis-Steele, a[i] = a[i-d] + a[i] */
+  static __thread float nb[SMP_T];
+  for (int d = 1; d < SMP_T; d <<= 1) {
+    for (int i = 0; i < SMP_T; i++) nb[i] = i >= d ? a[i - d] + a[i] : a[i];
+    memcpy(a, nb, sizeof nb);
+  }
+}
+
+static int smp_desc(const void *x, const void *y) {
+  uint64_t a = *(const uint64_t *)x, b = *(const uint64_t *)y;
+  return a < b ? 1 : a > b ? -1 : 0;
+}
+
+int32_t or_sample(const float *logits, int n, const or_sample_params *p, const int32_t *recent,
+                  int n_recent, uint64_t counter) {
+  if (n <= 0) return 0;
+  uint8_t *pen = NULL;
+  if (p->repeat_penalty != 1.f && p->repeat_last_n > 0) {
+    pen = calloc((size_t)n, 1);
+    int lo = n_recent - p->repeat_last_n;
+    for (int q = lo < 0 ? 0 : lo; q < n_recent; q++)
+      if (recent[q] >= 0 && recent[q] < n) pen[recent[q]] = 1;
+  }
+  const int greedy = !(p->temperature > 0.f) || p->top_k == 1;
+  const float t = greedy ? 0.f : p->temperature, rp = p->repeat_penalty;
+  float *s = malloc(sizeof(float) * (size_t)n);
+  for (int i = 0; i < n; i++) {
+    float v = logits[i];
+    if (pen && pen[i]) v = v <= 0.f ? v * rp : v / rp;
+    if (t > 0.f) v = v / t;
+    s[i] = v;
+  }
+  free(pen);
+  uint64_t best = 0;
+  for (int i = 0; i < n; i++) {
+    uint64_t k = ((uint64_t)smp_okey(s[i]) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+    if (k > best) best = k;
+  }
+  const int arg = (int)(0xFFFFFFFFu - (uint32_t)best);
+  const float mx = smp_okey_value((uint32_t)(best >> 32));
+  int pick = arg;
+  const float u = or_uniform24(p->seed, counter);
+  if (greedy) {
+  } else if (p->top_k <= 0 && !(p->top_p < 1.f)) {
+    const int C = (n + SMP_T - 1) / SMP_T;
+    float cum[SMP_T];
+    for (int th = 0; th < SMP_T; th++) {
+      int c0 = th * C < n ? th * C : n, c1 = c0 + C < n ? c0 + C : n;
+      float local = 0.f;
+      for (int i = c0; i < c1; i++) local = local + or_exp_nonpos(s[i] - mx);
+      cum[th] = local;
+    }
+    smp_scan(cum);
+    const float target = u * cum[SMP_T - 1];
+    for (int th = 0; th < SMP_T; th++) {
+      int c0 = th * C < n ? th * C : n, c1 = c0 + C < n ? c0 + C : n, hit = -1;
+      float acc = th ? cum[th - 1] : 0.f;
+      for (int i = c0; i < c1; i++) {
+        acc = acc + or_exp_nonpos(s[i] - mx);
+        if (acc > target) {
+          hit = i;
+          break;
+        }
+      }
+      if (hit >= 0) {
+        pick = hit;
+        break;
+      }
+    }
+  } else {
+    int K = (p->top_k <= 0 || p->top_k > SMP_MAXK) ? SMP_MAXK : p->top_k;
+    if (K > n) K = n;
+    uint64_t *keys = malloc(sizeof(uint64_t) * (size_t)n);
+    for (int i = 0; i < n; i++) keys[i] = ((uint64_t)smp_okey(s[i]) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+    qsort(keys, (size_t)n, sizeof(uint64_t), smp_desc);
+    float cum[SMP_T];
+    const float v0 = smp_okey_value((uint32_t)(keys[0] >> 32));
+    for (int i = 0; i < SMP_T; i++) cum[i] = i < K ? or_exp_nonpos(smp_okey_value((uint32_t)(keys[i] >> 32)) - v0) : 0.f;
+    smp_scan(cum);
+    int c = K - 1;
+    if (p->top_p < 1.f) {
+      const float thr = p->top_p * cum[SMP_T - 1];
+      for (int i = 0; i < SMP_T; i++)
+        if (cum[i] >= thr) {
+          c = i;
+          break;
+        }
+      if (c > K - 1) c = K - 1;
+    }
+    const float target = u * cum[c];
+    int slot = 0;
+    for (int i = 0; i <= c; i++)
+      if (cum[i] > target) {
+        slot = i;
+        break;
+      }
+    pick = (int)(0xFFFFFFFFu - (uint32_t)keys[slot]);
+    free(keys);
+  }
+  free(s);
+  return pick;
+}

@@ -114,6 +114,31 @@ int or_model_set_kv(or_model *m, int layer, int pos0, int n, const float *k, con
 const float *or_model_kcache(const or_model *m, int layer);
 const float *or_model_vcache(const or_model *m, int layer);
 
+/* ---- sampler ---------------------------------------------------------------
+ * The reference has no sampler (it picks with model.Argmax; sampling is its
+ * roadmap item ROADMAP.md:42-45), so this restates the B200 build's own
+ * sampling rule (temperature, top-k, top-p, repetition penalty, seeded
+ * draw) operation for operation: float32 operations rounded one at a time,
+ * fmaf where the rule fuses, and every sum in the rule's fixed association.
+ * It is the checker of the device sampler, token for token. */
+typedef struct {
+  float temperature;
+  int top_k;
+  float top_p;
+  float repeat_penalty;
+  int repeat_last_n;
+  int reserved;
+  uint64_t seed;
+} or_sample_params;
+
+/* e^x for x <= 0 by the rule's own method (0 below -87 and for NaN). */
+float or_exp_nonpos(float x);
+/* The draw in [0, 1): splitmix64 of (seed, counter), 24 bits. */
+float or_uniform24(uint64_t seed, uint64_t counter);
+/* One token from logits[n]; recent[n_recent] = context ids, oldest first. */
+int32_t or_sample(const float *logits, int n, const or_sample_params *p, const int32_t *recent,
+                  int n_recent, uint64_t counter);
+
 #ifdef __cplusplus
 }
 #endif

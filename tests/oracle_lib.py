@@ -33,7 +33,15 @@ _SIGS = {
     "or_model_open": (P, [P, C.c_size_t, I, I, C.c_char_p, I]), "or_model_free": (None, [P]),
     "or_model_forward": (I, [P, C.c_int32, I, P, I]), "or_model_set_kv": (I, [P, I, I, I, P, P]),
     "or_model_kcache": (P, [P, I]), "or_model_vcache": (P, [P, I]),
+    "or_exp_nonpos": (F, [F]), "or_uniform24": (F, [C.c_uint64, C.c_uint64]),
+    "or_sample": (C.c_int32, [P, I, P, P, I, C.c_uint64]),
 }
+
+
+class SampleParams(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float),
+                ("repeat_penalty", C.c_float), ("repeat_last_n", C.c_int), ("reserved", C.c_int),
+                ("seed", C.c_uint64)]
 
 _lib = None
 
@@ -144,6 +152,23 @@ def attn_decode(q, kc, vc, kv_len, n_heads, n_kv, head_dim, scale):
 def argmax(x) -> int:
     x = np.ascontiguousarray(x, np.float32)
     return int(lib().or_argmax(_p(x), x.size))
+
+
+def sample(logits, temperature=0.8, top_k=40, top_p=0.95, repeat_penalty=1.0, repeat_last_n=64, seed=0,
+           recent=(), counter=0) -> int:
+    """The sampler's rule on the host (the checker of gb_gpu_sample)."""
+    x = np.ascontiguousarray(logits, np.float32)
+    r = np.ascontiguousarray(np.asarray(recent, np.int32))
+    prm = SampleParams(temperature, top_k, top_p, repeat_penalty, repeat_last_n, 0, seed)
+    return int(lib().or_sample(_p(x), x.size, C.byref(prm), _p(r) if r.size else None, r.size, counter))
+
+
+def exp_nonpos(x: float) -> float:
+    return float(lib().or_exp_nonpos(x))
+
+
+def uniform24(seed: int, counter: int) -> float:
+    return float(lib().or_uniform24(seed, counter))
 
 
 class Gguf:
