@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>  // CUtensorMap (the encoder is reached through cudaGetDriverEntryPoint)
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdint.h>
@@ -155,6 +156,35 @@ int gb_peer_argmax_launch(const GbPeer &p, int slot, int32_t *token, int32_t *hi
                           int max_len, unsigned *err, cudaStream_t st, bool pdl);
 // Advance the position (and the tensor-parallel step counter when non-null).
 int gb_advance_pos_launch(int32_t *pos, unsigned *epoch, cudaStream_t st);
+
+// gb_prefill.cu: the batched prefill kernels. The GEMM multiplies T token
+// rows of a binary16 activation (TMA map tmap_a over [T][nsb*256]) by a
+// tiled weight matrix on the tensor cores: PLAIN y[T][ldy] = A W^T, RESID
+// y += A W^T, SWIGLU act[T][ld_act] = silu(A Wg^T) * (A Wu^T) over gate/up
+// pairs (rows and ntiles then count one half).
+struct GbTcGemm {
+  const uint8_t *w = nullptr;
+  int type_a = 0, type_b = 0, split_tile = 1 << 30;
+  int rows = 0, ntiles = 0, nsb = 0;
+  int epi = GB_EPI_PLAIN;
+  int T = 0;
+  float *y = nullptr;
+  int ldy = 0;
+  __half *act = nullptr;
+  int ld_act = 0;
+  unsigned *err = nullptr;
+  CUtensorMap tmap_a;
+};
+int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map);
+int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st);
+int gb_embed_rows_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *tokens, int T, int vocab,
+                         float *x, int32_t *fed, int pos0, int max_len, unsigned *err, cudaStream_t st);
+int gb_rmsnorm_rows_f16_launch(const float *x, const float *w, int rows, int n, float eps, __half *out,
+                               cudaStream_t st);
+int gb_rope_kv_launch(const float *qkv, int T, int q_rows, int kv_rows, int hd, const double *rope_cs, int pos0,
+                      int max_len, int kv_f16, float *q_out, void *kcache, void *vcache, cudaStream_t st);
+int gb_attn_prefill_launch(const float *q, int T, int pos0, int n_heads, int n_kv, int hd, const void *kcache,
+                           const void *vcache, int kv_f16, int max_len, __half *out, cudaStream_t st);
 
 // gb_sample.cu: one token from logits[n]; parameters by value (p_host) or
 // from device memory (p_dev, for graph replays); the penalty window is

@@ -169,6 +169,11 @@ struct gb_model {
   GbSampleParams *sample_p = nullptr; // device copy of the sampler parameters
   bool sampling = false;              // next/generate sample instead of argmax
   cudaGraphExec_t graph_sample = nullptr;
+  // batched prefill workspace (allocated on first use): kPrefillChunk token rows
+  float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr;
+  __half *pf_a16 = nullptr, *pf_act16 = nullptr;
+  int32_t *pf_tokens = nullptr;
+  CUtensorMap pf_map_dim, pf_map_q, pf_map_ffn;
   unsigned *err = nullptr;
   float *gemv_part = nullptr;
   unsigned *tile_counter = nullptr;
@@ -872,6 +877,91 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
 
 }  // namespace
 
+namespace {
+
+constexpr int kPrefillChunk = 512;  // token rows per batched pass (4 M-tiles of the GEMM)
+
+int prefill_workspace(gb_model *m) {
+  if (m->pf_x) return GB_OK;
+  const gb_config &c = m->c;
+  const int Tc = kPrefillChunk, qkv = m->q_local + 2 * m->kv_local;
+  const size_t a16 = (size_t)Tc * std::max(c.dim, m->q_local);
+  int rc;
+  if ((rc = dalloc(m, &m->pf_x, (size_t)Tc * c.dim, "model: prefill workspace")) ||
+      (rc = dalloc(m, &m->pf_qkv, (size_t)Tc * qkv, "model: prefill workspace")) ||
+      (rc = dalloc(m, &m->pf_q, (size_t)Tc * m->q_local, "model: prefill workspace")) ||
+      (rc = dalloc(m, &m->pf_a16, a16, "model: prefill workspace")) ||
+      (rc = dalloc(m, &m->pf_act16, (size_t)Tc * m->ffn_local, "model: prefill workspace")) ||
+      (rc = dalloc(m, &m->pf_tokens, (size_t)Tc, "model: prefill workspace")))
+    return rc;
+  if ((rc = gb_tmap_f16_rows(m->pf_a16, Tc, c.dim, &m->pf_map_dim)) ||
+      (rc = gb_tmap_f16_rows(m->pf_a16, Tc, m->q_local, &m->pf_map_q)) ||
+      (rc = gb_tmap_f16_rows(m->pf_act16, Tc, m->ffn_local, &m->pf_map_ffn)))
+    return rc;
+  return GB_OK;
+}
+
+GbTcGemm tc_args(const Tiled &t, int epi, int T, const CUtensorMap &map, gb_model *m) {
+  GbTcGemm g;
+  g.w = t.w;
+  g.type_a = t.type_a;
+  g.type_b = t.type_b;
+  g.split_tile = t.split_tile;
+  g.rows = t.rows;
+  g.ntiles = t.ntiles;
+  g.nsb = t.nsb;
+  g.epi = epi;
+  g.T = T;
+  g.err = m->err;
+  g.tmap_a = map;
+  return g;
+}
+
+// Tokens [0, T) of one chunk at positions p0..: every layer's K/V; the
+// residual stream of the last layer is not needed (the next step reads only
+// the cache), so that layer stops after its K/V.
+int prefill_chunk(gb_model *m, int T, int p0) {
+  const gb_config &c = m->c;
+  cudaStream_t st = m->st;
+  const int hd = c.head_dim, qkv = m->q_local + 2 * m->kv_local;
+  int rc = gb_embed_rows_launch(m->embd_type, m->embd.w, m->embd_nsb, c.dim, m->pf_tokens, T, c.vocab, m->pf_x,
+                                m->fed, p0, c.max_len, m->err, st);
+  if (rc) return rc;
+  for (int l = 0; l < c.layers; l++) {
+    gb_model::Layer &L = m->layers[(size_t)l];
+    if ((rc = gb_rmsnorm_rows_f16_launch(m->pf_x, L.attn_norm, T, c.dim, c.eps, m->pf_a16, st))) return rc;
+    GbTcGemm g = tc_args(L.qkv, GB_EPI_PLAIN, T, m->pf_map_dim, m);
+    g.y = m->pf_qkv;
+    g.ldy = qkv;
+    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+    if ((rc = gb_rope_kv_launch(m->pf_qkv, T, m->q_local, m->kv_local, hd, m->rope_cs, p0, c.max_len, c.kv_f16,
+                                m->pf_q, L.kc, L.vc, st)))
+      return rc;
+    if (l == c.layers - 1) break;
+    if ((rc = gb_attn_prefill_launch(m->pf_q, T, p0, m->q_local / hd, m->kv_local / hd, hd, L.kc, L.vc, c.kv_f16,
+                                     c.max_len, m->pf_a16, st)))
+      return rc;
+    g = tc_args(L.wo, GB_EPI_RESID, T, m->pf_map_q, m);
+    g.y = m->pf_x;
+    g.ldy = c.dim;
+    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+    if ((rc = gb_rmsnorm_rows_f16_launch(m->pf_x, L.ffn_norm, T, c.dim, c.eps, m->pf_a16, st))) return rc;
+    g = tc_args(L.gu, GB_EPI_SWIGLU, T, m->pf_map_dim, m);
+    g.rows = m->ffn_local;  // one half of the gate/up pairs
+    g.ntiles = L.gu.ntiles / 2;
+    g.act = m->pf_act16;
+    g.ld_act = m->ffn_local;
+    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+    g = tc_args(L.down, GB_EPI_RESID, T, m->pf_map_ffn, m);
+    g.y = m->pf_x;
+    g.ldy = c.dim;
+    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+  }
+  return GB_OK;
+}
+
+}  // namespace
+
 // ---- C ABI: model -------------------------------------------------------------
 extern "C" {
 
@@ -951,6 +1041,50 @@ int gb_model_generate(gb_model *m, int32_t token, int pos, int n, int32_t *out_t
     GB_CUDA(cudaMemcpyAsync(out_tokens, m->gen + pos, sizeof(int32_t) * (size_t)n, cudaMemcpyDeviceToHost, m->st),
             "model: tokens");
   return check_err(m);
+}
+
+
+int gb_model_prefill(gb_model *m, const int32_t *tokens, int n, int pos0, float *host_logits) {
+  gb_clear_error();
+  if (!m || !tokens || n <= 0) return gb_fail(GB_ERR_INVALID, "model: bad prefill arguments");
+  if (pos0 < 0 || pos0 + n > m->c.max_len)
+    return gb_fail(GB_ERR_INVALID, "model: %d tokens from position %d exceed the %d-token cache", n, pos0,
+                   m->c.max_len);
+  for (int i = 0; i < n; i++)
+    if (tokens[i] < 0 || tokens[i] >= m->c.vocab)
+      return gb_fail(GB_ERR_INVALID, "model: token %d outside the vocabulary", tokens[i]);
+  if (m->c.tp_world > 1) return gb_fail(GB_ERR_UNSUPPORTED, "model: batched prefill under tensor parallelism");
+  int rc;
+  if (n > 1 && (rc = prefill_workspace(m))) return rc;
+  for (int c0 = 0; c0 < n - 1; c0 += kPrefillChunk) {
+    const int T = std::min(kPrefillChunk, n - 1 - c0);
+    GB_CUDA(cudaMemcpyAsync(m->pf_tokens, tokens + c0, sizeof(int32_t) * (size_t)T, cudaMemcpyHostToDevice, m->st),
+            "model: prefill tokens");
+    if ((rc = prefill_chunk(m, T, pos0 + c0))) return rc;
+    GB_CUDA(cudaStreamSynchronize(m->st), "model: prefill");  // the next chunk's tokens reuse the buffer
+  }
+  // the last token through the decode step: its logits, and its own K/V
+  return gb_model_forward(m, tokens[n - 1], pos0 + n - 1, host_logits);
+}
+
+int gb_linear_matmul_f16(gb_linear *l, void *stream, const uint16_t *x, int T, float *y) {
+  gb_clear_error();
+  if (!l || !x || !y || T < 0) return gb_fail(GB_ERR_INVALID, "model: linear: bad matmul arguments");
+  if ((uintptr_t)x % 16 || (uintptr_t)y % 16) return gb_fail(GB_ERR_INVALID, "model: linear: x and y must be 16-byte aligned");
+  if (T == 0) return GB_OK;
+  GbTcGemm g;
+  g.w = l->t.w;
+  g.type_a = g.type_b = l->t.type_a;
+  g.rows = l->t.rows;
+  g.ntiles = l->t.ntiles;
+  g.nsb = l->t.nsb;
+  g.epi = GB_EPI_PLAIN;
+  g.T = T;
+  g.y = y;
+  g.ldy = l->t.rows;
+  int rc = gb_tmap_f16_rows(x, T, l->t.cols, &g.tmap_a);
+  if (rc) return rc;
+  return gb_tc_gemm_launch(g, (cudaStream_t)stream);
 }
 
 int gb_model_set_sampler(gb_model *m, const gb_sample_params *p) {

@@ -86,7 +86,8 @@ _SIGS = {
     "gb_gpu_matvec_q": (I, [P, P, I, P, P, P, I, I, I]), "gb_gpu_ones": (I, [I, C.POINTER(P)]),
     "gb_free": (I, [P]), "gb_gpu_dequant_rows": (I, [P, P, I, P, I, I, I, I, P]),
     "gb_gpu_argmax": (I, [P, P, P, I, P]), "gb_gpu_sample": (I, [P, P, P, I, P, P, I, U64, P]),
-    "gb_model_set_sampler": (I, [P, P]),
+    "gb_model_set_sampler": (I, [P, P]), "gb_model_prefill": (I, [P, P, I, I, P]),
+    "gb_linear_matmul_f16": (I, [P, P, P, I, P]),
     "gb_linear_upload": (I, [I, I, P, S, I, I, C.POINTER(P)]), "gb_linear_matvec": (I, [P, P, P, P]),
     "gb_linear_info": (I, [P, C.POINTER(I), C.POINTER(I), C.POINTER(I), C.POINTER(S)]),
     "gb_linear_free": (I, [P]),
@@ -248,6 +249,10 @@ class Linear:
     def matvec(self, x, y, stream=None):
         _check(lib().gb_linear_matvec(self.h, _stream(stream), _ptr(x), _ptr(y)))
 
+    def matmul_f16(self, x16, T: int, y, stream=None):
+        """y[T][rows] = x16[T][cols] W^T on the tensor cores (x16 binary16, y float32)."""
+        _check(lib().gb_linear_matmul_f16(self.h, _stream(stream), _ptr(x16), T, _ptr(y)))
+
     def weight_bytes(self) -> int:
         s = S()
         _check(lib().gb_linear_info(self.h, None, None, None, C.byref(s)))
@@ -310,6 +315,14 @@ class Model:
         out = np.empty(max(n, 1), dtype=np.int32)
         _check(lib().gb_model_generate(self.h, token, pos, n, out.ctypes.data))
         return out[:n]
+
+    def prefill(self, tokens, pos0: int = 0, out: np.ndarray | None = None) -> np.ndarray:
+        """Feed tokens at pos0.. (batched); the logits of the last one."""
+        t = np.ascontiguousarray(np.asarray(tokens, np.int32))
+        if out is None:
+            out = self._logits
+        _check(lib().gb_model_prefill(self.h, t.ctypes.data, t.size, pos0, out.ctypes.data))
+        return out
 
     def set_sampler(self, params: SampleParams | None) -> None:
         """Token rule of next/generate/decode_async: None = greedy argmax."""

@@ -161,6 +161,13 @@ int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes,
 /* (*Linear).MatVec, model/model.go:109 for batch 1: y[rows] = W x[cols]
  * (x and y device pointers). */
 int gb_linear_matvec(gb_linear *l, void *stream, const float *x, float *y);
+/* Added: the prefill GEMM on the tensor cores (tcgen05), the batched
+ * MatVecQ of the reference's roadmap (ROADMAP.md:99-101): y[T][rows] =
+ * x[T][cols] W^T with x binary16 on the device (row stride cols, 16-byte
+ * aligned) and y float32 (row stride rows). W's elements are the
+ * reference's float32 element values rounded to binary16; products
+ * accumulate in float32. */
+int gb_linear_matmul_f16(gb_linear *l, void *stream, const uint16_t *x, int T, float *y);
 /* Bytes of the tiled weight buffer and the type's algorithmic bytes. */
 int gb_linear_info(const gb_linear *l, int *typ, int *rows, int *cols, size_t *weight_bytes);
 int gb_linear_free(gb_linear *l);
@@ -214,6 +221,13 @@ int gb_model_generate(gb_model *m, int32_t token, int pos, int n, int32_t *out_t
 int gb_model_start(gb_model *m, int32_t token, int pos);
 int gb_model_decode_async(gb_model *m, int n);
 int gb_model_read_tokens(gb_model *m, int pos0, int n, int32_t *out_tokens);
+/* Added (the reference's roadmap "Batched prefill", ROADMAP.md:36-41): feed
+ * tokens[0..n) at positions pos0..pos0+n-1. The first n-1 go through every
+ * layer at once (tensor-core GEMMs over binary16 activations and weights with
+ * float32 accumulation, causal attention over the cache; chunks of up to 512
+ * tokens), writing their K/V; the last goes through the decode step, whose
+ * logits are copied to host_logits[vocab] (NULL: not copied). One GPU only. */
+int gb_model_prefill(gb_model *m, const int32_t *tokens, int n, int pos0, float *host_logits);
 /* Added: the token rule of gb_model_next / generate / decode_async. NULL
  * (the default) is greedy model.Argmax; otherwise the sampler above with
  * counter = the position of the step and the penalty window = the tokens fed
