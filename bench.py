@@ -62,6 +62,30 @@ def peaks():
         return 6650.0, "fallback 6.65 TB/s (no MEASURED_PEAKS.json)"
 
 
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, cuBLAS burst)"
+    except Exception:
+        return 1590.0, "fallback 1.59 PFLOP/s (no MEASURED_PEAKS.json)"
+
+
+def prefill_flops(c, T):
+    """Algorithmic FLOPs of gb_model_prefill over T tokens: the first T-1 through the
+    batched layers (every GEMM 2*rows*cols per token; the last layer stops after its
+    q|k|v; causal attention 4*head_dim per (query head, visible key)), the last token
+    through one decode step (counted as its GEMV FLOPs)."""
+    q, kv = c.heads * c.head_dim, c.kv_heads * c.head_dim
+    qkv = 2 * c.dim * (q + 2 * kv)
+    rest = 2 * q * c.dim + 2 * c.dim * 2 * c.ffn + 2 * c.ffn * c.dim
+    n = T - 1
+    gemm = n * (c.layers * qkv + (c.layers - 1) * rest)
+    attn = (c.layers - 1) * 4 * c.heads * c.head_dim * (n * (n + 1) // 2)
+    decode = c.layers * (qkv + rest) + 2 * c.dim * c.vocab
+    return gemm + attn + decode
+
+
 def ncu_traffic(config):
     """DRAM bytes per launch of the dominant kernel (gate/up + SwiGLU GEMV) from the
     committed ncu summary profiles/step_kernels_8b_traffic.md (line
@@ -289,6 +313,29 @@ def run_ours(args, cfg, world, rank, local):
     peak, peak_src = peaks()
     achieved = gu_bytes / (gu_ms / 1e3) / 1e9
     breakdown = {k: round(statistics.median(p[k][0] for p in prof), 4) for k in prof[0]}
+
+    # batched prefill of a 512-token prompt (one GPU; the timed decode above is done,
+    # so overwriting cache positions 0..511 does not touch it)
+    prefill = None
+    if world == 1 and args.prefill_tokens > 1:
+        pt = prompt_tokens(spec, args.prefill_tokens)
+        m.prefill(pt, 0)  # warm-up (allocates the workspace)
+        torch.cuda.synchronize()
+        reps = 3
+        ev0.record(stream)
+        for _ in range(reps):
+            m.prefill(pt, 0)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        pms = ev0.elapsed_time(ev1) / reps
+        tpk, tsrc = tensor_peak()
+        fl = prefill_flops(c, len(pt))
+        prefill = {"tokens": len(pt), "value": round(len(pt) / (pms / 1e3), 1), "unit": "tok/s",
+                   "ms": round(pms, 3), "tflops": round(fl / (pms / 1e3) / 1e12, 1),
+                   "frac_of_tensor_peak": round(fl / (pms / 1e3) / 1e12 / tpk, 4), "peak_source": tsrc,
+                   "how": "gb_model_prefill from host token ids: tcgen05 GEMMs (binary16 operands, f32 accumulate) "
+                          "+ tensor-core causal attention, last token through the decode step; CUDA events, "
+                          f"mean of {reps}"}
     result = {
         "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
@@ -307,6 +354,7 @@ def run_ours(args, cfg, world, rank, local):
                           "frac": round(bytes_tok * tok_s / 1e9 / peak, 4),
                           "roofline_tok_s": round(peak * 1e9 / bytes_tok, 1)},
         "kernel_ms_per_step": breakdown,
+        "prefill": prefill,
         "e2e": e2e,
         "gpu_launches": m.launches_per_step() * args.steps,
         "clocks": clk,
@@ -406,6 +454,8 @@ def main():
     ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=512,
+                    help="prompt length of the batched-prefill measurement (0 = skip)")
     ap.add_argument("--layers", type=int, default=0,
                     help="truncate the model to this many layers (small ncu captures only; not a bench line)")
     args = ap.parse_args()

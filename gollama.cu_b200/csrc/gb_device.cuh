@@ -196,3 +196,31 @@ GB_DEV uint4 gb_ld_stream16(const void *p) {
 // which represents x to within s/2/254^2 (about 6e-8 of the block's largest
 // magnitude, the float32 rounding level). Quantized matrix-vector products
 // then run on dp4a with exact int32 sums (gb_gemv.cu).
+
+// ---- mma.sync m16n8k16 (f16 in, f32 accumulate) and ldmatrix, shared by the
+// attention kernels
+GB_DEV uint32_t h2pack(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+// fp16 rounding of (x0, x1) and of the residues
+GB_DEV void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+  hi = h2pack(h0, h1);
+  lo = h2pack(__float2half_rn(x0 - __half2float(h0)), __float2half_rn(x1 - __half2float(h1)));
+}
+GB_DEV void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+GB_DEV void ldsm_x4(uint32_t r[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(gb_smem_u32(p)));
+}
+GB_DEV void ldsm_x4_t(uint32_t r[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(gb_smem_u32(p)));
+}

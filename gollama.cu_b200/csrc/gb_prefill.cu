@@ -90,48 +90,12 @@ constexpr uint32_t idesc_f16(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-// ---- one stage of weight bytes per tile -----------------------------------
-// The 16-byte units of a super-block that K-stage kc (elements 64kc..64kc+63)
-// needs, as (byte offset in the sb-block, bytes) pieces; packed in this
-// order in the stage's raw region of the tile.
-struct Piece {
-  int off, len;
-};
-GB_HD int stage_pieces(int typ, int kc, Piece *pc) {
-  switch (typ) {
-    case GB_T_Q4_K:
-    case GB_T_Q4_0:
-      pc[0] = {0, 512};
-      pc[1] = {(1 + 2 * kc) * 512, 1024};
-      return 2;
-    case GB_T_Q8_0:
-      pc[0] = {0, 512};
-      pc[1] = {(1 + 4 * kc) * 512, 2048};
-      return 2;
-    case GB_T_Q6_K: {
-      const int c = kc >> 1;
-      pc[0] = {c * 4 * 512, 2048};        // ql bytes 64c..64c+63
-      pc[1] = {(8 + 2 * c) * 512, 1024};  // qh bytes 32c..32c+31
-      pc[2] = {12 * 512, 512};            // the 16 int8 scales
-      pc[3] = {13 * 512, 64};             // d of the 32 rows
-      return 4;
-    }
-    case GB_T_F16:
-    case GB_T_BF16:
-      pc[0] = {8 * kc * 512, 4096};
-      return 1;
-    case GB_T_F32:
-      pc[0] = {16 * kc * 512, 8192};
-      return 1;
-  }
-  return 0;
-}
-GB_HD int stage_raw_bytes(int typ) {
-  Piece pc[4];
-  int n = stage_pieces(typ, 0, pc), b = 0;
-  for (int i = 0; i < n; i++) b += pc[i].len;
-  return b;
-}
+// ---- raw weight units ---------------------------------------------------------
+// The producer stages weight bytes per tile in "raw units": for quantized
+// types the tile's whole sb-block (one bulk copy covers four K-stages), for
+// float types the stage's contiguous quarter of it.
+GB_HD int raw_spr(int typ) { return gb_float_type(typ) ? 1 : 4; }  // K-stages per raw unit
+GB_HD int raw_unit_bytes(int typ) { return gb_tiled_sb_bytes(typ) / (4 / raw_spr(typ)); }
 
 GB_DEV uint4 lds16(const uint8_t *p) { return *(const uint4 *)p; }
 GB_DEV uint32_t pack_h2(float a, float b) {
@@ -143,143 +107,121 @@ GB_DEV uint8_t byte_of(const uint4 &v, int i) {
   return (uint8_t)(w >> (8 * (i & 3)));
 }
 
-// Decode K-stage kc of row `lane` of one tile from its raw stage bytes into
-// the fp16 B tile row rB (swizzled). Values are the reference's float32
-// element values rounded to binary16.
-GB_DEV void dequant_stage(int typ, int kc, const uint8_t *raw, int lane, uint8_t *btile, int rB) {
-  uint8_t *row = btile + rB * 128;
-  const int sw = rB & 7;
-  auto put = [&](int c, const float *v) {
-    uint4 o;
-    o.x = pack_h2(v[0], v[1]);
-    o.y = pack_h2(v[2], v[3]);
-    o.z = pack_h2(v[4], v[5]);
-    o.w = pack_h2(v[6], v[7]);
-    *(uint4 *)(row + ((c ^ sw) << 4)) = o;
-  };
+// Exact small integer n (0 <= n < 2^23) as float without the conversion unit.
+GB_DEV float u2f(uint32_t n) { return __fsub_rn(__uint_as_float(0x4B000000u | n), 8388608.f); }
+
+// Q4_K scale and min of sub-block j from the 12 scale bytes (bytes 4..15 of
+// the block's first unit): quant.ScaleMinQ4K, quant/quant.go:90, in registers.
+GB_DEV void q4k_scale_reg(const uint4 &h, int j, uint32_t &sc, uint32_t &m) {
+  if (j < 4) {
+    sc = byte_of(h, 4 + j) & 63u;
+    m = byte_of(h, 8 + j) & 63u;
+  } else {
+    const uint32_t a = byte_of(h, 8 + j), lo = byte_of(h, j), hi = byte_of(h, 4 + j);
+    sc = (a & 0xFu) | ((lo >> 6) << 4);
+    m = (a >> 4) | ((hi >> 6) << 4);
+  }
+}
+
+// Decode output chunk c (elements 8c..8c+7) of K-stage kc of row `lane` of
+// one tile, as eight binary16 values, from the tile's whole sb-block
+// (quantized types) or from the stage's piece of it (float types): the
+// reference's float32 element values (quant/quant.go:44-132) rounded to
+// nearest even.
+GB_DEV uint4 dequant_chunk(int typ, int kc, const uint8_t *raw, int lane, int c) {
   float v[8];
   switch (typ) {
-    case GB_T_Q4_K: {  // quant/quant.go:97-112: (d*sc)*q - dmin*m
+    case GB_T_Q4_K: {  // (d*sc)*q - dmin*m
       const uint4 h = lds16(raw + lane * 16);
-      const uint4 q0 = lds16(raw + 512 + lane * 16), q1 = lds16(raw + 1024 + lane * 16);
+      const int hi = c >> 2, b0 = (c & 3) * 8;
+      const uint4 q = lds16(raw + 512 * (1 + 2 * kc + (b0 >> 4)) + lane * 16);
       const float d = gb_half_to_float((uint16_t)(h.x & 0xFFFF)), dmin = gb_half_to_float((uint16_t)(h.x >> 16));
-      uint8_t s[12];
+      uint32_t sc, m;
+      q4k_scale_reg(h, 2 * kc + hi, sc, m);
+      const float ds = __fmul_rn(d, u2f(sc)), dm = __fmul_rn(dmin, u2f(m));
+      const uint32_t w0 = (b0 & 15) ? q.z : q.x, w1 = (b0 & 15) ? q.w : q.y;
 #pragma unroll
-      for (int i = 0; i < 12; i++) s[i] = byte_of(h, 4 + i);
-      uint8_t m0, m1;
-      const uint8_t sc0 = gb_q4k_scale(s, 2 * kc, &m0), sc1 = gb_q4k_scale(s, 2 * kc + 1, &m1);
-      const float ds0 = __fmul_rn(d, (float)sc0), dm0 = __fmul_rn(dmin, (float)m0);
-      const float ds1 = __fmul_rn(d, (float)sc1), dm1 = __fmul_rn(dmin, (float)m1);
-#pragma unroll
-      for (int c = 0; c < 8; c++) {
-        const bool hi = c >= 4;
-        const int b0 = (c & 3) * 8;
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const int bi = b0 + e;
-          const uint8_t q = bi < 16 ? byte_of(q0, bi) : byte_of(q1, bi - 16);
-          const int nib = hi ? (q >> 4) : (q & 0xF);
-          v[e] = __fsub_rn(__fmul_rn(hi ? ds1 : ds0, (float)nib), hi ? dm1 : dm0);
-        }
-        put(c, v);
+      for (int e = 0; e < 8; e++) {
+        const uint32_t by = ((e < 4 ? w0 : w1) >> (8 * (e & 3))) & 0xFFu;
+        v[e] = __fsub_rn(__fmul_rn(ds, u2f(hi ? by >> 4 : by & 0xFu)), dm);
       }
       break;
     }
-    case GB_T_Q4_0: {  // quant/quant.go:56-65: d*(q-8)
+    case GB_T_Q4_0: {  // d*(q-8)
       const uint4 dd = lds16(raw + lane * 16);
+      const int b = c >> 2, k = 2 * kc + b, cc = c & 3;
+      const float d = gb_half_to_float((uint16_t)(byte_of(dd, 2 * k) | byte_of(dd, 2 * k + 1) << 8));
+      const uint4 q = lds16(raw + 512 * (1 + k) + lane * 16);
+      const uint32_t w0 = (cc & 1) ? q.z : q.x, w1 = (cc & 1) ? q.w : q.y;
 #pragma unroll
-      for (int b = 0; b < 2; b++) {
-        const int k = 2 * kc + b;
-        const float d = gb_half_to_float((uint16_t)(byte_of(dd, 2 * k) | byte_of(dd, 2 * k + 1) << 8));
-        const uint4 q = lds16(raw + 512 * (1 + b) + lane * 16);
-#pragma unroll
-        for (int cc = 0; cc < 4; cc++) {
-          const bool hi = cc >= 2;
-#pragma unroll
-          for (int e = 0; e < 8; e++) {
-            const uint8_t qb = byte_of(q, (cc & 1) * 8 + e);
-            const int nib = hi ? (qb >> 4) : (qb & 0xF);
-            v[e] = __fmul_rn(d, __fsub_rn((float)nib, 8.f));
-          }
-          put(4 * b + cc, v);
-        }
+      for (int e = 0; e < 8; e++) {
+        const uint32_t by = ((e < 4 ? w0 : w1) >> (8 * (e & 3))) & 0xFFu;
+        v[e] = __fmul_rn(d, __fsub_rn(u2f(cc >= 2 ? by >> 4 : by & 0xFu), 8.f));
       }
       break;
     }
-    case GB_T_Q8_0: {  // quant/quant.go:44-55: d*q
+    case GB_T_Q8_0: {  // d*q
       const uint4 dd = lds16(raw + lane * 16);
+      const int b = c >> 2, k = 2 * kc + b, u = (c >> 1) & 1, hlf = c & 1;
+      const float d = gb_half_to_float((uint16_t)(byte_of(dd, 2 * k) | byte_of(dd, 2 * k + 1) << 8));
+      const uint4 q = lds16(raw + 512 * (1 + 2 * k + u) + lane * 16);
+      const uint32_t w0 = hlf ? q.z : q.x, w1 = hlf ? q.w : q.y;
 #pragma unroll
-      for (int b = 0; b < 2; b++) {
-        const int k = 2 * kc + b;
-        const float d = gb_half_to_float((uint16_t)(byte_of(dd, 2 * k) | byte_of(dd, 2 * k + 1) << 8));
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-          const uint4 q = lds16(raw + 512 * (1 + 2 * b + u) + lane * 16);
-#pragma unroll
-          for (int hlf = 0; hlf < 2; hlf++) {
-#pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = __fmul_rn(d, (float)(int8_t)byte_of(q, hlf * 8 + e));
-            put(4 * b + 2 * u + hlf, v);
-          }
-        }
+      for (int e = 0; e < 8; e++) {
+        const int by = (int)(int8_t)(((e < 4 ? w0 : w1) >> (8 * (e & 3))) & 0xFFu);
+        v[e] = __fmul_rn(d, (float)by);
       }
       break;
     }
-    case GB_T_Q6_K: {  // quant/quant.go:114-132: d*sc*(q-32)
-      const uint8_t *ql = raw, *qh = raw + 2048, *sc = raw + 3072, *dp = raw + 3584;
-      const int c = kc >> 1, q0 = (kc & 1) * 2;
+    case GB_T_Q6_K: {  // d*sc*(q-32)
+      const int cq = kc >> 1, quarter = (kc & 1) * 2 + (c >> 2), l0 = (c & 3) * 8;
+      const uint8_t *ql = raw + cq * 4 * 512, *qh = raw + (8 + 2 * cq) * 512, *scp = raw + 12 * 512, *dp = raw + 13 * 512;
+      const int qlb = l0 + ((quarter & 1) ? 32 : 0);
       const float d = gb_half_to_float(*(const uint16_t *)(dp + lane * 2));
-      const uint4 s4 = lds16(sc + lane * 16);
+      const uint4 s4 = lds16(scp + lane * 16);
+      const uint4 L = lds16(ql + (qlb >> 4) * 512 + lane * 16);
+      const uint4 H = lds16(qh + (l0 >> 4) * 512 + lane * 16);
+      const int scv = (int)(int8_t)byte_of(s4, cq * 8 + 2 * quarter + (l0 >> 4));
+      const float dsc = __fmul_rn(d, (float)scv);
+      const uint32_t l0w = (qlb & 15) ? L.z : L.x, l1w = (qlb & 15) ? L.w : L.y;
+      const uint32_t h0w = (l0 & 15) ? H.z : H.x, h1w = (l0 & 15) ? H.w : H.y;
 #pragma unroll
-      for (int oc = 0; oc < 8; oc++) {
-        const int quarter = q0 + (oc >> 2), l0 = (oc & 3) * 8;
-        const int qlb = l0 + ((quarter & 1) ? 32 : 0);  // ql byte within the chunk's 64
-        const uint4 L = lds16(ql + (qlb >> 4) * 512 + lane * 16);
-        const uint4 H = lds16(qh + (l0 >> 4) * 512 + lane * 16);
-        const int scv = (int8_t)byte_of(s4, c * 8 + 2 * quarter + (l0 >> 4));
-        const float dsc = __fmul_rn(d, (float)scv);
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const uint8_t lb = byte_of(L, (qlb & 15) + e), hb = byte_of(H, (l0 & 15) + e);
-          const int lo = quarter >= 2 ? (lb >> 4) : (lb & 0xF);
-          const int q = lo | (((hb >> (2 * quarter)) & 3) << 4);
-          v[e] = __fmul_rn(dsc, (float)(q - 32));
-        }
-        put(oc, v);
+      for (int e = 0; e < 8; e++) {
+        const uint32_t lb = ((e < 4 ? l0w : l1w) >> (8 * (e & 3))) & 0xFFu;
+        const uint32_t hb = ((e < 4 ? h0w : h1w) >> (8 * (e & 3))) & 0xFFu;
+        const uint32_t lo = quarter >= 2 ? (lb >> 4) : (lb & 0xFu);
+        const uint32_t qv = lo | (((hb >> (2 * quarter)) & 3u) << 4);
+        v[e] = __fmul_rn(dsc, __fsub_rn(u2f(qv), 32.f));
       }
       break;
     }
     case GB_T_F16:
+      return lds16(raw + c * 512 + lane * 16);
+    case GB_T_BF16: {
+      const uint4 u = lds16(raw + c * 512 + lane * 16);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int c2 = 0; c2 < 8; c2++) *(uint4 *)(row + ((c2 ^ sw) << 4)) = lds16(raw + c2 * 512 + lane * 16);
-      break;
-    case GB_T_BF16:
-#pragma unroll
-      for (int c2 = 0; c2 < 8; c2++) {
-        const uint4 u = lds16(raw + c2 * 512 + lane * 16);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          v[2 * i] = __uint_as_float(w[i] << 16);
-          v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-        }
-        put(c2, v);
+      for (int i = 0; i < 4; i++) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
       }
       break;
-    case GB_T_F32:
-#pragma unroll
-      for (int c2 = 0; c2 < 8; c2++) {
-        const uint4 a = lds16(raw + (2 * c2) * 512 + lane * 16), b = lds16(raw + (2 * c2 + 1) * 512 + lane * 16);
-        v[0] = __uint_as_float(a.x), v[1] = __uint_as_float(a.y), v[2] = __uint_as_float(a.z), v[3] = __uint_as_float(a.w);
-        v[4] = __uint_as_float(b.x), v[5] = __uint_as_float(b.y), v[6] = __uint_as_float(b.z), v[7] = __uint_as_float(b.w);
-        put(c2, v);
-      }
-      break;
-    default: {
-#pragma unroll
-      for (int c2 = 0; c2 < 8; c2++) *(uint4 *)(row + ((c2 ^ sw) << 4)) = make_uint4(0, 0, 0, 0);
     }
+    case GB_T_F32: {
+      const uint4 a = lds16(raw + (2 * c) * 512 + lane * 16), b = lds16(raw + (2 * c + 1) * 512 + lane * 16);
+      v[0] = __uint_as_float(a.x), v[1] = __uint_as_float(a.y), v[2] = __uint_as_float(a.z), v[3] = __uint_as_float(a.w);
+      v[4] = __uint_as_float(b.x), v[5] = __uint_as_float(b.y), v[6] = __uint_as_float(b.z), v[7] = __uint_as_float(b.w);
+      break;
+    }
+    default:
+      return make_uint4(0, 0, 0, 0);
   }
+  uint4 o;
+  o.x = pack_h2(v[0], v[1]);
+  o.y = pack_h2(v[2], v[3]);
+  o.z = pack_h2(v[4], v[5]);
+  o.w = pack_h2(v[6], v[7]);
+  return o;
 }
 
 struct TcArgs {
@@ -292,8 +234,10 @@ struct TcArgs {
   int ldy;
   __half *act;            // SWIGLU: act[T][ld_act] = silu(g) * u
   int ld_act;
-  int nstage;
-  int raw_tile;           // raw bytes per tile per stage (max over the two types)
+  int nstage;             // A/B ring slots (one K-stage each)
+  int rstage;             // raw ring slots (one raw unit each)
+  int spr;                // K-stages per raw unit (4: quantized types, 1: float types)
+  int raw_tile;           // raw bytes per tile per raw unit (max over the two types)
   unsigned *err;
 };
 
@@ -311,32 +255,41 @@ GB_DEV const uint8_t *sb_block(const TcArgs &g, int tile, int sb, int up, int &t
          ((size_t)(tile - g.split_tile) * g.nsb + sb) * gb_tiled_sb_bytes(typ);
 }
 
-// BN: weight rows of the CTA (128, or 256 for gate/up pairs); NDQ = BN/32
-// dequant warps (one 32-row tile each), then the producer warp, then the
-// MMA warp.
+// BN: weight rows of the CTA (128, or 256 for gate/up pairs) in NT = BN/32
+// tiles. 16 dequant warps: warp w decodes tile w % NT, output chunks
+// [(w / NT) * CPT, +CPT) of each row (one row per lane), so every SM
+// scheduler has four decoding warps to interleave; then the producer warp,
+// then the MMA warp.
+constexpr int kDQ = 16;
 template <int BN, int EPI>
-__global__ void __launch_bounds__((BN / 32 + 2) * 32, 1)
+__global__ void __launch_bounds__((kDQ + 2) * 32, 1)
     gemm_tc_kernel(const TcArgs g, const __grid_constant__ CUtensorMap tmap_a) {
-  constexpr int NDQ = BN / 32;
+  constexpr int NDQ = kDQ, NT = BN / 32, CPT = 8 * NT / NDQ;
+  static_assert(NDQ % NT == 0 && CPT >= 1, "dequant split");
   constexpr int BBytes = BN * 128;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kMaxStagesTC], bfull[kMaxStagesTC], empty[kMaxStagesTC], accf;
+  __shared__ __align__(8) uint64_t afull[kMaxStagesTC], bfull[kMaxStagesTC], empty[kMaxStagesTC];
+  __shared__ __align__(8) uint64_t rfull[kMaxStagesTC], rempty[kMaxStagesTC], accf;
   __shared__ uint32_t tmem_base;
   __shared__ int bad;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NS = g.nstage;
+  const int NS = g.nstage, RS = g.rstage, SPR = g.spr;
   const int nk = g.nsb * 4;                 // K stages
   const int m0 = blockIdx.y * kBM;          // first token row
   const int tile0 = blockIdx.x * 4;         // first weight tile (of each half for pairs)
-  // [NS] A tiles | [NS] B tiles (1024-aligned) | [NS][NDQ] raw stage regions
+  // [NS] A tiles | [NS] B tiles (1024-aligned) | [RS][NT] raw units
   uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *A0 = base, *B0 = base + (size_t)NS * kABytes, *R0 = B0 + (size_t)NS * BBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; s++) {
-      gb_mbar_init(&full[s], 1);
-      gb_mbar_init(&bfull[s], NDQ * 32);
+      gb_mbar_init(&afull[s], 1);
+      gb_mbar_init(&bfull[s], NDQ);
       gb_mbar_init(&empty[s], 1);
+    }
+    for (int r = 0; r < RS; r++) {
+      gb_mbar_init(&rfull[r], 1);
+      gb_mbar_init(&rempty[r], NDQ);
     }
     gb_mbar_init(&accf, 1);
     bad = 0;
@@ -352,44 +305,52 @@ __global__ void __launch_bounds__((BN / 32 + 2) * 32, 1)
   const uint32_t tmem = tmem_base;
 
   if (warp == NDQ) {
-    // producer: activation tile by TMA, the weight tiles' raw stage bytes by bulk copies
+    // producer: per raw unit the tiles' weight bytes (one bulk copy per tile),
+    // per K-stage the activation tile by TMA
     if (lane == 0) {
-      int issued = 0;
+      int a_issued = 0, r_issued = 0;
       for (int k = 0; k < nk; k++) {
+        if (k % SPR == 0) {
+          const int r = k / SPR, rs = r % RS;
+          if (r >= RS && !gb_mbar_wait(&rempty[rs], ((r / RS) - 1) & 1)) {
+            bad = 1;
+            if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
+            break;
+          }
+          const int sb = k >> 2, kc = k & 3;
+          uint32_t bytes = 0;
+          for (int j = 0; j < NT; j++) {
+            const int up = g.pair && j >= 4, tile = tile0 + (g.pair ? (j & 3) : j);
+            if (tile >= g.ntiles) continue;
+            int typ;
+            (void)sb_block(g, tile, sb, up, typ);
+            bytes += (uint32_t)raw_unit_bytes(typ);
+          }
+          gb_mbar_expect_tx(&rfull[rs], bytes);
+          for (int j = 0; j < NT; j++) {
+            const int up = g.pair && j >= 4, tile = tile0 + (g.pair ? (j & 3) : j);
+            if (tile >= g.ntiles) continue;
+            int typ;
+            const uint8_t *src = sb_block(g, tile, sb, up, typ);
+            const int ub = raw_unit_bytes(typ);
+            gb_bulk_g2s(R0 + ((size_t)rs * NT + j) * g.raw_tile, src + (SPR == 1 ? (size_t)kc * ub : 0), (uint32_t)ub,
+                        &rfull[rs]);
+          }
+          r_issued = r + 1;
+        }
         const int s = k % NS;
         if (k >= NS && !gb_mbar_wait(&empty[s], ((k / NS) - 1) & 1)) {
           bad = 1;
           if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
           break;
         }
-        const int sb = k >> 2, kc = k & 3;
-        uint32_t bytes = kABytes;
-        for (int j = 0; j < NDQ; j++) {
-          const int up = g.pair && j >= 4, tile = tile0 + (g.pair ? (j & 3) : j);
-          if (tile >= g.ntiles) continue;
-          int typ;
-          (void)sb_block(g, tile, sb, up, typ);
-          bytes += (uint32_t)stage_raw_bytes(typ);
-        }
-        gb_mbar_expect_tx(&full[s], bytes);
-        tma_load_2d(A0 + (size_t)s * kABytes, &tmap_a, k * kBK, m0, &full[s]);
-        for (int j = 0; j < NDQ; j++) {
-          const int up = g.pair && j >= 4, tile = tile0 + (g.pair ? (j & 3) : j);
-          if (tile >= g.ntiles) continue;
-          int typ;
-          const uint8_t *src = sb_block(g, tile, sb, up, typ);
-          Piece pc[4];
-          const int np = stage_pieces(typ, kc, pc);
-          uint8_t *dst = R0 + ((size_t)s * NDQ + j) * g.raw_tile;
-          for (int i = 0; i < np; i++) {
-            gb_bulk_g2s(dst, src + pc[i].off, (uint32_t)pc[i].len, &full[s]);
-            dst += pc[i].len;
-          }
-        }
-        issued = k + 1;
+        gb_mbar_expect_tx(&afull[s], kABytes);
+        tma_load_2d(A0 + (size_t)s * kABytes, &tmap_a, k * kBK, m0, &afull[s]);
+        a_issued = k + 1;
       }
       // copies still in flight land (bounded) before the CTA exits
-      for (int j = issued > NS ? issued - NS : 0; j < issued; j++) (void)gb_mbar_wait(&full[j % NS], (j / NS) & 1);
+      for (int j = a_issued > NS ? a_issued - NS : 0; j < a_issued; j++) (void)gb_mbar_wait(&afull[j % NS], (j / NS) & 1);
+      for (int j = r_issued > RS ? r_issued - RS : 0; j < r_issued; j++) (void)gb_mbar_wait(&rfull[j % RS], (j / RS) & 1);
     }
   } else if (warp == NDQ + 1) {
     // MMA issue: one thread
@@ -398,7 +359,7 @@ __global__ void __launch_bounds__((BN / 32 + 2) * 32, 1)
       for (int k = 0; k < nk; k++) {
         const int s = k % NS;
         const uint32_t ph = (k / NS) & 1;
-        if (!gb_mbar_wait(&full[s], ph) || !gb_mbar_wait(&bfull[s], ph)) {
+        if (!gb_mbar_wait(&afull[s], ph) || !gb_mbar_wait(&bfull[s], ph)) {
           bad = 1;
           if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
           break;
@@ -414,37 +375,48 @@ __global__ void __launch_bounds__((BN / 32 + 2) * 32, 1)
       mma_commit(&accf);  // all issued MMAs done (also after an early stop)
     }
   } else {
-    // dequant warps: warp j decodes tile j of the CTA, one row per lane
-    const int j = warp;
+    // dequant warps
+    const int j = warp % NT, part = warp / NT;
     const int up = g.pair && j >= 4, tile = tile0 + (g.pair ? (j & 3) : j);
     const bool valid = tile < g.ntiles;
+    const int rB = j * 32 + lane, sw = lane & 7;  // B row; its 128-byte swizzle phase
     for (int k = 0; k < nk; k++) {
-      const int s = k % NS;
-      const uint32_t ph = (k / NS) & 1;
-      if (!gb_mbar_wait(&full[s], ph)) {
+      const int s = k % NS, r = k / SPR, rs = r % RS;
+      // the raw unit has landed; the B slot's previous MMAs are done
+      if ((k % SPR == 0 && !gb_mbar_wait(&rfull[rs], (r / RS) & 1)) ||
+          (k >= NS && !gb_mbar_wait(&empty[s], ((k / NS) - 1) & 1))) {
         if (lane == 0 && g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
         bad = 1;
         break;
       }
       int typ = -1;  // a tile past the matrix decodes to zeros
       if (valid) (void)sb_block(g, tile, k >> 2, up, typ);
-      dequant_stage(typ, k & 3, R0 + ((size_t)s * NDQ + j) * g.raw_tile, lane, B0 + (size_t)s * BBytes, j * 32 + lane);
+      const uint8_t *raw = R0 + ((size_t)rs * NT + j) * g.raw_tile;
+      uint8_t *row = B0 + (size_t)s * BBytes + (size_t)rB * 128;
+#pragma unroll
+      for (int ci = 0; ci < CPT; ci++) {
+        const int c = part * CPT + ci;
+        *(uint4 *)(row + ((c ^ sw) << 4)) = dequant_chunk(typ, k & 3, raw, lane, c);
+      }
       gb_fence_proxy_async();
-      gb_mbar_arrive(&bfull[s]);
+      __syncwarp();
+      if (lane == 0) {
+        gb_mbar_arrive(&bfull[s]);
+        if (k % SPR == SPR - 1 || k == nk - 1) gb_mbar_arrive(&rempty[rs]);
+      }
     }
-    // epilogue: accumulators -> registers -> global
+    // epilogue: accumulators -> registers -> global. Warp w reads TMEM lanes
+    // 32*(w%4).. (tcgen05.ld's rule) and a quarter of the columns.
     const bool ok = gb_mbar_wait(&accf, 0);
     tc_fence_after();
     if (!ok) {
       if (lane == 0 && g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
     } else if (!bad) {
-      const int quarter = warp & 3;  // tcgen05.ld reaches TMEM lanes 32*(warp%4)..+31
+      const int quarter = warp & 3, cq = warp >> 2;
       const int m = m0 + quarter * 32 + lane;
       const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
       if constexpr (EPI == GB_EPI_SWIGLU) {
-        // warps 0-3 take columns 0..63 of gate and up, warps 4-7 columns 64..127
-        const int c0 = (warp >> 2) * 64;
-        for (int cc = c0; cc < c0 + 64; cc += 16) {
+        for (int cc = cq * 32; cc < cq * 32 + 32; cc += 16) {
           float gv[16], uv[16];
           tmem_ld16(trow + cc, gv);
           tmem_ld16(trow + 128 + cc, uv);
@@ -464,7 +436,7 @@ __global__ void __launch_bounds__((BN / 32 + 2) * 32, 1)
           }
         }
       } else {
-        for (int cc = 0; cc < BN; cc += 16) {
+        for (int cc = cq * (BN / 4); cc < (cq + 1) * (BN / 4); cc += 16) {
           float v[16];
           tmem_ld16(trow + cc, v);
           const int n = tile0 * 32 + cc;
@@ -481,7 +453,9 @@ __global__ void __launch_bounds__((BN / 32 + 2) * 32, 1)
               *(float4 *)(dst + i) = o;
             }
           } else {
-            for (int i = 0; i < 16 && n + i < g.rows; i++) dst[i] = EPI == GB_EPI_RESID ? dst[i] + v[i] : v[i];
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+              if (n + i < g.rows) dst[i] = EPI == GB_EPI_RESID ? dst[i] + v[i] : v[i];
           }
         }
       }
@@ -689,6 +663,197 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float *q, int T
   }
 }
 
+
+// Causal attention of T query tokens on the tensor cores (flash-attention
+// style): one CTA per (QT tokens, KV head) with 64 query rows (token, group
+// head); four warps of 16 rows; K/V tiles of 64 positions double-buffered
+// in shared memory in the cache's own [16-byte dim chunk][position] order;
+// S = Q K^T and O += P V with mma.sync m16n8k16. q and p are each split into
+// a binary16 value and its binary16 residue (two MMAs), which keeps about 22
+// bits of both, so the scores and weights carry float32-level precision and
+// only the cache's binary16 K/V limit the result. Online softmax in float32.
+constexpr int kFM = 64, kFK = 64;
+GB_DEV void cp_async16(void *dst, const void *src, bool zero) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(gb_smem_u32(dst)), "l"(src),
+               "r"(zero ? 0 : 16)
+               : "memory");
+}
+GB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+GB_DEV void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+GB_DEV void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+template <bool F16, int HD>
+__global__ void __launch_bounds__(128) attn_prefill_mma_kernel(const float *q, int T, int pos0, int n_heads,
+                                                               int n_kv, const void *kcache, const void *vcache,
+                                                               int max_len, float scale, __half *out) {
+  constexpr int NC = HD / 8;                 // 16-byte chunks of a K/V row
+  constexpr int TILE = NC * kFK * 8;         // halves of one K (or V) tile
+  extern __shared__ __align__(128) uint16_t kvs[];  // [2 buffers][K, V][NC][kFK][8]
+  const int G = n_heads / n_kv, QT = kFM / G, kvh = blockIdx.y, t0 = blockIdx.x * QT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g4 = lane >> 2, t4 = lane & 3;
+  const int tlast = min(T, t0 + QT) - 1;
+  const int kv_end = pos0 + tlast + 1;
+  const int ntile = (kv_end + kFK - 1) / kFK;
+
+  // this thread's two rows (g4 and g4 + 8 of the warp's 16)
+  int qpos[2];
+  bool rvalid[2];
+  const float *qrow[2];
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const int r = warp * 16 + g4 + 8 * i, tq = r / G, gi = r % G, t = t0 + tq;
+    rvalid[i] = tq < QT && t < T;
+    qpos[i] = rvalid[i] ? pos0 + t : -1;
+    qrow[i] = q + ((size_t)(rvalid[i] ? t : 0) * n_heads + (size_t)(kvh * G + gi)) * HD;
+  }
+  // Q fragments (scaled), split into binary16 value and residue
+  uint32_t qh[HD / 16][4], ql[HD / 16][4];
+#pragma unroll
+  for (int ks = 0; ks < HD / 16; ks++) {
+#pragma unroll
+    for (int half = 0; half < 2; half++)
+#pragma unroll
+      for (int i = 0; i < 2; i++) {
+        const int d = ks * 16 + half * 8 + 2 * t4;
+        const float x0 = rvalid[i] ? qrow[i][d] * scale : 0.f, x1 = rvalid[i] ? qrow[i][d + 1] * scale : 0.f;
+        split2(x0, x1, qh[ks][half * 2 + i], ql[ks][half * 2 + i]);
+      }
+  }
+
+  auto stage = [&](int buf, int kb) {
+    uint16_t *Kd = kvs + (size_t)buf * 2 * TILE, *Vd = Kd + TILE;
+    for (int i = threadIdx.x; i < NC * kFK; i += blockDim.x) {
+      const int c = i / kFK, j = i % kFK, p = kb + j;
+      const bool in = p < kv_end;
+      uint16_t *kd = Kd + ((size_t)c * kFK + j) * 8, *vd = Vd + ((size_t)c * kFK + j) * 8;
+      if constexpr (F16) {
+        const size_t off = (((size_t)kvh * NC + c) * max_len + (in ? p : 0)) * 8;
+        cp_async16(kd, (const uint16_t *)kcache + off, !in);
+        cp_async16(vd, (const uint16_t *)vcache + off, !in);
+      } else {
+        float kf[8], vf[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) kf[e] = vf[e] = 0.f;
+        if (in) {
+          const float *kb4 = (const float *)kcache;
+          const float4 a = *(const float4 *)(kb4 + (((size_t)kvh * (HD / 4) + 2 * c) * max_len + p) * 4);
+          const float4 b = *(const float4 *)(kb4 + (((size_t)kvh * (HD / 4) + 2 * c + 1) * max_len + p) * 4);
+          const float4 va = *(const float4 *)((const float *)vcache + ((size_t)kvh * max_len + p) * HD + 8 * c);
+          const float4 vb = *(const float4 *)((const float *)vcache + ((size_t)kvh * max_len + p) * HD + 8 * c + 4);
+          kf[0] = a.x, kf[1] = a.y, kf[2] = a.z, kf[3] = a.w, kf[4] = b.x, kf[5] = b.y, kf[6] = b.z, kf[7] = b.w;
+          vf[0] = va.x, vf[1] = va.y, vf[2] = va.z, vf[3] = va.w, vf[4] = vb.x, vf[5] = vb.y, vf[6] = vb.z, vf[7] = vb.w;
+        }
+        *(uint4 *)kd = make_uint4(pack_h2(kf[0], kf[1]), pack_h2(kf[2], kf[3]), pack_h2(kf[4], kf[5]), pack_h2(kf[6], kf[7]));
+        *(uint4 *)vd = make_uint4(pack_h2(vf[0], vf[1]), pack_h2(vf[2], vf[3]), pack_h2(vf[4], vf[5]), pack_h2(vf[6], vf[7]));
+      }
+    }
+    cp_async_commit();
+  };
+
+  float o[NC][4];
+#pragma unroll
+  for (int nd = 0; nd < NC; nd++) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  if (ntile > 0) stage(0, 0);
+  for (int it = 0; it < ntile; it++) {
+    const int kb = it * kFK, buf = it & 1;
+    if (it + 1 < ntile) {
+      stage(buf ^ 1, kb + kFK);
+      cp_async_wait1();
+    } else {
+      cp_async_wait0();
+    }
+    __syncthreads();
+    const uint16_t *Kt = kvs + (size_t)buf * 2 * TILE, *Vt = Kt + TILE;
+    // S = Q K^T for 64 keys: 8 blocks of 8
+    float sc[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; nb++) sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ks++)
+#pragma unroll
+      for (int nb = 0; nb < 8; nb += 2) {
+        const int m = lane >> 3, c = 2 * ks + (m & 1), key = 8 * (nb + (m >> 1)) + (lane & 7);
+        uint32_t b[4];
+        ldsm_x4(b, Kt + ((size_t)c * kFK + key) * 8);
+        mma16816(sc[nb], qh[ks], b[0], b[1]);
+        mma16816(sc[nb], ql[ks], b[0], b[1]);
+        mma16816(sc[nb + 1], qh[ks], b[2], b[3]);
+        mma16816(sc[nb + 1], ql[ks], b[2], b[3]);
+      }
+    // causal mask and online softmax (rows g4 and g4+8)
+    float mt[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int i = e >> 1, key = kb + 8 * nb + 2 * t4 + (e & 1);
+        if (key > qpos[i]) sc[nb][e] = -INFINITY;
+        mt[i] = fmaxf(mt[i], sc[nb][e]);
+      }
+    float alpha[2], base[2];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      mt[i] = fmaxf(mt[i], __shfl_xor_sync(0xffffffffu, mt[i], 1));
+      mt[i] = fmaxf(mt[i], __shfl_xor_sync(0xffffffffu, mt[i], 2));
+      const float mn = fmaxf(mrow[i], mt[i]);
+      base[i] = mn == -INFINITY ? 0.f : mn;
+      alpha[i] = expf(mrow[i] - base[i]);
+      mrow[i] = mn;
+      lrow[i] *= alpha[i];
+    }
+#pragma unroll
+    for (int nd = 0; nd < NC; nd++) {
+      o[nd][0] *= alpha[0], o[nd][1] *= alpha[0];
+      o[nd][2] *= alpha[1], o[nd][3] *= alpha[1];
+    }
+    // P (split) as A fragments, 16 keys per k-step
+    uint32_t ph[4][4], pl[4][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; nb++) {
+      const float p0 = expf(sc[nb][0] - base[0]), p1 = expf(sc[nb][1] - base[0]);
+      const float p2 = expf(sc[nb][2] - base[1]), p3 = expf(sc[nb][3] - base[1]);
+      lrow[0] += p0 + p1;
+      lrow[1] += p2 + p3;
+      const int kk = nb >> 1, hi = nb & 1;
+      split2(p0, p1, ph[kk][hi * 2 + 0], pl[kk][hi * 2 + 0]);
+      split2(p2, p3, ph[kk][hi * 2 + 1], pl[kk][hi * 2 + 1]);
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++)
+#pragma unroll
+      for (int nd = 0; nd < NC; nd += 2) {
+        const int m = lane >> 3, key = 16 * kk + 8 * (m & 1) + (lane & 7), c = nd + (m >> 1);
+        uint32_t b[4];
+        ldsm_x4_t(b, Vt + ((size_t)c * kFK + key) * 8);
+        mma16816(o[nd], ph[kk], b[0], b[1]);
+        mma16816(o[nd], pl[kk], b[0], b[1]);
+        mma16816(o[nd + 1], ph[kk], b[2], b[3]);
+        mma16816(o[nd + 1], pl[kk], b[2], b[3]);
+      }
+    __syncthreads();  // the buffer is restaged two tiles later
+  }
+  // normalise and store
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    float l = lrow[i];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    lrow[i] = l > 0.f ? 1.f / l : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    if (!rvalid[i]) continue;
+    const int r = warp * 16 + g4 + 8 * i, t = t0 + r / G, gi = r % G;
+    __half *orow = out + ((size_t)t * n_heads + (size_t)(kvh * G + gi)) * HD;
+#pragma unroll
+    for (int nd = 0; nd < NC; nd++)
+      *(uint32_t *)(orow + 8 * nd + 2 * t4) = pack_h2(o[nd][2 * i] * lrow[i], o[nd][2 * i + 1] * lrow[i]);
+  }
+}
+
 }  // namespace
 
 // ---- launchers ------------------------------------------------------------------
@@ -736,18 +901,31 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   g.act = a.act;
   g.ld_act = a.ld_act;
   g.err = a.err;
-  g.raw_tile = (std::max(stage_raw_bytes(a.type_a), stage_raw_bytes(a.type_b)) + 127) & ~127;
-  const int BN = g.pair ? 256 : 128, NDQ = BN / 32;
-  const size_t stage = (size_t)kABytes + (size_t)BN * 128 + (size_t)NDQ * g.raw_tile;
-  const size_t budget = 227 * 1024 - 1024 - 256;  // dynamic smem minus the alignment slack and statics
-  int ns = (int)(budget / stage);
-  if (ns > kMaxStagesTC) ns = kMaxStagesTC;
-  if (ns < 2) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: stage of %zu bytes does not fit", stage);
+  g.spr = std::min(raw_spr(a.type_a), raw_spr(a.type_b));
+  if (raw_spr(a.type_a) != raw_spr(a.type_b))
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: mixed quantized and float tiles");
+  g.raw_tile = (std::max(raw_unit_bytes(a.type_a), raw_unit_bytes(a.type_b)) + 127) & ~127;
+  const int BN = g.pair ? 256 : 128, NT = BN / 32;
+  const size_t ab = (size_t)kABytes + (size_t)BN * 128, rb = (size_t)NT * g.raw_tile;
+  const size_t budget = 227 * 1024 - 1024 - 512;  // dynamic smem minus the alignment slack and statics
+  // (A/B slots, raw slots) in order of preference: two raw units in flight
+  // keep the copy of the next super-block under the decode of this one
+  static const int pref[9][2] = {{4, 3}, {4, 2}, {3, 3}, {3, 2}, {2, 3}, {2, 2}, {4, 1}, {3, 1}, {2, 1}};
+  int ns = 0, rsn = 0;
+  for (const auto &p : pref)
+    if (p[0] * ab + p[1] * rb <= budget) {
+      ns = p[0];
+      rsn = p[1];
+      break;
+    }
+  if (!ns) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: stages do not fit");
   g.nstage = ns;
-  const size_t smem = (size_t)ns * stage + 1024;
+  g.rstage = rsn;
+  const size_t stage = ab;
+  const size_t smem = (size_t)ns * stage + (size_t)rsn * rb + 1024;
   dim3 grid((unsigned)((a.rows + 127) / 128), (unsigned)((a.T + kBM - 1) / kBM));
   if (g.pair) grid.x = (unsigned)((a.rows + 127) / 128);  // rows = FFN rows of one half
-  const dim3 block((unsigned)((NDQ + 2) * 32));
+  const dim3 block((unsigned)((kDQ + 2) * 32));
   void (*kern)(TcArgs, CUtensorMap) = nullptr;
   switch (a.epi) {
     case GB_EPI_PLAIN: kern = gemm_tc_kernel<128, GB_EPI_PLAIN>; break;
@@ -787,6 +965,20 @@ int gb_rope_kv_launch(const float *qkv, int T, int q_rows, int kv_rows, int hd, 
 int gb_attn_prefill_launch(const float *q, int T, int pos0, int n_heads, int n_kv, int hd, const void *kcache,
                            const void *vcache, int kv_f16, int max_len, __half *out, cudaStream_t st) {
   const int G = n_heads / n_kv;
+  if ((hd == 64 || hd == 128) && G <= kFM) {
+    // tensor-core path
+    const int QT = kFM / G;
+    const size_t smem = (size_t)2 * 2 * (hd / 8) * kFK * 16;
+    void (*kern)(const float *, int, int, int, int, const void *, const void *, int, float, __half *) =
+        hd == 64 ? (kv_f16 ? attn_prefill_mma_kernel<true, 64> : attn_prefill_mma_kernel<false, 64>)
+                 : (kv_f16 ? attn_prefill_mma_kernel<true, 128> : attn_prefill_mma_kernel<false, 128>);
+    GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+            "gpu: prefill attention");
+    kern<<<dim3((unsigned)((T + QT - 1) / QT), (unsigned)n_kv), 128, smem, st>>>(
+        q, T, pos0, n_heads, n_kv, kcache, vcache, max_len, 1.f / sqrtf((float)hd), out);
+    GB_CUDA(cudaGetLastError(), "gpu: prefill attention");
+    return GB_OK;
+  }
   if (hd % 32 || hd > 128 || G * kPQ > 16 * 8)
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill attention: head_dim %d, group %d", hd, G);
   const size_t smem = sizeof(float) * ((size_t)2 * kPK * (hd + 1) + (size_t)kPQ * G * hd);
