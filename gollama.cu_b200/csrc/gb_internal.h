@@ -186,6 +186,13 @@ int gb_rope_kv_launch(const float *qkv, int T, int q_rows, int kv_rows, int hd, 
 int gb_attn_prefill_launch(const float *q, int T, int pos0, int n_heads, int n_kv, int hd, const void *kcache,
                            const void *vcache, int kv_f16, int max_len, __half *out, cudaStream_t st);
 
+// gb_paged.cu: batched decode attention through per-sequence page tables.
+size_t gb_paged_part_floats(int B, int n_kv, int S, int G, int hd);
+int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool, int kv_f16, const int32_t *block_table,
+                         const int32_t *seq_lens, int B, int max_pages, int n_pages, int page_size, int n_heads,
+                         int n_kv, int hd, float scale, float *out, float *part, unsigned *counter, int S,
+                         unsigned *err, cudaStream_t st);
+
 // gb_sample.cu: one token from logits[n]; parameters by value (p_host) or
 // from device memory (p_dev, for graph replays); the penalty window is
 // recent[n_recent] or, for the model, fed[pos-N+1..pos]; counter = *pos when

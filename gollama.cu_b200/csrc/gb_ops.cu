@@ -430,6 +430,10 @@ struct gb_kernels {
   size_t ws_floats = 0;
   unsigned *ws_counter = nullptr;
   int ws_nkv = 0;
+  float *pws = nullptr;  // paged attention: split partials + counters
+  size_t pws_floats = 0;
+  unsigned *pws_counter = nullptr;
+  size_t pws_counters = 0;
 };
 
 // The kernel names backend/gpu binds (backend/gpu/gpu.go:24); each has an
@@ -470,6 +474,8 @@ int gb_gpu_close(gb_kernels *k) {
   if (!k) return GB_OK;
   if (k->ws) cudaFree(k->ws);
   if (k->ws_counter) cudaFree(k->ws_counter);
+  if (k->pws) cudaFree(k->pws);
+  if (k->pws_counter) cudaFree(k->pws_counter);
   delete k;
   return GB_OK;
 }
@@ -773,6 +779,46 @@ int gb_gpu_sample(gb_kernels *k, void *stream, const float *logits, int n, const
     return gb_fail(GB_ERR_INVALID, "gpu: sample: bad arguments");
   return gb_sample_launch(logits, n, p, nullptr, recent, n_recent, nullptr, nullptr, 0, counter, out, nullptr,
                           nullptr, (cudaStream_t)stream);
+}
+
+int gb_gpu_attn_decode_paged(gb_kernels *k, void *stream, const float *q, const void *k_pool, const void *v_pool,
+                             int kv_f16, const int32_t *block_table, const int32_t *seq_lens, int batch,
+                             int max_pages, int n_pages, int page_size, int n_heads, int n_kv, int head_dim,
+                             float scale, float *out) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (batch < 0 || max_pages <= 0 || n_pages <= 0 || page_size <= 0 || !q || !k_pool || !v_pool || !block_table ||
+      !seq_lens || !out)
+    return gb_fail(GB_ERR_INVALID, "gpu: paged attention: bad arguments");
+  if (n_kv <= 0 || n_heads % n_kv)
+    return gb_fail(GB_ERR_INVALID, "gpu: paged attention: %d heads is not a multiple of %d KV heads", n_heads, n_kv);
+  if (batch == 0) return GB_OK;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, k->device);
+  // splits of each sequence's positions: about two CTAs per SM in all
+  const long long max_chunks = ((long long)max_pages * page_size + 31) / 32;
+  long long S = (2LL * sms + (long long)n_kv * batch - 1) / ((long long)n_kv * batch);
+  if (S > max_chunks) S = max_chunks;
+  if (S > 32) S = 32;
+  if (S < 1) S = 1;
+  const size_t need = gb_paged_part_floats(batch, n_kv, (int)S, n_heads / n_kv, head_dim);
+  const size_t cnt = (size_t)batch * n_kv;
+  if (need > k->pws_floats || cnt > k->pws_counters) {
+    if (k->pws) cudaFree(k->pws);
+    if (k->pws_counter) cudaFree(k->pws_counter);
+    k->pws = nullptr;
+    k->pws_counter = nullptr;
+    k->pws_floats = k->pws_counters = 0;
+    GB_CUDA(cudaMalloc(&k->pws, need * sizeof(float)), "gpu: paged attention: workspace");
+    GB_CUDA(cudaMalloc(&k->pws_counter, cnt * sizeof(unsigned)), "gpu: paged attention: workspace");
+    GB_CUDA(cudaMemsetAsync(k->pws_counter, 0, cnt * sizeof(unsigned), (cudaStream_t)stream),
+            "gpu: paged attention: workspace");
+    k->pws_floats = need;
+    k->pws_counters = cnt;
+  }
+  return gb_attn_paged_launch(q, k_pool, v_pool, kv_f16, block_table, seq_lens, batch, max_pages, n_pages, page_size,
+                              n_heads, n_kv, head_dim, scale, out, k->pws, k->pws_counter, (int)S, nullptr,
+                              (cudaStream_t)stream);
 }
 
 // model.Argmax, model/model.go:376.

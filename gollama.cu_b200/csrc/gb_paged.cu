@@ -1,0 +1,243 @@
+// gb_paged.cu -- decode attention over a paged KV cache for a batch of
+// sequences (the reference's roadmap "Paged KV cache plus continuous
+// batching ... the attention kernel reads through a page table",
+// ROADMAP.md:197-202; per sequence the arithmetic of cpu.AttnDecode,
+// backend/cpu/cpu.go:140-168, whose GPU twin is (*Kernels).AttnDecode,
+// backend/gpu/gpu.go:118).
+//
+// Pool layout: k_pool / v_pool = [n_pages][n_kv][page_size][head_dim]
+// (binary16 or float32); sequence b's logical page i lives in physical page
+// block_table[b * max_pages + i]; its keys are positions [0, seq_lens[b]).
+// One CTA per (KV head, sequence, split of the pages): eight warps take the
+// split's 32-position chunks in turn, lane = position for the scores of the
+// group's query heads (q in shared memory), then lane = 4 dimensions for
+// P V; online softmax per warp, the warps merged in shared memory, and the
+// splits of a sequence merged by the last CTA to finish (a counter per
+// (sequence, KV head)). float32 arithmetic throughout.
+#include <math.h>
+
+#include "gb_device.cuh"
+#include "gb_internal.h"
+
+namespace {
+
+constexpr int kPW = 8;          // warps per CTA
+constexpr int kPMaxG = 8;       // query heads per KV head
+constexpr int kPMaxHD = 128;    // head_dim
+constexpr int kPDL = kPMaxHD / 32;
+
+template <bool F16>
+GB_DEV float ld_kv(const void *pool, size_t i) {
+  if constexpr (F16) return gb_half_to_float(((const uint16_t *)pool)[i]);
+  else return ((const float *)pool)[i];
+}
+
+// Eight consecutive elements (index a multiple of 8) as float.
+template <bool F16>
+GB_DEV void ld8(const void *pool, size_t i, float *o) {
+  if constexpr (F16) {
+    const uint4 u = *(const uint4 *)((const uint16_t *)pool + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      o[2 * j] = gb_half_to_float((uint16_t)(w[j] & 0xFFFF));
+      o[2 * j + 1] = gb_half_to_float((uint16_t)(w[j] >> 16));
+    }
+  } else {
+    const float4 x = *(const float4 *)((const float *)pool + i), y = *(const float4 *)((const float *)pool + i + 4);
+    o[0] = x.x, o[1] = x.y, o[2] = x.z, o[3] = x.w, o[4] = y.x, o[5] = y.y, o[6] = y.z, o[7] = y.w;
+  }
+}
+
+struct PagedArgs {
+  const float *q;           // [B][n_heads][hd]
+  const void *k_pool, *v_pool;
+  const int32_t *block_table;  // [B][max_pages]
+  const int32_t *seq_lens;     // [B]
+  int B, n_heads, n_kv, hd, page_size, max_pages, n_pages;
+  float scale;
+  float *out;               // [B][n_heads][hd]
+  float *part;              // [B][n_kv][S][G][hd + 2] split partials (m, l, acc)
+  unsigned *counter;        // [B][n_kv], zero between launches
+  int S;                    // splits of the pages
+  unsigned *err;
+};
+
+template <bool F16>
+__global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a) {
+  const int h = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
+  const int G = a.n_heads / a.n_kv, hd = a.hd, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __shared__ float qs[kPMaxG][kPMaxHD];
+  __shared__ float wm[kPW][kPMaxG], wl[kPW][kPMaxG];
+  __shared__ float wacc[kPW][kPMaxG][kPMaxHD];
+  __shared__ unsigned last;
+  const int L = a.seq_lens[b];
+  for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
+    qs[i / hd][i % hd] = a.q[((size_t)b * a.n_heads + (size_t)h * G + i / hd) * hd + i % hd];
+  __syncthreads();
+  // this split's 32-position chunks: [c0, c1)
+  const int nchunk = (L + 31) / 32;
+  const int c0 = (int)((long long)nchunk * sp / a.S), c1 = (int)((long long)nchunk * (sp + 1) / a.S);
+  float m[kPMaxG], l[kPMaxG], acc[kPMaxG][kPDL];
+#pragma unroll
+  for (int g = 0; g < kPMaxG; g++) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int d = 0; d < kPDL; d++) acc[g][d] = 0.f;
+  }
+  const int DL = hd / 32;
+  for (int ch = c0 + warp; ch < c1; ch += kPW) {
+    const int p = ch * 32 + lane;  // this lane's position
+    const bool in = p < L;
+    size_t krow = 0;
+    if (in) {
+      const int lp = p / a.page_size, off = p % a.page_size;
+      int phys = a.block_table[(size_t)b * a.max_pages + lp];
+      if (phys < 0 || phys >= a.n_pages) {
+        if (a.err) atomicOr(a.err, GB_DEVERR_POS);
+        phys = 0;
+      }
+      krow = (((size_t)phys * a.n_kv + h) * a.page_size + off) * hd;
+    }
+    float s[kPMaxG];
+#pragma unroll
+    for (int g = 0; g < kPMaxG; g++) s[g] = 0.f;
+    if (in)
+      for (int d0 = 0; d0 < hd; d0 += 8) {  // this lane's key row, 8 dimensions a load
+        float kv[8];
+        ld8<F16>(a.k_pool, krow + d0, kv);
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+#pragma unroll
+          for (int g = 0; g < kPMaxG; g++)
+            if (g < G) s[g] = fmaf(qs[g][d0 + e], kv[e], s[g]);
+      }
+#pragma unroll
+    for (int g = 0; g < kPMaxG; g++) {
+      if (g >= G) break;
+      const float sv = in ? s[g] * a.scale : -INFINITY;
+      const float mn = fmaxf(m[g], gb_warp_max(sv));
+      const float alpha = expf(m[g] - mn), pe = in ? expf(sv - mn) : 0.f;
+      l[g] = l[g] * alpha + gb_warp_sum(pe);
+      m[g] = mn;
+#pragma unroll
+      for (int d = 0; d < kPDL; d++) acc[g][d] *= alpha;
+      s[g] = pe;
+    }
+    // P V: lane holds dimensions lane + 32 i
+    for (int j = 0; j < 32; j++) {
+      const int pj = ch * 32 + j;
+      if (pj >= L) break;
+      const int lp = pj / a.page_size, off = pj % a.page_size;
+      int phys = a.block_table[(size_t)b * a.max_pages + lp];
+      phys = (phys < 0 || phys >= a.n_pages) ? 0 : phys;
+      const size_t vrow = (((size_t)phys * a.n_kv + h) * a.page_size + off) * hd;
+      float vv[kPDL];
+#pragma unroll
+      for (int d = 0; d < kPDL; d++) vv[d] = d < DL ? ld_kv<F16>(a.v_pool, vrow + lane + 32 * d) : 0.f;
+#pragma unroll
+      for (int g = 0; g < kPMaxG; g++) {
+        if (g >= G) break;
+        const float pg = __shfl_sync(0xffffffffu, s[g], j);
+#pragma unroll
+        for (int d = 0; d < kPDL; d++) acc[g][d] = fmaf(pg, vv[d], acc[g][d]);
+      }
+    }
+  }
+  // merge the warps (in warp order)
+#pragma unroll
+  for (int g = 0; g < kPMaxG; g++) {
+    if (g >= G) break;
+    if (lane == 0) {
+      wm[warp][g] = m[g];
+      wl[warp][g] = l[g];
+    }
+#pragma unroll
+    for (int d = 0; d < kPDL; d++)
+      if (d < DL) wacc[warp][g][lane + 32 * d] = acc[g][d];
+  }
+  __syncthreads();
+  float *dst = a.part + (((size_t)b * a.n_kv + h) * a.S + sp) * G * (hd + 2);
+  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+    const int g = i / hd, d = i % hd;
+    float M = -INFINITY;
+    for (int w = 0; w < kPW; w++) M = fmaxf(M, wm[w][g]);
+    float Lsum = 0.f, A = 0.f;
+    for (int w = 0; w < kPW; w++) {
+      const float f = wm[w][g] == -INFINITY ? 0.f : expf(wm[w][g] - M);
+      Lsum += wl[w][g] * f;
+      A += wacc[w][g][d] * f;
+    }
+    dst[(size_t)g * (hd + 2) + 2 + d] = A;
+    if (d == 0) {
+      dst[(size_t)g * (hd + 2)] = M;
+      dst[(size_t)g * (hd + 2) + 1] = Lsum;
+    }
+  }
+  // the last split of (sequence, KV head) merges the splits (in split order)
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(a.counter + (size_t)b * a.n_kv + h, 1u) == (unsigned)(a.S - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const float *src = a.part + ((size_t)b * a.n_kv + h) * a.S * G * (hd + 2);
+  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+    const int g = i / hd, d = i % hd;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < a.S; s2++) M = fmaxf(M, __ldcg(src + ((size_t)s2 * G + g) * (hd + 2)));
+    float Lsum = 0.f, A = 0.f;
+    for (int s2 = 0; s2 < a.S; s2++) {
+      const float *ps = src + ((size_t)s2 * G + g) * (hd + 2);
+      const float ms = __ldcg(ps);
+      const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+      Lsum += __ldcg(ps + 1) * f;
+      A += __ldcg(ps + 2 + d) * f;
+    }
+    a.out[((size_t)b * a.n_heads + (size_t)h * G + g) * hd + d] = Lsum > 0.f ? A / Lsum : 0.f;
+  }
+  if (threadIdx.x == 0) a.counter[(size_t)b * a.n_kv + h] = 0u;  // ready for the next launch
+}
+
+}  // namespace
+
+size_t gb_paged_part_floats(int B, int n_kv, int S, int G, int hd) {
+  return (size_t)B * n_kv * S * G * (hd + 2);
+}
+
+int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool, int kv_f16, const int32_t *block_table,
+                         const int32_t *seq_lens, int B, int max_pages, int n_pages, int page_size, int n_heads,
+                         int n_kv, int hd, float scale, float *out, float *part, unsigned *counter, int S,
+                         unsigned *err, cudaStream_t st) {
+  if (B <= 0) return GB_OK;
+  if (n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > kPMaxG || hd % 32 || hd > kPMaxHD || page_size <= 0)
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: paged attention: %d heads, %d KV heads, head_dim %d, page %d", n_heads,
+                   n_kv, hd, page_size);
+  PagedArgs a;
+  a.q = q;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.block_table = block_table;
+  a.seq_lens = seq_lens;
+  a.B = B;
+  a.n_heads = n_heads;
+  a.n_kv = n_kv;
+  a.hd = hd;
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.n_pages = n_pages;
+  a.scale = scale;
+  a.out = out;
+  a.part = part;
+  a.counter = counter;
+  a.S = S;
+  a.err = err;
+  const dim3 grid((unsigned)n_kv, (unsigned)B, (unsigned)S);
+  if (kv_f16)
+    attn_paged_kernel<true><<<grid, kPW * 32, 0, st>>>(a);
+  else
+    attn_paged_kernel<false><<<grid, kPW * 32, 0, st>>>(a);
+  GB_CUDA(cudaGetLastError(), "gpu: paged attention");
+  return GB_OK;
+}

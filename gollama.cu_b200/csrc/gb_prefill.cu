@@ -109,6 +109,8 @@ GB_DEV uint8_t byte_of(const uint4 &v, int i) {
 
 // Exact small integer n (0 <= n < 2^23) as float without the conversion unit.
 GB_DEV float u2f(uint32_t n) { return __fsub_rn(__uint_as_float(0x4B000000u | n), 8388608.f); }
+// Byte i of w as the float 2^23 + byte (its bit pattern 0x4B0000bb).
+GB_DEV float magic_byte(uint32_t w, int i) { return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540 + i)); }
 
 // Q4_K scale and min of sub-block j from the 12 scale bytes (bytes 4..15 of
 // the block's first unit): quant.ScaleMinQ4K, quant/quant.go:90, in registers.
@@ -123,15 +125,29 @@ GB_DEV void q4k_scale_reg(const uint4 &h, int j, uint32_t &sc, uint32_t &m) {
   }
 }
 
+// Eight values v = (b - off) * d (+ c) of the bytes of w0, w1 (b small
+// integers), from their magic-number floats: one byte permute, one add and one
+// multiply (or fused multiply-add) per value.
+GB_DEV void bytes8_scaled(uint32_t w0, uint32_t w1, float off, float d, float c, bool fused, float *v) {
+  const float k = -8388608.f - off;  // exact: 2^23 + off needs 24 bits at most
+#pragma unroll
+  for (int e = 0; e < 8; e++) {
+    const float q = __fadd_rn(magic_byte(e < 4 ? w0 : w1, e & 3), k);
+    v[e] = fused ? __fmaf_rn(d, q, c) : __fmul_rn(d, q);
+  }
+}
+
 // Decode output chunk c (elements 8c..8c+7) of K-stage kc of row `lane` of
 // one tile, as eight binary16 values, from the tile's whole sb-block
-// (quantized types) or from the stage's piece of it (float types): the
-// reference's float32 element values (quant/quant.go:44-132) rounded to
-// nearest even.
+// (quantized types) or from the stage's piece of it (float types). The values
+// are the reference's element values (quant/quant.go:44-132) in float32,
+// rounded to binary16; Q4_K's (d*sc)*q - dmin*m is formed with one fused
+// rounding instead of two (at most one float32 ulp apart, below the
+// binary16 rounding that follows).
 GB_DEV uint4 dequant_chunk(int typ, int kc, const uint8_t *raw, int lane, int c) {
   float v[8];
   switch (typ) {
-    case GB_T_Q4_K: {  // (d*sc)*q - dmin*m
+    case GB_T_Q4_K: {
       const uint4 h = lds16(raw + lane * 16);
       const int hi = c >> 2, b0 = (c & 3) * 8;
       const uint4 q = lds16(raw + 512 * (1 + 2 * kc + (b0 >> 4)) + lane * 16);
@@ -139,12 +155,10 @@ GB_DEV uint4 dequant_chunk(int typ, int kc, const uint8_t *raw, int lane, int c)
       uint32_t sc, m;
       q4k_scale_reg(h, 2 * kc + hi, sc, m);
       const float ds = __fmul_rn(d, u2f(sc)), dm = __fmul_rn(dmin, u2f(m));
-      const uint32_t w0 = (b0 & 15) ? q.z : q.x, w1 = (b0 & 15) ? q.w : q.y;
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const uint32_t by = ((e < 4 ? w0 : w1) >> (8 * (e & 3))) & 0xFFu;
-        v[e] = __fsub_rn(__fmul_rn(ds, u2f(hi ? by >> 4 : by & 0xFu)), dm);
-      }
+      uint32_t w0 = (b0 & 15) ? q.z : q.x, w1 = (b0 & 15) ? q.w : q.y;
+      w0 = (hi ? w0 >> 4 : w0) & 0x0F0F0F0Fu;
+      w1 = (hi ? w1 >> 4 : w1) & 0x0F0F0F0Fu;
+      bytes8_scaled(w0, w1, 0.f, ds, -dm, true, v);
       break;
     }
     case GB_T_Q4_0: {  // d*(q-8)
@@ -152,25 +166,19 @@ GB_DEV uint4 dequant_chunk(int typ, int kc, const uint8_t *raw, int lane, int c)
       const int b = c >> 2, k = 2 * kc + b, cc = c & 3;
       const float d = gb_half_to_float((uint16_t)(byte_of(dd, 2 * k) | byte_of(dd, 2 * k + 1) << 8));
       const uint4 q = lds16(raw + 512 * (1 + k) + lane * 16);
-      const uint32_t w0 = (cc & 1) ? q.z : q.x, w1 = (cc & 1) ? q.w : q.y;
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const uint32_t by = ((e < 4 ? w0 : w1) >> (8 * (e & 3))) & 0xFFu;
-        v[e] = __fmul_rn(d, __fsub_rn(u2f(cc >= 2 ? by >> 4 : by & 0xFu), 8.f));
-      }
+      uint32_t w0 = (cc & 1) ? q.z : q.x, w1 = (cc & 1) ? q.w : q.y;
+      w0 = (cc >= 2 ? w0 >> 4 : w0) & 0x0F0F0F0Fu;
+      w1 = (cc >= 2 ? w1 >> 4 : w1) & 0x0F0F0F0Fu;
+      bytes8_scaled(w0, w1, 8.f, d, 0.f, false, v);
       break;
     }
-    case GB_T_Q8_0: {  // d*q
+    case GB_T_Q8_0: {  // d*q: int8 q as the unsigned byte q+128
       const uint4 dd = lds16(raw + lane * 16);
       const int b = c >> 2, k = 2 * kc + b, u = (c >> 1) & 1, hlf = c & 1;
       const float d = gb_half_to_float((uint16_t)(byte_of(dd, 2 * k) | byte_of(dd, 2 * k + 1) << 8));
       const uint4 q = lds16(raw + 512 * (1 + 2 * k + u) + lane * 16);
-      const uint32_t w0 = hlf ? q.z : q.x, w1 = hlf ? q.w : q.y;
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const int by = (int)(int8_t)(((e < 4 ? w0 : w1) >> (8 * (e & 3))) & 0xFFu);
-        v[e] = __fmul_rn(d, (float)by);
-      }
+      const uint32_t w0 = (hlf ? q.z : q.x) ^ 0x80808080u, w1 = (hlf ? q.w : q.y) ^ 0x80808080u;
+      bytes8_scaled(w0, w1, 128.f, d, 0.f, false, v);
       break;
     }
     case GB_T_Q6_K: {  // d*sc*(q-32)
@@ -183,16 +191,13 @@ GB_DEV uint4 dequant_chunk(int typ, int kc, const uint8_t *raw, int lane, int c)
       const uint4 H = lds16(qh + (l0 >> 4) * 512 + lane * 16);
       const int scv = (int)(int8_t)byte_of(s4, cq * 8 + 2 * quarter + (l0 >> 4));
       const float dsc = __fmul_rn(d, (float)scv);
-      const uint32_t l0w = (qlb & 15) ? L.z : L.x, l1w = (qlb & 15) ? L.w : L.y;
-      const uint32_t h0w = (l0 & 15) ? H.z : H.x, h1w = (l0 & 15) ? H.w : H.y;
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const uint32_t lb = ((e < 4 ? l0w : l1w) >> (8 * (e & 3))) & 0xFFu;
-        const uint32_t hb = ((e < 4 ? h0w : h1w) >> (8 * (e & 3))) & 0xFFu;
-        const uint32_t lo = quarter >= 2 ? (lb >> 4) : (lb & 0xFu);
-        const uint32_t qv = lo | (((hb >> (2 * quarter)) & 3u) << 4);
-        v[e] = __fmul_rn(dsc, __fsub_rn(u2f(qv), 32.f));
-      }
+      uint32_t l0w = (qlb & 15) ? L.z : L.x, l1w = (qlb & 15) ? L.w : L.y;
+      uint32_t h0w = (l0 & 15) ? H.z : H.x, h1w = (l0 & 15) ? H.w : H.y;
+      const int sh = 2 * quarter;
+      l0w = (quarter >= 2 ? l0w >> 4 : l0w) & 0x0F0F0F0Fu;
+      l1w = (quarter >= 2 ? l1w >> 4 : l1w) & 0x0F0F0F0Fu;
+      const uint32_t q0 = l0w | (((h0w >> sh) & 0x03030303u) << 4), q1 = l1w | (((h1w >> sh) & 0x03030303u) << 4);
+      bytes8_scaled(q0, q1, 32.f, dsc, 0.f, false, v);
       break;
     }
     case GB_T_F16:
@@ -234,6 +239,7 @@ struct TcArgs {
   int ldy;
   __half *act;            // SWIGLU: act[T][ld_act] = silu(g) * u
   int ld_act;
+  int mt;                 // 128-token tiles per CTA (one TMEM accumulator each)
   int nstage;             // A/B ring slots (one K-stage each)
   int rstage;             // raw ring slots (one raw unit each)
   int spr;                // K-stages per raw unit (4: quantized types, 1: float types)
@@ -273,13 +279,14 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
   __shared__ uint32_t tmem_base;
   __shared__ int bad;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NS = g.nstage, RS = g.rstage, SPR = g.spr;
+  const int NS = g.nstage, RS = g.rstage, SPR = g.spr, MT = g.mt;
   const int nk = g.nsb * 4;                 // K stages
-  const int m0 = blockIdx.y * kBM;          // first token row
+  const int m0 = blockIdx.y * kBM * MT;     // first token row
+  const int ABytes = kABytes * MT;          // the stage's activation tiles
   const int tile0 = blockIdx.x * 4;         // first weight tile (of each half for pairs)
   // [NS] A tiles | [NS] B tiles (1024-aligned) | [RS][NT] raw units
   uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t *A0 = base, *B0 = base + (size_t)NS * kABytes, *R0 = B0 + (size_t)NS * BBytes;
+  uint8_t *A0 = base, *B0 = base + (size_t)NS * ABytes, *R0 = B0 + (size_t)NS * BBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; s++) {
@@ -296,7 +303,7 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
     gb_mbar_fence_init();
   }
   if (warp == NDQ + 1) {
-    tmem_alloc(&tmem_base, BN);
+    tmem_alloc(&tmem_base, (uint32_t)(BN * MT));
     tmem_relinquish();
   }
   tc_fence_before();
@@ -344,8 +351,9 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
           if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
           break;
         }
-        gb_mbar_expect_tx(&afull[s], kABytes);
-        tma_load_2d(A0 + (size_t)s * kABytes, &tmap_a, k * kBK, m0, &afull[s]);
+        gb_mbar_expect_tx(&afull[s], (uint32_t)ABytes);
+        for (int mt = 0; mt < MT; mt++)
+          tma_load_2d(A0 + (size_t)s * ABytes + (size_t)mt * kABytes, &tmap_a, k * kBK, m0 + mt * kBM, &afull[s]);
         a_issued = k + 1;
       }
       // copies still in flight land (bounded) before the CTA exits
@@ -365,11 +373,13 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
           break;
         }
         tc_fence_after();
-        const uint64_t ad = sdesc_sw128(gb_smem_u32(A0 + (size_t)s * kABytes));
         const uint64_t bd = sdesc_sw128(gb_smem_u32(B0 + (size_t)s * BBytes));
+        for (int mt = 0; mt < MT; mt++) {
+          const uint64_t ad = sdesc_sw128(gb_smem_u32(A0 + (size_t)s * ABytes + (size_t)mt * kABytes));
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; kk++)  // K = 16 per instruction: +32 bytes in the swizzled row
-          mma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (k | kk) != 0);
+          for (int kk = 0; kk < kBK / 16; kk++)  // K = 16 per instruction: +32 bytes in the swizzled row
+            mma_f16(tmem + (uint32_t)(mt * BN), ad + 2 * kk, bd + 2 * kk, idesc, (k | kk) != 0);
+        }
         mma_commit(&empty[s]);  // the slot is free once these MMAs have read it
       }
       mma_commit(&accf);  // all issued MMAs done (also after an early stop)
@@ -413,8 +423,9 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
       if (lane == 0 && g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
     } else if (!bad) {
       const int quarter = warp & 3, cq = warp >> 2;
-      const int m = m0 + quarter * 32 + lane;
-      const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+      for (int mt = 0; mt < MT; mt++) {
+      const int m = m0 + mt * kBM + quarter * 32 + lane;
+      const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mt * BN);
       if constexpr (EPI == GB_EPI_SWIGLU) {
         for (int cc = cq * 32; cc < cq * 32 + 32; cc += 16) {
           float gv[16], uv[16];
@@ -459,13 +470,14 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
           }
         }
       }
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == NDQ + 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, (uint32_t)(BN * MT));
   }
 }
 
@@ -906,7 +918,19 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: mixed quantized and float tiles");
   g.raw_tile = (std::max(raw_unit_bytes(a.type_a), raw_unit_bytes(a.type_b)) + 127) & ~127;
   const int BN = g.pair ? 256 : 128, NT = BN / 32;
-  const size_t ab = (size_t)kABytes + (size_t)BN * 128, rb = (size_t)NT * g.raw_tile;
+  // token tiles per CTA: one decode of a weight stage feeds MT MMAs; more
+  // tiles per CTA mean fewer CTAs. Pick MT minimising waves x (decode + MT),
+  // the decode of a stage costing about two MMA groups.
+  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + 127) / 128, mt_max = g.pair ? 2 : 4;
+  int mt = 1;
+  double best = 1e30;
+  for (int c = 1; c <= mt_max && c <= std::max(1, mtiles); c *= 2) {
+    const long long ctas = (long long)ntn * ((mtiles + c - 1) / c);
+    const double cost = (double)((ctas + 147) / 148) * (2.0 + c);
+    if (cost < best - 1e-9) best = cost, mt = c;
+  }
+  g.mt = mt;
+  const size_t ab = (size_t)kABytes * mt + (size_t)BN * 128, rb = (size_t)NT * g.raw_tile;
   const size_t budget = 227 * 1024 - 1024 - 512;  // dynamic smem minus the alignment slack and statics
   // (A/B slots, raw slots) in order of preference: two raw units in flight
   // keep the copy of the next super-block under the decode of this one
@@ -923,7 +947,7 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   g.rstage = rsn;
   const size_t stage = ab;
   const size_t smem = (size_t)ns * stage + (size_t)rsn * rb + 1024;
-  dim3 grid((unsigned)((a.rows + 127) / 128), (unsigned)((a.T + kBM - 1) / kBM));
+  dim3 grid((unsigned)((a.rows + 127) / 128), (unsigned)((a.T + kBM * mt - 1) / (kBM * mt)));
   if (g.pair) grid.x = (unsigned)((a.rows + 127) / 128);  // rows = FFN rows of one half
   const dim3 block((unsigned)((kDQ + 2) * 32));
   void (*kern)(TcArgs, CUtensorMap) = nullptr;

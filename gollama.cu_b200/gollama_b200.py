@@ -86,6 +86,7 @@ _SIGS = {
     "gb_gpu_matvec_q": (I, [P, P, I, P, P, P, I, I, I]), "gb_gpu_ones": (I, [I, C.POINTER(P)]),
     "gb_free": (I, [P]), "gb_gpu_dequant_rows": (I, [P, P, I, P, I, I, I, I, P]),
     "gb_gpu_argmax": (I, [P, P, P, I, P]), "gb_gpu_sample": (I, [P, P, P, I, P, P, I, U64, P]),
+    "gb_gpu_attn_decode_paged": (I, [P, P, P, P, P, I, P, P, I, I, I, I, I, I, I, F, P]),
     "gb_model_set_sampler": (I, [P, P]), "gb_model_prefill": (I, [P, P, I, I, P]),
     "gb_linear_matmul_f16": (I, [P, P, P, I, P]),
     "gb_linear_upload": (I, [I, I, P, S, I, I, C.POINTER(P)]), "gb_linear_matvec": (I, [P, P, P, P]),
@@ -231,6 +232,12 @@ class Kernels:
 
     def argmax(self, x, n, out, stream=None):
         _check(lib().gb_gpu_argmax(self.h, _stream(stream), _ptr(x), n, _ptr(out)))
+
+    def attn_decode_paged(self, q, k_pool, v_pool, kv_f16, block_table, seq_lens, batch, max_pages, n_pages,
+                          page_size, n_heads, n_kv, head_dim, scale, out, stream=None):
+        _check(lib().gb_gpu_attn_decode_paged(self.h, _stream(stream), _ptr(q), _ptr(k_pool), _ptr(v_pool),
+                                              int(kv_f16), _ptr(block_table), _ptr(seq_lens), batch, max_pages,
+                                              n_pages, page_size, n_heads, n_kv, head_dim, scale, _ptr(out)))
 
     def sample(self, logits, n, params: SampleParams, recent, n_recent, counter, out, stream=None):
         _check(lib().gb_gpu_sample(self.h, _stream(stream), _ptr(logits), n, C.byref(params),

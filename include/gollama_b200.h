@@ -93,6 +93,20 @@ int gb_gpu_attn_decode(gb_kernels *k, void *stream, const float *q, const float 
 int gb_gpu_attn_decode_noalloc(gb_kernels *k, void *stream, const float *q, const float *kcache,
                                const float *vcache, float *out, int kv_len, int n_heads, int n_kv,
                                int head_dim, float scale);
+/* Added (the reference's roadmap "Paged KV cache plus continuous batching",
+ * ROADMAP.md:197-202): decode attention for `batch` sequences whose K/V live
+ * in pages of a shared pool, k_pool / v_pool = [n_pages][n_kv][page_size]
+ * [head_dim] (binary16 when kv_f16, else float32). Sequence b attends over
+ * positions [0, seq_lens[b]); position p is row p % page_size of physical
+ * page block_table[b * max_pages + p / page_size] (entries outside
+ * [0, n_pages) read page 0). q and out are [batch][n_heads][head_dim]
+ * float32; per sequence the arithmetic of AttnDecode. head_dim <= 128 and a
+ * multiple of 32, at most 8 query heads per KV head. Scratch lives in `k`
+ * (grown on demand); calls on `k` must not overlap on the GPU. */
+int gb_gpu_attn_decode_paged(gb_kernels *k, void *stream, const float *q, const void *k_pool, const void *v_pool,
+                             int kv_f16, const int32_t *block_table, const int32_t *seq_lens, int batch,
+                             int max_pages, int n_pages, int page_size, int n_heads, int n_kv, int head_dim,
+                             float scale, float *out);
 /* (*Kernels).MatVecF16, backend/gpu/gpu.go:126: y[b] = W x[b]. */
 int gb_gpu_matvec_f16(gb_kernels *k, void *stream, const uint16_t *w, const float *x, float *y,
                       int rows, int cols, int batch);
