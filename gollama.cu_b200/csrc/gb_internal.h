@@ -173,8 +173,15 @@ struct GbTcGemm {
   __half *act = nullptr;
   int ld_act = 0;
   unsigned *err = nullptr;
+  float *part = nullptr;       // split-K partials (may be null: no split)
+  size_t part_floats = 0;
   CUtensorMap tmap_a;
 };
+struct GbTcPlan {
+  int mt = 1, splits = 1;
+  size_t part_floats = 0;
+};
+GbTcPlan gb_tc_gemm_plan(const GbTcGemm &a, int sms);
 int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map);
 int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st);
 int gb_embed_rows_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *tokens, int T, int vocab,

@@ -142,6 +142,8 @@ struct gb_linear {
   Tiled t;
   float *part = nullptr;
   unsigned *tile_counter = nullptr;
+  float *mm_part = nullptr;  // split-K partials of matmul_f16 (grown on demand)
+  size_t mm_part_floats = 0;
 };
 
 struct gb_model {
@@ -173,6 +175,8 @@ struct gb_model {
   float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr;
   __half *pf_a16 = nullptr, *pf_act16 = nullptr;
   int32_t *pf_tokens = nullptr;
+  float *pf_part = nullptr;  // split-K partials of the prefill GEMMs
+  size_t pf_part_floats = 0;
   CUtensorMap pf_map_dim, pf_map_q, pf_map_ffn;
   unsigned *err = nullptr;
   float *gemv_part = nullptr;
@@ -894,6 +898,10 @@ int prefill_workspace(gb_model *m) {
       (rc = dalloc(m, &m->pf_act16, (size_t)Tc * m->ffn_local, "model: prefill workspace")) ||
       (rc = dalloc(m, &m->pf_tokens, (size_t)Tc, "model: prefill workspace")))
     return rc;
+  // split-K partials: a plan never has more CTAs with partials than SMs, each
+  // at most 4 token tiles x 128 columns (or 2 x 256 for the gate/up pairs)
+  m->pf_part_floats = (size_t)m->sms * 4 * 128 * 128;
+  if ((rc = dalloc(m, &m->pf_part, m->pf_part_floats, "model: prefill workspace"))) return rc;
   if ((rc = gb_tmap_f16_rows(m->pf_a16, Tc, c.dim, &m->pf_map_dim)) ||
       (rc = gb_tmap_f16_rows(m->pf_a16, Tc, m->q_local, &m->pf_map_q)) ||
       (rc = gb_tmap_f16_rows(m->pf_act16, Tc, m->ffn_local, &m->pf_map_ffn)))
@@ -913,6 +921,8 @@ GbTcGemm tc_args(const Tiled &t, int epi, int T, const CUtensorMap &map, gb_mode
   g.epi = epi;
   g.T = T;
   g.err = m->err;
+  g.part = m->pf_part;
+  g.part_floats = m->pf_part_floats;
   g.tmap_a = map;
   return g;
 }
@@ -1084,6 +1094,19 @@ int gb_linear_matmul_f16(gb_linear *l, void *stream, const uint16_t *x, int T, f
   g.ldy = l->t.rows;
   int rc = gb_tmap_f16_rows(x, T, l->t.cols, &g.tmap_a);
   if (rc) return rc;
+  const GbTcPlan plan = gb_tc_gemm_plan(g, 148);
+  if (plan.part_floats > l->mm_part_floats) {
+    // the first call (or a larger T) grows the split-K scratch; the device
+    // is synchronized first, as a previous launch may still read the old one
+    GB_CUDA(cudaDeviceSynchronize(), "model: linear: matmul scratch");
+    if (l->mm_part) cudaFree(l->mm_part);
+    l->mm_part = nullptr;
+    l->mm_part_floats = 0;
+    GB_CUDA(cudaMalloc(&l->mm_part, plan.part_floats * sizeof(float)), "model: linear: matmul scratch");
+    l->mm_part_floats = plan.part_floats;
+  }
+  g.part = l->mm_part;
+  g.part_floats = l->mm_part_floats;
   return gb_tc_gemm_launch(g, (cudaStream_t)stream);
 }
 
@@ -1268,6 +1291,7 @@ static void free_linear(gb_linear *l) {
   if (l->t.w) cudaFree(l->t.w);
   if (l->part) cudaFree(l->part);
   if (l->tile_counter) cudaFree(l->tile_counter);
+  if (l->mm_part) cudaFree(l->mm_part);
   delete l;
 }
 

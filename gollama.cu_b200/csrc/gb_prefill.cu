@@ -240,6 +240,8 @@ struct TcArgs {
   __half *act;            // SWIGLU: act[T][ld_act] = silu(g) * u
   int ld_act;
   int mt;                 // 128-token tiles per CTA (one TMEM accumulator each)
+  int splits;             // K split over gridDim.z (> 1: fp32 partials to `part`, reduced by splitk_reduce)
+  float *part;
   int nstage;             // A/B ring slots (one K-stage each)
   int rstage;             // raw ring slots (one raw unit each)
   int spr;                // K-stages per raw unit (4: quantized types, 1: float types)
@@ -280,7 +282,9 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
   __shared__ int bad;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NS = g.nstage, RS = g.rstage, SPR = g.spr, MT = g.mt;
-  const int nk = g.nsb * 4;                 // K stages
+  // this CTA's K stages [k0, k0 + nkl): whole raw units of split blockIdx.z
+  const int nu = g.nsb * 4 / SPR, u0 = nu * (int)blockIdx.z / g.splits, u1 = nu * ((int)blockIdx.z + 1) / g.splits;
+  const int k0 = u0 * SPR, nkl = (u1 - u0) * SPR;
   const int m0 = blockIdx.y * kBM * MT;     // first token row
   const int ABytes = kABytes * MT;          // the stage's activation tiles
   const int tile0 = blockIdx.x * 4;         // first weight tile (of each half for pairs)
@@ -316,9 +320,10 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
     // per K-stage the activation tile by TMA
     if (lane == 0) {
       int a_issued = 0, r_issued = 0;
-      for (int k = 0; k < nk; k++) {
-        if (k % SPR == 0) {
-          const int r = k / SPR, rs = r % RS;
+      for (int kl = 0; kl < nkl; kl++) {
+        const int k = k0 + kl;
+        if (kl % SPR == 0) {
+          const int r = kl / SPR, rs = r % RS;
           if (r >= RS && !gb_mbar_wait(&rempty[rs], ((r / RS) - 1) & 1)) {
             bad = 1;
             if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
@@ -345,8 +350,8 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
           }
           r_issued = r + 1;
         }
-        const int s = k % NS;
-        if (k >= NS && !gb_mbar_wait(&empty[s], ((k / NS) - 1) & 1)) {
+        const int s = kl % NS;
+        if (kl >= NS && !gb_mbar_wait(&empty[s], ((kl / NS) - 1) & 1)) {
           bad = 1;
           if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
           break;
@@ -354,7 +359,7 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
         gb_mbar_expect_tx(&afull[s], (uint32_t)ABytes);
         for (int mt = 0; mt < MT; mt++)
           tma_load_2d(A0 + (size_t)s * ABytes + (size_t)mt * kABytes, &tmap_a, k * kBK, m0 + mt * kBM, &afull[s]);
-        a_issued = k + 1;
+        a_issued = kl + 1;
       }
       // copies still in flight land (bounded) before the CTA exits
       for (int j = a_issued > NS ? a_issued - NS : 0; j < a_issued; j++) (void)gb_mbar_wait(&afull[j % NS], (j / NS) & 1);
@@ -364,9 +369,9 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
     // MMA issue: one thread
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(kBM, BN);
-      for (int k = 0; k < nk; k++) {
-        const int s = k % NS;
-        const uint32_t ph = (k / NS) & 1;
+      for (int kl = 0; kl < nkl; kl++) {
+        const int s = kl % NS;
+        const uint32_t ph = (kl / NS) & 1;
         if (!gb_mbar_wait(&afull[s], ph) || !gb_mbar_wait(&bfull[s], ph)) {
           bad = 1;
           if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
@@ -378,7 +383,7 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
           const uint64_t ad = sdesc_sw128(gb_smem_u32(A0 + (size_t)s * ABytes + (size_t)mt * kABytes));
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; kk++)  // K = 16 per instruction: +32 bytes in the swizzled row
-            mma_f16(tmem + (uint32_t)(mt * BN), ad + 2 * kk, bd + 2 * kk, idesc, (k | kk) != 0);
+            mma_f16(tmem + (uint32_t)(mt * BN), ad + 2 * kk, bd + 2 * kk, idesc, (kl | kk) != 0);
         }
         mma_commit(&empty[s]);  // the slot is free once these MMAs have read it
       }
@@ -390,11 +395,11 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
     const int up = g.pair && j >= 4, tile = tile0 + (g.pair ? (j & 3) : j);
     const bool valid = tile < g.ntiles;
     const int rB = j * 32 + lane, sw = lane & 7;  // B row; its 128-byte swizzle phase
-    for (int k = 0; k < nk; k++) {
-      const int s = k % NS, r = k / SPR, rs = r % RS;
+    for (int kl = 0; kl < nkl; kl++) {
+      const int k = k0 + kl, s = kl % NS, r = kl / SPR, rs = r % RS;
       // the raw unit has landed; the B slot's previous MMAs are done
-      if ((k % SPR == 0 && !gb_mbar_wait(&rfull[rs], (r / RS) & 1)) ||
-          (k >= NS && !gb_mbar_wait(&empty[s], ((k / NS) - 1) & 1))) {
+      if ((kl % SPR == 0 && !gb_mbar_wait(&rfull[rs], (r / RS) & 1)) ||
+          (kl >= NS && !gb_mbar_wait(&empty[s], ((kl / NS) - 1) & 1))) {
         if (lane == 0 && g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
         bad = 1;
         break;
@@ -412,7 +417,7 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
       __syncwarp();
       if (lane == 0) {
         gb_mbar_arrive(&bfull[s]);
-        if (k % SPR == SPR - 1 || k == nk - 1) gb_mbar_arrive(&rempty[rs]);
+        if (kl % SPR == SPR - 1) gb_mbar_arrive(&rempty[rs]);
       }
     }
     // epilogue: accumulators -> registers -> global. Warp w reads TMEM lanes
@@ -421,6 +426,21 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
     tc_fence_after();
     if (!ok) {
       if (lane == 0 && g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
+    } else if (!bad && g.splits > 1) {
+      // this split's fp32 partial of the tile: [MT*128 token rows][BN columns]
+      const int quarter = warp & 3, cq = warp >> 2;
+      float *pt = g.part + (((size_t)blockIdx.y * gridDim.x + blockIdx.x) * g.splits + blockIdx.z) * (size_t)(MT * kBM) * BN;
+      for (int mt = 0; mt < MT; mt++) {
+        const int rl = mt * kBM + quarter * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mt * BN);
+        for (int cc = cq * (BN / 4); cc < (cq + 1) * (BN / 4); cc += 16) {
+          float v[16];
+          tmem_ld16(trow + cc, v);
+          float *dst = pt + (size_t)rl * BN + cc;
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) *(float4 *)(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        }
+      }
     } else if (!bad) {
       const int quarter = warp & 3, cq = warp >> 2;
       for (int mt = 0; mt < MT; mt++) {
@@ -866,6 +886,32 @@ __global__ void __launch_bounds__(128) attn_prefill_mma_kernel(const float *q, i
   }
 }
 
+// Sum of the split-K partials of gemm_tc_kernel in split order (deterministic)
+// and the epilogue: PLAIN y = sum, RESID y += sum, SWIGLU act = silu(g) * u.
+template <int EPI>
+__global__ void splitk_reduce_kernel(const float *part, int S, int MT, int BN, int ntn, int T, int rows, float *y,
+                                     int ldy, __half *act, int ld_act) {
+  const long long total = (long long)T * rows;
+  const size_t tile = (size_t)MT * kBM * BN;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / rows), n = (int)(i % rows);
+    const int mg = m / (MT * kBM), rl = m % (MT * kBM);
+    const float *p = part + ((size_t)mg * ntn + (n >> 7)) * S * tile + (size_t)rl * BN + (n & 127);
+    float v = 0.f, u = 0.f;
+    for (int z = 0; z < S; z++) {
+      v += __ldcg(p + z * tile);
+      if constexpr (EPI == GB_EPI_SWIGLU) u += __ldcg(p + z * tile + 128);
+    }
+    if constexpr (EPI == GB_EPI_SWIGLU) {
+      act[(size_t)m * ld_act + n] = __float2half_rn(v / (1.f + (float)exp(-(double)v)) * u);  // cpu.SiluMul
+    } else if constexpr (EPI == GB_EPI_RESID) {
+      y[(size_t)m * ldy + n] += v;
+    } else {
+      y[(size_t)m * ldy + n] = v;
+    }
+  }
+}
+
 }  // namespace
 
 // ---- launchers ------------------------------------------------------------------
@@ -890,6 +936,26 @@ int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map) {
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return gb_fail(GB_ERR_CUDA, "gpu: prefill: tensor map encode failed (%d)", (int)r);
   return GB_OK;
+}
+
+// Token tiles per CTA (MT: one weight decode feeds MT MMAs; at most 512 TMEM
+// columns) and K splits (S: enough CTAs for one wave over the SMs when the
+// weight tiles alone are too few; whole raw units per split).
+GbTcPlan gb_tc_gemm_plan(const GbTcGemm &a, int sms) {
+  GbTcPlan p;
+  const bool pair = a.epi == GB_EPI_SWIGLU;
+  const int BN = pair ? 256 : 128, mt_max = pair ? 2 : 4;
+  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + 127) / 128;
+  int mt = 1;
+  while (mt * 2 <= mt_max && mt * 2 <= mtiles) mt *= 2;
+  const int mg = (mtiles + mt - 1) / mt;
+  const int spr = gb_float_type(a.type_a) ? 1 : 4, nu = a.nsb * 4 / spr;
+  int S = sms / std::max(1, ntn * mg);
+  S = std::max(1, std::min(S, std::min(nu, 8)));
+  p.mt = mt;
+  p.splits = S;
+  p.part_floats = S > 1 ? (size_t)ntn * mg * S * mt * kBM * BN : 0;
+  return p;
 }
 
 int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
@@ -918,17 +984,15 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: mixed quantized and float tiles");
   g.raw_tile = (std::max(raw_unit_bytes(a.type_a), raw_unit_bytes(a.type_b)) + 127) & ~127;
   const int BN = g.pair ? 256 : 128, NT = BN / 32;
-  // token tiles per CTA: one decode of a weight stage feeds MT MMAs; more
-  // tiles per CTA mean fewer CTAs. Pick MT minimising waves x (decode + MT),
-  // the decode of a stage costing about two MMA groups.
-  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + 127) / 128, mt_max = g.pair ? 2 : 4;
-  int mt = 1;
-  double best = 1e30;
-  for (int c = 1; c <= mt_max && c <= std::max(1, mtiles); c *= 2) {
-    const long long ctas = (long long)ntn * ((mtiles + c - 1) / c);
-    const double cost = (double)((ctas + 147) / 148) * (2.0 + c);
-    if (cost < best - 1e-9) best = cost, mt = c;
+  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + 127) / 128;
+  GbTcPlan plan = gb_tc_gemm_plan(a, 148);
+  if (plan.splits > 1 && (!a.part || a.part_floats < plan.part_floats)) {  // no room for partials: one split
+    plan.splits = 1;
+    plan.part_floats = 0;
   }
+  const int mt = plan.mt;
+  g.splits = plan.splits;
+  g.part = a.part;
   g.mt = mt;
   const size_t ab = (size_t)kABytes * mt + (size_t)BN * 128, rb = (size_t)NT * g.raw_tile;
   const size_t budget = 227 * 1024 - 1024 - 512;  // dynamic smem minus the alignment slack and statics
@@ -947,8 +1011,7 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   g.rstage = rsn;
   const size_t stage = ab;
   const size_t smem = (size_t)ns * stage + (size_t)rsn * rb + 1024;
-  dim3 grid((unsigned)((a.rows + 127) / 128), (unsigned)((a.T + kBM * mt - 1) / (kBM * mt)));
-  if (g.pair) grid.x = (unsigned)((a.rows + 127) / 128);  // rows = FFN rows of one half
+  const dim3 grid((unsigned)ntn, (unsigned)((mtiles + mt - 1) / mt), (unsigned)g.splits);
   const dim3 block((unsigned)((kDQ + 2) * 32));
   void (*kern)(TcArgs, CUtensorMap) = nullptr;
   switch (a.epi) {
@@ -960,6 +1023,24 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "gpu: prefill GEMM");
   kern<<<grid, block, smem, st>>>(g, a.tmap_a);
   GB_CUDA(cudaGetLastError(), "gpu: prefill GEMM");
+  if (g.splits > 1) {
+    const long long total = (long long)a.T * a.rows;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    switch (a.epi) {
+      case GB_EPI_PLAIN:
+        splitk_reduce_kernel<GB_EPI_PLAIN><<<blocks, 256, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows, a.y,
+                                                                   a.ldy, nullptr, 0);
+        break;
+      case GB_EPI_RESID:
+        splitk_reduce_kernel<GB_EPI_RESID><<<blocks, 256, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows, a.y,
+                                                                   a.ldy, nullptr, 0);
+        break;
+      default:
+        splitk_reduce_kernel<GB_EPI_SWIGLU><<<blocks, 256, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows,
+                                                                    nullptr, 0, a.act, a.ld_act);
+    }
+    GB_CUDA(cudaGetLastError(), "gpu: prefill split-K reduce");
+  }
   return GB_OK;
 }
 

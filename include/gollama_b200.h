@@ -180,7 +180,10 @@ int gb_linear_matvec(gb_linear *l, void *stream, const float *x, float *y);
  * x[T][cols] W^T with x binary16 on the device (row stride cols, 16-byte
  * aligned) and y float32 (row stride rows). W's elements are the
  * reference's float32 element values rounded to binary16; products
- * accumulate in float32. */
+ * accumulate in float32. When the weight tiles alone are too few to fill the
+ * GPU, K is split and fp32 partials are summed in a fixed order by a second
+ * kernel (deterministic); their scratch is allocated by the first call that
+ * needs it (after a device synchronisation). */
 int gb_linear_matmul_f16(gb_linear *l, void *stream, const uint16_t *x, int T, float *y);
 /* Bytes of the tiled weight buffer and the type's algorithmic bytes. */
 int gb_linear_info(const gb_linear *l, int *typ, int *rows, int *cols, size_t *weight_bytes);
