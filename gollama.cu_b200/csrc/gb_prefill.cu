@@ -6,7 +6,7 @@
 // backend/gpu/gpu.go:82-86 is the API it generalises).
 //
 // The GEMM is a tcgen05 kernel for sm_100a. Per CTA: 128 token rows x 128
-// weight rows (256 for the fused gate/up pairs), K in stages of 64:
+// weight rows (64 gate + 64 up rows for the fused gate/up pairs), K in stages of 64:
 //  * a producer warp TMA-loads the fp16 activation tile (128-byte swizzle)
 //    and bulk-copies the raw quantized bytes of the stage's weight tiles
 //    (the decode path's tiled layout: per 32-row tile and super-block, a
@@ -263,7 +263,7 @@ GB_DEV const uint8_t *sb_block(const TcArgs &g, int tile, int sb, int up, int &t
          ((size_t)(tile - g.split_tile) * g.nsb + sb) * gb_tiled_sb_bytes(typ);
 }
 
-// BN: weight rows of the CTA (128, or 256 for gate/up pairs) in NT = BN/32
+// BN: weight rows of the CTA (128: 4 tiles, or 2 gate + 2 up tiles) in NT = BN/32
 // tiles. 16 dequant warps: warp w decodes tile w % NT, output chunks
 // [(w / NT) * CPT, +CPT) of each row (one row per lane), so every SM
 // scheduler has four decoding warps to interleave; then the producer warp,
@@ -287,7 +287,9 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
   const int k0 = u0 * SPR, nkl = (u1 - u0) * SPR;
   const int m0 = blockIdx.y * kBM * MT;     // first token row
   const int ABytes = kABytes * MT;          // the stage's activation tiles
-  const int tile0 = blockIdx.x * 4;         // first weight tile (of each half for pairs)
+  // first weight tile: 4 per CTA, or for gate/up pairs 2 of each half (B rows
+  // 0..63 gate, 64..127 up; TMEM columns likewise)
+  const int tile0 = blockIdx.x * (g.pair ? 2 : 4);
   // [NS] A tiles | [NS] B tiles (1024-aligned) | [RS][NT] raw units
   uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *A0 = base, *B0 = base + (size_t)NS * ABytes, *R0 = B0 + (size_t)NS * BBytes;
@@ -332,7 +334,7 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
           const int sb = k >> 2, kc = k & 3;
           uint32_t bytes = 0;
           for (int j = 0; j < NT; j++) {
-            const int up = g.pair && j >= 4, tile = tile0 + (g.pair ? (j & 3) : j);
+            const int up = g.pair && j >= 2, tile = tile0 + (g.pair ? (j & 1) : j);
             if (tile >= g.ntiles) continue;
             int typ;
             (void)sb_block(g, tile, sb, up, typ);
@@ -340,7 +342,7 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
           }
           gb_mbar_expect_tx(&rfull[rs], bytes);
           for (int j = 0; j < NT; j++) {
-            const int up = g.pair && j >= 4, tile = tile0 + (g.pair ? (j & 3) : j);
+            const int up = g.pair && j >= 2, tile = tile0 + (g.pair ? (j & 1) : j);
             if (tile >= g.ntiles) continue;
             int typ;
             const uint8_t *src = sb_block(g, tile, sb, up, typ);
@@ -392,7 +394,7 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
   } else {
     // dequant warps
     const int j = warp % NT, part = warp / NT;
-    const int up = g.pair && j >= 4, tile = tile0 + (g.pair ? (j & 3) : j);
+    const int up = g.pair && j >= 2, tile = tile0 + (g.pair ? (j & 1) : j);
     const bool valid = tile < g.ntiles;
     const int rB = j * 32 + lane, sw = lane & 7;  // B row; its 128-byte swizzle phase
     for (int kl = 0; kl < nkl; kl++) {
@@ -447,10 +449,11 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
       const int m = m0 + mt * kBM + quarter * 32 + lane;
       const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mt * BN);
       if constexpr (EPI == GB_EPI_SWIGLU) {
-        for (int cc = cq * 32; cc < cq * 32 + 32; cc += 16) {
+        {
+          const int cc = cq * 16;  // gate columns cc..cc+15, up columns 64+cc..
           float gv[16], uv[16];
           tmem_ld16(trow + cc, gv);
-          tmem_ld16(trow + 128 + cc, uv);
+          tmem_ld16(trow + 64 + cc, uv);
           const int n = tile0 * 32 + cc;
           if (m < g.T && n < g.rows) {
             uint4 o[2];
@@ -888,26 +891,36 @@ __global__ void __launch_bounds__(128) attn_prefill_mma_kernel(const float *q, i
 
 // Sum of the split-K partials of gemm_tc_kernel in split order (deterministic)
 // and the epilogue: PLAIN y = sum, RESID y += sum, SWIGLU act = silu(g) * u.
+// One thread per 4 consecutive output columns of one token row (16-byte
+// partial reads); grid (column groups, token rows).
 template <int EPI>
 __global__ void splitk_reduce_kernel(const float *part, int S, int MT, int BN, int ntn, int T, int rows, float *y,
                                      int ldy, __half *act, int ld_act) {
-  const long long total = (long long)T * rows;
+  const int m = blockIdx.y, n = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (n >= rows) return;
   const size_t tile = (size_t)MT * kBM * BN;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int m = (int)(i / rows), n = (int)(i % rows);
-    const int mg = m / (MT * kBM), rl = m % (MT * kBM);
-    const float *p = part + ((size_t)mg * ntn + (n >> 7)) * S * tile + (size_t)rl * BN + (n & 127);
-    float v = 0.f, u = 0.f;
-    for (int z = 0; z < S; z++) {
-      v += __ldcg(p + z * tile);
-      if constexpr (EPI == GB_EPI_SWIGLU) u += __ldcg(p + z * tile + 128);
-    }
+  const int mg = m / (MT * kBM), rl = m % (MT * kBM);
+  const int oc = EPI == GB_EPI_SWIGLU ? 64 : 128;  // output columns of one weight tile group
+  const float *p = part + ((size_t)mg * ntn + n / oc) * S * tile + (size_t)rl * BN + (n % oc);
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = v;
+  for (int z = 0; z < S; z++) {
+    const float4 a = __ldcg((const float4 *)(p + z * tile));
+    v.x += a.x, v.y += a.y, v.z += a.z, v.w += a.w;
     if constexpr (EPI == GB_EPI_SWIGLU) {
-      act[(size_t)m * ld_act + n] = __float2half_rn(v / (1.f + (float)exp(-(double)v)) * u);  // cpu.SiluMul
+      const float4 b = __ldcg((const float4 *)(p + z * tile + 64));
+      u.x += b.x, u.y += b.y, u.z += b.z, u.w += b.w;
+    }
+  }
+  const float vv[4] = {v.x, v.y, v.z, v.w}, uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    if (n + i >= rows) break;
+    if constexpr (EPI == GB_EPI_SWIGLU) {
+      act[(size_t)m * ld_act + n + i] = __float2half_rn(vv[i] / (1.f + (float)exp(-(double)vv[i])) * uu[i]);  // cpu.SiluMul
     } else if constexpr (EPI == GB_EPI_RESID) {
-      y[(size_t)m * ldy + n] += v;
+      y[(size_t)m * ldy + n + i] += vv[i];
     } else {
-      y[(size_t)m * ldy + n] = v;
+      y[(size_t)m * ldy + n + i] = vv[i];
     }
   }
 }
@@ -944,8 +957,8 @@ int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map) {
 GbTcPlan gb_tc_gemm_plan(const GbTcGemm &a, int sms) {
   GbTcPlan p;
   const bool pair = a.epi == GB_EPI_SWIGLU;
-  const int BN = pair ? 256 : 128, mt_max = pair ? 2 : 4;
-  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + 127) / 128;
+  const int BN = 128, mt_max = 4, oc = pair ? 64 : 128;
+  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + oc - 1) / oc;
   int mt = 1;
   while (mt * 2 <= mt_max && mt * 2 <= mtiles) mt *= 2;
   const int mg = (mtiles + mt - 1) / mt;
@@ -983,8 +996,8 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   if (raw_spr(a.type_a) != raw_spr(a.type_b))
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: mixed quantized and float tiles");
   g.raw_tile = (std::max(raw_unit_bytes(a.type_a), raw_unit_bytes(a.type_b)) + 127) & ~127;
-  const int BN = g.pair ? 256 : 128, NT = BN / 32;
-  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + 127) / 128;
+  const int BN = 128, NT = BN / 32;
+  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + (g.pair ? 63 : 127)) / (g.pair ? 64 : 128);
   GbTcPlan plan = gb_tc_gemm_plan(a, 148);
   if (plan.splits > 1 && (!a.part || a.part_floats < plan.part_floats)) {  // no room for partials: one split
     plan.splits = 1;
@@ -1017,26 +1030,25 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   switch (a.epi) {
     case GB_EPI_PLAIN: kern = gemm_tc_kernel<128, GB_EPI_PLAIN>; break;
     case GB_EPI_RESID: kern = gemm_tc_kernel<128, GB_EPI_RESID>; break;
-    case GB_EPI_SWIGLU: kern = gemm_tc_kernel<256, GB_EPI_SWIGLU>; break;
+    case GB_EPI_SWIGLU: kern = gemm_tc_kernel<128, GB_EPI_SWIGLU>; break;
     default: return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: epilogue %d", a.epi);
   }
   GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "gpu: prefill GEMM");
   kern<<<grid, block, smem, st>>>(g, a.tmap_a);
   GB_CUDA(cudaGetLastError(), "gpu: prefill GEMM");
   if (g.splits > 1) {
-    const long long total = (long long)a.T * a.rows;
-    const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+    const dim3 blocks((unsigned)((a.rows + 4 * 128 - 1) / (4 * 128)), (unsigned)a.T);
     switch (a.epi) {
       case GB_EPI_PLAIN:
-        splitk_reduce_kernel<GB_EPI_PLAIN><<<blocks, 256, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows, a.y,
+        splitk_reduce_kernel<GB_EPI_PLAIN><<<blocks, 128, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows, a.y,
                                                                    a.ldy, nullptr, 0);
         break;
       case GB_EPI_RESID:
-        splitk_reduce_kernel<GB_EPI_RESID><<<blocks, 256, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows, a.y,
+        splitk_reduce_kernel<GB_EPI_RESID><<<blocks, 128, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows, a.y,
                                                                    a.ldy, nullptr, 0);
         break;
       default:
-        splitk_reduce_kernel<GB_EPI_SWIGLU><<<blocks, 256, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows,
+        splitk_reduce_kernel<GB_EPI_SWIGLU><<<blocks, 128, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows,
                                                                     nullptr, 0, a.act, a.ld_act);
     }
     GB_CUDA(cudaGetLastError(), "gpu: prefill split-K reduce");
