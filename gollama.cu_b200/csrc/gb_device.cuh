@@ -55,6 +55,16 @@ GB_DEV float gb_dequant_elem(int typ, const uint8_t *blk, int e) {
       int nib = hi ? (q >> 4) : (q & 0xF);
       return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)nib), __fmul_rn(dmin, (float)m));
     }
+    case GB_T_Q5_K: {  // ggml block_q5_K (not decoded by the reference): (d*sc)*q - dmin*m, q 5 bits
+      float d = gb_half_to_float((uint16_t)(blk[0] | blk[1] << 8));
+      float dmin = gb_half_to_float((uint16_t)(blk[2] | blk[3] << 8));
+      int chunk = e >> 6, w = e & 63, l = w & 31, hi = w >> 5;
+      uint8_t m;
+      uint8_t sc = gb_q4k_scale(blk + 4, 2 * chunk + hi, &m);
+      uint8_t q = blk[48 + chunk * 32 + l];
+      int v = (hi ? (q >> 4) : (q & 0xF)) | (((blk[16 + l] >> (2 * chunk + hi)) & 1) << 4);
+      return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)v), __fmul_rn(dmin, (float)m));
+    }
     case GB_T_Q6_K: {  // quant/quant.go:114-132: d*sc*(q-32)
       int chunk = e >> 7, w = e & 127, quarter = w >> 5, l = w & 31, is = l >> 4;
       const uint8_t *l0 = blk + chunk * 64, *h0 = blk + 128 + chunk * 32;

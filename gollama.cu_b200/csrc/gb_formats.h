@@ -10,6 +10,9 @@
 // and one 1-D TMA bulk copy moves a whole sb-block into shared memory.
 //   Q4_K: 9 units = the raw 144-byte block cut in 16-byte pieces
 //         (unit 0 = d, dmin, 12 scale bytes; units 1..8 = the 128 quant bytes).
+//   Q5_K: 11 units = the raw 176-byte block cut in 16-byte pieces (unit 0 =
+//         d, dmin, 12 scale bytes; units 1..2 = the 32 fifth-bit bytes qh;
+//         units 3..10 = the 128 low-nibble bytes qs).
 //   Q6_K: 13 units = raw bytes [0,208) (ql 8, qh 4, scales 1), then the
 //         32 rows' 2-byte d at 13*512 + l*2 (sb-block 6720 bytes = 32*210).
 //   Q4_0: the 8 raw 18-byte blocks of the super-block are regrouped:
@@ -38,7 +41,7 @@
 #define GB_DEVERR_TIMEOUT 4u  // a bounded mbarrier wait ran out
 
 enum {
-  GB_T_F32 = 0, GB_T_F16 = 1, GB_T_Q4_0 = 2, GB_T_Q8_0 = 8, GB_T_Q4_K = 12, GB_T_Q6_K = 14,
+  GB_T_F32 = 0, GB_T_F16 = 1, GB_T_Q4_0 = 2, GB_T_Q8_0 = 8, GB_T_Q4_K = 12, GB_T_Q5_K = 13, GB_T_Q6_K = 14,
   GB_T_BF16 = 30
 };
 
@@ -47,7 +50,7 @@ GB_HD int gb_block_size(int t) {
   switch (t) {
     case GB_T_F32: case GB_T_F16: case GB_T_BF16: return 1;
     case GB_T_Q4_0: case GB_T_Q8_0: return 32;
-    case GB_T_Q4_K: case GB_T_Q6_K: return 256;
+    case GB_T_Q4_K: case GB_T_Q5_K: case GB_T_Q6_K: return 256;
   }
   return 0;
 }
@@ -58,6 +61,7 @@ GB_HD int gb_type_size(int t) {
     case GB_T_Q4_0: return 18;
     case GB_T_Q8_0: return 34;
     case GB_T_Q4_K: return 144;
+    case GB_T_Q5_K: return 176;
     case GB_T_Q6_K: return 210;
   }
   return 0;
@@ -72,13 +76,14 @@ GB_HD int64_t gb_row_bytes(int t, int64_t n) {
 // and F32; BF16 added, as the embedding accepts any known type).
 GB_HD bool gb_float_type(int t) { return t == GB_T_F16 || t == GB_T_BF16 || t == GB_T_F32; }
 GB_HD bool gb_tiled_type(int t) {
-  return t == GB_T_Q4_0 || t == GB_T_Q8_0 || t == GB_T_Q4_K || t == GB_T_Q6_K || gb_float_type(t);
+  return t == GB_T_Q4_0 || t == GB_T_Q8_0 || t == GB_T_Q4_K || t == GB_T_Q5_K || t == GB_T_Q6_K || gb_float_type(t);
 }
 GB_HD int gb_tiled_units(int t) {
-  return t == GB_T_Q6_K ? 13 : t == GB_T_Q8_0 ? 17 : (t == GB_T_F16 || t == GB_T_BF16) ? 32 : t == GB_T_F32 ? 64 : 9;
+  return t == GB_T_Q6_K ? 13 : t == GB_T_Q5_K ? 11 : t == GB_T_Q8_0 ? 17 : (t == GB_T_F16 || t == GB_T_BF16) ? 32 : t == GB_T_F32 ? 64 : 9;
 }
 GB_HD int gb_tiled_sb_bytes(int t) {
   return t == GB_T_Q6_K ? 6720
+         : t == GB_T_Q5_K ? 5632
          : t == GB_T_Q8_0 ? 8704
          : (t == GB_T_F16 || t == GB_T_BF16) ? 16384
          : t == GB_T_F32 ? 32768
@@ -104,5 +109,5 @@ GB_HD int gb_tiled_offset(int t, int lane, int b) {
 }
 // Raw bytes per super-block of one row (256 elements).
 GB_HD int gb_sb_raw_bytes(int t) {
-  return t == GB_T_Q6_K ? 210 : t == GB_T_Q8_0 ? 272 : (t == GB_T_F16 || t == GB_T_BF16) ? 512 : t == GB_T_F32 ? 1024 : 144;
+  return t == GB_T_Q6_K ? 210 : t == GB_T_Q5_K ? 176 : t == GB_T_Q8_0 ? 272 : (t == GB_T_F16 || t == GB_T_BF16) ? 512 : t == GB_T_F32 ? 1024 : 144;
 }

@@ -117,6 +117,64 @@ GB_DEV float sb_dot<GB_T_Q4_K>(const uint8_t *st, int lane, const uint32_t *xa, 
   return d * (xs * (A + (254.f * B + C) * kL2)) - dmin * tm;
 }
 
+// Q5_K (ggml block_q5_K; the reference has no decoder for it): the Q4_K
+// factorisation with 5-bit quants q = nibble | fifth bit << 4 (0..31). Both
+// families are formed shifted (no factor 16: 16*31 does not fit a byte).
+template <>
+GB_DEV float sb_dot<GB_T_Q5_K>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)sl;
+  const uint4 *u = (const uint4 *)st;
+  const uint4 h = u[lane];
+  const float d = gb_half_to_float((uint16_t)(h.x & 0xFFFFu));
+  const float dmin = gb_half_to_float((uint16_t)(h.x >> 16));
+  const uint32_t sc03 = h.y & 0x3F3F3F3Fu, m03 = h.z & 0x3F3F3F3Fu;
+  const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+  const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+  const uint4 qh0 = u[1 * 32 + lane], qh1 = u[2 * 32 + lane];
+  const uint32_t qhw[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
+  int IA = 0, IB = 0, IC = 0;
+  float tm = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const uint4 q0 = u[(3 + 2 * c) * 32 + lane], q1 = u[(4 + 2 * c) * 32 + lane];
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint4 *pa = (const uint4 *)(xa + 16 * c), *pb = (const uint4 *)(xb + 16 * c),
+                *pc = (const uint4 *)(xc + 16 * c);
+    int A0 = 0, B0 = 0, C0 = 0, A1 = 0, B1 = 0, C1 = 0;
+#pragma unroll
+    for (int v = 0; v < 2; v++) {
+      const uint4 la = pa[v], lb = pb[v], lc = pc[v], ha = pa[2 + v], hb = pb[2 + v], hc = pc[2 + v];
+      const uint32_t a4[4] = {la.x, la.y, la.z, la.w}, b4[4] = {lb.x, lb.y, lb.z, lb.w},
+                     c4[4] = {lc.x, lc.y, lc.z, lc.w};
+      const uint32_t A4[4] = {ha.x, ha.y, ha.z, ha.w}, B4[4] = {hb.x, hb.y, hb.z, hb.w},
+                     C4[4] = {hc.x, hc.y, hc.z, hc.w};
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const uint32_t w = qw[4 * v + k], hb5 = qhw[4 * v + k];
+        const uint32_t lo = (w & 0x0F0F0F0Fu) | (((hb5 >> (2 * c)) & 0x01010101u) << 4);
+        const uint32_t hi = ((w >> 4) & 0x0F0F0F0Fu) | (((hb5 >> (2 * c + 1)) & 0x01010101u) << 4);
+        A0 = gb_dp4a_us(lo, a4[k], A0);
+        B0 = gb_dp4a_us(lo, b4[k], B0);
+        C0 = gb_dp4a_us(lo, c4[k], C0);
+        A1 = gb_dp4a_us(hi, A4[k], A1);
+        B1 = gb_dp4a_us(hi, B4[k], B1);
+        C1 = gb_dp4a_us(hi, C4[k], C1);
+      }
+    }
+    const int j0 = 2 * c, j1 = 2 * c + 1;
+    const int sc0 = byte_i(j0 < 4 ? sc03 : sc47, j0 & 3), sc1 = byte_i(j1 < 4 ? sc03 : sc47, j1 & 3);
+    IA += sc0 * A0 + sc1 * A1;
+    IB += sc0 * B0 + sc1 * B1;
+    IC += sc0 * C0 + sc1 * C1;
+    const float m0 = (float)byte_i(j0 < 4 ? m03 : m47, j0 & 3), m1 = (float)byte_i(j1 < 4 ? m03 : m47, j1 & 3);
+    tm = fmaf(m0, xsum[4 * c] + xsum[4 * c + 1], tm);
+    tm = fmaf(m1, xsum[4 * c + 2] + xsum[4 * c + 3], tm);
+  }
+  // |I| < 8 * 63 * 32 * 31 * 127 < 2^27: exact in int32, float error 2^-24
+  return d * (xs * ((float)IA + (254.f * (float)IB + (float)IC) * kL2)) - dmin * tm;
+}
+
 // Q6_K: quant/quant.go:114 layout; y = d*sc*(q-32) over 16-element sub-blocks.
 // The -32 enters the dp4a sums as their starting value -32*(limb sums).
 template <>
@@ -932,12 +990,15 @@ KernelFn pick_w(int ta, int tb, int epi) {
   if (ta == tb) {
     if (ta == GB_T_Q4_K) return pick_epi<GB_T_Q4_K, GB_T_Q4_K, W>(epi);
     if (ta == GB_T_Q6_K) return pick_epi<GB_T_Q6_K, GB_T_Q6_K, W>(epi);
+    if (ta == GB_T_Q5_K) return pick_epi<GB_T_Q5_K, GB_T_Q5_K, W>(epi);
     if (ta == GB_T_Q4_0) return pick_epi<GB_T_Q4_0, GB_T_Q4_0, W>(epi);
     if (ta == GB_T_Q8_0) return pick_epi<GB_T_Q8_0, GB_T_Q8_0, W>(epi);
   } else if (ta == GB_T_Q4_K && tb == GB_T_Q6_K && epi == GB_EPI_QKV) {
     return gemv_kernel<GB_T_Q4_K, GB_T_Q6_K, GB_EPI_QKV, W>;
   } else if (ta == GB_T_Q6_K && tb == GB_T_Q4_K && epi == GB_EPI_QKV) {
     return gemv_kernel<GB_T_Q6_K, GB_T_Q4_K, GB_EPI_QKV, W>;
+  } else if (ta == GB_T_Q5_K && tb == GB_T_Q6_K && epi == GB_EPI_QKV) {  // Q5_K_M: q, k Q5_K, v Q6_K
+    return gemv_kernel<GB_T_Q5_K, GB_T_Q6_K, GB_EPI_QKV, W>;
   }
   return nullptr;
 }

@@ -118,6 +118,7 @@ const char *tname(int t) {
     case GB_T_Q4_0: return "Q4_0";
     case GB_T_Q8_0: return "Q8_0";
     case GB_T_Q4_K: return "Q4_K";
+    case GB_T_Q5_K: return "Q5_K";
     case GB_T_Q6_K: return "Q6_K";
     case GB_T_BF16: return "BF16";
   }

@@ -161,6 +161,22 @@ GB_DEV uint4 dequant_chunk(int typ, int kc, const uint8_t *raw, int lane, int c)
       bytes8_scaled(w0, w1, 0.f, ds, -dm, true, v);
       break;
     }
+    case GB_T_Q5_K: {  // as Q4_K with the fifth bit of each quant from qh (units 1-2)
+      const uint4 h = lds16(raw + lane * 16);
+      const int hi = c >> 2, b0 = (c & 3) * 8, bit = 2 * kc + hi;
+      const uint4 q = lds16(raw + 512 * (3 + 2 * kc + (b0 >> 4)) + lane * 16);
+      const uint4 qh = lds16(raw + 512 * (1 + (b0 >> 4)) + lane * 16);
+      const float d = gb_half_to_float((uint16_t)(h.x & 0xFFFF)), dmin = gb_half_to_float((uint16_t)(h.x >> 16));
+      uint32_t sc, m;
+      q4k_scale_reg(h, bit, sc, m);
+      const float ds = __fmul_rn(d, u2f(sc)), dm = __fmul_rn(dmin, u2f(m));
+      uint32_t w0 = (b0 & 15) ? q.z : q.x, w1 = (b0 & 15) ? q.w : q.y;
+      const uint32_t h0 = (b0 & 15) ? qh.z : qh.x, h1 = (b0 & 15) ? qh.w : qh.y;
+      w0 = ((hi ? w0 >> 4 : w0) & 0x0F0F0F0Fu) | (((h0 >> bit) & 0x01010101u) << 4);
+      w1 = ((hi ? w1 >> 4 : w1) & 0x0F0F0F0Fu) | (((h1 >> bit) & 0x01010101u) << 4);
+      bytes8_scaled(w0, w1, 0.f, ds, -dm, true, v);
+      break;
+    }
     case GB_T_Q4_0: {  // d*(q-8)
       const uint4 dd = lds16(raw + lane * 16);
       const int b = c >> 2, k = 2 * kc + b, cc = c & 3;

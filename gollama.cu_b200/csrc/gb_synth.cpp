@@ -7,6 +7,8 @@
 //   Q4_0: d = f16(|N(0,sigma)|/8), 16 uniform quant bytes            (sigma 0.02)
 //   Q4_K: d, dmin = f16(|N(0,sigma)|), 12 uniform scale bytes,
 //         128 uniform quant bytes                                      (sigma 0.01)
+//   Q5_K: d, dmin = f16(|N(0,sigma)|), 12 scale + 32 qh + 128 qs uniform
+//         bytes                                                        (sigma 0.005)
 //   Q6_K: 128 ql + 64 qh uniform bytes, 16 int8 scales uniform in
 //         [-32,31], d = f16(|N(0,sigma)|)                              (sigma 0.002)
 //   norms: float32 1 + N(0, 0.01)
@@ -132,6 +134,11 @@ void gen_block(int typ, uint64_t seed, uint32_t tensor, uint64_t block, float si
       put16(p + 2, f16_from((float)fabs(r.normal() * sigma)));
       r.bytes(p + 4, 140);
       break;
+    case GB_T_Q5_K:
+      put16(p, f16_from((float)fabs(r.normal() * sigma)));
+      put16(p + 2, f16_from((float)fabs(r.normal() * sigma)));
+      r.bytes(p + 4, 172);
+      break;
     case GB_T_Q6_K:
       r.bytes(p, 192);
       for (int i = 0; i < 16; i++) p[192 + i] = (uint8_t)(int8_t)((int)(r.next() % 64) - 32);
@@ -173,6 +180,7 @@ float default_sigma(int typ) {
     case GB_T_Q8_0: return 0.02f;
     case GB_T_F16: return 0.02f;
     case GB_T_Q4_K: return 0.01f;
+    case GB_T_Q5_K: return 0.005f;
     case GB_T_Q6_K: return 0.002f;
   }
   return 0.01f;
@@ -194,12 +202,14 @@ std::vector<TensorSpec> model_tensors(const gb_synth_spec &s) {
     if (s.mix == 3) return (int)GB_T_Q6_K;
     if (s.mix == 4) return (int)GB_T_Q8_0;
     if (s.mix == 5) return (int)GB_T_F16;
+    if (s.mix == 6) return six ? (int)GB_T_Q6_K : (int)GB_T_Q5_K;  // Q5_K_M
     return six ? (int)GB_T_Q6_K : (int)GB_T_Q4_K;
   };
   auto sig = [&](int t) {
     if (t == GB_T_Q4_0 || t == GB_T_Q8_0) return 0.02f;
     if (t == GB_T_F16) return 0.02f;
     if (t == GB_T_Q4_K) return 0.01f / 128.f;
+    if (t == GB_T_Q5_K) return 0.01f / 256.f;  // 5-bit quants: twice the range of Q4_K's
     return 0.002f / 32.f;
   };
   auto mat = [&](const std::string &n, int rows, int cols, bool six) {

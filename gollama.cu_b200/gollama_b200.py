@@ -24,9 +24,9 @@ LIB_PATH = os.path.join(HERE, "libgollama_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "gollama_b200.h")
 
 OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_IO, ERR_NCCL, ERR_TIMEOUT, ERR_DEVICE = range(8)
-F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, BF16 = 0, 1, 2, 8, 12, 14, 30
+F32, F16, Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 2, 8, 12, 13, 14, 30
 BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144),
-         Q6_K: (256, 210)}
+         Q5_K: (256, 176), Q6_K: (256, 210)}
 
 
 def row_bytes(typ: int, n: int) -> int:

@@ -169,7 +169,7 @@ int gb_gpu_sample(gb_kernels *k, void *stream, const float *logits, int n, const
 typedef struct gb_linear gb_linear;
 /* uploadLinear, model/model.go:77: uploads a [rows][cols] matrix given as
  * raw ggml bytes on the host and repacks it on the device into 32-row
- * tiles. Supported: Q4_0, Q8_0, Q4_K, Q6_K, F16, BF16, F32 with cols a multiple of 256. */
+ * tiles. Supported: Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, F16, BF16, F32 with cols a multiple of 256. */
 int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes, int rows,
                      int cols, gb_linear **out);
 /* (*Linear).MatVec, model/model.go:109 for batch 1: y[rows] = W x[cols]
@@ -318,7 +318,8 @@ typedef struct {
   float rope_base, eps;
   int mix;        /* 0 = all Q4_0 with tied head; 1 = Q4_K_M mix (Q6_K attn_v,
                      even-layer ffn_down and output); 2 = all Q4_K; 3 = all Q6_K;
-                     4 = all Q8_0; 5 = all F16 */
+                     4 = all Q8_0; 5 = all F16; 6 = Q5_K_M mix (as 1 with Q5_K
+                     in place of Q4_K) */
   uint64_t seed;
 } gb_synth_spec;
 /* Fills spec with a BASELINE preset: 1 = Llama-3.2-1B Q4_0, 3 = 3B Q4_K_M,

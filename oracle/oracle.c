@@ -21,7 +21,7 @@ int or_block_size(int typ) {
     case OR_F32: case OR_F16: case OR_BF16: return 1;
     case 24: case 25: case 26: case 27: case 28: return 1; /* I8..F64 */
     case OR_Q4_0: case 3: case 6: case 7: case OR_Q8_0: case 9: case 20: return 32;
-    case 10: case 11: case OR_Q4_K: case 13: case OR_Q6_K: case 15:
+    case 10: case 11: case OR_Q4_K: case OR_Q5_K: case OR_Q6_K: case 15:
     case 16: case 17: case 18: case 19: case 21: case 22: case 23: case 29: return 256;
   }
   return 0;
@@ -34,7 +34,7 @@ int or_type_size(int typ) {
     case OR_Q4_0: return 18; case 3: return 20;     case 6: return 22;      case 7: return 24;
     case OR_Q8_0: return 34; case 9: return 36;
     case 10: return 84;     case 11: return 110;    case OR_Q4_K: return 144;
-    case 13: return 176;    case OR_Q6_K: return 210; case 15: return 292;
+    case OR_Q5_K: return 176; case OR_Q6_K: return 210; case 15: return 292;
     case 16: return 66;     case 17: return 74;     case 18: return 98;     case 19: return 50;
     case 20: return 18;     case 21: return 110;    case 22: return 82;     case 23: return 136;
     case 29: return 56;
@@ -124,6 +124,33 @@ static void dequant_q4k(const uint8_t *blk, float *out) {
   }
 }
 
+/* Q5_K. The reference lists the type (gguf/types.go:53: 256 elements in 176
+ * bytes) but quant.Dequantize has no case for it; this restates the published
+ * ggml block_q5_K layout: d and dmin (binary16), 12 scale bytes packed as for
+ * Q4_K, qh[32] holding the fifth bits, qs[128] the low four. Element 64j + l
+ * of the block is (d*sc)*q - dmin*m of sub-block 2j with
+ * q = (qs[32j+l] & 15) | bit 2j of qh[l] << 4, element 64j + 32 + l the same
+ * with the high nibble, bit 2j+1 and sub-block 2j+1 (float32 as dequantQ4K). */
+static void dequant_q5k(const uint8_t *blk, float *out) {
+  float d = half_at(blk), dmin = half_at(blk + 2);
+  const uint8_t *scales = blk + 4, *qh = blk + 16, *q = blk + 48;
+  for (int chunk = 0; chunk < 4; chunk++) {
+    uint8_t sc1, m1, sc2, m2;
+    or_scale_min_q4k(scales, 2 * chunk, &sc1, &m1);
+    or_scale_min_q4k(scales, 2 * chunk + 1, &sc2, &m2);
+    float d1 = d * (float)sc1, min1 = dmin * (float)m1;
+    float d2 = d * (float)sc2, min2 = dmin * (float)m2;
+    const uint8_t *qs = q + chunk * 32;
+    float *y = out + chunk * 64;
+    for (int l = 0; l < 32; l++) {
+      int lo = (qs[l] & 0xF) | (((qh[l] >> (2 * chunk)) & 1) << 4);
+      int hi = (qs[l] >> 4) | (((qh[l] >> (2 * chunk + 1)) & 1) << 4);
+      y[l] = d1 * (float)lo - min1;
+      y[l + 32] = d2 * (float)hi - min2;
+    }
+  }
+}
+
 /* quant/quant.go:114 dequantQ6K. */
 static void dequant_q6k(const uint8_t *blk, float *out) {
   const uint8_t *ql = blk, *qh = blk + 128;
@@ -185,6 +212,9 @@ int or_dequantize(int typ, const uint8_t *data, int64_t len, float *out, int64_t
       return 0;
     case OR_Q4_K:
       for (int64_t b = 0; b < n / 256; b++) dequant_q4k(data + b * 144, out + b * 256);
+      return 0;
+    case OR_Q5_K:
+      for (int64_t b = 0; b < n / 256; b++) dequant_q5k(data + b * 176, out + b * 256);
       return 0;
     case OR_Q6_K:
       for (int64_t b = 0; b < n / 256; b++) dequant_q6k(data + b * 210, out + b * 256);

@@ -30,7 +30,7 @@ extern "C" {
 /* ggml type ids (gguf/types.go:8-37). */
 enum {
   OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q8_0 = 8, OR_Q4_K = 12,
-  OR_Q6_K = 14, OR_BF16 = 30
+  OR_Q5_K = 13, OR_Q6_K = 14, OR_BF16 = 30
 };
 
 /* gguf/types.go:47-57 block size / type size; 0 when unknown. */

@@ -5,12 +5,12 @@
 * q8_0 / q4_0: the known-answer blocks of quant/quant_test.go:TestQ8Q4
   (d = 0.5; Q8_0 quants j-16; Q4_0 nibbles lo=j, hi=15-j) with the values the
   reference test asserts.
-* q4_k / q6_k: blocks built here from chosen scales, mins and quants, packed
-  by the ggml layout rules (6-bit scale/min packing of get_scale_min_k4; Q6_K
-  ql/qh bit placement), with the expected values computed directly from the
+* q4_k / q5_k / q6_k: blocks built here from chosen scales, mins and quants,
+  packed by the ggml layout rules (6-bit scale/min packing of get_scale_min_k4;
+  Q5_K fifth bits in qh; Q6_K ql/qh bit placement), with the expected values computed directly from the
   chosen numbers (d*sc*q - dmin*m and d*sc*(q-32)). All chosen values make the
   products exact in float32, so the expectations do not depend on rounding.
-  The reference has no Q4_K/Q6_K known-answer test; these pin the decoders
+  The reference has no Q4_K/Q6_K/Q5_K known-answer test; these pin the decoders
   to the format, independently of the code under test.
 * roundtrip.gguf: the file of gguf/gguf_test.go:TestRoundTrip (metadata and
   two tensors), written by the writer below, which follows gguf/writer.go.
@@ -83,6 +83,26 @@ def q4_k_block(d, dmin, sc, m, q):
         for l in range(32):
             lo, hi = q[chunk * 64 + l], q[chunk * 64 + 32 + l]
             blk[16 + chunk * 32 + l] = lo | (hi << 4)
+    want = []
+    for e in range(256):
+        j = e // 32
+        want.append(d * sc[j] * q[e] - dmin * m[j])
+    return bytes(blk), want
+
+
+def q5_k_block(d, dmin, sc, m, q):
+    """q: 256 five-bit quants 0..31 in element order. The published ggml
+    block_q5_K layout: d, dmin, the Q4_K scale packing, qh[32] (bit 2j of byte
+    l = fifth bit of element 64j+l, bit 2j+1 that of 64j+32+l), qs[128]."""
+    blk = bytearray(176)
+    blk[0:2] = struct.pack("<H", half_bits(d))
+    blk[2:4] = struct.pack("<H", half_bits(dmin))
+    blk[4:16] = pack_q4k_scales(sc, m)
+    for chunk in range(4):
+        for l in range(32):
+            lo, hi = q[chunk * 64 + l], q[chunk * 64 + 32 + l]
+            blk[48 + chunk * 32 + l] = (lo & 0xF) | ((hi & 0xF) << 4)
+            blk[16 + l] |= ((lo >> 4) << (2 * chunk)) | ((hi >> 4) << (2 * chunk + 1))
     want = []
     for e in range(256):
         j = e // 32
@@ -206,6 +226,17 @@ def main():
     for d, scales, qv in q6k:
         blk, want = q6_k_block(d, scales, qv)
         out["q6_k"].append({"block": blk.hex(), "want": want})
+    # Q5_K (the reference lists the type but has no decoder): every 5-bit value,
+    # high scale bits, and a block of extremes
+    q5k = []
+    qv = [int(x) for x in rng.integers(0, 32, 256)]
+    qv[:32] = list(range(32))
+    q5k.append((0.25, 0.5, [3, 63, 17, 1, 40, 33, 63, 16], [63, 2, 0, 31, 17, 48, 1, 63], qv))
+    q5k.append((1.0, 0.0625, [63] * 8, [0, 63] * 4, [31 if i % 3 else 16 for i in range(256)]))
+    out["q5_k"] = []
+    for d, dmin, sc, m, qv in q5k:
+        blk, want = q5_k_block(d, dmin, sc, m, qv)
+        out["q5_k"].append({"block": blk.hex(), "want": want})
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(out, f, indent=1)
     with open(os.path.join(HERE, "roundtrip.gguf"), "wb") as f:

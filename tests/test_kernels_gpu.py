@@ -9,7 +9,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-Q4_0, Q8_0, Q4_K, Q6_K, F32, F16, BF16 = 2, 8, 12, 14, 0, 1, 30
+Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, F32, F16, BF16 = 2, 8, 12, 13, 14, 0, 1, 30
 
 
 def randf(rng, n, scale):
@@ -39,7 +39,7 @@ def host(t):
 
 def rand_quant(rng, typ, rows, cols):
     # backend/gpu/gpu_test.go:221 randQuant: random bytes, scale fields overwritten
-    ts, bs = {Q4_0: (18, 32), Q8_0: (34, 32), Q4_K: (144, 256), Q6_K: (210, 256)}[typ]
+    ts, bs = {Q4_0: (18, 32), Q8_0: (34, 32), Q4_K: (144, 256), Q5_K: (176, 256), Q6_K: (210, 256)}[typ]
     w = rng.integers(0, 256, rows * cols // bs * ts, dtype=np.uint8)
 
     def scale(off, mag):
@@ -52,7 +52,7 @@ def rand_quant(rng, typ, rows, cols):
         scale(0, 0.02)
     elif typ == Q8_0:  # not in randQuant (the reference has no Q8_0 GPU kernel); same recipe
         scale(0, 0.002)
-    elif typ == Q4_K:
+    elif typ in (Q4_K, Q5_K):  # Q5_K: not in randQuant (no reference kernel); the Q4_K recipe
         scale(0, 0.002)
         scale(2, 0.002)
     else:
@@ -163,7 +163,7 @@ TILED_SHAPES = [(64, 256), (300, 1024), (300, 4096), (4096, 4096), (1000, 14336)
 
 
 @pytest.mark.parametrize("rows,cols", TILED_SHAPES)
-@pytest.mark.parametrize("typ", [Q4_0, Q8_0, Q4_K, Q6_K])
+@pytest.mark.parametrize("typ", [Q4_0, Q8_0, Q4_K, Q5_K, Q6_K])
 def test_linear_tiled_vs_oracle(gb, orc, cuda, typ, rows, cols):
     rng = np.random.default_rng(rows * 7 + cols + typ)
     w = rand_quant(rng, typ, rows, cols)
@@ -213,7 +213,7 @@ def test_linear_tiled_synthetic_recipe(gb, orc, cuda, typ):
     lin.close()
 
 
-@pytest.mark.parametrize("typ,cols", [(Q4_0, 512), (Q8_0, 512), (Q4_K, 1024), (Q6_K, 1024), (F16, 64)])
+@pytest.mark.parametrize("typ,cols", [(Q4_0, 512), (Q8_0, 512), (Q4_K, 1024), (Q5_K, 1024), (Q6_K, 1024), (F16, 64)])
 def test_dequant_rows_bit_exact(kernels, orc, typ, cols):
     rng = np.random.default_rng(typ)
     rows = 40

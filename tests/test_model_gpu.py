@@ -21,6 +21,8 @@ MODELS = {
     "q80_all": dict(layers=2, dim=512, ffn=768, heads=8, kv_heads=2, head_dim=64, vocab=700, ctx_len=96, mix=4, seed=17),
     # all F16 matrices (model.uploadLinear's F16 case, MatVecF16)
     "f16_all": dict(layers=2, dim=512, ffn=768, heads=8, kv_heads=2, head_dim=64, vocab=700, ctx_len=96, mix=5, seed=18),
+    # Q5_K_M mix (Q5_K with Q6_K attn_v, even-layer ffn_down and output; Q5_K embedding)
+    "q5km": dict(layers=2, dim=512, ffn=768, heads=8, kv_heads=2, head_dim=128, vocab=900, ctx_len=96, mix=6, seed=19),
 }
 
 

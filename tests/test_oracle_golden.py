@@ -7,7 +7,7 @@ import struct
 import numpy as np
 import pytest
 
-Q4_0, Q8_0, Q4_K, Q6_K, F32, F16, BF16 = 2, 8, 12, 14, 0, 1, 30
+Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, F32, F16, BF16 = 2, 8, 12, 13, 14, 0, 1, 30
 
 
 def test_f16_known(orc, golden):
@@ -43,7 +43,7 @@ def test_q8_q4_known_answers(orc, golden):
         assert got.tolist() == golden[key]["want"]
 
 
-@pytest.mark.parametrize("key,typ", [("q4_k", Q4_K), ("q6_k", Q6_K)])
+@pytest.mark.parametrize("key,typ", [("q4_k", Q4_K), ("q5_k", Q5_K), ("q6_k", Q6_K)])
 def test_kquant_hand_derived(orc, golden, key, typ):
     for case in golden[key]:
         blk = np.frombuffer(bytes.fromhex(case["block"]), np.uint8)
@@ -94,6 +94,27 @@ def np_dequant(typ, raw, n):
                 mj = dmin[:, 0:1] * m[:, j:j + 1].astype(np.float32)
                 out[:, c * 64 + half * 32: c * 64 + half * 32 + 32] = dj * nib.astype(np.float32) - mj
         return out.reshape(-1)
+    if typ == Q5_K:
+        blk = raw.reshape(-1, 176)
+        d, dmin = np_half(blk[:, 0:2].copy()), np_half(blk[:, 2:4].copy())
+        s = blk[:, 4:16].astype(np.int32)
+        sc = np.zeros((blk.shape[0], 8), np.int32)
+        m = np.zeros((blk.shape[0], 8), np.int32)
+        sc[:, :4] = s[:, :4] & 63
+        m[:, :4] = s[:, 4:8] & 63
+        sc[:, 4:] = (s[:, 8:12] & 0xF) | ((s[:, 0:4] >> 6) << 4)
+        m[:, 4:] = (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 6) << 4)
+        qh = blk[:, 16:48].astype(np.int32)
+        q = blk[:, 48:].reshape(-1, 4, 32).astype(np.int32)
+        out = np.zeros((blk.shape[0], 256), np.float32)
+        for c in range(4):
+            for half, nib in ((0, q[:, c] & 0xF), (1, q[:, c] >> 4)):
+                j = 2 * c + half
+                q5 = nib | (((qh >> j) & 1) << 4)
+                dj = d[:, 0:1] * sc[:, j:j + 1].astype(np.float32)
+                mj = dmin[:, 0:1] * m[:, j:j + 1].astype(np.float32)
+                out[:, c * 64 + half * 32: c * 64 + half * 32 + 32] = dj * q5.astype(np.float32) - mj
+        return out.reshape(-1)
     if typ == Q6_K:
         blk = raw.reshape(-1, 210)
         ql, qh, sc = blk[:, :128], blk[:, 128:192], blk[:, 192:208].view(np.int8)
@@ -113,14 +134,14 @@ def np_dequant(typ, raw, n):
     raise ValueError(typ)
 
 
-@pytest.mark.parametrize("typ,bs,ts", [(Q4_0, 32, 18), (Q4_K, 256, 144), (Q6_K, 256, 210)])
+@pytest.mark.parametrize("typ,bs,ts", [(Q4_0, 32, 18), (Q4_K, 256, 144), (Q5_K, 256, 176), (Q6_K, 256, 210)])
 def test_oracle_vs_independent_numpy(orc, typ, bs, ts):
     rng = np.random.default_rng(typ)
     nblk = 64
     raw = rng.integers(0, 256, nblk * ts, dtype=np.uint8)
     # finite binary16 scales (random bytes may encode inf/NaN)
     for b in range(nblk):
-        for off in ((0,) if typ == Q4_0 else (0, 2) if typ == Q4_K else (208,)):
+        for off in ((0,) if typ == Q4_0 else (0, 2) if typ in (Q4_K, Q5_K) else (208,)):
             raw[b * ts + off: b * ts + off + 2] = np.array([rng.normal(0, 0.01)], np.float16).view(np.uint8)
     got = orc.dequantize(typ, raw, nblk * bs)
     want = np_dequant(typ, raw, nblk * bs)

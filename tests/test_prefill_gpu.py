@@ -12,14 +12,14 @@ import numpy as np
 import pytest
 import torch
 
-from test_kernels_gpu import BF16, F16, F32, Q4_0, Q4_K, Q6_K, Q8_0, rand_quant
+from test_kernels_gpu import BF16, F16, F32, Q4_0, Q4_K, Q5_K, Q6_K, Q8_0, rand_quant
 from test_model_gpu import MODELS
 
 pytestmark = pytest.mark.gpu
 
 
 def weight_bytes(rng, typ, rows, cols):
-    if typ in (Q4_0, Q8_0, Q4_K, Q6_K):
+    if typ in (Q4_0, Q8_0, Q4_K, Q5_K, Q6_K):
         return rand_quant(rng, typ, rows, cols)
     vals = rng.standard_normal(rows * cols) * 0.05
     if typ == BF16:
@@ -29,7 +29,7 @@ def weight_bytes(rng, typ, rows, cols):
 
 @pytest.mark.parametrize("rows,cols,T", [(128, 256, 1), (300, 1024, 77), (1000, 4096, 128), (4096, 4096, 300),
                                          (256, 512, 512)])
-@pytest.mark.parametrize("typ", [Q4_0, Q8_0, Q4_K, Q6_K, F16, BF16, F32])
+@pytest.mark.parametrize("typ", [Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, F16, BF16, F32])
 def test_matmul_f16_vs_reference(gb, orc, cuda, typ, rows, cols, T):
     rng = np.random.default_rng(rows + cols + T + typ)
     w = weight_bytes(rng, typ, rows, cols)
@@ -79,7 +79,7 @@ def check_kv(kv_got, kv_want, what=""):
 
 
 @pytest.mark.parametrize("name", ["q4km_hd64", "q40_tied", "q4km_hd128", "q4k_all", "gqa3_hd64", "gqa8_hd128",
-                                  "q80_all", "f16_all"])
+                                  "q80_all", "f16_all", "q5km"])
 @pytest.mark.parametrize("n", [2, 37])
 def test_prefill_vs_decode(gb, cuda, name, n):
     cfg = MODELS[name]
