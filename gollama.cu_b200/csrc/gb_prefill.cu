@@ -286,7 +286,7 @@ GB_DEV const uint8_t *sb_block(const TcArgs &g, int tile, int sb, int up, int &t
 // then the MMA warp.
 constexpr int kDQ = 16;
 template <int BN, int EPI>
-__global__ void __launch_bounds__((kDQ + 2) * 32, 1)
+__global__ void __launch_bounds__((kDQ + 3) * 32, 1)
     gemm_tc_kernel(const TcArgs g, const __grid_constant__ CUtensorMap tmap_a) {
   constexpr int NDQ = kDQ, NT = BN / 32, CPT = 8 * NT / NDQ;
   static_assert(NDQ % NT == 0 && CPT >= 1, "dequant split");
@@ -333,41 +333,49 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (warp == NDQ) {
-    // producer: per raw unit the tiles' weight bytes (one bulk copy per tile),
-    // per K-stage the activation tile by TMA
+  if (warp == NDQ + 2) {
+    // raw producer: each raw unit (the tiles' weight bytes, one bulk copy per
+    // tile) as soon as its slot is free, running ahead of the activation ring
     if (lane == 0) {
-      int a_issued = 0, r_issued = 0;
+      const int nr = nkl / SPR;
+      int r_issued = 0;
+      for (int r = 0; r < nr; r++) {
+        const int rs = r % RS, k = k0 + r * SPR;
+        if (r >= RS && !gb_mbar_wait(&rempty[rs], ((r / RS) - 1) & 1)) {
+          bad = 1;
+          if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
+          break;
+        }
+        const int sb = k >> 2, kc = k & 3;
+        uint32_t bytes = 0;
+        for (int j = 0; j < NT; j++) {
+          const int up = g.pair && j >= 2, tile = tile0 + (g.pair ? (j & 1) : j);
+          if (tile >= g.ntiles) continue;
+          int typ;
+          (void)sb_block(g, tile, sb, up, typ);
+          bytes += (uint32_t)raw_unit_bytes(typ);
+        }
+        gb_mbar_expect_tx(&rfull[rs], bytes);
+        for (int j = 0; j < NT; j++) {
+          const int up = g.pair && j >= 2, tile = tile0 + (g.pair ? (j & 1) : j);
+          if (tile >= g.ntiles) continue;
+          int typ;
+          const uint8_t *src = sb_block(g, tile, sb, up, typ);
+          const int ub = raw_unit_bytes(typ);
+          gb_bulk_g2s(R0 + ((size_t)rs * NT + j) * g.raw_tile, src + (SPR == 1 ? (size_t)kc * ub : 0), (uint32_t)ub,
+                      &rfull[rs]);
+        }
+        r_issued = r + 1;
+      }
+      // copies still in flight land (bounded) before the CTA exits
+      for (int j = r_issued > RS ? r_issued - RS : 0; j < r_issued; j++) (void)gb_mbar_wait(&rfull[j % RS], (j / RS) & 1);
+    }
+  } else if (warp == NDQ) {
+    // activation producer: per K-stage the MT activation tiles by TMA
+    if (lane == 0) {
+      int a_issued = 0;
       for (int kl = 0; kl < nkl; kl++) {
         const int k = k0 + kl;
-        if (kl % SPR == 0) {
-          const int r = kl / SPR, rs = r % RS;
-          if (r >= RS && !gb_mbar_wait(&rempty[rs], ((r / RS) - 1) & 1)) {
-            bad = 1;
-            if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
-            break;
-          }
-          const int sb = k >> 2, kc = k & 3;
-          uint32_t bytes = 0;
-          for (int j = 0; j < NT; j++) {
-            const int up = g.pair && j >= 2, tile = tile0 + (g.pair ? (j & 1) : j);
-            if (tile >= g.ntiles) continue;
-            int typ;
-            (void)sb_block(g, tile, sb, up, typ);
-            bytes += (uint32_t)raw_unit_bytes(typ);
-          }
-          gb_mbar_expect_tx(&rfull[rs], bytes);
-          for (int j = 0; j < NT; j++) {
-            const int up = g.pair && j >= 2, tile = tile0 + (g.pair ? (j & 1) : j);
-            if (tile >= g.ntiles) continue;
-            int typ;
-            const uint8_t *src = sb_block(g, tile, sb, up, typ);
-            const int ub = raw_unit_bytes(typ);
-            gb_bulk_g2s(R0 + ((size_t)rs * NT + j) * g.raw_tile, src + (SPR == 1 ? (size_t)kc * ub : 0), (uint32_t)ub,
-                        &rfull[rs]);
-          }
-          r_issued = r + 1;
-        }
         const int s = kl % NS;
         if (kl >= NS && !gb_mbar_wait(&empty[s], ((kl / NS) - 1) & 1)) {
           bad = 1;
@@ -379,9 +387,7 @@ __global__ void __launch_bounds__((kDQ + 2) * 32, 1)
           tma_load_2d(A0 + (size_t)s * ABytes + (size_t)mt * kABytes, &tmap_a, k * kBK, m0 + mt * kBM, &afull[s]);
         a_issued = kl + 1;
       }
-      // copies still in flight land (bounded) before the CTA exits
       for (int j = a_issued > NS ? a_issued - NS : 0; j < a_issued; j++) (void)gb_mbar_wait(&afull[j % NS], (j / NS) & 1);
-      for (int j = r_issued > RS ? r_issued - RS : 0; j < r_issued; j++) (void)gb_mbar_wait(&rfull[j % RS], (j / RS) & 1);
     }
   } else if (warp == NDQ + 1) {
     // MMA issue: one thread
@@ -1041,7 +1047,7 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   const size_t stage = ab;
   const size_t smem = (size_t)ns * stage + (size_t)rsn * rb + 1024;
   const dim3 grid((unsigned)ntn, (unsigned)((mtiles + mt - 1) / mt), (unsigned)g.splits);
-  const dim3 block((unsigned)((kDQ + 2) * 32));
+  const dim3 block((unsigned)((kDQ + 3) * 32));
   void (*kern)(TcArgs, CUtensorMap) = nullptr;
   switch (a.epi) {
     case GB_EPI_PLAIN: kern = gemm_tc_kernel<128, GB_EPI_PLAIN>; break;
