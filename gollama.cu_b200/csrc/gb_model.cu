@@ -248,39 +248,90 @@ int upload_vec(gb_model *m, const std::vector<float> &v, float **dst, const char
   return GB_OK;
 }
 
+// Host side of the uploads: two pinned buffers used in turn, so that the
+// rows of the next chunk are gathered (by several host threads) while the
+// previous chunk's copy to the device and its repack run on the stream.
+struct Uploader {
+  uint8_t *pin[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  size_t cap = 0;
+  int cur = 0;
+  int init(size_t bytes) {
+    cap = bytes;
+    for (int i = 0; i < 2; i++) {
+      GB_CUDA(cudaMallocHost(&pin[i], cap), "model: pinned upload buffer");
+      GB_CUDA(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming), "model: upload event");
+    }
+    return GB_OK;
+  }
+  ~Uploader() {
+    for (int i = 0; i < 2; i++) {
+      if (ev[i]) {
+        cudaEventSynchronize(ev[i]);
+        cudaEventDestroy(ev[i]);
+      }
+      if (pin[i]) cudaFreeHost(pin[i]);
+    }
+  }
+};
+
+// Gather n rows of sub_rb bytes (source stride rb) into dst with several threads.
+void gather_rows(uint8_t *dst, const uint8_t *src, size_t rb, size_t sub_rb, int n) {
+  const int nt = std::max(1, std::min(gb_host_threads(), (int)(((size_t)n * sub_rb) >> 22)));  // 4 MB a thread
+  auto work = [&](int t) {
+    for (int r = (int)((long long)n * t / nt); r < (int)((long long)n * (t + 1) / nt); r++)
+      memcpy(dst + (size_t)r * sub_rb, src + (size_t)r * rb, sub_rb);
+  };
+  if (nt == 1) {
+    work(0);
+    return;
+  }
+  std::vector<std::thread> th;
+  for (int t = 0; t < nt; t++) th.emplace_back(work, t);
+  for (auto &x : th) x.join();
+}
+
 // Upload rows [r0, r0+nr) and column super-blocks [c0, c0+nc) (in elements,
-// multiples of 256) of a raw matrix into tiles [tile0, ...) of dst.
+// multiples of 256) of a raw matrix into tiles [tile0, ...) of dst, in chunks
+// of whole 32-row tiles that fit a pinned buffer. Stream-ordered: the caller
+// synchronizes the stream before using the tiles.
 int upload_tiles(const GbTensor *t, int r0, int nr, int c0, int nc, uint8_t *dst_base,
                  int dst_tile0, int dst_tile_mul, cudaStream_t st, uint8_t *staging,
-                 size_t staging_bytes) {
+                 size_t staging_bytes, Uploader *up) {
   const int typ = t->type;
   const size_t rb = (size_t)gb_row_bytes(typ, t->cols());
   const size_t sub_rb = (size_t)gb_row_bytes(typ, nc), coff = (size_t)gb_row_bytes(typ, c0);
-  const size_t need = sub_rb * (size_t)nr;
-  if (need > staging_bytes) return gb_fail(GB_ERR_INVALID, "model: staging buffer too small");
-  std::vector<uint8_t> host(need);
-  for (int r = 0; r < nr; r++) memcpy(host.data() + (size_t)r * sub_rb, t->data + (size_t)(r0 + r) * rb + coff, sub_rb);
-  GB_CUDA(cudaMemcpyAsync(staging, host.data(), need, cudaMemcpyHostToDevice, st), "model: upload");
-  const int nsb = nc / 256, ntiles = (nr + 31) / 32;
+  const int nsb = nc / 256;
   const size_t sbb = (size_t)gb_tiled_sb_bytes(typ);
-  if (dst_tile_mul == 1) {
-    int rc = gb_repack_launch(typ, staging, nr, nc, dst_base + (size_t)dst_tile0 * nsb * sbb, st);
-    if (rc) return rc;
-  } else {
-    // interleaved destination (gate/up pairs): repack into a scratch region
-    // after the raw bytes, then place each sb-block at slot dst_tile0 of its
-    // (row-block, super-block) pair, so that a gate/up unit is contiguous
-    uint8_t *tmp = staging + ((need + 255) / 256) * 256;
-    size_t tb = (size_t)ntiles * nsb * sbb;
-    if (((need + 255) / 256) * 256 + tb > staging_bytes)
+  const int cr = std::max(32, (int)(up->cap / sub_rb) / 32 * 32);  // rows per chunk
+  if ((size_t)cr * sub_rb > up->cap) return gb_fail(GB_ERR_INVALID, "model: pinned upload buffer too small");
+  for (int i = 0; i < nr; i += cr) {
+    const int n = std::min(cr, nr - i), ntiles = (n + 31) / 32, t0 = i / 32;
+    const size_t need = sub_rb * (size_t)n;
+    if (((need + 255) / 256) * 256 + (size_t)ntiles * nsb * sbb > staging_bytes)
       return gb_fail(GB_ERR_INVALID, "model: staging buffer too small");
-    int rc = gb_repack_launch(typ, staging, nr, nc, tmp, st);
-    if (rc) return rc;
-    GB_CUDA(cudaMemcpy2DAsync(dst_base + (size_t)dst_tile0 * sbb, (size_t)dst_tile_mul * sbb, tmp, sbb, sbb,
-                              (size_t)ntiles * nsb, cudaMemcpyDeviceToDevice, st),
-            "model: place sb-blocks");
+    const int b = up->cur;
+    GB_CUDA(cudaEventSynchronize(up->ev[b]), "model: upload");  // this buffer's previous copy is done
+    gather_rows(up->pin[b], t->data + (size_t)(r0 + i) * rb + coff, rb, sub_rb, n);
+    GB_CUDA(cudaMemcpyAsync(staging, up->pin[b], need, cudaMemcpyHostToDevice, st), "model: upload");
+    GB_CUDA(cudaEventRecord(up->ev[b], st), "model: upload");
+    up->cur ^= 1;
+    if (dst_tile_mul == 1) {
+      int rc = gb_repack_launch(typ, staging, n, nc, dst_base + ((size_t)dst_tile0 + t0) * nsb * sbb, st);
+      if (rc) return rc;
+    } else {
+      // interleaved destination (gate/up pairs): repack into a scratch region
+      // after the raw bytes, then place each sb-block at slot dst_tile0 of its
+      // (row-block, super-block) pair, so that a gate/up unit is contiguous
+      uint8_t *tmp = staging + ((need + 255) / 256) * 256;
+      int rc = gb_repack_launch(typ, staging, n, nc, tmp, st);
+      if (rc) return rc;
+      GB_CUDA(cudaMemcpy2DAsync(dst_base + ((size_t)dst_tile0 + (size_t)dst_tile_mul * t0 * nsb) * sbb,
+                                (size_t)dst_tile_mul * sbb, tmp, sbb, sbb, (size_t)ntiles * nsb,
+                                cudaMemcpyDeviceToDevice, st),
+              "model: place sb-blocks");
+    }
   }
-  GB_CUDA(cudaStreamSynchronize(st), "model: upload");
   return GB_OK;
 }
 
@@ -701,6 +752,12 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
   staging_bytes = staging_bytes * 2 + (1 << 20);
   uint8_t *staging = nullptr;
   if ((rc = dalloc(m, &staging, staging_bytes, "model: staging"))) return fail(rc);
+  // pinned host chunks: 32 MB, at least one 32-row tile of the widest row
+  size_t widest = 0;
+  for (auto &t : f->tensors)
+    if (t.cols() > 0) widest = std::max<size_t>(widest, (size_t)gb_row_bytes(t.type, t.cols()));
+  Uploader up;
+  if ((rc = up.init(std::max<size_t>((size_t)32 << 20, 32 * widest)))) return fail(rc);
 
   // token embedding (full, for the lookup) -- tiled
   if (!gb_tiled_type(embd->type))
@@ -715,7 +772,7 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
     int chunk = (int)std::max<size_t>(32, (staging_bytes / 2 / (size_t)gb_row_bytes(embd->type, c.dim)) / 32 * 32);
     for (int r0 = 0; r0 < c.vocab; r0 += chunk) {
       int nr = std::min(chunk, c.vocab - r0);
-      if ((rc = upload_tiles(embd, r0, nr, 0, c.dim, m->embd.w, r0 / 32, 1, m->st, staging, staging_bytes)))
+      if ((rc = upload_tiles(embd, r0, nr, 0, c.dim, m->embd.w, r0 / 32, 1, m->st, staging, staging_bytes, &up)))
         return fail(rc);
     }
   }
@@ -750,24 +807,24 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
                           tq + tk + tv, c.dim / 256, m->q_local + 2 * m->kv_local, c.dim)))
       return fail(rc);
     const size_t sba = (size_t)gb_tiled_sb_bytes(wq->type) * (c.dim / 256);
-    if ((rc = upload_tiles(wq, R * m->q_local, m->q_local, 0, c.dim, L.qkv.w, 0, 1, m->st, staging, staging_bytes)) ||
-        (rc = upload_tiles(wk, R * m->kv_local, m->kv_local, 0, c.dim, L.qkv.w, tq, 1, m->st, staging, staging_bytes)) ||
+    if ((rc = upload_tiles(wq, R * m->q_local, m->q_local, 0, c.dim, L.qkv.w, 0, 1, m->st, staging, staging_bytes, &up)) ||
+        (rc = upload_tiles(wk, R * m->kv_local, m->kv_local, 0, c.dim, L.qkv.w, tq, 1, m->st, staging, staging_bytes, &up)) ||
         (rc = upload_tiles(wv, R * m->kv_local, m->kv_local, 0, c.dim, L.qkv.w + (size_t)(tq + tk) * sba, 0, 1,
-                           m->st, staging, staging_bytes)))
+                           m->st, staging, staging_bytes, &up)))
       return fail(rc);
     // o: all dim rows, this rank's input columns
     if ((rc = alloc_tiled(m, &L.wo, wo->type, wo->type, 1 << 30, c.dim / 32, m->q_local / 256, c.dim, m->q_local)) ||
-        (rc = upload_tiles(wo, 0, c.dim, R * m->q_local, m->q_local, L.wo.w, 0, 1, m->st, staging, staging_bytes)))
+        (rc = upload_tiles(wo, 0, c.dim, R * m->q_local, m->q_local, L.wo.w, 0, 1, m->st, staging, staging_bytes, &up)))
       return fail(rc);
     // gate/up: this rank's FFN rows; per (row-block, super-block) the gate then the up sb-block
     const int tf = m->ffn_local / 32;
     if ((rc = alloc_tiled(m, &L.gu, wg->type, wg->type, 1 << 30, 2 * tf, c.dim / 256, 2 * m->ffn_local, c.dim)) ||
-        (rc = upload_tiles(wg, R * m->ffn_local, m->ffn_local, 0, c.dim, L.gu.w, 0, 2, m->st, staging, staging_bytes)) ||
-        (rc = upload_tiles(wu, R * m->ffn_local, m->ffn_local, 0, c.dim, L.gu.w, 1, 2, m->st, staging, staging_bytes)))
+        (rc = upload_tiles(wg, R * m->ffn_local, m->ffn_local, 0, c.dim, L.gu.w, 0, 2, m->st, staging, staging_bytes, &up)) ||
+        (rc = upload_tiles(wu, R * m->ffn_local, m->ffn_local, 0, c.dim, L.gu.w, 1, 2, m->st, staging, staging_bytes, &up)))
       return fail(rc);
     // down: all dim rows, this rank's FFN columns
     if ((rc = alloc_tiled(m, &L.down, wd->type, wd->type, 1 << 30, c.dim / 32, m->ffn_local / 256, c.dim, m->ffn_local)) ||
-        (rc = upload_tiles(wd, 0, c.dim, R * m->ffn_local, m->ffn_local, L.down.w, 0, 1, m->st, staging, staging_bytes)))
+        (rc = upload_tiles(wd, 0, c.dim, R * m->ffn_local, m->ffn_local, L.down.w, 0, 1, m->st, staging, staging_bytes, &up)))
       return fail(rc);
     // KV caches, head-major (see gb_attn.cu)
     const size_t elems = (size_t)(m->kv_local) * c.max_len;
@@ -798,7 +855,7 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
     for (int r0 = 0; r0 < m->vocab_local; r0 += chunk) {
       int nr = std::min(chunk, m->vocab_local - r0);
       if ((rc = upload_tiles(head, m->vocab_off + r0, nr, 0, c.dim, m->head.w, r0 / 32, 1, m->st, staging,
-                             staging_bytes)))
+                             staging_bytes, &up)))
         return fail(rc);
     }
   } else {
