@@ -200,6 +200,13 @@ int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool,
                          int n_kv, int hd, float scale, float *out, float *part, unsigned *counter, int S,
                          unsigned *err, cudaStream_t st);
 
+int gb_rope_kv_paged_launch(const float *qkv, int T, int q_rows, int kv_rows, int hd, const double *rope_cs,
+                            const int32_t *pos, const int32_t *table, int max_pages, int page_size, int n_pages,
+                            int max_len, float *q_out, uint16_t *kpool, uint16_t *vpool, unsigned *err,
+                            cudaStream_t st);
+int gb_f32_to_f16_launch(const float *x, __half *y, size_t n, cudaStream_t st);
+int gb_argmax_rows_launch(const float *x, int rows, int n, int32_t *out, cudaStream_t st);
+
 // gb_sample.cu: one token from logits[n]; parameters by value (p_host) or
 // from device memory (p_dev, for graph replays); the penalty window is
 // recent[n_recent] or, for the model, fed[pos-N+1..pos]; counter = *pos when

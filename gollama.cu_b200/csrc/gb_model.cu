@@ -1168,6 +1168,252 @@ int gb_linear_matmul_f16(gb_linear *l, void *stream, const uint16_t *x, int T, f
   return gb_tc_gemm_launch(g, (cudaStream_t)stream);
 }
 
+}  // extern "C"
+
+// ---- continuous batching: a decode step for many sequences at once ---------
+// Every active sequence owns pages of a paged KV pool (per layer
+// [n_pages][n_kv][page_size][head_dim] binary16); a step takes one token per
+// listed sequence and runs them as the rows of one batched pass (the
+// prefill kernels: tensor-core GEMMs over binary16 activations, RoPE/KV
+// append through the page tables, the paged attention), then the output
+// RMSNorm, the lm_head GEMM and a first-maximum argmax per row.
+struct gb_engine {
+  gb_model *m = nullptr;
+  int page_size = 0, n_pages = 0, max_batch = 0, max_pages = 0, max_pos = 0;
+  std::vector<uint16_t *> kpool, vpool;
+  std::vector<int> free_pages;
+  struct Seq {
+    bool live = false;
+    int len = 0;
+    std::vector<int> pages;
+  };
+  std::vector<Seq> seqs;
+  float *attn32 = nullptr, *logits = nullptr, *part = nullptr;
+  size_t part_floats = 0;
+  unsigned *counter = nullptr;
+  int32_t *d_in = nullptr;   // tokens [B] | pos [B] | lens [B] | table [B][max_pages]
+  int32_t *h_in = nullptr;   // pinned copy of d_in
+  int32_t *d_next = nullptr;
+  std::vector<void *> allocs;
+};
+
+namespace {
+
+void free_engine(gb_engine *e) {
+  if (!e) return;
+  if (e->m && e->m->st) cudaStreamSynchronize(e->m->st);
+  for (void *p : e->allocs) cudaFree(p);
+  if (e->h_in) cudaFreeHost(e->h_in);
+  delete e;
+}
+
+template <class T>
+int ealloc(gb_engine *e, T **p, size_t n, const char *what) {
+  void *q = nullptr;
+  GB_CUDA(cudaMalloc(&q, std::max<size_t>(n * sizeof(T), 16)), what);
+  GB_CUDA(cudaMemsetAsync(q, 0, std::max<size_t>(n * sizeof(T), 16), e->m->st), what);
+  e->allocs.push_back(q);
+  *p = (T *)q;
+  return GB_OK;
+}
+
+int engine_forward(gb_engine *e, int n) {
+  gb_model *m = e->m;
+  const gb_config &c = m->c;
+  cudaStream_t st = m->st;
+  const int hd = c.head_dim, qkv = m->q_local + 2 * m->kv_local, nkv = m->kv_local / hd, G = c.heads / c.kv_heads;
+  const int32_t *tok = e->d_in, *pos = e->d_in + e->max_batch, *lens = e->d_in + 2 * e->max_batch,
+                *table = e->d_in + 3 * e->max_batch;
+  int rc = gb_embed_rows_launch(m->embd_type, m->embd.w, m->embd_nsb, c.dim, tok, n, c.vocab, m->pf_x, nullptr, 0,
+                                c.max_len, m->err, st);
+  if (rc) return rc;
+  // paged attention splits: about two CTAs per SM, within the scratch
+  long long S = (2LL * m->sms + (long long)nkv * n - 1) / ((long long)nkv * n);
+  S = std::min<long long>(S, std::max(1, e->max_pages * e->page_size / 32));
+  S = std::min<long long>(S, 32);
+  S = std::min<long long>(S, (long long)(e->part_floats / gb_paged_part_floats(n, nkv, 1, G, hd)));
+  S = std::max<long long>(S, 1);
+  for (int l = 0; l < c.layers; l++) {
+    gb_model::Layer &L = m->layers[(size_t)l];
+    if ((rc = gb_rmsnorm_rows_f16_launch(m->pf_x, L.attn_norm, n, c.dim, c.eps, m->pf_a16, st))) return rc;
+    GbTcGemm g = tc_args(L.qkv, GB_EPI_PLAIN, n, m->pf_map_dim, m);
+    g.y = m->pf_qkv;
+    g.ldy = qkv;
+    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+    if ((rc = gb_rope_kv_paged_launch(m->pf_qkv, n, m->q_local, m->kv_local, hd, m->rope_cs, pos, table, e->max_pages,
+                                      e->page_size, e->n_pages, c.max_len, m->pf_q, e->kpool[(size_t)l],
+                                      e->vpool[(size_t)l], m->err, st)))
+      return rc;
+    if ((rc = gb_attn_paged_launch(m->pf_q, e->kpool[(size_t)l], e->vpool[(size_t)l], 1, table, lens, n, e->max_pages,
+                                   e->n_pages, e->page_size, m->q_local / hd, nkv, hd, 1.f / sqrtf((float)hd),
+                                   e->attn32, e->part, e->counter, (int)S, m->err, st)))
+      return rc;
+    if ((rc = gb_f32_to_f16_launch(e->attn32, m->pf_a16, (size_t)n * m->q_local, st))) return rc;
+    g = tc_args(L.wo, GB_EPI_RESID, n, m->pf_map_q, m);
+    g.y = m->pf_x;
+    g.ldy = c.dim;
+    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+    if ((rc = gb_rmsnorm_rows_f16_launch(m->pf_x, L.ffn_norm, n, c.dim, c.eps, m->pf_a16, st))) return rc;
+    g = tc_args(L.gu, GB_EPI_SWIGLU, n, m->pf_map_dim, m);
+    g.rows = m->ffn_local;
+    g.ntiles = L.gu.ntiles / 2;
+    g.act = m->pf_act16;
+    g.ld_act = m->ffn_local;
+    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+    g = tc_args(L.down, GB_EPI_RESID, n, m->pf_map_ffn, m);
+    g.y = m->pf_x;
+    g.ldy = c.dim;
+    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+  }
+  if ((rc = gb_rmsnorm_rows_f16_launch(m->pf_x, m->out_norm, n, c.dim, c.eps, m->pf_a16, st))) return rc;
+  GbTcGemm g = tc_args(m->head, GB_EPI_PLAIN, n, m->pf_map_dim, m);
+  g.y = e->logits;
+  g.ldy = c.vocab;
+  if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+  return gb_argmax_rows_launch(e->logits, n, c.vocab, e->d_next, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int gb_engine_create(gb_model *m, int page_size, int n_pages, int max_batch, gb_engine **out) {
+  gb_clear_error();
+  if (!m || !out || page_size <= 0 || n_pages <= 0 || max_batch <= 0)
+    return gb_fail(GB_ERR_INVALID, "engine: bad arguments");
+  if (m->c.tp_world > 1) return gb_fail(GB_ERR_UNSUPPORTED, "engine: continuous batching under tensor parallelism");
+  if (max_batch > kPrefillChunk)
+    return gb_fail(GB_ERR_UNSUPPORTED, "engine: at most %d sequences a step", kPrefillChunk);
+  if (m->c.head_dim % 32 || m->c.head_dim > 128 || m->c.heads / m->c.kv_heads > 8)
+    return gb_fail(GB_ERR_UNSUPPORTED, "engine: head_dim %d, %d query heads per KV head", m->c.head_dim,
+                   m->c.heads / m->c.kv_heads);
+  int rc = prefill_workspace(m);
+  if (rc) return rc;
+  std::unique_ptr<gb_engine, void (*)(gb_engine *)> e(new gb_engine, free_engine);
+  e->m = m;
+  e->page_size = page_size;
+  e->n_pages = n_pages;
+  e->max_batch = max_batch;
+  e->max_pos = m->c.max_len;  // the RoPE table's positions
+  e->max_pages = (e->max_pos + page_size - 1) / page_size;
+  const gb_config &c = m->c;
+  const int hd = c.head_dim, nkv = m->kv_local / hd, G = c.heads / c.kv_heads;
+  const size_t pool = (size_t)n_pages * nkv * page_size * hd;
+  e->kpool.resize((size_t)c.layers);
+  e->vpool.resize((size_t)c.layers);
+  for (int l = 0; l < c.layers; l++)
+    if ((rc = ealloc(e.get(), &e->kpool[(size_t)l], pool, "engine: KV pool")) ||
+        (rc = ealloc(e.get(), &e->vpool[(size_t)l], pool, "engine: KV pool")))
+      return rc;
+  e->part_floats = gb_paged_part_floats(max_batch, nkv, 4, G, hd);
+  if ((rc = ealloc(e.get(), &e->attn32, (size_t)max_batch * m->q_local, "engine: work")) ||
+      (rc = ealloc(e.get(), &e->logits, (size_t)max_batch * c.vocab, "engine: work")) ||
+      (rc = ealloc(e.get(), &e->part, e->part_floats, "engine: work")) ||
+      (rc = ealloc(e.get(), &e->counter, (size_t)max_batch * nkv, "engine: work")) ||
+      (rc = ealloc(e.get(), &e->d_in, (size_t)max_batch * (3 + e->max_pages), "engine: work")) ||
+      (rc = ealloc(e.get(), &e->d_next, (size_t)max_batch, "engine: work")))
+    return rc;
+  GB_CUDA(cudaMallocHost(&e->h_in, sizeof(int32_t) * (size_t)max_batch * (3 + e->max_pages)), "engine: staging");
+  for (int p = n_pages - 1; p >= 0; p--) e->free_pages.push_back(p);
+  GB_CUDA(cudaStreamSynchronize(m->st), "engine: create");
+  *out = e.release();
+  return GB_OK;
+}
+
+int gb_engine_add(gb_engine *e, int *seq_id) {
+  gb_clear_error();
+  if (!e || !seq_id) return gb_fail(GB_ERR_INVALID, "engine: null argument");
+  for (size_t i = 0; i < e->seqs.size(); i++)
+    if (!e->seqs[i].live) {
+      e->seqs[i] = gb_engine::Seq();
+      e->seqs[i].live = true;
+      *seq_id = (int)i;
+      return GB_OK;
+    }
+  e->seqs.emplace_back();
+  e->seqs.back().live = true;
+  *seq_id = (int)e->seqs.size() - 1;
+  return GB_OK;
+}
+
+int gb_engine_release(gb_engine *e, int seq_id) {
+  gb_clear_error();
+  if (!e || seq_id < 0 || seq_id >= (int)e->seqs.size() || !e->seqs[(size_t)seq_id].live)
+    return gb_fail(GB_ERR_INVALID, "engine: no sequence %d", seq_id);
+  gb_engine::Seq &q = e->seqs[(size_t)seq_id];
+  for (int p : q.pages) e->free_pages.push_back(p);
+  q = gb_engine::Seq();
+  return GB_OK;
+}
+
+int gb_engine_seq_len(const gb_engine *e, int seq_id) {
+  if (!e || seq_id < 0 || seq_id >= (int)e->seqs.size() || !e->seqs[(size_t)seq_id].live) return -1;
+  return e->seqs[(size_t)seq_id].len;
+}
+
+int gb_engine_free_pages(const gb_engine *e) { return e ? (int)e->free_pages.size() : -1; }
+
+int gb_engine_step(gb_engine *e, int n, const int32_t *seq_ids, const int32_t *tokens, float *host_logits,
+                   int32_t *next) {
+  gb_clear_error();
+  if (!e || n <= 0 || !seq_ids || !tokens) return gb_fail(GB_ERR_INVALID, "engine: bad step arguments");
+  if (n > e->max_batch) return gb_fail(GB_ERR_INVALID, "engine: %d sequences, at most %d", n, e->max_batch);
+  gb_model *m = e->m;
+  // validate every row before touching any state
+  int need_pages = 0;
+  for (int t = 0; t < n; t++) {
+    const int id = seq_ids[t];
+    if (id < 0 || id >= (int)e->seqs.size() || !e->seqs[(size_t)id].live)
+      return gb_fail(GB_ERR_INVALID, "engine: no sequence %d", id);
+    for (int u = 0; u < t; u++)
+      if (seq_ids[u] == id) return gb_fail(GB_ERR_INVALID, "engine: sequence %d twice in one step", id);
+    if (tokens[t] < 0 || tokens[t] >= m->c.vocab)
+      return gb_fail(GB_ERR_INVALID, "model: token %d outside the vocabulary", tokens[t]);
+    const int len = e->seqs[(size_t)id].len;
+    if (len >= e->max_pos) return gb_fail(GB_ERR_INVALID, "engine: sequence %d is full (%d positions)", id, len);
+    if ((int)e->seqs[(size_t)id].pages.size() <= len / e->page_size) need_pages++;
+  }
+  if (need_pages > (int)e->free_pages.size())
+    return gb_fail(GB_ERR_UNSUPPORTED, "engine: out of KV pages (%d needed, %zu free)", need_pages,
+                   e->free_pages.size());
+  int32_t *h = e->h_in;
+  const int B = e->max_batch;
+  for (int t = 0; t < n; t++) {
+    gb_engine::Seq &q = e->seqs[(size_t)seq_ids[t]];
+    if ((int)q.pages.size() <= q.len / e->page_size) {  // its next position starts a page
+      q.pages.push_back(e->free_pages.back());
+      e->free_pages.pop_back();
+    }
+    h[t] = tokens[t];
+    h[B + t] = q.len;
+    h[2 * B + t] = q.len + 1;
+    int32_t *row = h + 3 * B + (size_t)t * e->max_pages;
+    for (int i = 0; i < e->max_pages; i++) row[i] = i < (int)q.pages.size() ? q.pages[(size_t)i] : -1;
+  }
+  GB_CUDA(cudaMemcpyAsync(e->d_in, h, sizeof(int32_t) * (size_t)B * (3 + e->max_pages), cudaMemcpyHostToDevice, m->st),
+          "engine: step inputs");
+  int rc = engine_forward(e, n);
+  if (!rc && host_logits)
+    rc = cudaMemcpyAsync(host_logits, e->logits, sizeof(float) * (size_t)n * m->c.vocab, cudaMemcpyDeviceToHost,
+                         m->st) == cudaSuccess
+             ? GB_OK
+             : gb_fail(GB_ERR_CUDA, "engine: logits");
+  if (!rc && next)
+    rc = cudaMemcpyAsync(next, e->d_next, sizeof(int32_t) * (size_t)n, cudaMemcpyDeviceToHost, m->st) == cudaSuccess
+             ? GB_OK
+             : gb_fail(GB_ERR_CUDA, "engine: tokens");
+  if (!rc) rc = check_err(m);
+  if (rc) return rc;
+  for (int t = 0; t < n; t++) e->seqs[(size_t)seq_ids[t]].len++;
+  return GB_OK;
+}
+
+int gb_engine_free(gb_engine *e) {
+  gb_clear_error();
+  free_engine(e);
+  return GB_OK;
+}
+
 int gb_model_set_sampler(gb_model *m, const gb_sample_params *p) {
   gb_clear_error();
   if (!m) return gb_fail(GB_ERR_INVALID, "model: null model");

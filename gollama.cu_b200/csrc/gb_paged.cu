@@ -16,6 +16,8 @@
 // (sequence, KV head)). float32 arithmetic throughout.
 #include <math.h>
 
+#include <algorithm>
+
 #include "gb_device.cuh"
 #include "gb_internal.h"
 
@@ -200,6 +202,81 @@ __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a)
   if (threadIdx.x == 0) a.counter[(size_t)b * a.n_kv + h] = 0u;  // ready for the next launch
 }
 
+// ---- batched decode helpers (one row per sequence) --------------------------
+
+// RoPE of row t's q and k at position pos[t] (the model's float64 angle
+// table, cpu.RoPE's rotation), q to q_out[t], k and v (binary16) into the
+// pools at row pos % page_size of page table[t][pos / page_size].
+__global__ void rope_kv_paged_kernel(const float *qkv, int q_rows, int kv_rows, int hd, const double *rope_cs,
+                                     const int32_t *pos, const int32_t *table, int max_pages, int page_size,
+                                     int n_pages, int max_len, float *q_out, uint16_t *kpool, uint16_t *vpool,
+                                     unsigned *err) {
+  const int t = blockIdx.x, p = pos[t];
+  const int n_kv = kv_rows / hd;
+  const bool ok = p >= 0 && p < max_len && p / page_size < max_pages;
+  int page = ok ? table[(size_t)t * max_pages + p / page_size] : -1;
+  if (!ok || page < 0 || page >= n_pages) {
+    if (threadIdx.x == 0 && err) atomicOr(err, GB_DEVERR_POS);
+    return;
+  }
+  const int off = p % page_size;
+  const float *row = qkv + (size_t)t * (q_rows + 2 * kv_rows);
+  const double *cs = rope_cs + (size_t)p * hd;
+  const int pairs = (q_rows + kv_rows) / 2;
+  for (int i = threadIdx.x; i < pairs + kv_rows; i += blockDim.x) {
+    if (i < pairs) {
+      const int r = 2 * i, rr = r < q_rows ? r : r - q_rows, jj = (rr % hd) >> 1;
+      const double c = cs[2 * jj], sn = cs[2 * jj + 1], x0 = row[r], x1 = row[r + 1];
+      const float o0 = (float)__dsub_rn(__dmul_rn(x0, c), __dmul_rn(x1, sn));
+      const float o1 = (float)__dadd_rn(__dmul_rn(x0, sn), __dmul_rn(x1, c));
+      if (r < q_rows) {
+        q_out[(size_t)t * q_rows + r] = o0;
+        q_out[(size_t)t * q_rows + r + 1] = o1;
+      } else {
+        const int h = rr / hd, d = rr % hd;
+        const size_t idx = (((size_t)page * n_kv + h) * page_size + off) * hd + d;
+        kpool[idx] = gb_float_to_half_rn(o0);
+        kpool[idx + 1] = gb_float_to_half_rn(o1);
+      }
+    } else {
+      const int rr = i - pairs, h = rr / hd, d = rr % hd;
+      vpool[(((size_t)page * n_kv + h) * page_size + off) * hd + d] = gb_float_to_half_rn(row[q_rows + kv_rows + rr]);
+    }
+  }
+}
+
+__global__ void f32_to_f16_kernel(const float *x, __half *y, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    y[i] = __float2half_rn(x[i]);
+}
+
+// First maximum of each row (model.Argmax's rule; NaN never wins).
+__global__ void argmax_rows_kernel(const float *x, int n, int32_t *out) {
+  const float *row = x + (size_t)blockIdx.x * n;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = row[i];
+    if (v != v) continue;
+    uint32_t b = __float_as_uint(v);
+    if ((b << 1) == 0u) b = 0u;
+    const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    const unsigned long long key = ((unsigned long long)k << 32) | (0xFFFFFFFFu - (uint32_t)i);
+    best = key > best ? key : best;
+  }
+  __shared__ unsigned long long red[32];
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(0xffffffffu, best, o);
+    best = w > best ? w : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = red[w] > best ? red[w] : best;
+    best = red[0] > best ? red[0] : best;
+    out[blockIdx.x] = best ? (int32_t)(0xFFFFFFFFu - (uint32_t)best) : 0;
+  }
+}
+
 }  // namespace
 
 size_t gb_paged_part_floats(int B, int n_kv, int S, int G, int hd) {
@@ -239,5 +316,31 @@ int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool,
   else
     attn_paged_kernel<false><<<grid, kPW * 32, 0, st>>>(a);
   GB_CUDA(cudaGetLastError(), "gpu: paged attention");
+  return GB_OK;
+}
+
+int gb_rope_kv_paged_launch(const float *qkv, int T, int q_rows, int kv_rows, int hd, const double *rope_cs,
+                            const int32_t *pos, const int32_t *table, int max_pages, int page_size, int n_pages,
+                            int max_len, float *q_out, uint16_t *kpool, uint16_t *vpool, unsigned *err,
+                            cudaStream_t st) {
+  if (T <= 0) return GB_OK;
+  rope_kv_paged_kernel<<<T, 256, 0, st>>>(qkv, q_rows, kv_rows, hd, rope_cs, pos, table, max_pages, page_size, n_pages,
+                                          max_len, q_out, kpool, vpool, err);
+  GB_CUDA(cudaGetLastError(), "engine: RoPE/KV append");
+  return GB_OK;
+}
+
+int gb_f32_to_f16_launch(const float *x, __half *y, size_t n, cudaStream_t st) {
+  if (!n) return GB_OK;
+  const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
+  f32_to_f16_kernel<<<blocks, 256, 0, st>>>(x, y, n);
+  GB_CUDA(cudaGetLastError(), "engine: convert");
+  return GB_OK;
+}
+
+int gb_argmax_rows_launch(const float *x, int rows, int n, int32_t *out, cudaStream_t st) {
+  if (rows <= 0) return GB_OK;
+  argmax_rows_kernel<<<rows, 1024, 0, st>>>(x, n, out);
+  GB_CUDA(cudaGetLastError(), "engine: argmax");
   return GB_OK;
 }

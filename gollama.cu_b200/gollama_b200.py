@@ -89,6 +89,9 @@ _SIGS = {
     "gb_gpu_attn_decode_paged": (I, [P, P, P, P, P, I, P, P, I, I, I, I, I, I, I, F, P]),
     "gb_model_set_sampler": (I, [P, P]), "gb_model_prefill": (I, [P, P, I, I, P]),
     "gb_linear_matmul_f16": (I, [P, P, P, I, P]),
+    "gb_engine_create": (I, [P, I, I, I, C.POINTER(P)]), "gb_engine_add": (I, [P, C.POINTER(I)]),
+    "gb_engine_release": (I, [P, I]), "gb_engine_seq_len": (I, [P, I]), "gb_engine_free_pages": (I, [P]),
+    "gb_engine_step": (I, [P, I, P, P, P, P]), "gb_engine_free": (I, [P]),
     "gb_linear_upload": (I, [I, I, P, S, I, I, C.POINTER(P)]), "gb_linear_matvec": (I, [P, P, P, P]),
     "gb_linear_info": (I, [P, C.POINTER(I), C.POINTER(I), C.POINTER(I), C.POINTER(S)]),
     "gb_linear_free": (I, [P]),
@@ -384,6 +387,45 @@ class Model:
 
     def __exit__(self, *a):
         self.close()
+
+
+class Engine:
+    """Continuous batching over a Model: paged KV, one batched pass per step."""
+
+    def __init__(self, model: "Model", page_size: int = 16, n_pages: int = 1024, max_batch: int = 64):
+        h = P()
+        _check(lib().gb_engine_create(model.h, page_size, n_pages, max_batch, C.byref(h)))
+        self.h, self.model, self.vocab = h, model, model.config.vocab
+
+    def add(self) -> int:
+        i = C.c_int()
+        _check(lib().gb_engine_add(self.h, C.byref(i)))
+        return i.value
+
+    def release(self, seq_id: int) -> None:
+        _check(lib().gb_engine_release(self.h, seq_id))
+
+    def seq_len(self, seq_id: int) -> int:
+        return lib().gb_engine_seq_len(self.h, seq_id)
+
+    def free_pages(self) -> int:
+        return lib().gb_engine_free_pages(self.h)
+
+    def step(self, seq_ids, tokens, logits: bool = True):
+        """One token per sequence; returns (logits [n][vocab] or None, next tokens [n])."""
+        ids = np.ascontiguousarray(np.asarray(seq_ids, np.int32))
+        toks = np.ascontiguousarray(np.asarray(tokens, np.int32))
+        n = ids.size
+        out = np.empty((n, self.vocab), np.float32) if logits else None
+        nxt = np.empty(n, np.int32)
+        _check(lib().gb_engine_step(self.h, n, ids.ctypes.data, toks.ctypes.data,
+                                    out.ctypes.data if logits else None, nxt.ctypes.data))
+        return out, nxt
+
+    def close(self):
+        if self.h:
+            _check(lib().gb_engine_free(self.h))
+            self.h = None
 
 
 class SynthImage:

@@ -245,6 +245,38 @@ int gb_model_read_tokens(gb_model *m, int pos0, int n, int32_t *out_tokens);
  * tokens), writing their K/V; the last goes through the decode step, whose
  * logits are copied to host_logits[vocab] (NULL: not copied). One GPU only. */
 int gb_model_prefill(gb_model *m, const int32_t *tokens, int n, int pos0, float *host_logits);
+/* ---- continuous batching (added; the reference's roadmap "Paged KV cache
+ * plus continuous batching", ROADMAP.md:197-202) ---------------------------
+ * An engine over a loaded model (one GPU) decodes many sequences at once.
+ * Each sequence owns pages of a paged KV pool (per layer
+ * [n_pages][n_kv][page_size][head_dim] binary16) taken from a free list as it
+ * grows and returned by gb_engine_release. A step feeds one token to each of
+ * n listed sequences (at their next positions) and runs them as the rows of
+ * one batched pass: the prefill's tensor-core GEMMs (binary16 operands, f32
+ * accumulate), RoPE and K/V append through the page tables, the paged
+ * attention, then the output RMSNorm and lm_head; logits agree with the
+ * one-sequence decode to the prefill's tolerance. Sequences may join and
+ * leave between steps. The engine shares the model's stream and prefill
+ * workspace: do not interleave its calls with the model's on other threads. */
+typedef struct gb_engine gb_engine;
+/* page_size positions per page, n_pages pages per layer, at most max_batch
+ * (<= 512) sequences per step. */
+int gb_engine_create(gb_model *m, int page_size, int n_pages, int max_batch, gb_engine **out);
+/* A new, empty sequence; its id is reused after gb_engine_release. */
+int gb_engine_add(gb_engine *e, int *seq_id);
+int gb_engine_release(gb_engine *e, int seq_id);
+/* Positions fed so far (-1: no such sequence); free pages of the pool. */
+int gb_engine_seq_len(const gb_engine *e, int seq_id);
+int gb_engine_free_pages(const gb_engine *e);
+/* One token for each of seq_ids[0..n) (distinct live sequences). The logits
+ * of each row are copied to host_logits[n][vocab] and the first maximum of
+ * each row (model.Argmax's rule) to next[n]; either may be NULL. Fails
+ * (GB_ERR_UNSUPPORTED) without changing any sequence when the pool has too
+ * few free pages for the step. */
+int gb_engine_step(gb_engine *e, int n, const int32_t *seq_ids, const int32_t *tokens, float *host_logits,
+                   int32_t *next);
+int gb_engine_free(gb_engine *e);
+
 /* Added: the token rule of gb_model_next / generate / decode_async. NULL
  * (the default) is greedy model.Argmax; otherwise the sampler above with
  * counter = the position of the step and the penalty window = the tokens fed
