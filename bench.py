@@ -336,6 +336,32 @@ def run_ours(args, cfg, world, rank, local):
                    "how": "gb_model_prefill from host token ids: tcgen05 GEMMs (binary16 operands, f32 accumulate) "
                           "+ tensor-core causal attention, last token through the decode step; CUDA events, "
                           f"mean of {reps}"}
+    # continuous batching: the engine decodes B sequences per step (one GPU)
+    batched = None
+    if world == 1 and args.batch > 1:
+        e = gb.Engine(m, page_size=64, n_pages=args.batch * 4, max_batch=args.batch)
+        ids = [e.add() for _ in range(args.batch)]
+        btoks = prompt_tokens(spec, args.batch)
+        for _ in range(4):  # warm-up: positions 0..3 of every sequence
+            _, btoks = e.step(ids, btoks, logits=False)
+        torch.cuda.synchronize()
+        nsteps = 32
+        w0 = time.perf_counter()
+        ev0.record(stream)
+        for _ in range(nsteps):
+            _, btoks = e.step(ids, btoks, logits=False)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - w0
+        bms = ev0.elapsed_time(ev1) / nsteps
+        batched = {"batch": args.batch, "value": round(args.batch * nsteps / (bms * nsteps / 1e3), 1), "unit": "tok/s",
+                   "ms_per_step": round(bms, 3), "e2e_tok_s": round(args.batch * nsteps / wall, 1),
+                   "positions": f"4..{4 + nsteps - 1}",
+                   "how": "gb_engine_step: B sequences one token each per step through the tensor-core GEMMs and the "
+                          "paged attention; value = CUDA events around 32 steps, each synchronous (ids in, next tokens "
+                          "out, status check), e2e = wall clock of the same loop"}
+        e.close()
+
     result = {
         "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
@@ -355,6 +381,7 @@ def run_ours(args, cfg, world, rank, local):
                           "roofline_tok_s": round(peak * 1e9 / bytes_tok, 1)},
         "kernel_ms_per_step": breakdown,
         "prefill": prefill,
+        "batched_decode": batched,
         "e2e": e2e,
         "gpu_launches": m.launches_per_step() * args.steps,
         "clocks": clk,
@@ -454,6 +481,8 @@ def main():
     ap.add_argument("--config", default="8b", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=64,
+                    help="sequences per step of the continuous-batching measurement (0 = skip)")
     ap.add_argument("--prefill-tokens", type=int, default=512,
                     help="prompt length of the batched-prefill measurement (0 = skip)")
     ap.add_argument("--layers", type=int, default=0,
