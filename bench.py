@@ -317,25 +317,28 @@ def run_ours(args, cfg, world, rank, local):
     # batched prefill of a 512-token prompt (one GPU; the timed decode above is done,
     # so overwriting cache positions 0..511 does not touch it)
     prefill = None
-    if world == 1 and args.prefill_tokens > 1:
+    if args.prefill_tokens > 1:
         pt = prompt_tokens(spec, args.prefill_tokens)
         m.prefill(pt, 0)  # warm-up (allocates the workspace)
         torch.cuda.synchronize()
+        barrier(world)
         reps = 3
         ev0.record(stream)
         for _ in range(reps):
             m.prefill(pt, 0)
         ev1.record(stream)
         torch.cuda.synchronize()
-        pms = ev0.elapsed_time(ev1) / reps
+        barrier(world)
+        pms = max_over_ranks(ev0.elapsed_time(ev1) / reps, world)
         tpk, tsrc = tensor_peak()
         fl = prefill_flops(c, len(pt))
         prefill = {"tokens": len(pt), "value": round(len(pt) / (pms / 1e3), 1), "unit": "tok/s",
                    "ms": round(pms, 3), "tflops": round(fl / (pms / 1e3) / 1e12, 1),
                    "frac_of_tensor_peak": round(fl / (pms / 1e3) / 1e12 / tpk, 4), "peak_source": tsrc,
                    "how": "gb_model_prefill from host token ids: tcgen05 GEMMs (binary16 operands, f32 accumulate) "
-                          "+ tensor-core causal attention, last token through the decode step; CUDA events, "
-                          f"mean of {reps}"}
+                          "+ tensor-core causal attention, last token through the decode step; under tensor "
+                          "parallelism the o/down partials summed by NCCL all-reduces; CUDA events, "
+                          f"mean of {reps}, max over ranks"}
     # continuous batching: the engine decodes B sequences per step (one GPU)
     batched = None
     if world == 1 and args.batch > 1:

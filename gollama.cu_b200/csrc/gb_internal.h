@@ -145,6 +145,7 @@ int gb_embed_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32
                     cudaStream_t st, bool pdl);
 // x += y with per-32 sums of squares: the residual after a collective.
 int gb_resid_launch(float *x, const float *y, int n, float *ssq, cudaStream_t st, bool pdl);
+int gb_add_launch(const float *a, const float *b, float *out, int n, cudaStream_t st);
 // Tensor parallel: wait for every rank's partial in peer slot `slot`, then
 // x += sum of the partials (rank order, identical on every rank) with per-32
 // sums of squares.

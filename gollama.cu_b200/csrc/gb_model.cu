@@ -177,6 +177,7 @@ struct gb_model {
   __half *pf_a16 = nullptr, *pf_act16 = nullptr;
   int32_t *pf_tokens = nullptr;
   float *pf_part = nullptr;  // split-K partials of the prefill GEMMs
+  float *pf_tmp = nullptr;   // tensor parallel: this rank's o / down partial [chunk][dim]
   size_t pf_part_floats = 0;
   CUtensorMap pf_map_dim, pf_map_q, pf_map_ffn;
   unsigned *err = nullptr;
@@ -960,6 +961,7 @@ int prefill_workspace(gb_model *m) {
   // at most 4 token tiles x 128 columns (or 2 x 256 for the gate/up pairs)
   m->pf_part_floats = (size_t)m->sms * 4 * 128 * 128;
   if ((rc = dalloc(m, &m->pf_part, m->pf_part_floats, "model: prefill workspace"))) return rc;
+  if (c.tp_world > 1 && (rc = dalloc(m, &m->pf_tmp, (size_t)Tc * c.dim, "model: prefill workspace"))) return rc;
   if ((rc = gb_tmap_f16_rows(m->pf_a16, Tc, c.dim, &m->pf_map_dim)) ||
       (rc = gb_tmap_f16_rows(m->pf_a16, Tc, m->q_local, &m->pf_map_q)) ||
       (rc = gb_tmap_f16_rows(m->pf_act16, Tc, m->ffn_local, &m->pf_map_ffn)))
@@ -983,6 +985,23 @@ GbTcGemm tc_args(const Tiled &t, int epi, int T, const CUtensorMap &map, gb_mode
   g.part_floats = m->pf_part_floats;
   g.tmap_a = map;
   return g;
+}
+
+// x += A W^T for the row-parallel o and down projections. Under tensor
+// parallelism each rank's product over its input columns is a partial: the
+// ranks' partials are summed by an NCCL all-reduce on the model stream (every
+// rank makes the same calls in the same order), then added to x.
+int row_parallel(gb_model *m, const Tiled &w, int T, const CUtensorMap &map) {
+  const gb_config &c = m->c;
+  const bool tp = c.tp_world > 1;
+  GbTcGemm g = tc_args(w, tp ? GB_EPI_PLAIN : GB_EPI_RESID, T, map, m);
+  g.y = tp ? m->pf_tmp : m->pf_x;
+  g.ldy = c.dim;
+  int rc = gb_tc_gemm_launch(g, m->st);
+  if (rc || !tp) return rc;
+  GB_NCCL(nccl()->allReduce(m->pf_tmp, m->pf_tmp, (size_t)T * c.dim, ncclFloat, ncclSum, m->comm, m->st),
+          "model: prefill all-reduce");
+  return gb_add_launch(m->pf_x, m->pf_tmp, m->pf_x, T * c.dim, m->st);
 }
 
 // Tokens [0, T) of one chunk at positions p0..: every layer's K/V; the
@@ -1009,10 +1028,7 @@ int prefill_chunk(gb_model *m, int T, int p0) {
     if ((rc = gb_attn_prefill_launch(m->pf_q, T, p0, m->q_local / hd, m->kv_local / hd, hd, L.kc, L.vc, c.kv_f16,
                                      c.max_len, m->pf_a16, st)))
       return rc;
-    g = tc_args(L.wo, GB_EPI_RESID, T, m->pf_map_q, m);
-    g.y = m->pf_x;
-    g.ldy = c.dim;
-    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+    if ((rc = row_parallel(m, L.wo, T, m->pf_map_q))) return rc;
     if ((rc = gb_rmsnorm_rows_f16_launch(m->pf_x, L.ffn_norm, T, c.dim, c.eps, m->pf_a16, st))) return rc;
     g = tc_args(L.gu, GB_EPI_SWIGLU, T, m->pf_map_dim, m);
     g.rows = m->ffn_local;  // one half of the gate/up pairs
@@ -1020,10 +1036,7 @@ int prefill_chunk(gb_model *m, int T, int p0) {
     g.act = m->pf_act16;
     g.ld_act = m->ffn_local;
     if ((rc = gb_tc_gemm_launch(g, st))) return rc;
-    g = tc_args(L.down, GB_EPI_RESID, T, m->pf_map_ffn, m);
-    g.y = m->pf_x;
-    g.ldy = c.dim;
-    if ((rc = gb_tc_gemm_launch(g, st))) return rc;
+    if ((rc = row_parallel(m, L.down, T, m->pf_map_ffn))) return rc;
   }
   return GB_OK;
 }
@@ -1121,7 +1134,6 @@ int gb_model_prefill(gb_model *m, const int32_t *tokens, int n, int pos0, float 
   for (int i = 0; i < n; i++)
     if (tokens[i] < 0 || tokens[i] >= m->c.vocab)
       return gb_fail(GB_ERR_INVALID, "model: token %d outside the vocabulary", tokens[i]);
-  if (m->c.tp_world > 1) return gb_fail(GB_ERR_UNSUPPORTED, "model: batched prefill under tensor parallelism");
   int rc;
   if (n > 1 && (rc = prefill_workspace(m))) return rc;
   for (int c0 = 0; c0 < n - 1; c0 += kPrefillChunk) {

@@ -392,6 +392,12 @@ int gb_embed_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32
   return GB_OK;
 }
 
+int gb_add_launch(const float *a, const float *b, float *out, int n, cudaStream_t st) {
+  add_kernel<<<blocks_for(n, 256), 256, 0, st>>>(a, b, out, n);
+  GB_CUDA(cudaGetLastError(), "gpu: add");
+  return GB_OK;
+}
+
 int gb_resid_launch(float *x, const float *y, int n, float *ssq, cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];
   int groups = n / 32;

@@ -243,7 +243,9 @@ int gb_model_read_tokens(gb_model *m, int pos0, int n, int32_t *out_tokens);
  * layer at once (tensor-core GEMMs over binary16 activations and weights with
  * float32 accumulation, causal attention over the cache; chunks of up to 512
  * tokens), writing their K/V; the last goes through the decode step, whose
- * logits are copied to host_logits[vocab] (NULL: not copied). One GPU only. */
+ * logits are copied to host_logits[vocab] (NULL: not copied; under tensor
+ * parallelism every rank makes the call with the same tokens, the o and down
+ * partials are summed by NCCL all-reduces, and rank 0 receives the logits). */
 int gb_model_prefill(gb_model *m, const int32_t *tokens, int n, int pos0, float *host_logits);
 /* ---- continuous batching (added; the reference's roadmap "Paged KV cache
  * plus continuous batching", ROADMAP.md:197-202) ---------------------------

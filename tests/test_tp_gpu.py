@@ -15,6 +15,7 @@ pytestmark = pytest.mark.gpu
 # per rank), vocabulary rows and the per-rank q width (a 256 multiple)
 CFG = dict(layers=2, dim=512, ffn=1024, heads=8, kv_heads=2, head_dim=64, vocab=1024, ctx_len=96, mix=1, seed=21)
 TOKENS = [7, 300, 1023, 0]
+PREFILL = [int(t) for t in np.random.default_rng(5).integers(0, 1024, 40)]
 
 
 def _free_port():
@@ -42,10 +43,13 @@ def _rank(rank, world, port, out_dir):
         m = gb.Model(img, max_len=64, device=rank, tp_rank=rank, tp_world=world, nccl_id=obj[0])
         logits = [m.forward(t, p).copy() for p, t in enumerate(TOKENS)]
         toks = m.generate(int(np.argmax(logits[-1])), len(TOKENS), 6)
+        # batched prefill over both ranks (all-reduced o/down partials)
+        pre = m.prefill(PREFILL, 0).copy()
         m.close()
         if rank == 0:
             np.save(os.path.join(out_dir, "tp_logits.npy"), np.stack(logits))
             np.save(os.path.join(out_dir, "tp_tokens.npy"), toks)
+            np.save(os.path.join(out_dir, "tp_prefill.npy"), pre)
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -71,5 +75,16 @@ def test_two_gpu_step_matches_one_gpu_and_cpu(gb, orc, cuda, tmp_path):
         assert (d <= 1e-3 + 1e-4 * np.abs(want)).all(), f"pos {p}: max abs diff {d.max():.3g}"
     one_toks = m.generate(int(np.argmax(tp[-1])), len(TOKENS), 6)
     assert list(tp_toks) == list(one_toks)
+    # the two-GPU prefill against the one-GPU prefill (binary16 GEMMs on both;
+    # the sharded sums differ in rounding) and against 40 one-GPU decode steps
+    one_pre = m.prefill(PREFILL, 0).copy()
+    tp_pre = np.load(tmp_path / "tp_prefill.npy")
+    rel = lambda a, b: float(np.abs(a.astype(np.float64) - b).max() / np.abs(b).max())
+    assert rel(tp_pre, one_pre) < 5e-3, rel(tp_pre, one_pre)
+    d = gb.Model(img, max_len=64)
+    for p, t in enumerate(PREFILL):
+        dec = d.forward(t, p).copy()
+    d.close()
+    assert rel(tp_pre, dec) < 5e-3, rel(tp_pre, dec)
     m.close()
     om.close()
