@@ -1090,11 +1090,22 @@ int gb_model_forward(gb_model *m, int32_t token, int pos, float *host_logits) {
             "model: logits all-gather");
     src = m->logits_full;
   }
+  // a page-locked caller buffer takes the copy directly; pageable memory goes
+  // through the model's pinned staging buffer and one host copy
+  bool pinned = false;
+  if (host_logits) {
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, host_logits) == cudaSuccess)
+      pinned = pa.type == cudaMemoryTypeHost;
+    else
+      (void)cudaGetLastError();  // not a CUDA pointer: leave no error for the next launch check
+  }
   if (host_logits)
-    GB_CUDA(cudaMemcpyAsync(m->h_logits, src, sizeof(float) * (size_t)m->c.vocab, cudaMemcpyDeviceToHost, m->st),
+    GB_CUDA(cudaMemcpyAsync(pinned ? host_logits : m->h_logits, src, sizeof(float) * (size_t)m->c.vocab,
+                            cudaMemcpyDeviceToHost, m->st),
             "model: logits");
   if ((rc = check_err(m))) return rc;
-  if (host_logits) memcpy(host_logits, m->h_logits, sizeof(float) * (size_t)m->c.vocab);
+  if (host_logits && !pinned) memcpy(host_logits, m->h_logits, sizeof(float) * (size_t)m->c.vocab);
   return GB_OK;
 }
 

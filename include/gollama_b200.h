@@ -222,7 +222,9 @@ int gb_model_load_mem(const void *gguf, size_t len, const gb_model_opts *opts, g
 int gb_model_config(const gb_model *m, gb_config *c);
 /* (*Model).Forward, model/model.go:313: logits of `token` at `pos` copied
  * into host_logits[vocab] (on rank 0 when tp_world > 1; other ranks may
- * pass NULL). Same validation and errors as the reference. */
+ * pass NULL). Same validation and errors as the reference. A page-locked
+ * host_logits (cudaHostAlloc / registered) receives the device copy
+ * directly; pageable memory goes through an internal pinned buffer. */
 int gb_model_forward(gb_model *m, int32_t token, int pos, float *host_logits);
 /* Added: one greedy step entirely on the device; only the next token id
  * comes back to the host (model.Argmax applied on the device). */

@@ -31,6 +31,21 @@ def test_host_argmax_rule(gb):
     assert gb.argmax(np.array([-np.inf, -np.inf], np.float32)) == 0
 
 
+def test_host_argmax_matches_oracle(gb, orc):
+    # the library's two-pass (vectorised) form against the oracle's walk of
+    # model.Argmax: ties, NaN at 0 and later, signed zeros, infinities, and
+    # lengths around the 16-element blocks
+    rng = np.random.default_rng(11)
+    specials = np.array([0.0, -0.0, 1.0, -1.0, 3.0, 3.0, np.inf, -np.inf, np.nan, 2.5], np.float32)
+    for t in range(3000):
+        n = int(rng.integers(1, 80)) if t % 4 else int(rng.integers(1, 5000))
+        x = rng.standard_normal(n).astype(np.float32) if t % 3 == 0 else rng.choice(specials, n)
+        assert gb.argmax(x) == orc.argmax(x), x
+    big = rng.standard_normal(128256).astype(np.float32)
+    big[[5, 70000, 128255]] = 9.0  # the first of three equal maxima
+    assert gb.argmax(big) == orc.argmax(big) == 5
+
+
 def test_model_load_rejects_bad_files_without_gpu(gb, tmp_path):
     p = tmp_path / "bad.gguf"
     p.write_bytes(b"GGUF" + b"\0" * 4)
