@@ -104,6 +104,21 @@ def test_graph_and_eager_identical(gb, cuda):
     b.close()
 
 
+def test_forward_into_page_locked_buffer(gb, cuda):
+    # a page-locked caller buffer receives the device copy directly; the same
+    # position recomputed into pageable memory (through the staging buffer)
+    # gives the same bytes
+    img, _ = make(gb, "q4km_hd64")
+    m = gb.Model(img, max_len=64)
+    pinned = torch.empty(m.config.vocab, dtype=torch.float32, pin_memory=True).numpy()
+    pageable = np.empty(m.config.vocab, np.float32)
+    for pos, tok in enumerate([5, 17, 999]):
+        m.forward(tok, pos, out=pinned)
+        m.forward(tok, pos, out=pageable)
+        assert pinned.tobytes() == pageable.tobytes()
+    m.close()
+
+
 @pytest.mark.parametrize("name", ["q4km_hd64", "q40_tied", "q4km_hd128"])
 def test_greedy_generation_matches_cpu(gb, orc, cuda, name):
     # cmd/gollama/run.go:110-136: prompt fed one token at a time, then greedy
