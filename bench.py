@@ -372,18 +372,20 @@ def run_ours(args, cfg, world, rank, local):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "q4_k/q6_k/q4_0 weights x int8-limb activations (dp4a), f32 accumulate",
         "data": "synthetic: seeded random-init weights" + (", KV prefilled with seeded N(0,1) fp16" if cfg["prefill"] else ""),
-        "config": {"workload": cfg["workload"], "model": f"preset {cfg['preset']} (dim {c.dim}, {c.layers} layers, "
-                   f"{c.heads}/{c.kv_heads} heads, ffn {c.ffn}, vocab {c.vocab})", "global_batch": 1,
-                   "seq_len": c.max_len, "parallelism": f"tp{world}",
-                   "l2": f"inputs larger than L2: {bytes_tok / 1e9:.2f} GB read per token vs 126 MB L2"},
+        "config": bench_config(cfg, spec, world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": ncu_traffic(args.config) if world == 1 else None,
                      "kernel": "gemv_kernel, gate/up + SwiGLU (one launch per layer)",
-                     "bytes_per_launch": gu_bytes, "avg_launch_ms": round(gu_ms, 5), "peak_source": peak_src},
+                     "bytes_per_launch": gu_bytes, "avg_launch_ms": round(gu_ms, 5), "peak_source": peak_src,
+                     "timing": "CUDA events around each gate/up launch of an eager decode step (median of 5 steps); "
+                               "in eager mode every launch runs alone, without the overlap of the graph's "
+                               "programmatic dependent launches"},
         "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": round(bytes_tok * tok_s / 1e9, 1),
                           "frac": round(bytes_tok * tok_s / 1e9 / peak, 4),
                           "roofline_tok_s": round(peak * 1e9 / bytes_tok, 1)},
-        "kernel_ms_per_step": breakdown,
+        "kernel_ms_per_step": dict(breakdown, how="CUDA events between the launches of one eager decode step: "
+                                   "launches serialized (no PDL overlap), so the classes add up to more than "
+                                   "ms_per_step"),
         "prefill": prefill,
         "batched_decode": batched,
         "e2e": e2e,
@@ -391,38 +393,104 @@ def run_ours(args, cfg, world, rank, local):
         "clocks": clk,
         "first_tokens": [int(t) for t in toks_out[:8]],
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(src, spec, cfg, p0, t0)
+    # logits of the first timed position for the oracle check (every rank takes part)
+    plog = m.forward(t0, p0).copy() if rank == 0 else m.forward_no_logits(t0, p0)
     m.close()
     if rank == 0:
+        om = oracle_model(image_bytes(src), spec, cfg)
+        result["parity"] = parity_check(om, plog, t0, p0, spec.vocab)
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(om, spec, p0, t0)
+        om.close()
         print(json.dumps(result), flush=True)
 
 
-def oracle_model(img_or_path, spec, cfg, p0, t0):
-    """The C restatement of the reference's backend/cpu forward over the same image."""
+def model_bytes(spec, kv_len, kv_f16):
+    """Algorithmic HBM bytes of one decode step of the whole (unsharded) model at
+    kv_len cached positions: every weight matrix once, the norms, the K/V read
+    and the new K/V row, the embedding row (the arithmetic of gb_model_step_bytes
+    at one GPU)."""
+    bs = {2: (32, 18), 8: (32, 34), 12: (256, 144), 13: (256, 176), 14: (256, 210), 1: (1, 2), 0: (1, 4)}
+
+    def rb(t, n):
+        return n // bs[t][0] * bs[t][1]
+
+    def qt(six):
+        m = spec.mix
+        return {0: 2, 2: 12, 3: 14, 4: 8, 5: 1}.get(m, (14 if six else (13 if m == 6 else 12)))
+
+    q, kv = spec.heads * spec.head_dim, spec.kv_heads * spec.head_dim
+    w = 0
+    for i in range(spec.layers):
+        w += (q + kv) * rb(qt(False), spec.dim) + kv * rb(qt(True), spec.dim) + spec.dim * rb(qt(False), q)
+        w += 2 * spec.ffn * rb(qt(False), spec.dim) + spec.dim * rb(qt(i % 2 == 0), spec.ffn)
+    w += spec.vocab * rb(qt(spec.mix != 0), spec.dim)
+    norms = 4 * spec.dim * (2 * spec.layers + 1)
+    esz = 2 if kv_f16 else 4
+    kvb = spec.layers * kv_len * 2 * kv * esz + spec.layers * 2 * kv * esz
+    return w + norms + kvb + rb(qt(False), spec.dim)
+
+
+def bench_config(cfg, spec, world):
+    """The `config` object of the JSON line (the same for both arms)."""
+    kv_len = cfg["prefill"] + cfg["prompt"] + cfg["window"] // 2
+    gb_tok = model_bytes(spec, kv_len, cfg["kv_f16"]) / 1e9
+    return {"workload": cfg["workload"],
+            "model": f"preset {cfg['preset']} (dim {spec.dim}, {spec.layers} layers, {spec.heads}/{spec.kv_heads} "
+                     f"heads, ffn {spec.ffn}, vocab {spec.vocab})",
+            "global_batch": 1, "seq_len": cfg["max_len"], "parallelism": f"tp{world}",
+            "l2": f"inputs larger than L2: {gb_tok:.2f} GB of weights and KV read per token vs 126 MB L2"}
+
+
+def _orc():
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle_lib as orc
 
-    import gollama_b200 as gb
+    return orc
 
-    if isinstance(img_or_path, str):
-        raw = np.fromfile(img_or_path, np.uint8)
-    else:
-        raw = img_or_path.view()
+
+def oracle_model(raw, spec, cfg):
+    """The C restatement of the reference's backend/cpu forward over the bench's
+    image, with the same KV prefill and prompt (oracle library only)."""
+    orc = _orc()
     om = orc.OracleModel(raw, cfg["max_len"], bool(cfg["kv_f16"]))
     kv_dim = spec.kv_heads * spec.head_dim
     if cfg["prefill"]:
         for layer in range(spec.layers):
-            k, v = gb.synth_kv_normal(KV_SEED, layer, 0, cfg["prefill"], kv_dim, bool(cfg["kv_f16"]))
+            k, v = orc.synth_kv_normal(KV_SEED, layer, 0, cfg["prefill"], kv_dim, bool(cfg["kv_f16"]))
             om.set_kv(layer, 0, k, v)
     toks = prompt_tokens(spec, cfg["prompt"] + 1)
     for pos in range(cfg["prompt"]):
         om.forward(toks[pos], pos, spec.vocab)
-    return om, raw
+    return om
 
 
-def cpu_baseline(src, spec, cfg, p0, t0):
-    om, raw = oracle_model(src, spec, cfg, p0, t0)
+def image_bytes(src):
+    """The GGUF bytes of the bench's model: an in-memory image or a file."""
+    if isinstance(src, str):
+        return np.fromfile(src, np.uint8)
+    return src.view()
+
+
+def parity_check(om, logits, t0, p0, vocab):
+    """One decode step of the oracle against the device step's logits, with the
+    bars of the parity tests: |got - want| <= 1e-3 + 1e-4 |want|, greedy token
+    equal unless the oracle's top two logits are within 1e-3."""
+    orc = _orc()
+    want = om.forward(t0, p0, vocab).astype(np.float64)
+    got = np.asarray(logits, np.float64)
+    err = np.abs(got - want)
+    top2 = np.sort(want)[-2:]
+    tok_ref, tok = orc.argmax(want.astype(np.float32)), orc.argmax(np.asarray(logits, np.float32))
+    return {"position": p0, "max_abs": float(err.max()), "max_rel": float((err / np.maximum(np.abs(want), 1e-30)).max()),
+            "max_excess_over_bar": float((err - 1e-4 * np.abs(want)).max()),
+            "within_1e-3_abs_1e-4_rel": bool((err <= 1e-3 + 1e-4 * np.abs(want)).all()),
+            "token": int(tok), "token_oracle": int(tok_ref), "token_match": bool(tok == tok_ref),
+            "near_tie": bool(top2[1] - top2[0] < 1e-3),
+            "how": "one oracle step (C restatement of cpuForward) on the bench's image, KV and prompt"}
+
+
+def cpu_baseline(om, spec, p0, t0):
     cores = os.cpu_count() or 1
     t = time.perf_counter()
     om.forward(t0, p0, spec.vocab, threads=1)
@@ -430,7 +498,6 @@ def cpu_baseline(src, spec, cfg, p0, t0):
     t = time.perf_counter()
     om.forward(t0, p0, spec.vocab, threads=cores)
     tn = time.perf_counter() - t
-    om.close()
     return {"value": round(1 / t1, 4), "unit": "tok/s", "cores": 1, "kind": "port",
             "sample": f"1 decode token at position {p0} of the bench workload, C restatement of backend/cpu "
                       "+ cpuForward, single thread (the reference's Go path is single-threaded)",
@@ -438,39 +505,41 @@ def cpu_baseline(src, spec, cfg, p0, t0):
 
 
 def run_reference(args, cfg, world, rank):
-    """The reference's CPU path (backend/cpu + cpuForward restated in C: Go is not on this image),
-    all host threads, rank 0 only. Each step is one decode token of the same workload."""
+    """The reference's CPU path (backend/cpu + cpuForward restated in C: Go is not on
+    this image), all host threads, rank 0 only. Each step is one decode token of the
+    same workload. Only the oracle library is loaded: it builds the same synthetic
+    image (oracle/synth.c) and picks tokens with model.Argmax's rule."""
     if rank != 0:
         return
-    import gollama_b200 as gb
-
-    spec = gb.synth_preset(cfg["preset"], seed=SEED)
-    img = gb.SynthImage(spec)
+    orc = _orc()
+    spec = orc.synth_preset(cfg["preset"], seed=SEED)
+    if cfg.get("layers"):
+        spec.layers = cfg["layers"]
+    raw = orc.synth_model(spec)
     p0 = cfg["prefill"] + cfg["prompt"]
     toks = prompt_tokens(spec, cfg["prompt"] + 1)
-    om, _ = oracle_model(img, spec, cfg, p0, toks[-1])
+    om = oracle_model(raw, spec, cfg)
     cores = os.cpu_count() or 1
     window = cfg["window"]
     tok = toks[-1]
     for i in range(args.warmup):
-        tok = gb.argmax(om.forward(tok, p0 + i % window, spec.vocab, threads=cores))
+        tok = orc.argmax(om.forward(tok, p0 + i % window, spec.vocab, threads=cores))
     t = time.perf_counter()
     tok = toks[-1]
     for i in range(args.steps):
         logits = om.forward(tok, p0 + i % window, spec.vocab, threads=cores)
-        tok = gb.argmax(logits)
+        tok = orc.argmax(logits)
     wall = time.perf_counter() - t
     om.close()
     v = args.steps / wall
     sample = (f"{args.steps} decode tokens of the bench workload ({cfg['workload']}), C restatement of "
-              f"backend/cpu + cpuForward, {cores} threads")
+              f"backend/cpu + cpuForward, {cores} host threads")
     print(json.dumps({"metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1e3, 3),
                       "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "impl": "reference",
                       "dtype": "f32 weights dequantized per token, f64 accumulate",
-                      "data": "synthetic: seeded random-init weights",
-                      "config": {"workload": cfg["workload"], "global_batch": 1, "seq_len": cfg["max_len"],
-                                 "parallelism": "host threads"},
+                      "data": "synthetic: seeded random-init weights" + (", KV prefilled with seeded N(0,1) fp16" if cfg["prefill"] else ""),
+                      "config": bench_config(cfg, spec, world), "host_threads": cores,
                       "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port",
                                        "sample": sample},
                       "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),

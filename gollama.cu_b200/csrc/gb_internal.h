@@ -51,6 +51,7 @@ struct GbPeer {
   unsigned *my_flag = nullptr;            // this rank's flags [slots]
   unsigned *done = nullptr;               // [slots] local row-block counters (zero between launches)
   const unsigned *epoch = nullptr;        // device step counter
+  unsigned wait_limit = 1u << 22;         // polls of a peer flag (~100 ns each) before a wait gives up
 };
 
 struct GbGemvPlan {

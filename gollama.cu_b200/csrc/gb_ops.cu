@@ -219,16 +219,14 @@ __global__ void argmax_kernel(const float *x, int n, int32_t *out) {
   }
 }
 
-// Reduce per-rank argmax keys (tensor-parallel lm_head) to the token.
-// Iterations of a peer-flag wait (each sleeps ~100 ns): about half a second.
-constexpr unsigned kPeerWaitLimit = 1u << 22;
-
-// Wait (bounded) until rank q's flag of peer slot `slot` carries this step's
-// value (read over NVLink for another rank); false on timeout.
+// Wait (bounded by p.wait_limit polls, each sleeping ~100 ns; the default
+// 2^22 is about half a second) until rank q's flag of peer slot `slot`
+// carries this step's value (read over NVLink for another rank); false on
+// timeout.
 GB_DEV bool peer_wait(const GbPeer &p, int slot, int q) {
   const unsigned ep = *p.epoch + 1u;
   const unsigned *f = p.flags[q] + slot;
-  for (unsigned i = 0; i < kPeerWaitLimit; i++) {
+  for (unsigned i = 0; i < p.wait_limit; i++) {
     if (gb_ld_acquire_sys(f) == ep) return true;
     __nanosleep(64);
   }
@@ -436,6 +434,7 @@ int gb_advance_pos_launch(int32_t *pos, unsigned *epoch, cudaStream_t st) {
 
 struct gb_kernels {
   int device = 0;
+  unsigned *status = nullptr;  // device error word of calls given no status word of their own
   float *ws = nullptr;  // attention partials + counters
   size_t ws_floats = 0;
   unsigned *ws_counter = nullptr;
@@ -473,6 +472,14 @@ int gb_gpu_load(int device, gb_kernels **out) {
   GB_CUDA(cudaFuncGetAttributes(&fa, rmsnorm_kernel), "gpu: load kernels");
   gb_kernels *k = new gb_kernels();
   k->device = device;
+  cudaError_t e = cudaMalloc(&k->status, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(k->status, 0, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    if (k->status) cudaFree(k->status);
+    delete k;
+    return gb_cuda_fail(e, "gpu: load kernels");
+  }
   *out = k;
   return GB_OK;
 }
@@ -486,6 +493,7 @@ int gb_gpu_close(gb_kernels *k) {
   if (k->ws_counter) cudaFree(k->ws_counter);
   if (k->pws) cudaFree(k->pws);
   if (k->pws_counter) cudaFree(k->pws_counter);
+  if (k->status) cudaFree(k->status);
   delete k;
   return GB_OK;
 }
@@ -778,6 +786,37 @@ int gb_gpu_argmax(gb_kernels *k, void *stream, const float *x, int n, int32_t *o
   if (n <= 0) return gb_fail(GB_ERR_INVALID, "gpu: argmax: empty vector");
   argmax_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, out);
   GB_CUDA(cudaGetLastError(), "gpu: argmax");
+  return GB_OK;
+}
+
+int gb_gpu_peer_resid(gb_kernels *k, void *stream, int world, const float *const *bufs,
+                      const unsigned *const *flags, const unsigned *step, int slot, int dim, float *x, int n,
+                      float *ssq, unsigned wait_limit, unsigned *status) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (world < 1 || world > 32 || !bufs || !flags || !step || slot < 0 || !x || !ssq || n <= 0 || n % 32 ||
+      n > dim)
+    return gb_fail(GB_ERR_INVALID, "gpu: peer residual: bad arguments");
+  GbPeer p;
+  p.world = world;
+  p.dim = dim;
+  p.bufs = bufs;
+  p.flags = flags;
+  p.epoch = step;
+  p.wait_limit = wait_limit ? wait_limit : p.wait_limit;
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned *word = status ? status : k->status;
+  int rc = gb_peer_resid_launch(p, slot, x, n, ssq, word, st, false);
+  if (rc || status) return rc;
+  // no status word of the caller's: wait for the call and report its outcome
+  unsigned h = 0;
+  GB_CUDA(cudaMemcpyAsync(&h, k->status, sizeof h, cudaMemcpyDeviceToHost, st), "gpu: peer residual");
+  GB_CUDA(cudaStreamSynchronize(st), "gpu: peer residual");
+  if (h) {
+    GB_CUDA(cudaMemsetAsync(k->status, 0, sizeof h, st), "gpu: peer residual");
+    GB_CUDA(cudaStreamSynchronize(st), "gpu: peer residual");
+    return gb_fail(GB_ERR_TIMEOUT, "gpu: peer residual: a rank's flag did not arrive within %u polls", p.wait_limit);
+  }
   return GB_OK;
 }
 

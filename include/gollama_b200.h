@@ -89,7 +89,10 @@ int gb_gpu_attn_decode(gb_kernels *k, void *stream, const float *q, const float 
  * call on a device resolves the arrays' addresses for that device, so make
  * it before any stream capture. Every call on a device shares the arrays:
  * calls whose work overlaps on the GPU (other streams, other threads) race
- * and must be serialized by the caller. */
+ * and must be serialized by the caller. The addresses are kept for the life
+ * of the process: after a cudaDeviceReset (or any other end of the device's
+ * primary context) they are stale, and this entry point must not be called
+ * again on that device. */
 int gb_gpu_attn_decode_noalloc(gb_kernels *k, void *stream, const float *q, const float *kcache,
                                const float *vcache, float *out, int kv_len, int n_heads, int n_kv,
                                int head_dim, float scale);
@@ -131,6 +134,23 @@ int gb_gpu_dequant_rows(gb_kernels *k, void *stream, int typ, const uint8_t *w, 
 /* Added: greedy argmax of n floats on the device into *out (device int32),
  * with model.Argmax's tie rule (model/model.go:376: first maximum wins). */
 int gb_gpu_argmax(gb_kernels *k, void *stream, const float *x, int n, int32_t *out);
+
+/* Added (tensor parallelism; the reference is single-GPU, so no reference
+ * interface): the partial-sum exchange that follows a row-split GEMV, as a
+ * per-op call. bufs and flags are device arrays of `world` device pointers
+ * (this rank's own buffers and the peers' buffers mapped into this process,
+ * e.g. with CUDA IPC): rank q's partial of `slot` is bufs[q] + slot*dim and
+ * its flag is flags[q][slot]. Once every rank's flag equals *step + 1 (step a
+ * device word), x[0..n) += the partials summed in rank order and ssq[n/32]
+ * receives the per-32 sums of squares of the new x. Each flag wait is bounded
+ * by wait_limit polls of ~100 ns (0: the default, about half a second); a
+ * wait that runs out skips the sum and ORs GB_DEVERR_TIMEOUT (4) into
+ * *status (a device word), leaving the device usable. status NULL: the call
+ * waits for the stream and returns GB_ERR_TIMEOUT instead. n is a multiple
+ * of 32, n <= dim, world <= 32. */
+int gb_gpu_peer_resid(gb_kernels *k, void *stream, int world, const float *const *bufs,
+                      const unsigned *const *flags, const unsigned *step, int slot, int dim, float *x, int n,
+                      float *ssq, unsigned wait_limit, unsigned *status);
 
 /* ---- sampling (added; the reference's roadmap item, ROADMAP.md:42-45) ----
  * One token from a logits vector on the device:

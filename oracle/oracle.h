@@ -139,6 +139,24 @@ float or_uniform24(uint64_t seed, uint64_t counter);
 int32_t or_sample(const float *logits, int n, const or_sample_params *p, const int32_t *recent,
                   int n_recent, uint64_t counter);
 
+/* ---- synthetic inputs (synth.c) -------------------------------------------
+ * The benchmark's seeded GGUF models and KV prefill, built without the
+ * product library (the same bytes as its generator; tests/test_oracle_synth.py). */
+typedef struct {
+  int layers, dim, ffn, heads, kv_heads, head_dim, vocab, ctx_len;
+  float rope_base, eps;
+  int mix; /* 0 Q4_0 tied head; 1 Q4_K_M; 2 Q4_K; 3 Q6_K; 4 Q8_0; 5 F16; 6 Q5_K_M */
+  uint64_t seed;
+} or_synth_spec;
+/* Presets 1 (1B Q4_0), 3 (3B Q4_K_M), 8 (8B Q4_K_M), 70 (70B Q4_K_M). */
+int or_synth_preset(int preset, or_synth_spec *s);
+/* The GGUF image in host memory (or_synth_free). 0 on success. */
+int or_synth_model(const or_synth_spec *s, uint8_t **img, size_t *len);
+void or_synth_free(uint8_t *img);
+/* N(0,1) K and V rows [n][kv_dim] of one layer for positions [pos0, pos0+n),
+ * rounded through binary16 when f16 != 0. */
+int or_synth_kv_normal(uint64_t seed, int layer, int pos0, int n, int kv_dim, int f16, float *k, float *v);
+
 #ifdef __cplusplus
 }
 #endif

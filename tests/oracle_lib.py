@@ -35,6 +35,8 @@ _SIGS = {
     "or_model_kcache": (P, [P, I]), "or_model_vcache": (P, [P, I]),
     "or_exp_nonpos": (F, [F]), "or_uniform24": (F, [C.c_uint64, C.c_uint64]),
     "or_sample": (C.c_int32, [P, I, P, P, I, C.c_uint64]),
+    "or_synth_preset": (I, [I, P]), "or_synth_model": (I, [P, C.POINTER(P), C.POINTER(C.c_size_t)]),
+    "or_synth_free": (None, [P]), "or_synth_kv_normal": (I, [C.c_uint64, I, I, I, I, I, P, P]),
 }
 
 
@@ -42,6 +44,13 @@ class SampleParams(C.Structure):
     _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float),
                 ("repeat_penalty", C.c_float), ("repeat_last_n", C.c_int), ("reserved", C.c_int),
                 ("seed", C.c_uint64)]
+
+class SynthSpec(C.Structure):
+    """or_synth_spec: the shape, weight mix and seed of a synthetic model."""
+    _fields_ = [("layers", C.c_int), ("dim", C.c_int), ("ffn", C.c_int), ("heads", C.c_int),
+                ("kv_heads", C.c_int), ("head_dim", C.c_int), ("vocab", C.c_int), ("ctx_len", C.c_int),
+                ("rope_base", C.c_float), ("eps", C.c_float), ("mix", C.c_int), ("seed", C.c_uint64)]
+
 
 _lib = None
 
@@ -213,3 +222,41 @@ class OracleModel:
         if self.h:
             lib().or_model_free(self.h)
             self.h = None
+
+
+def synth_preset(preset: int, **over) -> SynthSpec:
+    s = SynthSpec()
+    if lib().or_synth_preset(preset, C.byref(s)):
+        raise ValueError(f"unknown preset {preset}")
+    for k, v in over.items():
+        setattr(s, k, v)
+    return s
+
+
+def synth_spec(**kw) -> SynthSpec:
+    """Defaults as the product's synth_spec: vocab 128256, ctx 2048, Q4_K_M, seed 0."""
+    s = SynthSpec(vocab=128256, rope_base=500000.0, eps=1e-5, ctx_len=2048, mix=1, seed=0)
+    for k, v in kw.items():
+        setattr(s, k, v)
+    if "head_dim" not in kw:
+        s.head_dim = s.dim // s.heads
+    return s
+
+
+def synth_model(spec: SynthSpec) -> np.ndarray:
+    """The synthetic GGUF image of spec (the bytes the product's generator writes)."""
+    p, n = C.c_void_p(), C.c_size_t()
+    if lib().or_synth_model(C.byref(spec), C.byref(p), C.byref(n)):
+        raise ValueError("or_synth_model failed")
+    try:
+        return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_uint8)), (n.value,)).copy()
+    finally:
+        lib().or_synth_free(p)
+
+
+def synth_kv_normal(seed: int, layer: int, pos0: int, n: int, kv_dim: int, f16: bool):
+    k = np.empty((n, kv_dim), np.float32)
+    v = np.empty((n, kv_dim), np.float32)
+    if lib().or_synth_kv_normal(seed, layer, pos0, n, kv_dim, int(f16), _p(k), _p(v)):
+        raise ValueError("or_synth_kv_normal failed")
+    return k, v

@@ -1,0 +1,133 @@
+"""Parity against cpuForward (model/model_test.go:114-175) on the model shapes
+the benchmark runs (the reference's TestForwardVsCPU, model/model_test.go:180-219,
+on its real 3B and 8B): the 8B preset decoding after an 8192-position prefilled
+fp16 cache, the 3B preset after a 32-token prompt, a 70B-shaped model cut to two
+layers, and a model whose norm weights carry outlier features. Logits within
+1e-3 abs + 1e-4 rel, greedy tokens equal except at near-ties (< 1e-3)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from test_model_gpu import check_logits, near_tie
+
+pytestmark = pytest.mark.gpu
+
+KV_SEED = 1  # bench.py's prefill seed
+
+
+def prompt_ids(vocab, n, seed=0):
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]
+
+
+def greedy_check(name, m, om, tok, pos0, steps, vocab, orc, gb):
+    """`steps` greedy decode steps from (tok, pos0), every one compared."""
+    for i in range(steps):
+        got = m.forward(tok, pos0 + i).copy()
+        want = om.forward(tok, pos0 + i, vocab)
+        check_logits(f"{name} pos {pos0 + i}", got, want)
+        if near_tie(want):
+            return
+        assert gb.argmax(got) == orc.argmax(want), f"{name} pos {pos0 + i}: greedy token differs"
+        tok = orc.argmax(want)
+
+
+def test_8b_preset_after_8192_prefilled_positions(gb, orc, cuda):
+    # BASELINE config 4 (the bench's default workload) at positions 8192-8194
+    spec = gb.synth_preset(8)
+    img = gb.SynthImage(spec)
+    raw = img.view()
+    n_pos = 8192
+    m = gb.Model(img, max_len=8320, kv_f16=1)
+    m.fill_kv_normal(KV_SEED, n_pos)
+    om = orc.OracleModel(raw, 8320, True)
+    kv_dim = spec.kv_heads * spec.head_dim
+    for layer in range(spec.layers):
+        k, v = orc.synth_kv_normal(KV_SEED, layer, 0, n_pos, kv_dim, True)
+        om.set_kv(layer, 0, k, v)
+    t0 = prompt_ids(spec.vocab, 1)[-1]
+    greedy_check("8B", m, om, t0, n_pos, 3, spec.vocab, orc, gb)
+    m.close()
+    om.close()
+    img.close()
+
+
+def test_3b_preset_after_32_token_prompt(gb, orc, cuda):
+    # prompt fed one token at a time, then greedy
+    spec = gb.synth_preset(3)
+    img = gb.SynthImage(spec)
+    raw = img.view()
+    m = gb.Model(img, max_len=4096, kv_f16=1)
+    om = orc.OracleModel(raw, 4096, True)
+    toks = prompt_ids(spec.vocab, 33)
+    for pos in range(32):
+        got = m.forward(toks[pos], pos).copy()
+        want = om.forward(toks[pos], pos, spec.vocab)
+        if pos in (0, 15, 31):
+            check_logits(f"3B prompt pos {pos}", got, want)
+    greedy_check("3B", m, om, toks[32], 32, 4, spec.vocab, orc, gb)
+    m.close()
+    om.close()
+    img.close()
+
+
+def test_70b_shape_two_layers(gb, orc, cuda):
+    # BASELINE config 5's shapes (dim 8192, 64/8 heads, FFN 28672, Q4_K_M),
+    # cut to two layers so the oracle finishes in seconds
+    spec = gb.synth_preset(70, layers=2)
+    img = gb.SynthImage(spec)
+    raw = img.view()
+    m = gb.Model(img, max_len=256, kv_f16=1)
+    om = orc.OracleModel(raw, 256, True)
+    toks = prompt_ids(spec.vocab, 8, seed=5)
+    for pos in range(4):
+        got = m.forward(toks[pos], pos).copy()
+        check_logits(f"70B-shape pos {pos}", got, om.forward(toks[pos], pos, spec.vocab))
+    greedy_check("70B-shape", m, om, toks[4], 4, 3, spec.vocab, orc, gb)
+    m.close()
+    om.close()
+    img.close()
+
+
+def tensor_offset(orc, raw, name):
+    """Byte offset of a tensor's data inside the GGUF image `raw`."""
+    err = C.create_string_buffer(256)
+    h = orc.lib().or_gguf_parse(raw.ctypes.data, raw.nbytes, err, 256)
+    assert h, err.value
+    typ, nd = C.c_int(), C.c_int()
+    dims = (C.c_uint64 * 4)()
+    data, nbytes = C.c_void_p(), C.c_uint64()
+    rc = orc.lib().or_gguf_tensor(h, name.encode(), C.byref(typ), C.byref(nd), dims, C.byref(data), C.byref(nbytes))
+    orc.lib().or_gguf_free(h)
+    assert rc == 0, name
+    return data.value - raw.ctypes.data, int(nbytes.value)
+
+
+@pytest.mark.parametrize("kv_f16", [0, 1])
+def test_outlier_features_in_norm_weights(gb, orc, cuda, kv_f16):
+    # Llama-style outlier features: a few channels of the RMSNorm weights are
+    # hundreds to thousands of times the rest, so the normalised GEMV inputs
+    # have one dominant element in several 256-element blocks.
+    spec = gb.synth_spec(layers=2, dim=1024, ffn=1024, heads=8, kv_heads=2, head_dim=128, vocab=900,
+                         ctx_len=64, mix=1, seed=21)
+    img = gb.SynthImage(spec)
+    raw = np.array(img.view(), copy=True)
+    img.close()
+    rng = np.random.default_rng(4)
+    for name in ("blk.0.attn_norm.weight", "blk.0.ffn_norm.weight", "blk.1.attn_norm.weight",
+                 "blk.1.ffn_norm.weight", "output_norm.weight"):
+        off, nb = tensor_offset(orc, raw, name)
+        w = raw[off:off + nb].view(np.float32)
+        ch = rng.choice(spec.dim, 3, replace=False)
+        w[ch] *= np.float32(rng.choice([100.0, 300.0, 1000.0]))
+    m = gb.Model(bytes(raw), max_len=64, kv_f16=kv_f16)
+    om = orc.OracleModel(raw, 64, bool(kv_f16))
+    toks = prompt_ids(spec.vocab, 6, seed=8)
+    for pos, tok in enumerate(toks):
+        got = m.forward(tok, pos).copy()
+        want = om.forward(tok, pos, spec.vocab)
+        check_logits(f"outlier norms pos {pos}", got, want)
+        if not near_tie(want):
+            assert gb.argmax(got) == orc.argmax(want)
+    m.close()
+    om.close()

@@ -199,6 +199,27 @@ def test_linear_unquantized_vs_oracle(gb, orc, cuda, typ, rows, cols):
     lin.close()
 
 
+@pytest.mark.parametrize("ratio", [1e3, 1e4])
+@pytest.mark.parametrize("typ", [Q4_0, Q8_0, Q4_K, Q5_K, Q6_K])
+def test_linear_tiled_outlier_activations(gb, orc, cuda, typ, ratio):
+    # Heavy-tailed input: in 12 of the 16 256-element blocks one element is
+    # `ratio` times the rest (an outlier feature). The staged activation must
+    # keep every element to float32 accuracy, not only the block maximum, so
+    # the product stays within the reference's MatVecQ tolerance.
+    rows, cols = 300, 4096
+    rng = np.random.default_rng(int(ratio) + typ)
+    w = rand_quant(rng, typ, rows, cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+    blocks = np.arange(cols // 256)[rng.permutation(cols // 256)[:12]]
+    x[blocks * 256 + rng.integers(0, 256, blocks.size)] *= np.float32(ratio)
+    want = orc.matvec_q(typ, w, x, rows, cols)
+    lin = gb.Linear(typ, w, rows, cols)
+    dy = torch.zeros(rows, device="cuda")
+    lin.matvec(dev(x), dy)
+    assert_close(f"Linear[{typ}] outliers x{ratio:g}", host(dy), want, 1e-4, 1e-4)
+    lin.close()
+
+
 @pytest.mark.parametrize("typ", [Q4_0, Q4_K, Q6_K])
 def test_linear_tiled_synthetic_recipe(gb, orc, cuda, typ):
     # the BASELINE GEMV-sweep block recipe, one of its shapes

@@ -1,8 +1,10 @@
 """gb_gpu_attn_decode_noalloc (fixed device scratch, no allocation) against
-gb_gpu_attn_decode on the same seeded inputs, through the C ABI: the two
-entry points must agree within the AttnDecode tolerance of
-backend/gpu/gpu_test.go:265 on two calls in a row (the second call reuses
-the shared scratch after the first left its counters at zero)."""
+gb_gpu_attn_decode and against the CPU oracle's AttnDecode (cpu.AttnDecode,
+backend/cpu/cpu.go:143) on the same seeded inputs, through the C ABI: they
+must agree within the AttnDecode tolerance of backend/gpu/gpu_test.go:265 on
+two calls in a row (the second call reuses the shared scratch after the first
+left its counters at zero). Requests beyond the fixed scratch are refused
+before any launch."""
 import math
 
 import numpy as np
@@ -24,7 +26,7 @@ def _close(name, got, want):
 
 
 @pytest.mark.parametrize("nh,nkv,hd,kv_len", SHAPES)
-def test_noalloc_matches_allocating_entry_point(gb, cuda, nh, nkv, hd, kv_len):
+def test_noalloc_matches_allocating_entry_point(gb, orc, cuda, nh, nkv, hd, kv_len):
     rng = np.random.default_rng(100 + kv_len)
     q = torch.from_numpy((rng.random(nh * hd, dtype=np.float32) * 2 - 1)).cuda()
     kc = torch.from_numpy((rng.random(kv_len * nkv * hd, dtype=np.float32) * 2 - 1)).cuda()
@@ -36,6 +38,7 @@ def test_noalloc_matches_allocating_entry_point(gb, cuda, nh, nkv, hd, kv_len):
         k.attn_decode(q, kc, vc, want, kv_len, nh, nkv, hd, scale)
         torch.cuda.synchronize()
         want_h = want.cpu().numpy()
+        oracle = orc.attn_decode(q.cpu().numpy(), kc.cpu().numpy(), vc.cpu().numpy(), kv_len, nh, nkv, hd, scale)
         for call in range(2):
             got = torch.full((nh * hd,), float("nan"), device="cuda")
             rc = gb.lib().gb_gpu_attn_decode_noalloc(k.h, None, q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
@@ -43,6 +46,7 @@ def test_noalloc_matches_allocating_entry_point(gb, cuda, nh, nkv, hd, kv_len):
             assert rc == gb.OK, gb.lib().gb_last_error().decode()
             torch.cuda.synchronize()
             _close(f"call {call + 1}", got.cpu().numpy(), want_h)
+            _close(f"call {call + 1} vs oracle", got.cpu().numpy(), oracle)
     finally:
         k.close()
 
@@ -57,5 +61,26 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(gb, cuda):
                                                   1, 300, 300, 64, 0.125)
         assert rc == gb.ERR_UNSUPPORTED
         assert "at most 256" in gb.lib().gb_last_error().decode()
+    finally:
+        k.close()
+
+
+def test_noalloc_rejects_partials_beyond_its_scratch(gb, cuda):
+    # 128 KV heads, 8 query heads each, head_dim 128 and 16384 positions need
+    # 8 slices per KV head: 128 * 8 * 8 * 132 floats of partials, more than the
+    # 2^20 the static scratch holds. Refused before any launch (so the cache
+    # pointers are never read), with a message that names the limit.
+    t = torch.zeros(1024 * 128, device="cuda")
+    k = gb.Kernels(0)
+    try:
+        rc = gb.lib().gb_gpu_attn_decode_noalloc(k.h, None, t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(),
+                                                  16384, 1024, 128, 128, 0.0884)
+        assert rc == gb.ERR_UNSUPPORTED
+        msg = gb.lib().gb_last_error().decode()
+        assert "slice partials" in msg and str(1 << 20) in msg
+        # the scratch is still usable afterwards
+        y = torch.ones(64, device="cuda")
+        k.add(y, y, y, 64)
+        assert float(y.sum().item()) == 128.0
     finally:
         k.close()
