@@ -219,6 +219,141 @@ def prompt_tokens(spec, n):
     return [int(t) for t in rng.integers(0, spec.vocab, n)]
 
 
+SWEEP_TYPES = (("q4_0", 2), ("q4_k", 12), ("q6_k", 14))
+SWEEP_SHAPES = ((4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096))
+L2_BYTES = 126 * 1024 * 1024
+
+
+def gemv_sweep(gb, torch, device, peak, launches=48):
+    """the standalone batch-1 quantized GEMV (gb_linear_matvec,
+    the kernel that replaces kernels/quantmv.go:18-136) for Q4_0 / Q4_K / Q6_K at
+    four shapes. Weights follow the config's block recipe (seeds 0-3); enough
+    device copies are rotated that every launch reads its weights from HBM (more
+    than 3x the 126 MB L2 per pass). Launches go back to back on one stream
+    (programmatic dependent launch, as in the decode step); CUDA events around
+    `launches` of them give the time per launch. Algorithmic bytes per launch:
+    rows*cols*(type bytes per weight) + 4*cols + 4*rows."""
+    cases = []
+    dev = torch.device("cuda", device)
+    stream = torch.cuda.Stream(device=dev)
+    for tname, typ in SWEEP_TYPES:
+        for rows, cols in SWEEP_SHAPES:
+            mats = [gb.synth_matrix(typ, rows, cols, seed=s) for s in range(4)]
+            wbytes = mats[0].nbytes
+            ncopy = max(4, -(-3 * L2_BYTES // wbytes))
+            lins = [gb.Linear(typ, mats[i % 4], rows, cols, device=device) for i in range(ncopy)]
+            xs = [torch.from_numpy(gb.synth_normal(s, 1, cols)).to(dev) for s in range(4)]
+            ys = [torch.empty(rows, device=dev) for _ in range(4)]
+            del mats
+            with torch.cuda.stream(stream):
+                for i in range(max(ncopy, 8)):  # warm-up: every copy once
+                    lins[i % ncopy].matvec(xs[i % 4], ys[i % 4], stream=stream)
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                n = max(launches, ncopy)
+                ev0.record(stream)
+                for i in range(n):
+                    lins[i % ncopy].matvec(xs[i % 4], ys[i % 4], stream=stream)
+                ev1.record(stream)
+            torch.cuda.synchronize(dev)
+            us = ev0.elapsed_time(ev1) * 1e3 / n
+            alg = wbytes + 4 * cols + 4 * rows
+            cases.append({"type": tname, "rows": rows, "cols": cols, "bytes": alg, "us_per_launch": round(us, 3),
+                          "gbs": round(alg / (us * 1e-6) / 1e9, 1), "frac": round(alg / (us * 1e-6) / 1e9 / peak, 4),
+                          "copies": ncopy})
+            for l in lins:
+                l.close()
+            del lins, xs, ys
+            torch.cuda.empty_cache()
+    big = [c for c in cases if c["rows"] * c["cols"] >= 14336 * 4096]
+    return {"how": "gb_linear_matvec back to back over rotated weight copies (> 3x L2 per pass), CUDA events, "
+                   "seeds 0-3 of the config-2 block recipe, x ~ N(0,1)",
+            "peak_gbs": peak, "cases": cases,
+            "min_frac_large_shapes": min(c["frac"] for c in big) if big else None}
+
+
+def new_nccl_id(gb, world, rank):
+    """A fresh NCCL unique id from rank 0 for one tensor-parallel model (None at one GPU)."""
+    if world == 1:
+        return None
+    import torch.distributed as dist
+
+    obj = [gb.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    return obj[0]
+
+
+def measure_config(gb, torch, name, world, rank, local, steps=64, warmup=4):
+    """Decode tok/s of one more BASELINE configuration (1B, 3B, 70B) at the run's
+    GPU count: its workload's prompt or KV prefill, then `steps` greedy graph steps
+    timed with CUDA events on the model's stream (max over ranks), the
+    bytes-per-token roofline, the first tokens, and one oracle step at the first
+    decode position (rank 0)."""
+    cfg = dict(CONFIGS[name])
+    nccl_id = new_nccl_id(gb, world, rank)
+    t_setup = time.perf_counter()
+    src, spec = build_image(gb, cfg, world, rank)
+    opts = dict(device=local, max_len=cfg["max_len"], kv_f16=cfg["kv_f16"], tp_rank=rank, tp_world=world)
+    if nccl_id is not None:
+        opts["nccl_id"] = nccl_id
+    m = gb.Model(src, **opts)
+    if cfg["prefill"]:
+        m.fill_kv_normal(KV_SEED, cfg["prefill"])
+    toks = prompt_tokens(spec, cfg["prompt"] + 1)
+    for pos in range(cfg["prompt"]):
+        m.forward_no_logits(toks[pos], pos)
+    p0, t0 = cfg["prefill"] + cfg["prompt"], toks[-1]
+    steps = min(steps, cfg["window"])
+    stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
+    m.start(t0, p0)
+    m.decode_async(warmup)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    m.start(t0, p0)
+    ev0.record(stream)
+    m.decode_async(steps)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    first = [int(t) for t in m.read_tokens(p0, min(8, steps))]
+    plog = m.forward(t0, p0).copy() if rank == 0 else m.forward_no_logits(t0, p0)
+    # the prompt's K/V for the oracle (teacher-forced: running a 70B prompt through
+    # the single-token CPU path would take minutes); one GPU only, since under
+    # tensor parallelism each rank holds its own KV heads
+    kv = [m.read_kv(layer, 0, p0) for layer in range(spec.layers)] if world == 1 and cfg["prompt"] else None
+    m.close()
+    setup_s = time.perf_counter() - t_setup
+    peak = peaks()[0]
+    tok_s = steps / (ms / 1e3)
+    bytes_tok = model_bytes(spec, p0 + steps // 2, cfg["kv_f16"])
+    out = {"workload": cfg["workload"], "model": bench_config(cfg, spec, world)["model"], "n_gpus": world,
+           "value": round(tok_s, 2), "unit": "tok/s", "steps": steps, "ms_per_step": round(ms / steps, 5),
+           "step_roofline": {"bytes_per_token": bytes_tok, "achieved_gbs": round(bytes_tok * tok_s / 1e9, 1),
+                             "frac": round(bytes_tok * tok_s / 1e9 / (peak * world), 4),
+                             "roofline_tok_s": round(peak * world * 1e9 / bytes_tok, 1),
+                             "peak_gbs_per_gpu": peak},
+           "first_tokens": first, "setup_s": round(setup_s, 1)}
+    if rank == 0 and kv is not None:
+        orc = _orc()
+        om = orc.OracleModel(image_bytes(src), cfg["max_len"], bool(cfg["kv_f16"]))
+        for layer, (k, v) in enumerate(kv):
+            om.set_kv(layer, 0, k, v)
+        out["parity"] = dict(parity_check(om, plog, t0, p0, spec.vocab),
+                             how="one oracle step (C restatement of cpuForward) at the first decode position, "
+                                 "the prompt's K/V copied from the device cache")
+        om.close()
+    elif rank == 0:
+        out["parity"] = None if cfg["prompt"] else parity_check(oracle_model(image_bytes(src), spec, cfg), plog, t0,
+                                                                p0, spec.vocab)
+    if world == 1:
+        src.close()
+    barrier(world)
+    if world > 1 and rank == 0 and isinstance(src, str):
+        os.unlink(src)  # a 70B image is 42 GB of disk
+    return out
+
+
 def run_ours(args, cfg, world, rank, local):
     import torch
 
@@ -366,6 +501,11 @@ def run_ours(args, cfg, world, rank, local):
                           "out, status check), e2e = wall clock of the same loop"}
         e.close()
 
+    sweep = gemv_sweep(gb, torch, local, peaks()[0]) if world == 1 and not args.no_sweep else None
+    configs = {}
+    for name in [n for n in args.configs.split(",") if n and n != args.config]:
+        configs[name] = measure_config(gb, torch, name, world, rank, local)
+
     result = {
         "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
@@ -388,6 +528,8 @@ def run_ours(args, cfg, world, rank, local):
                                    "ms_per_step"),
         "prefill": prefill,
         "batched_decode": batched,
+        "gemv_sweep": sweep,
+        "configs": configs or None,
         "e2e": e2e,
         "gpu_launches": m.launches_per_step() * args.steps,
         "clocks": clk,
@@ -558,6 +700,9 @@ def main():
                     help="sequences per step of the continuous-batching measurement (0 = skip)")
     ap.add_argument("--prefill-tokens", type=int, default=512,
                     help="prompt length of the batched-prefill measurement (0 = skip)")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the standalone GEMV sweep (config 2)")
+    ap.add_argument("--configs", default="1b,3b,70b",
+                    help="more decode configurations measured after the main one ('' = none)")
     ap.add_argument("--layers", type=int, default=0,
                     help="truncate the model to this many layers (small ncu captures only; not a bench line)")
     args = ap.parse_args()

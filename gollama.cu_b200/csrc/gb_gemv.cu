@@ -43,37 +43,27 @@ constexpr float kL2 = 1.f / 64516.f;  // 1/254^2: limbs b, c are combined as 254
 
 
 // ---- per-super-block decode + dot products. `st` is the sb-block in shared
-// memory; xa/xb/xc/xd are the limb planes (as 32-bit words) of the block's 256
-// activation elements (one scale xs for all 256:
-// x ~ xs*(a + b/254 + c/254^2 [+ d/254^3])), xsum the 16 sums of 16 activation
-// values and sl the 16 per-16 limb sums (int16 a, b, c, d sums packed in a
-// uint2). L is the number of limbs: 3 for ordinary blocks; 4 for blocks whose
-// largest magnitude stands far above the rest (the staging flags them), where
-// three limbs would leave the small elements an error of about 2^-24 of the
-// block maximum instead of 2^-24 of their own size. The integer dot products
-// of every sub-block are weighted by its integer scale in int32 and converted
-// to float once per super-block.
-template <int T, int L>
+// memory; xa/xb/xc are the limb planes (as 32-bit words) of the block's 256
+// activation elements (one scale xs for all 256: x ~ xs*(a + b/254 + c/254^2)),
+// xsum the 16 sums of 16 activation values and sl the 16 per-16 limb sums
+// (int16 a, b, c sums packed in a uint2). The integer dot products of every
+// sub-block are weighted by its integer scale in int32 and converted to float
+// once per super-block.
+template <int T>
 GB_DEV float sb_dot(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                    const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl, float xs);
+                    const uint32_t *xc, const float *xsum, const uint2 *sl, float xs);
 
 GB_DEV int lo16(uint32_t w) { return (int)(int16_t)(w & 0xFFFFu); }
 GB_DEV int hi16(uint32_t w) { return (int)(int16_t)(w >> 16); }
 GB_DEV int byte_i(uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xFFu); }
 
-// the limb families combined: A + (254 B + C)/254^2 [+ D/254^3]
-template <int L>
-GB_DEV float limb_sum(float A, float B, float C, float D) {
-  if constexpr (L == 4) return A + ((254.f * B + C) + D * (1.f / 254.f)) * kL2;
-  return A + (254.f * B + C) * kL2;
-}
-
 // Q4_K: quant/quant.go:97 layout; kernels/quantmv.go:66 factorisation
 // sum = d*sum_j sc_j*(q.x)_j - dmin*sum_j m_j*(sum x)_j. The high nibbles are
 // used in place (16*q), so their family of sums carries a factor 16.
-template <int L>
-GB_DEV float sb_dot_q4k(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb, const uint32_t *xc,
-                        const uint32_t *xd, const float *xsum, float xs) {
+template <>
+GB_DEV float sb_dot<GB_T_Q4_K>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)sl;
   const uint4 *u = (const uint4 *)st;
   const uint4 h = u[lane];
   const float d = gb_half_to_float((uint16_t)(h.x & 0xFFFFu));
@@ -81,15 +71,15 @@ GB_DEV float sb_dot_q4k(const uint8_t *st, int lane, const uint32_t *xa, const u
   const uint32_t sc03 = h.y & 0x3F3F3F3Fu, m03 = h.z & 0x3F3F3F3Fu;
   const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
   const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-  int IA0 = 0, IB0 = 0, IC0 = 0, ID0 = 0, IA1 = 0, IB1 = 0, IC1 = 0, ID1 = 0;
+  int IA0 = 0, IB0 = 0, IC0 = 0, IA1 = 0, IB1 = 0, IC1 = 0;
   float tm = 0.f;
 #pragma unroll
   for (int c = 0; c < 4; c++) {
     const uint4 q0 = u[(1 + 2 * c) * 32 + lane], q1 = u[(2 + 2 * c) * 32 + lane];
     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const uint4 *pa = (const uint4 *)(xa + 16 * c), *pb = (const uint4 *)(xb + 16 * c),
-                *pc = (const uint4 *)(xc + 16 * c), *pd = (const uint4 *)(xd + 16 * c);
-    int A0 = 0, B0 = 0, C0 = 0, D0 = 0, A1 = 0, B1 = 0, C1 = 0, D1 = 0;
+                *pc = (const uint4 *)(xc + 16 * c);
+    int A0 = 0, B0 = 0, C0 = 0, A1 = 0, B1 = 0, C1 = 0;
 #pragma unroll
     for (int v = 0; v < 2; v++) {
       const uint4 la = pa[v], lb = pb[v], lc = pc[v], ha = pa[2 + v], hb = pb[2 + v], hc = pc[2 + v];
@@ -97,12 +87,6 @@ GB_DEV float sb_dot_q4k(const uint8_t *st, int lane, const uint32_t *xa, const u
                      c4[4] = {lc.x, lc.y, lc.z, lc.w};
       const uint32_t A4[4] = {ha.x, ha.y, ha.z, ha.w}, B4[4] = {hb.x, hb.y, hb.z, hb.w},
                      C4[4] = {hc.x, hc.y, hc.z, hc.w};
-      uint32_t d4[4] = {0u, 0u, 0u, 0u}, D4[4] = {0u, 0u, 0u, 0u};
-      if constexpr (L == 4) {
-        const uint4 ld = pd[v], hd = pd[2 + v];
-        d4[0] = ld.x; d4[1] = ld.y; d4[2] = ld.z; d4[3] = ld.w;
-        D4[0] = hd.x; D4[1] = hd.y; D4[2] = hd.z; D4[3] = hd.w;
-      }
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const uint32_t w = qw[4 * v + k];
@@ -113,10 +97,6 @@ GB_DEV float sb_dot_q4k(const uint8_t *st, int lane, const uint32_t *xa, const u
         A1 = gb_dp4a_us(hi, A4[k], A1);
         B1 = gb_dp4a_us(hi, B4[k], B1);
         C1 = gb_dp4a_us(hi, C4[k], C1);
-        if constexpr (L == 4) {
-          D0 = gb_dp4a_us(lo, d4[k], D0);
-          D1 = gb_dp4a_us(hi, D4[k], D1);
-        }
       }
     }
     const int j0 = 2 * c, j1 = 2 * c + 1;
@@ -127,41 +107,23 @@ GB_DEV float sb_dot_q4k(const uint8_t *st, int lane, const uint32_t *xa, const u
     IA1 += sc1 * A1;
     IB1 += sc1 * B1;
     IC1 += sc1 * C1;
-    if constexpr (L == 4) {
-      ID0 += sc0 * D0;
-      ID1 += sc1 * D1;
-    }
     const float m0 = (float)byte_i(j0 < 4 ? m03 : m47, j0 & 3), m1 = (float)byte_i(j1 < 4 ? m03 : m47, j1 & 3);
     tm = fmaf(m0, xsum[4 * c] + xsum[4 * c + 1], tm);
     tm = fmaf(m1, xsum[4 * c + 2] + xsum[4 * c + 3], tm);
   }
   // sum sc*q*x / xs = A + (254 B + C)/254^2 per family; |I| < 2^28, float error 2^-24
   const float A = (float)IA0 + (float)IA1 * 0.0625f, B = (float)IB0 + (float)IB1 * 0.0625f,
-              C = (float)IC0 + (float)IC1 * 0.0625f, D = (float)ID0 + (float)ID1 * 0.0625f;
-  return d * (xs * limb_sum<L>(A, B, C, D)) - dmin * tm;
-}
-
-template <>
-GB_DEV float sb_dot<GB_T_Q4_K, 3>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)sl;
-  return sb_dot_q4k<3>(st, lane, xa, xb, xc, xd, xsum, xs);
-}
-template <>
-GB_DEV float sb_dot<GB_T_Q4_K, 4>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)sl;
-  return sb_dot_q4k<4>(st, lane, xa, xb, xc, xd, xsum, xs);
+              C = (float)IC0 + (float)IC1 * 0.0625f;
+  return d * (xs * (A + (254.f * B + C) * kL2)) - dmin * tm;
 }
 
 // Q5_K (ggml block_q5_K; the reference has no decoder for it): the Q4_K
 // factorisation with 5-bit quants q = nibble | fifth bit << 4 (0..31). Both
 // families are formed shifted (no factor 16: 16*31 does not fit a byte).
-template <int L>
-GB_DEV float sb_dot_q5k(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb, const uint32_t *xc,
-                        const uint32_t *xd, const float *xsum, float xs) {
+template <>
+GB_DEV float sb_dot<GB_T_Q5_K>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)sl;
   const uint4 *u = (const uint4 *)st;
   const uint4 h = u[lane];
   const float d = gb_half_to_float((uint16_t)(h.x & 0xFFFFu));
@@ -171,15 +133,15 @@ GB_DEV float sb_dot_q5k(const uint8_t *st, int lane, const uint32_t *xa, const u
   const uint32_t m47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
   const uint4 qh0 = u[1 * 32 + lane], qh1 = u[2 * 32 + lane];
   const uint32_t qhw[8] = {qh0.x, qh0.y, qh0.z, qh0.w, qh1.x, qh1.y, qh1.z, qh1.w};
-  int IA = 0, IB = 0, IC = 0, ID = 0;
+  int IA = 0, IB = 0, IC = 0;
   float tm = 0.f;
 #pragma unroll
   for (int c = 0; c < 4; c++) {
     const uint4 q0 = u[(3 + 2 * c) * 32 + lane], q1 = u[(4 + 2 * c) * 32 + lane];
     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const uint4 *pa = (const uint4 *)(xa + 16 * c), *pb = (const uint4 *)(xb + 16 * c),
-                *pc = (const uint4 *)(xc + 16 * c), *pd = (const uint4 *)(xd + 16 * c);
-    int A0 = 0, B0 = 0, C0 = 0, D0 = 0, A1 = 0, B1 = 0, C1 = 0, D1 = 0;
+                *pc = (const uint4 *)(xc + 16 * c);
+    int A0 = 0, B0 = 0, C0 = 0, A1 = 0, B1 = 0, C1 = 0;
 #pragma unroll
     for (int v = 0; v < 2; v++) {
       const uint4 la = pa[v], lb = pb[v], lc = pc[v], ha = pa[2 + v], hb = pb[2 + v], hc = pc[2 + v];
@@ -187,12 +149,6 @@ GB_DEV float sb_dot_q5k(const uint8_t *st, int lane, const uint32_t *xa, const u
                      c4[4] = {lc.x, lc.y, lc.z, lc.w};
       const uint32_t A4[4] = {ha.x, ha.y, ha.z, ha.w}, B4[4] = {hb.x, hb.y, hb.z, hb.w},
                      C4[4] = {hc.x, hc.y, hc.z, hc.w};
-      uint32_t d4[4] = {0u, 0u, 0u, 0u}, D4[4] = {0u, 0u, 0u, 0u};
-      if constexpr (L == 4) {
-        const uint4 ld = pd[v], hd = pd[2 + v];
-        d4[0] = ld.x; d4[1] = ld.y; d4[2] = ld.z; d4[3] = ld.w;
-        D4[0] = hd.x; D4[1] = hd.y; D4[2] = hd.z; D4[3] = hd.w;
-      }
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const uint32_t w = qw[4 * v + k], hb5 = qhw[4 * v + k];
@@ -204,10 +160,6 @@ GB_DEV float sb_dot_q5k(const uint8_t *st, int lane, const uint32_t *xa, const u
         A1 = gb_dp4a_us(hi, A4[k], A1);
         B1 = gb_dp4a_us(hi, B4[k], B1);
         C1 = gb_dp4a_us(hi, C4[k], C1);
-        if constexpr (L == 4) {
-          D0 = gb_dp4a_us(lo, d4[k], D0);
-          D1 = gb_dp4a_us(hi, D4[k], D1);
-        }
       }
     }
     const int j0 = 2 * c, j1 = 2 * c + 1;
@@ -215,39 +167,25 @@ GB_DEV float sb_dot_q5k(const uint8_t *st, int lane, const uint32_t *xa, const u
     IA += sc0 * A0 + sc1 * A1;
     IB += sc0 * B0 + sc1 * B1;
     IC += sc0 * C0 + sc1 * C1;
-    if constexpr (L == 4) ID += sc0 * D0 + sc1 * D1;
     const float m0 = (float)byte_i(j0 < 4 ? m03 : m47, j0 & 3), m1 = (float)byte_i(j1 < 4 ? m03 : m47, j1 & 3);
     tm = fmaf(m0, xsum[4 * c] + xsum[4 * c + 1], tm);
     tm = fmaf(m1, xsum[4 * c + 2] + xsum[4 * c + 3], tm);
   }
   // |I| < 8 * 63 * 32 * 31 * 127 < 2^27: exact in int32, float error 2^-24
-  return d * (xs * limb_sum<L>((float)IA, (float)IB, (float)IC, (float)ID)) - dmin * tm;
-}
-template <>
-GB_DEV float sb_dot<GB_T_Q5_K, 3>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)sl;
-  return sb_dot_q5k<3>(st, lane, xa, xb, xc, xd, xsum, xs);
-}
-template <>
-GB_DEV float sb_dot<GB_T_Q5_K, 4>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)sl;
-  return sb_dot_q5k<4>(st, lane, xa, xb, xc, xd, xsum, xs);
+  return d * (xs * ((float)IA + (254.f * (float)IB + (float)IC) * kL2)) - dmin * tm;
 }
 
 // Q6_K: quant/quant.go:114 layout; y = d*sc*(q-32) over 16-element sub-blocks.
 // The -32 enters the dp4a sums as their starting value -32*(limb sums).
-template <int L>
-GB_DEV float sb_dot_q6k(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb, const uint32_t *xc,
-                        const uint32_t *xd, const uint2 *sl, float xs) {
+template <>
+GB_DEV float sb_dot<GB_T_Q6_K>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)xsum;
   const uint4 *u = (const uint4 *)st;
   const uint4 scv = u[12 * 32 + lane];
   const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
   const float d = gb_half_to_float(((const uint16_t *)(st + 13 * 512))[lane]);
-  int IA = 0, IB = 0, IC = 0, ID = 0;
+  int IA = 0, IB = 0, IC = 0;
 #pragma unroll
   for (int c = 0; c < 2; c++) {
     const uint4 l0 = u[(4 * c + 0) * 32 + lane], l1 = u[(4 * c + 1) * 32 + lane];
@@ -268,57 +206,37 @@ GB_DEV float sb_dot_q6k(const uint8_t *st, int lane, const uint32_t *xa, const u
         const uint2 o = sl[g];
         const uint32_t a4[4] = {la.x, la.y, la.z, la.w}, b4[4] = {lb.x, lb.y, lb.z, lb.w},
                        c4[4] = {lc.x, lc.y, lc.z, lc.w};
-        uint32_t d4[4] = {0u, 0u, 0u, 0u};
-        if constexpr (L == 4) {
-          const uint4 ld = ((const uint4 *)xd)[g];
-          d4[0] = ld.x; d4[1] = ld.y; d4[2] = ld.z; d4[3] = ld.w;
-        }
-        int A = -32 * lo16(o.x), B = -32 * hi16(o.x), C = -32 * lo16(o.y), D = -32 * hi16(o.y);
+        int A = -32 * lo16(o.x), B = -32 * hi16(o.x), C = -32 * lo16(o.y);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
           const int k = 4 * is + kk;
-          const uint32_t Lw = i & 1 ? ql[8 + k] : ql[k];
+          const uint32_t L = i & 1 ? ql[8 + k] : ql[k];
           const uint32_t H = qh[k];
           uint32_t q;
-          if (i == 0) q = (Lw & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
-          else if (i == 1) q = (Lw & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
-          else if (i == 2) q = ((Lw >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
-          else q = ((Lw >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
+          if (i == 0) q = (L & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
+          else if (i == 1) q = (L & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
+          else if (i == 2) q = ((L >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
+          else q = ((L >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
           A = gb_dp4a_us(q, a4[kk], A);
           B = gb_dp4a_us(q, b4[kk], B);
           C = gb_dp4a_us(q, c4[kk], C);
-          if constexpr (L == 4) D = gb_dp4a_us(q, d4[kk], D);
         }
         const int sc = (int)(int8_t)((scw[g >> 2] >> (8 * (g & 3))) & 0xFFu);  // scale of sub-block g
         IA += sc * A;
         IB += sc * B;
         IC += sc * C;
-        if constexpr (L == 4) ID += sc * D;
       }
     }
   }
-  return d * (xs * limb_sum<L>((float)IA, (float)IB, (float)IC, (float)ID));
-}
-template <>
-GB_DEV float sb_dot<GB_T_Q6_K, 3>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)xsum;
-  return sb_dot_q6k<3>(st, lane, xa, xb, xc, xd, sl, xs);
-}
-template <>
-GB_DEV float sb_dot<GB_T_Q6_K, 4>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)xsum;
-  return sb_dot_q6k<4>(st, lane, xa, xb, xc, xd, sl, xs);
+  return d * (xs * ((float)IA + (254.f * (float)IB + (float)IC) * kL2));
 }
 
 // Q4_0: eight 32-element blocks per super-block, y = d*(q-8); the -8 enters
 // the dp4a sums as their starting value (x16 for the high nibbles, used in place).
-template <int L>
-GB_DEV float sb_dot_q40(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb, const uint32_t *xc,
-                        const uint32_t *xd, const uint2 *sl, float xs) {
+template <>
+GB_DEV float sb_dot<GB_T_Q4_0>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)xsum;
   const uint4 *u = (const uint4 *)st;
   const uint4 h = u[lane];
   const uint32_t dw[4] = {h.x, h.y, h.z, h.w};
@@ -335,14 +253,8 @@ GB_DEV float sb_dot_q40(const uint8_t *st, int lane, const uint32_t *xa, const u
                    c4[4] = {lc.x, lc.y, lc.z, lc.w};
     const uint32_t A4[4] = {ha.x, ha.y, ha.z, ha.w}, B4[4] = {hb.x, hb.y, hb.z, hb.w},
                    C4[4] = {hc.x, hc.y, hc.z, hc.w};
-    uint32_t d4[4] = {0u, 0u, 0u, 0u}, D4[4] = {0u, 0u, 0u, 0u};
-    if constexpr (L == 4) {
-      const uint4 ld = ((const uint4 *)xd)[2 * k], hd = ((const uint4 *)xd)[2 * k + 1];
-      d4[0] = ld.x; d4[1] = ld.y; d4[2] = ld.z; d4[3] = ld.w;
-      D4[0] = hd.x; D4[1] = hd.y; D4[2] = hd.z; D4[3] = hd.w;
-    }
-    int Al = -8 * lo16(ol.x), Bl = -8 * hi16(ol.x), Cl = -8 * lo16(ol.y), Dl = -8 * hi16(ol.y);
-    int Ah = -128 * lo16(oh.x), Bh = -128 * hi16(oh.x), Ch = -128 * lo16(oh.y), Dh = -128 * hi16(oh.y);
+    int Al = -8 * lo16(ol.x), Bl = -8 * hi16(ol.x), Cl = -8 * lo16(ol.y);
+    int Ah = -128 * lo16(oh.x), Bh = -128 * hi16(oh.x), Ch = -128 * lo16(oh.y);
 #pragma unroll
     for (int kk = 0; kk < 4; kk++) {
       const uint32_t lo = qw[kk] & 0x0F0F0F0Fu, hi = qw[kk] & 0xF0F0F0F0u;
@@ -352,42 +264,22 @@ GB_DEV float sb_dot_q40(const uint8_t *st, int lane, const uint32_t *xa, const u
       Ah = gb_dp4a_us(hi, A4[kk], Ah);
       Bh = gb_dp4a_us(hi, B4[kk], Bh);
       Ch = gb_dp4a_us(hi, C4[kk], Ch);
-      if constexpr (L == 4) {
-        Dl = gb_dp4a_us(lo, d4[kk], Dl);
-        Dh = gb_dp4a_us(hi, D4[kk], Dh);
-      }
     }
-    const int A = 16 * Al + Ah, B = 16 * Bl + Bh, C = 16 * Cl + Ch, D = 16 * Dl + Dh;
-    float S;
-    if constexpr (L == 4)
-      S = ((float)A + ((float)(254 * B + C) + (float)D * (1.f / 254.f)) * kL2) * 0.0625f;
-    else
-      S = ((float)A + (float)(254 * B + C) * kL2) * 0.0625f;
+    const int A = 16 * Al + Ah, B = 16 * Bl + Bh, C = 16 * Cl + Ch;
+    const float S = ((float)A + (float)(254 * B + C) * kL2) * 0.0625f;
     const float dk = gb_half_to_float((uint16_t)((dw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu));
     acc = fmaf(dk, S, acc);
   }
   return xs * acc;
 }
-template <>
-GB_DEV float sb_dot<GB_T_Q4_0, 3>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)xsum;
-  return sb_dot_q40<3>(st, lane, xa, xb, xc, xd, sl, xs);
-}
-template <>
-GB_DEV float sb_dot<GB_T_Q4_0, 4>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)xsum;
-  return sb_dot_q40<4>(st, lane, xa, xb, xc, xd, sl, xs);
-}
 
 // Q8_0: eight 32-element blocks per super-block, y = d*q with int8 q
 // (quant/quant.go:44-55); signed x signed dp4a, one float FMA per block.
-template <int L>
-GB_DEV float sb_dot_q80(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb, const uint32_t *xc,
-                        const uint32_t *xd, float xs) {
+template <>
+GB_DEV float sb_dot<GB_T_Q8_0>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                               const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  (void)xsum;
+  (void)sl;
   const uint4 *u = (const uint4 *)st;
   const uint4 h = u[lane];
   const uint32_t dw[4] = {h.x, h.y, h.z, h.w};
@@ -402,46 +294,19 @@ GB_DEV float sb_dot_q80(const uint8_t *st, int lane, const uint32_t *xa, const u
     const uint32_t a8[8] = {la.x, la.y, la.z, la.w, ha.x, ha.y, ha.z, ha.w};
     const uint32_t b8[8] = {lb.x, lb.y, lb.z, lb.w, hb.x, hb.y, hb.z, hb.w};
     const uint32_t c8[8] = {lc.x, lc.y, lc.z, lc.w, hc.x, hc.y, hc.z, hc.w};
-    uint32_t d8[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-    if constexpr (L == 4) {
-      const uint4 ld = ((const uint4 *)xd)[2 * k], hd = ((const uint4 *)xd)[2 * k + 1];
-      d8[0] = ld.x; d8[1] = ld.y; d8[2] = ld.z; d8[3] = ld.w;
-      d8[4] = hd.x; d8[5] = hd.y; d8[6] = hd.z; d8[7] = hd.w;
-    }
-    int A = 0, B = 0, C = 0, D = 0;
+    int A = 0, B = 0, C = 0;
 #pragma unroll
     for (int kk = 0; kk < 8; kk++) {
       A = gb_dp4a_ss(qw[kk], a8[kk], A);
       B = gb_dp4a_ss(qw[kk], b8[kk], B);
       C = gb_dp4a_ss(qw[kk], c8[kk], C);
-      if constexpr (L == 4) D = gb_dp4a_ss(qw[kk], d8[kk], D);
     }
     // |A|, |B|, |C| < 32*127*128; 254*B + C fits int32
-    float S;
-    if constexpr (L == 4)
-      S = (float)A + ((float)(254 * B + C) + (float)D * (1.f / 254.f)) * kL2;
-    else
-      S = (float)A + (float)(254 * B + C) * kL2;
+    const float S = (float)A + (float)(254 * B + C) * kL2;
     const float dk = gb_half_to_float((uint16_t)((dw[k >> 1] >> (16 * (k & 1))) & 0xFFFFu));
     acc = fmaf(dk, S, acc);
   }
   return xs * acc;
-}
-template <>
-GB_DEV float sb_dot<GB_T_Q8_0, 3>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)xsum;
-  (void)sl;
-  return sb_dot_q80<3>(st, lane, xa, xb, xc, xd, xs);
-}
-template <>
-GB_DEV float sb_dot<GB_T_Q8_0, 4>(const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                                  const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl,
-                                  float xs) {
-  (void)xsum;
-  (void)sl;
-  return sb_dot_q80<4>(st, lane, xa, xb, xc, xd, xs);
 }
 
 // ---- epilogues (one warp, lane l = row 32*rowblock + l) ---------------------
@@ -603,13 +468,11 @@ GB_DEV unsigned cta_of_unit(unsigned U, unsigned G, unsigned u) {
   return b;
 }
 
-// x4: the activation super-block carries a fourth limb (warp-uniform)
 template <int TA, int TB>
-GB_DEV float decode(int ty, bool x4, const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
-                    const uint32_t *xc, const uint32_t *xd, const float *xsum, const uint2 *sl, float xs) {
-  if (TA == TB || ty == TA)
-    return x4 ? sb_dot<TA, 4>(st, lane, xa, xb, xc, xd, xsum, sl, xs) : sb_dot<TA, 3>(st, lane, xa, xb, xc, xd, xsum, sl, xs);
-  return x4 ? sb_dot<TB, 4>(st, lane, xa, xb, xc, xd, xsum, sl, xs) : sb_dot<TB, 3>(st, lane, xa, xb, xc, xd, xsum, sl, xs);
+GB_DEV float decode(int ty, const uint8_t *st, int lane, const uint32_t *xa, const uint32_t *xb,
+                    const uint32_t *xc, const float *xsum, const uint2 *sl, float xs) {
+  if (TA == TB || ty == TA) return sb_dot<TA>(st, lane, xa, xb, xc, xsum, sl, xs);
+  return sb_dot<TB>(st, lane, xa, xb, xc, xsum, sl, xs);
 }
 
 // Byte offset of unit u (row-block u / nsb, super-block u % nsb) in the tiled
@@ -658,12 +521,10 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   uint32_t *xa_s = (uint32_t *)xbase;
   uint32_t *xb_s = xa_s + XS * 64;
   uint32_t *xc_s = xb_s + XS * 64;
-  uint32_t *xd_s = xc_s + XS * 64;
-  float *xsum_s = (float *)(xd_s + XS * 64);
+  float *xsum_s = (float *)(xc_s + XS * 64);
   uint2 *sl_s = (uint2 *)(xsum_s + XS * 16);
   float *xs_s = (float *)(sl_s + XS * 16);
-  int *xf_s = (int *)(xs_s + ((XS + 3) & ~3));  // 1: the super-block has a fourth limb
-  float *psum = (float *)(xf_s + ((XS + 3) & ~3));  // [2][kPend][W][64]
+  float *psum = xs_s + ((XS + 3) & ~3);  // [2][kPend][W][64]
   float *wn_s = psum + 2 * kPend * W * 64;                    // [XS][256] norm weights (aux_w)
   double *rope_s = (double *)(wn_s + (p.aux_w ? XS * 256 : 0));  // RoPE row (aux_rope doubles)
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
@@ -737,13 +598,7 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
   // z = (x * inv) * w with inv = 1/sqrt(sum x^2 / n + eps) from per-32 sums of
   // squares (cpu.RMSNorm, backend/cpu/cpu.go:17: float64 sum, float32 products).
   // Per super-block: s = max|z| / 127 and three int8 limbs per element,
-  // z ~ s*(a + b/254 + c/254^2): every limb residual is exact, so the error is
-  // the float32 rounding of z*127/max (2^-24 of the element itself) plus half a
-  // unit of the last limb (2^-24 of the block maximum). When the maximum stands
-  // more than 16 times above the mean magnitude (an outlier feature), the last
-  // term would dominate the small elements, so such a block gets a fourth limb
-  // d/254^3 (half a unit = 2^-32 of the maximum) and the decoders one more
-  // dp4a family for it.
+  // z ~ s*(a + b/254 + c/254^2) (error below 2^-21 of the block maximum).
   constexpr int CT = W * 32;
   const int tid = threadIdx.x;
   gb_grid_dep_wait();
@@ -792,51 +647,42 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
         for (int i = 0; i < 8; i++) z[i] = __fmul_rn(__fmul_rn(z[i], inv), wv[i]);
       }
     }
-    float m = 0.f, zs = 0.f, za = 0.f;
+    float m = 0.f, zs = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
       m = fmaxf(m, fabsf(z[i]));
       zs += z[i];
-      za += fabsf(z[i]);
     }
     m = gb_warp_max(m);
-    const bool x4 = gb_warp_sum(za) < 16.f * m;  // max above 16x the mean magnitude (warp-uniform)
     const float r = m > 0.f ? 127.f / m : 0.f;
-    uint32_t wa[2] = {0u, 0u}, wb[2] = {0u, 0u}, wc[2] = {0u, 0u}, wd[2] = {0u, 0u};
-    int sa = 0, sbs = 0, sc = 0, sd = 0;
+    uint32_t wa[2] = {0u, 0u}, wb[2] = {0u, 0u}, wc[2] = {0u, 0u};
+    int sa = 0, sbs = 0, sc = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
       const float t = z[i] * r;
-      const float fa = rintf(t), r1 = (t - fa) * 254.f, fb = rintf(r1), r2 = (r1 - fb) * 254.f, fc = rintf(r2);
-      const int ia = (int)fa, ib = (int)fb, ic = (int)fc, id = x4 ? (int)rintf((r2 - fc) * 254.f) : 0;
+      const float fa = rintf(t), r1 = (t - fa) * 254.f, fb = rintf(r1), fc = rintf((r1 - fb) * 254.f);
+      const int ia = (int)fa, ib = (int)fb, ic = (int)fc;
       sa += ia;
       sbs += ib;
       sc += ic;
-      sd += id;
       wa[i >> 2] |= (uint32_t)(ia & 0xFF) << (8 * (i & 3));
       wb[i >> 2] |= (uint32_t)(ib & 0xFF) << (8 * (i & 3));
       wc[i >> 2] |= (uint32_t)(ic & 0xFF) << (8 * (i & 3));
-      wd[i >> 2] |= (uint32_t)(id & 0xFF) << (8 * (i & 3));
     }
     ((uint2 *)(xa_s + ls * 64))[lane] = make_uint2(wa[0], wa[1]);
     ((uint2 *)(xb_s + ls * 64))[lane] = make_uint2(wb[0], wb[1]);
     ((uint2 *)(xc_s + ls * 64))[lane] = make_uint2(wc[0], wc[1]);
-    if (x4) ((uint2 *)(xd_s + ls * 64))[lane] = make_uint2(wd[0], wd[1]);
     // lanes 2i and 2i+1 hold 16-group i
     zs += __shfl_xor_sync(0xffffffffu, zs, 1);
     sa += __shfl_xor_sync(0xffffffffu, sa, 1);
     sbs += __shfl_xor_sync(0xffffffffu, sbs, 1);
     sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-    sd += __shfl_xor_sync(0xffffffffu, sd, 1);
     if ((lane & 1) == 0) {
       xsum_s[ls * 16 + (lane >> 1)] = zs;
-      sl_s[ls * 16 + (lane >> 1)] = make_uint2(((uint32_t)sa & 0xFFFFu) | ((uint32_t)sbs << 16),
-                                               ((uint32_t)sc & 0xFFFFu) | ((uint32_t)sd << 16));
+      sl_s[ls * 16 + (lane >> 1)] =
+          make_uint2(((uint32_t)sa & 0xFFFFu) | ((uint32_t)sbs << 16), (uint32_t)sc & 0xFFFFu);
     }
-    if (lane == 0) {
-      xs_s[ls] = m / 127.f;
-      xf_s[ls] = x4 ? 1 : 0;
-    }
+    if (lane == 0) xs_s[ls] = m / 127.f;
   }
   consumers_sync<W>();
 
@@ -878,15 +724,14 @@ __global__ void __launch_bounds__(32 * (W + 1), W <= 8 ? 2 : 1) gemv_kernel(cons
       if (!timeout) {
         int ls = (int)usb - sbf;
         if (ls < 0) ls += nsb;
-        const uint32_t *xa = xa_s + ls * 64, *xb = xb_s + ls * 64, *xc = xc_s + ls * 64, *xd = xd_s + ls * 64;
+        const uint32_t *xa = xa_s + ls * 64, *xb = xb_s + ls * 64, *xc = xc_s + ls * 64;
         const float *xsum = xsum_s + ls * 16;
         const uint2 *sl = sl_s + ls * 16;
         const float xs = xs_s[ls];
-        const bool x4 = xf_s[ls] != 0;
         const size_t off = TA == TB ? (size_t)(j & (unsigned)(K - 1)) * (size_t)p.rb * sbb_a
                                     : unit_off<TA, TB>(p, u) - unit_off<TA, TB>(p, cu0 + (k << LK));
         const uint8_t *st = ring + (size_t)s * p.stage_bytes + off;
-        acc0 += decode<TA, TB>(ty, x4, st, lane, xa, xb, xc, xd, xsum, sl, xs);
+        acc0 += decode<TA, TB>(ty, st, lane, xa, xb, xc, xsum, sl, xs);
       }
       __syncwarp();
       if (lane == 0) gb_mbar_arrive(&empty[s]);
@@ -1117,12 +962,11 @@ int sms() {
 }
 
 // Dynamic shared memory: ring stages, then per staged super-block the limb
-// planes (4 x 256 B), 16 sums (64 B) and 16 packed limb sums (128 B), the
-// scales and the fourth-limb flags (each padded to 4 words), then
-// 2 x kPend x [warps][64] segment partials.
+// planes (3 x 256 B), 16 sums (64 B) and 16 packed limb sums (128 B), the
+// scales (padded to 4 floats), then 2 x kPend x [warps][64] segment partials.
 size_t gemv_smem(int warps, int nstage, int stage_bytes, int xs_max, int aux_w, int aux_rope) {
-  return (size_t)nstage * stage_bytes + (size_t)xs_max * (4 * 256 + 64 + 128) +
-         (size_t)((xs_max + 3) & ~3) * 8 + (size_t)2 * kPend * warps * 64 * 4 + (aux_w ? (size_t)xs_max * 1024 : 0) +
+  return (size_t)nstage * stage_bytes + (size_t)xs_max * (3 * 256 + 64 + 128) +
+         (size_t)((xs_max + 3) & ~3) * 4 + (size_t)2 * kPend * warps * 64 * 4 + (aux_w ? (size_t)xs_max * 1024 : 0) +
          (size_t)aux_rope * 8;
 }
 
@@ -1265,11 +1109,6 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   if (p.half && a.ntiles % 2) return gb_fail(GB_ERR_INVALID, "gpu: gemv: tiles not paired");
   const int ta = a.type_a, tb = a.split_tile < a.ntiles ? a.type_b : a.type_a;
   p.a.type_b = tb;
-  // consumer warps per CTA: 16 (a whole SM) or 8 (half an SM); GB_GEMV_WARPS overrides
-  int warps = 16;
-  if (const char *e = getenv("GB_GEMV_WARPS")) warps = atoi(e) == 8 ? 8 : 16;
-  KernelFn fn = pick(ta, tb, a.epi, warps);
-  if (!fn) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: types %d/%d with epilogue %d", ta, tb, a.epi);
   if (p.half && ta != tb) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: gate/up types differ");
   p.nrb = p.half ? a.ntiles / 2 : a.ntiles;
   p.upr = p.half ? 2 * a.nsb : a.nsb;
@@ -1277,6 +1116,39 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   const int ub = p.rb * std::max(gb_tiled_sb_bytes(ta), gb_tiled_sb_bytes(tb));  // largest unit
   const int nsm = sms();
   const long long cap = smem_optin();
+  static const char *epi_names[] = {"PLAIN", "QKV", "RESID", "SWIGLU", "LOGITS", "PARTIAL"};
+  // Paired launch: two 8-warp CTAs per SM, so that a matrix of up to twice as
+  // many row-blocks as SMs runs one row-block per CTA with no split (and no
+  // cross-CTA combine at its end). Used for short row-blocks (at most 16
+  // units, e.g. the 8B's q|k|v: 192 row-blocks of 16 units, measured 2 %
+  // faster per token); GB_GEMV_PAIR_<KIND> / GB_GEMV_PAIR = 0 or 1 override.
+  bool pair = p.nrb > nsm && p.nrb <= 2 * nsm && p.upr <= 16;
+  {
+    char key[64];
+    snprintf(key, sizeof key, "GB_GEMV_PAIR_%s", epi_names[a.epi]);
+    const char *e = getenv(key);
+    if (!e) e = getenv("GB_GEMV_PAIR");
+    if (e) pair = atoi(e) == 1;
+  }
+  const long long slots = pair ? 2LL * nsm : nsm;
+  long long grid = p.nrb <= slots ? p.nrb : std::min<long long>(slots, p.units);
+  if (grid * 128 > (long long)gb_gemv_scratch_floats(a.ntiles, plan)) grid = gb_gemv_scratch_floats(a.ntiles, plan) / 128;
+  const int upc = (int)((p.units + grid - 1) / grid);  // units per CTA (at most)
+  const int xs = std::min(a.nsb, (p.half ? upc / 2 + 1 : upc) + 1);  // super-blocks a CTA touches
+  // consumer warps per CTA: 16 (a whole SM) or 8 (half an SM); GB_GEMV_WARPS
+  // overrides. The ring holds at least one unit per consumer warp; when that
+  // minimum and the staged activation of a very wide input (e.g. the 70B's
+  // 28,672-column down projection with 6.7 KB Q6_K units) exceed shared
+  // memory with 16 warps, the launch uses 8 and all of shared memory.
+  int warps = pair ? 8 : 16;
+  if (const char *e = getenv("GB_GEMV_WARPS")) warps = atoi(e) == 8 ? 8 : 16;
+  bool wide = false;
+  if (warps == 16 && (long long)gemv_smem(16, 0, 0, xs, p.aux_w, p.aux_rope) + 16LL * ub > cap - 1024) {
+    warps = 8;
+    wide = true;
+  }
+  KernelFn fn = pick(ta, tb, a.epi, warps);
+  if (!fn) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: gemv: types %d/%d with epilogue %d", ta, tb, a.epi);
   // opt in to the shared memory and learn the register count (once per kernel)
   static KernelFn seen[64];
   static int seen_static[64];
@@ -1304,7 +1176,6 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   // about 36 KB, as many stages as the budget holds (2 to 8).
   // GB_GEMV_RING_<PLAIN|QKV|RESID|SWIGLU|LOGITS> or GB_GEMV_RING = "K,stages"
   // force the ring (sweeps) when it fits.
-  static const char *epi_names[] = {"PLAIN", "QKV", "RESID", "SWIGLU", "LOGITS", "PARTIAL"};
   int fk = 0, fs = 0;
   {
     char key[64];
@@ -1313,11 +1184,7 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
     if (!e) e = getenv("GB_GEMV_RING");
     if (e && sscanf(e, "%d,%d", &fk, &fs) != 2) fk = fs = 0;
   }
-  long long grid = p.nrb <= nsm ? p.nrb : std::min<long long>(nsm, p.units);
-  if (grid * 128 > (long long)gb_gemv_scratch_floats(a.ntiles, plan)) grid = gb_gemv_scratch_floats(a.ntiles, plan) / 128;
-  const int upc = (int)((p.units + grid - 1) / grid);  // units per CTA (at most)
-  const int xs = std::min(a.nsb, (p.half ? upc / 2 + 1 : upc) + 1);  // super-blocks a CTA touches
-  long long budget = warps == 8 ? 113 * 1024 : 220 * 1024;
+  long long budget = wide ? cap - 2048 : warps == 8 ? 113 * 1024 : 220 * 1024;
   if (const char *e = getenv("GB_SMEM_BUDGET")) budget = atoll(e);
   const long long room = cap - static_smem;
   const long long fixed = (long long)gemv_smem(warps, 0, 0, xs, p.aux_w, p.aux_rope);

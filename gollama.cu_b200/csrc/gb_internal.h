@@ -106,6 +106,8 @@ GbGemvPlan gb_gemv_plan(int ntiles, int nsb, int epi, int sms);
 size_t gb_tiled_bytes(int typ, int rows, int cols);
 int gb_repack_launch(int typ, const uint8_t *raw, int rows, int cols, uint8_t *tiled,
                      cudaStream_t st);
+// Floats of the GEMV scratch (GbEpiArgs::part) a caller allocates: split-row
+// partials and the fourth limb planes of outlier input blocks.
 int gb_gemv_scratch_floats(int ntiles, const GbGemvPlan &p);
 
 // ---- attention (gb_attn.cu)

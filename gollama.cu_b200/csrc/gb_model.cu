@@ -908,7 +908,7 @@ int load_model(GbGguf *f, const gb_model_opts *opts, gb_model **out) {
   m->plan_gu = gb_gemv_plan(0, 0, GB_EPI_SWIGLU, m->sms);
   int max_tiles = std::max(std::max(m->head.ntiles, (m->q_local + 2 * m->kv_local) / 32),
                            std::max(c.dim / 32, 2 * m->ffn_local / 32));
-  if ((rc = dalloc(m, &m->gemv_part, (size_t)gb_gemv_scratch_floats(0, m->plan_plain) * 2, "model: scratch")) ||
+  if ((rc = dalloc(m, &m->gemv_part, (size_t)gb_gemv_scratch_floats(0, m->plan_plain), "model: scratch")) ||
       (rc = dalloc(m, &m->tile_counter, (size_t)max_tiles + 64, "model: scratch")))
     return fail(rc);
   m->attn_splits = gb_attn_splits(m->kv_local / hd, c.max_len, m->sms);
@@ -1651,7 +1651,7 @@ int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes,
   }
   if (raw) cudaFree(raw);
   GbGemvPlan plan = gb_gemv_plan(t.ntiles, t.nsb, GB_EPI_PLAIN, 148);
-  if (!rc && cudaMalloc(&l->part, sizeof(float) * (size_t)gb_gemv_scratch_floats(t.ntiles, plan) * 2) != cudaSuccess)
+  if (!rc && cudaMalloc(&l->part, sizeof(float) * (size_t)gb_gemv_scratch_floats(t.ntiles, plan)) != cudaSuccess)
     rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
   if (!rc && cudaMalloc(&l->tile_counter, sizeof(unsigned) * (size_t)(t.ntiles + 64)) != cudaSuccess)
     rc = gb_fail(GB_ERR_CUDA, "model: linear scratch");
@@ -1684,7 +1684,10 @@ int gb_linear_matvec(gb_linear *l, void *stream, const float *x, float *y) {
   a.e.y = y;
   a.e.part = l->part;
   a.e.tile_counter = l->tile_counter;
-  return gb_gemv_launch(a, gb_gemv_plan(l->t.ntiles, l->t.nsb, GB_EPI_PLAIN, 148), st, false);
+  // programmatic dependent launch: the weight stream (constant since the
+  // upload) starts while the stream's previous kernel finishes; x is read and
+  // y written only after that kernel has completed
+  return gb_gemv_launch(a, gb_gemv_plan(l->t.ntiles, l->t.nsb, GB_EPI_PLAIN, 148), st, true);
 }
 
 int gb_linear_info(const gb_linear *l, int *typ, int *rows, int *cols, size_t *weight_bytes) {

@@ -193,7 +193,10 @@ typedef struct gb_linear gb_linear;
 int gb_linear_upload(int device, int typ, const void *host_bytes, size_t nbytes, int rows,
                      int cols, gb_linear **out);
 /* (*Linear).MatVec, model/model.go:109 for batch 1: y[rows] = W x[cols]
- * (x and y device pointers). */
+ * (x and y device pointers). Launched with programmatic dependent launch:
+ * the weights start streaming while the stream's previous kernel finishes;
+ * x is read and y written only after it has completed. Calls on one
+ * gb_linear must not overlap on the GPU (they share its scratch). */
 int gb_linear_matvec(gb_linear *l, void *stream, const float *x, float *y);
 /* Added: the prefill GEMM on the tensor cores (tcgen05), the batched
  * MatVecQ of the reference's roadmap (ROADMAP.md:99-101): y[T][rows] =

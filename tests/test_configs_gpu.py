@@ -52,20 +52,47 @@ def test_8b_preset_after_8192_prefilled_positions(gb, orc, cuda):
     img.close()
 
 
-def test_3b_preset_after_32_token_prompt(gb, orc, cuda):
-    # prompt fed one token at a time, then greedy
+def check_logits_f16_kv(name, got, want):
+    """The bar for binary16 caches. Both sides round every new K/V value to
+    binary16 (f16.From), but their float32 values differ in the last bits, so
+    a value that lies within that distance of a rounding boundary rounds to
+    neighbouring binary16 numbers (2^-11 apart, relative) -- about one value
+    in 10^4. Each such split moves the logits by up to ~1e-3 on its own
+    (measured: position 0, with no history, reaches 8e-4). So: 99.9% of the
+    logits within the bar, none beyond 5e-3."""
+    d = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    bad = d > 1e-3 + 1e-4 * np.abs(want)
+    assert bad.mean() <= 1e-3 and d.max() <= 5e-3, (
+        f"{name}: {int(bad.sum())} of {bad.size} logits beyond 1e-3 + 1e-4 |want|, max abs {d.max():.3g}")
+
+
+@pytest.mark.parametrize("kv_f16", [0, 1])
+def test_3b_preset_after_32_token_prompt(gb, orc, cuda, kv_f16):
+    # BASELINE config 3: prompt fed one token at a time, then greedy. With
+    # the reference's float32 cache every position meets the bar; with
+    # binary16 caches the rounding-boundary splits above apply.
     spec = gb.synth_preset(3)
     img = gb.SynthImage(spec)
     raw = img.view()
-    m = gb.Model(img, max_len=4096, kv_f16=1)
-    om = orc.OracleModel(raw, 4096, True)
+    m = gb.Model(img, max_len=4096, kv_f16=kv_f16)
+    om = orc.OracleModel(raw, 4096, bool(kv_f16))
+    check = check_logits if not kv_f16 else check_logits_f16_kv
     toks = prompt_ids(spec.vocab, 33)
     for pos in range(32):
         got = m.forward(toks[pos], pos).copy()
         want = om.forward(toks[pos], pos, spec.vocab)
-        if pos in (0, 15, 31):
-            check_logits(f"3B prompt pos {pos}", got, want)
-    greedy_check("3B", m, om, toks[32], 32, 4, spec.vocab, orc, gb)
+        check(f"3B kv_f16={kv_f16} prompt pos {pos}", got, want)
+        if not near_tie(want):
+            assert gb.argmax(got) == orc.argmax(want)
+    tok = toks[32]
+    for i in range(4):
+        got = m.forward(tok, 32 + i).copy()
+        want = om.forward(tok, 32 + i, spec.vocab)
+        check(f"3B kv_f16={kv_f16} pos {32 + i}", got, want)
+        if near_tie(want):
+            break
+        assert gb.argmax(got) == orc.argmax(want)
+        tok = orc.argmax(want)
     m.close()
     om.close()
     img.close()
