@@ -2,9 +2,10 @@
 plus continuous batching", ROADMAP.md:197-202): sequences that join and leave
 between steps are decoded together, one batched pass per step, each through
 its own pages of the paged KV pool. Every row's logits must match the same
-sequence decoded alone by the one-sequence model (gb_model_forward) to the
-prefill's tolerance: the batched pass uses the binary16-operand tensor-core
-GEMMs, the one-sequence decode the float32-exact GEMVs."""
+sequence decoded alone by the one-sequence model (gb_model_forward) and by
+cpuForward (model/model_test.go:114, the C oracle) to the prefill's
+tolerance: the batched pass uses the binary16-operand tensor-core GEMMs, the
+one-sequence decode the float32-exact GEMVs."""
 import numpy as np
 import pytest
 
@@ -25,7 +26,7 @@ def rel_err(a, b):
 
 
 @pytest.mark.parametrize("name,page", [("q4km_hd64", 16), ("q4km_hd128", 32), ("gqa8_hd128", 8), ("q5km", 16)])
-def test_engine_matches_one_sequence_decode(gb, cuda, name, page):
+def test_engine_matches_one_sequence_decode(gb, orc, cuda, name, page):
     cfg = MODELS[name]
     img = gb.SynthImage(gb.synth_spec(**cfg))
     rng = np.random.default_rng(7)
@@ -83,6 +84,24 @@ def test_engine_matches_one_sequence_decode(gb, cuda, name, page):
             assert errs[-1] < LOGIT_TOL, f"{name} seq {k} pos {p}: {errs[-1]:.3g}"
         r.close()
     print(f"{name}: {len(errs)} rows, worst {max(errs):.2e}, median {np.median(errs):.2e}")
+    # against cpuForward itself (the C restatement, binary16 KV semantics),
+    # each sequence on its own oracle: every row within the binary16-GEMM
+    # tolerance, and the engine's greedy token equal to model.Argmax of the
+    # oracle's logits wherever the oracle's top two are further apart than
+    # that tolerance
+    raw = np.array(img.view(), copy=True)
+    oracle_errs = []
+    for k in fed:
+        om = orc.OracleModel(raw, 96, True)
+        for p, t in enumerate(fed[k]):
+            want = om.forward(t, p, cfg["vocab"])
+            oracle_errs.append(rel_err(got[k][p], want))
+            assert oracle_errs[-1] < LOGIT_TOL, f"{name} seq {k} pos {p} vs oracle: {oracle_errs[-1]:.3g}"
+            top = np.sort(want.astype(np.float64))
+            if top[-1] - top[-2] > 2 * LOGIT_TOL * np.abs(want).max():
+                assert int(np.argmax(got[k][p])) == orc.argmax(want), f"{name} seq {k} pos {p}: greedy token"
+        om.close()
+    print(f"{name} vs oracle: worst {max(oracle_errs):.2e}, median {np.median(oracle_errs):.2e}")
     e.close()
     m.close()
 
