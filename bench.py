@@ -23,7 +23,6 @@ import argparse
 import datetime
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -88,18 +87,13 @@ def prefill_flops(c, T):
 
 def ncu_traffic(config):
     """DRAM bytes per launch of the dominant kernel (gate/up + SwiGLU GEMV) from the
-    committed ncu summary profiles/step_kernels_8b_traffic.md (line
-    `dram_bytes_per_launch[<config>] = N`); None when no capture covers the config."""
-    p = os.path.join(ROOT, "profiles", "step_kernels_8b_traffic.md")
+    ncu capture recorded in profiles/traffic.json (a static figure from an earlier
+    capture, not measured in this run); None when no capture covers the config."""
     try:
-        with open(p) as f:
-            for line in f:
-                m = re.match(r"dram_bytes_per_launch\[(\w+)\]\s*=\s*(\d+)", line.strip())
-                if m and m.group(1) == config:
-                    return int(m.group(2))
-    except OSError:
-        pass
-    return None
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return int(json.load(f)[config]["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError):
+        return None
 
 
 class ClockSampler:
@@ -224,7 +218,7 @@ SWEEP_SHAPES = ((4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096))
 L2_BYTES = 126 * 1024 * 1024
 
 
-def gemv_sweep(gb, torch, device, peak, launches=48):
+def gemv_sweep(gb, torch, device, peak, launches=48, types=None, shapes=None):
     """the standalone batch-1 quantized GEMV (gb_linear_matvec,
     the kernel that replaces kernels/quantmv.go:18-136) for Q4_0 / Q4_K / Q6_K at
     four shapes. Weights follow the config's block recipe (seeds 0-3); enough
@@ -237,7 +231,11 @@ def gemv_sweep(gb, torch, device, peak, launches=48):
     dev = torch.device("cuda", device)
     stream = torch.cuda.Stream(device=dev)
     for tname, typ in SWEEP_TYPES:
+        if types and tname not in types:
+            continue
         for rows, cols in SWEEP_SHAPES:
+            if shapes and f"{rows}x{cols}" not in shapes:
+                continue
             mats = [gb.synth_matrix(typ, rows, cols, seed=s) for s in range(4)]
             wbytes = mats[0].nbytes
             ncopy = max(4, -(-3 * L2_BYTES // wbytes))
@@ -515,6 +513,7 @@ def run_ours(args, cfg, world, rank, local):
         "config": bench_config(cfg, spec, world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": ncu_traffic(args.config) if world == 1 else None,
+                     "traffic_source": "static: profiles/traffic.json (one earlier ncu capture), not this run",
                      "kernel": "gemv_kernel, gate/up + SwiGLU (one launch per layer)",
                      "bytes_per_launch": gu_bytes, "avg_launch_ms": round(gu_ms, 5), "peak_source": peak_src,
                      "timing": "CUDA events around each gate/up launch of an eager decode step (median of 5 steps); "
@@ -703,6 +702,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the standalone GEMV sweep (config 2)")
     ap.add_argument("--configs", default="1b,3b,70b",
                     help="more decode configurations measured after the main one ('' = none)")
+    ap.add_argument("--sweep-only", default=None, metavar="TYPES:SHAPES",
+                    help="run only the GEMV sweep, e.g. q4_k:14336x4096 or all:all (profiling captures)")
     ap.add_argument("--layers", type=int, default=0,
                     help="truncate the model to this many layers (small ncu captures only; not a bench line)")
     args = ap.parse_args()
@@ -712,6 +713,16 @@ def main():
     if args.layers:
         cfg["layers"] = args.layers
         cfg["workload"] += f" [truncated to {args.layers} layers for profiling]"
+    if args.sweep_only:
+        import torch
+
+        import gollama_b200 as gb
+
+        t, _, sh = args.sweep_only.partition(":")
+        sweep = gemv_sweep(gb, torch, 0, peaks()[0], types=None if t == "all" else t.split(","),
+                           shapes=None if sh in ("", "all") else sh.split(","))
+        print(json.dumps({"gemv_sweep": sweep}), flush=True)
+        return
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":
