@@ -448,10 +448,11 @@ def run_ours(args, cfg, world, rank, local):
     achieved = gu_bytes / (gu_ms / 1e3) / 1e9
     breakdown = {k: round(statistics.median(p[k][0] for p in prof), 4) for k in prof[0]}
 
-    # batched prefill of a 512-token prompt (one GPU; the timed decode above is done,
-    # so overwriting cache positions 0..511 does not touch it)
-    prefill = None
-    if args.prefill_tokens > 1:
+    # batched prefill of a 512-token prompt (the timed decode above is done, so
+    # overwriting cache positions 0..511 does not touch it) and continuous
+    # batching (one GPU), first decoding the quantized weights in every GEMM,
+    # then through the model's binary16 weight copy
+    def time_prefill(weights):
         pt = prompt_tokens(spec, args.prefill_tokens)
         m.prefill(pt, 0)  # warm-up (allocates the workspace)
         torch.cuda.synchronize()
@@ -466,16 +467,16 @@ def run_ours(args, cfg, world, rank, local):
         pms = max_over_ranks(ev0.elapsed_time(ev1) / reps, world)
         tpk, tsrc = tensor_peak()
         fl = prefill_flops(c, len(pt))
-        prefill = {"tokens": len(pt), "value": round(len(pt) / (pms / 1e3), 1), "unit": "tok/s",
-                   "ms": round(pms, 3), "tflops": round(fl / (pms / 1e3) / 1e12, 1),
-                   "frac_of_tensor_peak": round(fl / (pms / 1e3) / 1e12 / tpk, 4), "peak_source": tsrc,
-                   "how": "gb_model_prefill from host token ids: tcgen05 GEMMs (binary16 operands, f32 accumulate) "
-                          "+ tensor-core causal attention, last token through the decode step; under tensor "
-                          "parallelism the o/down partials summed by NCCL all-reduces; CUDA events, "
-                          f"mean of {reps}, max over ranks"}
-    # continuous batching: the engine decodes B sequences per step (one GPU)
-    batched = None
-    if world == 1 and args.batch > 1:
+        return {"tokens": len(pt), "value": round(len(pt) / (pms / 1e3), 1), "unit": "tok/s",
+                "ms": round(pms, 3), "tflops": round(fl / (pms / 1e3) / 1e12, 1),
+                "frac_of_tensor_peak": round(fl / (pms / 1e3) / 1e12 / tpk, 4), "peak_source": tsrc,
+                "weights": weights,
+                "how": "gb_model_prefill from host token ids: tcgen05 GEMMs (binary16 operands, f32 accumulate) "
+                       "+ tensor-core causal attention, last token through the decode step; under tensor "
+                       "parallelism the o/down partials summed by NCCL all-reduces; CUDA events, "
+                       f"mean of {reps}, max over ranks"}
+
+    def time_engine(weights):
         e = gb.Engine(m, page_size=64, n_pages=args.batch * 4, max_batch=args.batch)
         ids = [e.add() for _ in range(args.batch)]
         btoks = prompt_tokens(spec, args.batch)
@@ -491,13 +492,28 @@ def run_ours(args, cfg, world, rank, local):
         torch.cuda.synchronize()
         wall = time.perf_counter() - w0
         bms = ev0.elapsed_time(ev1) / nsteps
-        batched = {"batch": args.batch, "value": round(args.batch * nsteps / (bms * nsteps / 1e3), 1), "unit": "tok/s",
-                   "ms_per_step": round(bms, 3), "e2e_tok_s": round(args.batch * nsteps / wall, 1),
-                   "positions": f"4..{4 + nsteps - 1}",
-                   "how": "gb_engine_step: B sequences one token each per step through the tensor-core GEMMs and the "
-                          "paged attention; value = CUDA events around 32 steps, each synchronous (ids in, next tokens "
-                          "out, status check), e2e = wall clock of the same loop"}
         e.close()
+        return {"batch": args.batch, "value": round(args.batch * nsteps / (bms * nsteps / 1e3), 1), "unit": "tok/s",
+                "ms_per_step": round(bms, 3), "e2e_tok_s": round(args.batch * nsteps / wall, 1),
+                "positions": f"4..{4 + nsteps - 1}", "weights": weights,
+                "how": "gb_engine_step: B sequences one token each per step through the tensor-core GEMMs and the "
+                       "paged attention; value = CUDA events around 32 steps, each synchronous (ids in, next tokens "
+                       "out, status check), e2e = wall clock of the same loop"}
+
+    prefill = time_prefill("quantized, decoded per call") if args.prefill_tokens > 1 else None
+    batched = time_engine("quantized, decoded per call") if world == 1 and args.batch > 1 else None
+    prefill16 = batched16 = None
+    if args.prefill_tokens > 1 or (world == 1 and args.batch > 1):
+        try:
+            w16 = m.cache_f16_weights()
+        except gb.GollamaError as exc:  # not enough device memory: reported, not measured
+            w16 = str(exc)
+        if isinstance(w16, int):
+            what = f"binary16 copy ({w16 / 1e9:.2f} GB, gb_model_cache_f16_weights), read by TMA"
+            prefill16 = time_prefill(what) if args.prefill_tokens > 1 else None
+            batched16 = time_engine(what) if world == 1 and args.batch > 1 else None
+        else:
+            prefill16 = batched16 = {"unavailable": w16}
 
     sweep = gemv_sweep(gb, torch, local, peaks()[0]) if world == 1 and not args.no_sweep else None
     configs = {}
@@ -525,8 +541,8 @@ def run_ours(args, cfg, world, rank, local):
         "kernel_ms_per_step": dict(breakdown, how="CUDA events between the launches of one eager decode step: "
                                    "launches serialized (no PDL overlap), so the classes add up to more than "
                                    "ms_per_step"),
-        "prefill": prefill,
-        "batched_decode": batched,
+        "prefill": prefill, "prefill_f16w": prefill16,
+        "batched_decode": batched, "batched_decode_f16w": batched16,
         "gemv_sweep": sweep,
         "configs": configs or None,
         "e2e": e2e,

@@ -180,14 +180,23 @@ struct GbTcGemm {
   float *part = nullptr;       // split-K partials (may be null: no split)
   size_t part_floats = 0;
   CUtensorMap tmap_a;
+  const __half *w16 = nullptr;  // the matrix's binary16 copy (gb_tc_f16_weights_launch) or null
+  CUtensorMap tmap_b;           // its tensor map, with w16
+  bool a16 = false;             // tmap_a16 is set: the activation with 16-row boxes
+  CUtensorMap tmap_a16;
 };
 struct GbTcPlan {
   int mt = 1, splits = 1;
   size_t part_floats = 0;
+  bool swap = false;  // tokens as the MMA's N (few token rows, binary16 weight copy)
 };
 GbTcPlan gb_tc_gemm_plan(const GbTcGemm &a, int sms);
-int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map);
+int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map, int box_rows = 128);
 int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st);
+// The binary16 copy of a GEMM's weights, the values the GEMM decodes to:
+// gb_tc_f16_rows(a) rows of a.nsb * 256 columns; writes its tensor map.
+size_t gb_tc_f16_rows(const GbTcGemm &a);
+int gb_tc_f16_weights_launch(const GbTcGemm &a, __half *w16, CUtensorMap *map, cudaStream_t st);
 int gb_embed_rows_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *tokens, int T, int vocab,
                          float *x, int32_t *fed, int pos0, int max_len, unsigned *err, cudaStream_t st);
 int gb_rmsnorm_rows_f16_launch(const float *x, const float *w, int rows, int n, float eps, __half *out,

@@ -132,9 +132,17 @@ struct Tiled {
   int rows = 0, cols = 0, ntiles = 0, nsb = 0;
   size_t bytes = 0;
   bool owned = true;
+  __half *w16 = nullptr;  // binary16 copy for the tensor-core GEMMs (gb_model_cache_f16_weights)
+  CUtensorMap map16;
 };
 
 enum { K_QKV = 0, K_ATTN, K_O, K_GU, K_DOWN, K_HEAD, K_OTHER, K_CLASSES };
+
+// Tensor maps of one binary16 activation buffer: 128-row boxes (the
+// dequantizing GEMM's token tiles) and 16-row boxes (the few-token GEMM).
+struct AMap {
+  CUtensorMap a128, a16;
+};
 
 }  // namespace
 
@@ -179,7 +187,7 @@ struct gb_model {
   float *pf_part = nullptr;  // split-K partials of the prefill GEMMs
   float *pf_tmp = nullptr;   // tensor parallel: this rank's o / down partial [chunk][dim]
   size_t pf_part_floats = 0;
-  CUtensorMap pf_map_dim, pf_map_q, pf_map_ffn;
+  AMap pf_map_dim, pf_map_q, pf_map_ffn;
   unsigned *err = nullptr;
   float *gemv_part = nullptr;
   unsigned *tile_counter = nullptr;
@@ -962,14 +970,17 @@ int prefill_workspace(gb_model *m) {
   m->pf_part_floats = (size_t)m->sms * 4 * 128 * 128;
   if ((rc = dalloc(m, &m->pf_part, m->pf_part_floats, "model: prefill workspace"))) return rc;
   if (c.tp_world > 1 && (rc = dalloc(m, &m->pf_tmp, (size_t)Tc * c.dim, "model: prefill workspace"))) return rc;
-  if ((rc = gb_tmap_f16_rows(m->pf_a16, Tc, c.dim, &m->pf_map_dim)) ||
-      (rc = gb_tmap_f16_rows(m->pf_a16, Tc, m->q_local, &m->pf_map_q)) ||
-      (rc = gb_tmap_f16_rows(m->pf_act16, Tc, m->ffn_local, &m->pf_map_ffn)))
-    return rc;
+  for (int box : {128, 16}) {
+    const auto pick = [box](AMap &a) { return box == 128 ? &a.a128 : &a.a16; };
+    if ((rc = gb_tmap_f16_rows(m->pf_a16, Tc, c.dim, pick(m->pf_map_dim), box)) ||
+        (rc = gb_tmap_f16_rows(m->pf_a16, Tc, m->q_local, pick(m->pf_map_q), box)) ||
+        (rc = gb_tmap_f16_rows(m->pf_act16, Tc, m->ffn_local, pick(m->pf_map_ffn), box)))
+      return rc;
+  }
   return GB_OK;
 }
 
-GbTcGemm tc_args(const Tiled &t, int epi, int T, const CUtensorMap &map, gb_model *m) {
+GbTcGemm tc_args(const Tiled &t, int epi, int T, const AMap &map, gb_model *m) {
   GbTcGemm g;
   g.w = t.w;
   g.type_a = t.type_a;
@@ -983,7 +994,13 @@ GbTcGemm tc_args(const Tiled &t, int epi, int T, const CUtensorMap &map, gb_mode
   g.err = m->err;
   g.part = m->pf_part;
   g.part_floats = m->pf_part_floats;
-  g.tmap_a = map;
+  g.tmap_a = map.a128;
+  g.tmap_a16 = map.a16;
+  g.a16 = true;
+  if (t.w16) {
+    g.w16 = t.w16;
+    g.tmap_b = t.map16;
+  }
   return g;
 }
 
@@ -991,7 +1008,7 @@ GbTcGemm tc_args(const Tiled &t, int epi, int T, const CUtensorMap &map, gb_mode
 // parallelism each rank's product over its input columns is a partial: the
 // ranks' partials are summed by an NCCL all-reduce on the model stream (every
 // rank makes the same calls in the same order), then added to x.
-int row_parallel(gb_model *m, const Tiled &w, int T, const CUtensorMap &map) {
+int row_parallel(gb_model *m, const Tiled &w, int T, const AMap &map) {
   const gb_config &c = m->c;
   const bool tp = c.tp_world > 1;
   GbTcGemm g = tc_args(w, tp ? GB_EPI_PLAIN : GB_EPI_RESID, T, map, m);
@@ -1158,6 +1175,45 @@ int gb_model_prefill(gb_model *m, const int32_t *tokens, int n, int pos0, float 
   return gb_model_forward(m, tokens[n - 1], pos0 + n - 1, host_logits);
 }
 
+int gb_model_cache_f16_weights(gb_model *m, size_t *bytes) {
+  gb_clear_error();
+  if (!m) return gb_fail(GB_ERR_INVALID, "model: null model");
+  // every matrix with the GEMM arguments it is used with (the gate/up pairs
+  // as one half's rows and tiles)
+  std::vector<std::pair<Tiled *, GbTcGemm>> mats;
+  for (auto &L : m->layers) {
+    mats.emplace_back(&L.qkv, tc_args(L.qkv, GB_EPI_PLAIN, 0, m->pf_map_dim, m));
+    mats.emplace_back(&L.wo, tc_args(L.wo, GB_EPI_RESID, 0, m->pf_map_q, m));
+    GbTcGemm g = tc_args(L.gu, GB_EPI_SWIGLU, 0, m->pf_map_dim, m);
+    g.rows = m->ffn_local;
+    g.ntiles = L.gu.ntiles / 2;
+    mats.emplace_back(&L.gu, g);
+    mats.emplace_back(&L.down, tc_args(L.down, GB_EPI_RESID, 0, m->pf_map_ffn, m));
+  }
+  mats.emplace_back(&m->head, tc_args(m->head, GB_EPI_PLAIN, 0, m->pf_map_dim, m));
+  size_t need = 0;
+  for (auto &e : mats)
+    if (!e.first->w16) need += gb_tc_f16_rows(e.second) * (size_t)e.second.nsb * 256 * sizeof(__half);
+  if (bytes) *bytes = need;
+  if (!need) return GB_OK;
+  size_t free_b = 0, total_b = 0;
+  GB_CUDA(cudaSetDevice(m->o.device), "model: binary16 weights");
+  GB_CUDA(cudaMemGetInfo(&free_b, &total_b), "model: binary16 weights");
+  if (need + ((size_t)1 << 30) > free_b)  // keep 1 GiB for the caller's workspaces
+    return gb_fail(GB_ERR_UNSUPPORTED, "model: binary16 weights need %.2f GB, %.2f GB free", need / 1e9, free_b / 1e9);
+  for (auto &e : mats) {
+    Tiled &t = *e.first;
+    if (t.w16) continue;
+    __half *w16 = nullptr;
+    int rc = dalloc(m, &w16, gb_tc_f16_rows(e.second) * (size_t)e.second.nsb * 256, "model: binary16 weights");
+    if (!rc) rc = gb_tc_f16_weights_launch(e.second, w16, &t.map16, m->st);
+    if (rc) return rc;
+    t.w16 = w16;
+  }
+  GB_CUDA(cudaStreamSynchronize(m->st), "model: binary16 weights");
+  return GB_OK;
+}
+
 int gb_linear_matmul_f16(gb_linear *l, void *stream, const uint16_t *x, int T, float *y) {
   gb_clear_error();
   if (!l || !x || !y || T < 0) return gb_fail(GB_ERR_INVALID, "model: linear: bad matmul arguments");
@@ -1174,7 +1230,13 @@ int gb_linear_matmul_f16(gb_linear *l, void *stream, const uint16_t *x, int T, f
   g.y = y;
   g.ldy = l->t.rows;
   int rc = gb_tmap_f16_rows(x, T, l->t.cols, &g.tmap_a);
+  if (!rc) rc = gb_tmap_f16_rows(x, T, l->t.cols, &g.tmap_a16, 16);
   if (rc) return rc;
+  g.a16 = true;
+  if (l->t.w16) {
+    g.w16 = l->t.w16;
+    g.tmap_b = l->t.map16;
+  }
   const GbTcPlan plan = gb_tc_gemm_plan(g, 148);
   if (plan.part_floats > l->mm_part_floats) {
     // the first call (or a larger T) grows the split-K scratch; the device
@@ -1189,6 +1251,32 @@ int gb_linear_matmul_f16(gb_linear *l, void *stream, const uint16_t *x, int T, f
   g.part = l->mm_part;
   g.part_floats = l->mm_part_floats;
   return gb_tc_gemm_launch(g, (cudaStream_t)stream);
+}
+
+int gb_linear_cache_f16_weights(gb_linear *l, size_t *bytes) {
+  gb_clear_error();
+  if (!l) return gb_fail(GB_ERR_INVALID, "model: linear: null linear");
+  GbTcGemm g;
+  g.w = l->t.w;
+  g.type_a = g.type_b = l->t.type_a;
+  g.rows = l->t.rows;
+  g.ntiles = l->t.ntiles;
+  g.nsb = l->t.nsb;
+  g.epi = GB_EPI_PLAIN;
+  const size_t n = gb_tc_f16_rows(g) * (size_t)g.nsb * 256;
+  if (bytes) *bytes = n * sizeof(__half);
+  if (l->t.w16) return GB_OK;
+  GB_CUDA(cudaSetDevice(l->device), "model: linear: binary16 weights");
+  __half *w16 = nullptr;
+  GB_CUDA(cudaMalloc(&w16, n * sizeof(__half)), "model: linear: binary16 weights");
+  int rc = gb_tc_f16_weights_launch(g, w16, &l->t.map16, nullptr);
+  if (!rc && cudaDeviceSynchronize() != cudaSuccess) rc = gb_fail(GB_ERR_CUDA, "model: linear: binary16 weights");
+  if (rc) {
+    cudaFree(w16);
+    return rc;
+  }
+  l->t.w16 = w16;
+  return GB_OK;
 }
 
 }  // extern "C"
@@ -1240,7 +1328,7 @@ int ealloc(gb_engine *e, T **p, size_t n, const char *what) {
   return GB_OK;
 }
 
-int engine_forward(gb_engine *e, int n) {
+int engine_forward(gb_engine *e, int n, int max_len) {
   gb_model *m = e->m;
   const gb_config &c = m->c;
   cudaStream_t st = m->st;
@@ -1250,9 +1338,11 @@ int engine_forward(gb_engine *e, int n) {
   int rc = gb_embed_rows_launch(m->embd_type, m->embd.w, m->embd_nsb, c.dim, tok, n, c.vocab, m->pf_x, nullptr, 0,
                                 c.max_len, m->err, st);
   if (rc) return rc;
-  // paged attention splits: about two CTAs per SM, within the scratch
+  // paged attention splits: about two CTAs per SM, within the scratch, and
+  // no more than give each split's warps one 32-position chunk each of the
+  // longest sequence
   long long S = (2LL * m->sms + (long long)nkv * n - 1) / ((long long)nkv * n);
-  S = std::min<long long>(S, std::max(1, e->max_pages * e->page_size / 32));
+  S = std::min<long long>(S, std::max(1, (max_len + 32 * 8 - 1) / (32 * 8)));
   S = std::min<long long>(S, 32);
   S = std::min<long long>(S, (long long)(e->part_floats / gb_paged_part_floats(n, nkv, 1, G, hd)));
   S = std::max<long long>(S, 1);
@@ -1401,8 +1491,10 @@ int gb_engine_step(gb_engine *e, int n, const int32_t *seq_ids, const int32_t *t
                    e->free_pages.size());
   int32_t *h = e->h_in;
   const int B = e->max_batch;
+  int max_len = 0;
   for (int t = 0; t < n; t++) {
     gb_engine::Seq &q = e->seqs[(size_t)seq_ids[t]];
+    max_len = std::max(max_len, q.len + 1);
     if ((int)q.pages.size() <= q.len / e->page_size) {  // its next position starts a page
       q.pages.push_back(e->free_pages.back());
       e->free_pages.pop_back();
@@ -1415,7 +1507,7 @@ int gb_engine_step(gb_engine *e, int n, const int32_t *seq_ids, const int32_t *t
   }
   GB_CUDA(cudaMemcpyAsync(e->d_in, h, sizeof(int32_t) * (size_t)B * (3 + e->max_pages), cudaMemcpyHostToDevice, m->st),
           "engine: step inputs");
-  int rc = engine_forward(e, n);
+  int rc = engine_forward(e, n, max_len);
   if (!rc && host_logits)
     rc = cudaMemcpyAsync(host_logits, e->logits, sizeof(float) * (size_t)n * m->c.vocab, cudaMemcpyDeviceToHost,
                          m->st) == cudaSuccess
@@ -1616,6 +1708,7 @@ int gb_tp_unique_id(uint8_t out[128]) {
 static void free_linear(gb_linear *l) {
   if (!l) return;
   if (l->t.w) cudaFree(l->t.w);
+  if (l->t.w16) cudaFree(l->t.w16);
   if (l->part) cudaFree(l->part);
   if (l->tile_counter) cudaFree(l->tile_counter);
   if (l->mm_part) cudaFree(l->mm_part);

@@ -127,17 +127,17 @@ __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a)
       for (int d = 0; d < kPDL; d++) acc[g][d] *= alpha;
       s[g] = pe;
     }
-    // P V: lane holds dimensions lane + 32 i
+    // P V: lane holds dimensions lane + 32 i; position j's V row sits where
+    // lane j's K row does (the pools share one layout), so the V loads of the
+    // 32 positions do not wait on one another
+    const unsigned long long krow_u = krow;
+#pragma unroll 8
     for (int j = 0; j < 32; j++) {
-      const int pj = ch * 32 + j;
-      if (pj >= L) break;
-      const int lp = pj / a.page_size, off = pj % a.page_size;
-      int phys = a.block_table[(size_t)b * a.max_pages + lp];
-      phys = (phys < 0 || phys >= a.n_pages) ? 0 : phys;
-      const size_t vrow = (((size_t)phys * a.n_kv + h) * a.page_size + off) * hd;
+      const bool pin = ch * 32 + j < L;
+      const size_t vrow = (size_t)__shfl_sync(0xffffffffu, krow_u, j);
       float vv[kPDL];
 #pragma unroll
-      for (int d = 0; d < kPDL; d++) vv[d] = d < DL ? ld_kv<F16>(a.v_pool, vrow + lane + 32 * d) : 0.f;
+      for (int d = 0; d < kPDL; d++) vv[d] = pin && d < DL ? ld_kv<F16>(a.v_pool, vrow + lane + 32 * d) : 0.f;
 #pragma unroll
       for (int g = 0; g < kPMaxG; g++) {
         if (g >= G) break;
@@ -161,6 +161,21 @@ __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a)
   }
   __syncthreads();
   float *dst = a.part + (((size_t)b * a.n_kv + h) * a.S + sp) * G * (hd + 2);
+  if (a.S == 1) {  // one split: its merge is the output (as the split merge below gives it)
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+      const int g = i / hd, d = i % hd;
+      float M = -INFINITY;
+      for (int w = 0; w < kPW; w++) M = fmaxf(M, wm[w][g]);
+      float Lsum = 0.f, A = 0.f;
+      for (int w = 0; w < kPW; w++) {
+        const float f = wm[w][g] == -INFINITY ? 0.f : expf(wm[w][g] - M);
+        Lsum += wl[w][g] * f;
+        A += wacc[w][g][d] * f;
+      }
+      a.out[((size_t)b * a.n_heads + (size_t)h * G + g) * hd + d] = Lsum > 0.f ? A / Lsum : 0.f;
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
     const int g = i / hd, d = i % hd;
     float M = -INFINITY;
@@ -213,6 +228,7 @@ __global__ void rope_kv_paged_kernel(const float *qkv, int q_rows, int kv_rows, 
                                      unsigned *err) {
   const int t = blockIdx.x, p = pos[t];
   const int n_kv = kv_rows / hd;
+  const int i = blockIdx.y * blockDim.x + threadIdx.x;  // this thread's item
   const bool ok = p >= 0 && p < max_len && p / page_size < max_pages;
   int page = ok ? table[(size_t)t * max_pages + p / page_size] : -1;
   if (!ok || page < 0 || page >= n_pages) {
@@ -223,7 +239,7 @@ __global__ void rope_kv_paged_kernel(const float *qkv, int q_rows, int kv_rows, 
   const float *row = qkv + (size_t)t * (q_rows + 2 * kv_rows);
   const double *cs = rope_cs + (size_t)p * hd;
   const int pairs = (q_rows + kv_rows) / 2;
-  for (int i = threadIdx.x; i < pairs + kv_rows; i += blockDim.x) {
+  if (i < pairs + kv_rows) {
     if (i < pairs) {
       const int r = 2 * i, rr = r < q_rows ? r : r - q_rows, jj = (rr % hd) >> 1;
       const double c = cs[2 * jj], sn = cs[2 * jj + 1], x0 = row[r], x1 = row[r + 1];
@@ -251,17 +267,35 @@ __global__ void f32_to_f16_kernel(const float *x, __half *y, size_t n) {
 }
 
 // First maximum of each row (model.Argmax's rule; NaN never wins).
+// Order key of element i with value v: larger value first, then lower index;
+// 0 for NaN (never wins) and the same key for +0 and -0.
+GB_DEV unsigned long long argmax_key(float v, int i) {
+  if (v != v) return 0ull;
+  uint32_t b = __float_as_uint(v);
+  if ((b << 1) == 0u) b = 0u;
+  const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)k << 32) | (0xFFFFFFFFu - (uint32_t)i);
+}
+
 __global__ void argmax_rows_kernel(const float *x, int n, int32_t *out) {
   const float *row = x + (size_t)blockIdx.x * n;
   unsigned long long best = 0ull;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = row[i];
-    if (v != v) continue;
-    uint32_t b = __float_as_uint(v);
-    if ((b << 1) == 0u) b = 0u;
-    const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    const unsigned long long key = ((unsigned long long)k << 32) | (0xFFFFFFFFu - (uint32_t)i);
-    best = key > best ? key : best;
+  if ((n & 3) == 0 && ((uintptr_t)row & 15) == 0) {  // four elements a load, eight loads in flight
+    const float4 *r4 = (const float4 *)row;
+    const int n4 = n >> 2;
+#pragma unroll 8
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+      const float4 v = r4[i];
+      const unsigned long long k0 = argmax_key(v.x, 4 * i), k1 = argmax_key(v.y, 4 * i + 1);
+      const unsigned long long k2 = argmax_key(v.z, 4 * i + 2), k3 = argmax_key(v.w, 4 * i + 3);
+      const unsigned long long a = k0 > k1 ? k0 : k1, c = k2 > k3 ? k2 : k3, m = a > c ? a : c;
+      best = m > best ? m : best;
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long key = argmax_key(row[i], i);
+      best = key > best ? key : best;
+    }
   }
   __shared__ unsigned long long red[32];
   for (int o = 16; o > 0; o >>= 1) {
@@ -324,7 +358,8 @@ int gb_rope_kv_paged_launch(const float *qkv, int T, int q_rows, int kv_rows, in
                             int max_len, float *q_out, uint16_t *kpool, uint16_t *vpool, unsigned *err,
                             cudaStream_t st) {
   if (T <= 0) return GB_OK;
-  rope_kv_paged_kernel<<<T, 256, 0, st>>>(qkv, q_rows, kv_rows, hd, rope_cs, pos, table, max_pages, page_size, n_pages,
+  const unsigned items = (unsigned)((q_rows + kv_rows) / 2 + kv_rows);
+  rope_kv_paged_kernel<<<dim3((unsigned)T, (items + 255) / 256), 256, 0, st>>>(qkv, q_rows, kv_rows, hd, rope_cs, pos, table, max_pages, page_size, n_pages,
                                           max_len, q_out, kpool, vpool, err);
   GB_CUDA(cudaGetLastError(), "engine: RoPE/KV append");
   return GB_OK;

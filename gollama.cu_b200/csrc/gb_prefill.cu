@@ -262,8 +262,13 @@ struct TcArgs {
   int rstage;             // raw ring slots (one raw unit each)
   int spr;                // K-stages per raw unit (4: quantized types, 1: float types)
   int raw_tile;           // raw bytes per tile per raw unit (max over the two types)
+  int npad;               // gemm_swap_kernel: token rows padded to 16 (the MMA's N)
   unsigned *err;
 };
+// With F16W the weights come from the model's binary16 weight copy (the
+// values dequant_chunk produces, row-major, gate/up rows grouped 64 + 64 per
+// CTA) through a second tensor map, one TMA box per K-stage: no raw ring and
+// no decode, the dequant warps only run the epilogue.
 
 GB_DEV const uint8_t *sb_block(const TcArgs &g, int tile, int sb, int up, int &typ) {
   if (g.pair) {
@@ -285,9 +290,10 @@ GB_DEV const uint8_t *sb_block(const TcArgs &g, int tile, int sb, int up, int &t
 // scheduler has four decoding warps to interleave; then the producer warp,
 // then the MMA warp.
 constexpr int kDQ = 16;
-template <int BN, int EPI>
+template <int BN, int EPI, bool F16W>
 __global__ void __launch_bounds__((kDQ + 3) * 32, 1)
-    gemm_tc_kernel(const TcArgs g, const __grid_constant__ CUtensorMap tmap_a) {
+    gemm_tc_kernel(const TcArgs g, const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b) {
   constexpr int NDQ = kDQ, NT = BN / 32, CPT = 8 * NT / NDQ;
   static_assert(NDQ % NT == 0 && CPT >= 1, "dequant split");
   constexpr int BBytes = BN * 128;
@@ -313,7 +319,7 @@ __global__ void __launch_bounds__((kDQ + 3) * 32, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; s++) {
       gb_mbar_init(&afull[s], 1);
-      gb_mbar_init(&bfull[s], NDQ);
+      gb_mbar_init(&bfull[s], F16W ? 1 : NDQ);
       gb_mbar_init(&empty[s], 1);
     }
     for (int r = 0; r < RS; r++) {
@@ -333,7 +339,25 @@ __global__ void __launch_bounds__((kDQ + 3) * 32, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (warp == NDQ + 2) {
+  if (warp == NDQ + 2 && F16W) {
+    // weight producer of the binary16 copy: per K-stage the CTA's BN weight
+    // rows by TMA (128-byte swizzle, the layout the MMA reads)
+    if (lane == 0) {
+      int b_issued = 0;
+      for (int kl = 0; kl < nkl; kl++) {
+        const int s = kl % NS;
+        if (kl >= NS && !gb_mbar_wait(&empty[s], ((kl / NS) - 1) & 1)) {
+          bad = 1;
+          if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
+          break;
+        }
+        gb_mbar_expect_tx(&bfull[s], (uint32_t)BBytes);
+        tma_load_2d(B0 + (size_t)s * BBytes, &tmap_b, (k0 + kl) * kBK, (int)blockIdx.x * BN, &bfull[s]);
+        b_issued = kl + 1;
+      }
+      for (int j = b_issued > NS ? b_issued - NS : 0; j < b_issued; j++) (void)gb_mbar_wait(&bfull[j % NS], (j / NS) & 1);
+    }
+  } else if (warp == NDQ + 2) {
     // raw producer: each raw unit (the tiles' weight bytes, one bulk copy per
     // tile) as soon as its slot is free, running ahead of the activation ring
     if (lane == 0) {
@@ -419,7 +443,7 @@ __global__ void __launch_bounds__((kDQ + 3) * 32, 1)
     const int up = g.pair && j >= 2, tile = tile0 + (g.pair ? (j & 1) : j);
     const bool valid = tile < g.ntiles;
     const int rB = j * 32 + lane, sw = lane & 7;  // B row; its 128-byte swizzle phase
-    for (int kl = 0; kl < nkl; kl++) {
+    for (int kl = 0; kl < (F16W ? 0 : nkl); kl++) {
       const int k = k0 + kl, s = kl % NS, r = kl / SPR, rs = r % RS;
       // the raw unit has landed; the B slot's previous MMAs are done
       if ((kl % SPR == 0 && !gb_mbar_wait(&rfull[rs], (r / RS) & 1)) ||
@@ -456,10 +480,12 @@ __global__ void __launch_bounds__((kDQ + 3) * 32, 1)
       float *pt = g.part + (((size_t)blockIdx.y * gridDim.x + blockIdx.x) * g.splits + blockIdx.z) * (size_t)(MT * kBM) * BN;
       for (int mt = 0; mt < MT; mt++) {
         const int rl = mt * kBM + quarter * 32 + lane;
+        if (m0 + mt * kBM + quarter * 32 >= g.T) break;  // the reduce reads token rows < T only
         const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mt * BN);
         for (int cc = cq * (BN / 4); cc < (cq + 1) * (BN / 4); cc += 16) {
           float v[16];
           tmem_ld16(trow + cc, v);
+          if (m0 + rl >= g.T) continue;
           float *dst = pt + (size_t)rl * BN + cc;
 #pragma unroll
           for (int i = 0; i < 16; i += 4) *(float4 *)(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
@@ -526,6 +552,180 @@ __global__ void __launch_bounds__((kDQ + 3) * 32, 1)
   }
 }
 
+// Few token rows (T <= 128) through the binary16 weight copy, with the
+// operands' roles swapped so that no MMA row is wasted: the CTA's 128 weight
+// rows are the MMA's M (TMEM lanes), the T token rows padded to 16 its N
+// (TMEM columns), and a stage moves 16 KB of weights but only 2*NP*64 bytes
+// of activations (16-row TMA boxes), so the ring holds twice the stages.
+// Warps 0-3 run the epilogue (warp q reads TMEM lanes 32q..32q+31: weight
+// rows), warp 4 is the TMA producer (both operands on one mbarrier), warp 5
+// allocates TMEM and issues the MMAs. Gate/up pairs: lanes 0-63 hold the
+// gate rows, 64-127 the up rows of the same 64 outputs; warps 2-3 hand the
+// up values to warps 0-1 through shared memory (an mbarrier, bounded wait).
+constexpr int kMaxStagesSW = 16;
+constexpr int kSwapThreads = 6 * 32;
+template <int EPI>
+__global__ void __launch_bounds__(kSwapThreads) gemm_swap_kernel(const TcArgs g, const __grid_constant__ CUtensorMap tmap_a16,
+                                                                 const __grid_constant__ CUtensorMap tmap_w) {
+  constexpr int WB = 128 * 128;  // weight bytes of a stage
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full[kMaxStagesSW], empty[kMaxStagesSW], accf, xch;
+  __shared__ uint32_t tmem_base;
+  __shared__ int bad;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NS = g.nstage, NP = g.npad, AB = NP * 128;  // NP: a power of two, 16..128
+  const uint32_t ncols = NP < 32 ? 32u : (uint32_t)NP;
+  const int nu = g.nsb * 4, u0 = nu * (int)blockIdx.z / g.splits, u1 = nu * ((int)blockIdx.z + 1) / g.splits;
+  const int k0 = u0, nkl = u1 - u0;
+  uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t *W0 = base, *A0 = base + (size_t)NS * WB;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; s++) {
+      gb_mbar_init(&full[s], 1);
+      gb_mbar_init(&empty[s], 1);
+    }
+    gb_mbar_init(&accf, 1);
+    gb_mbar_init(&xch, 2);
+    bad = 0;
+    gb_mbar_fence_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(&tmem_base, ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  if (warp == 4) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kl = 0; kl < nkl; kl++) {
+        const int s = kl % NS, k = k0 + kl;
+        if (kl >= NS && !gb_mbar_wait(&empty[s], ((kl / NS) - 1) & 1)) {
+          bad = 1;
+          if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
+          break;
+        }
+        gb_mbar_expect_tx(&full[s], (uint32_t)(WB + AB));
+        tma_load_2d(W0 + (size_t)s * WB, &tmap_w, k * kBK, (int)blockIdx.x * 128, &full[s]);
+        for (int j = 0; j < NP / 16; j++) tma_load_2d(A0 + (size_t)s * AB + j * 2048, &tmap_a16, k * kBK, 16 * j, &full[s]);
+        issued = kl + 1;
+      }
+      for (int j = issued > NS ? issued - NS : 0; j < issued; j++) (void)gb_mbar_wait(&full[j % NS], (j / NS) & 1);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(128, NP);
+      for (int kl = 0; kl < nkl; kl++) {
+        const int s = kl % NS;
+        if (!gb_mbar_wait(&full[s], (kl / NS) & 1)) {
+          bad = 1;
+          if (g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = sdesc_sw128(gb_smem_u32(W0 + (size_t)s * WB));
+        const uint64_t bd = sdesc_sw128(gb_smem_u32(A0 + (size_t)s * AB));
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; kk++) mma_f16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kl | kk) != 0);
+        mma_commit(&empty[s]);
+      }
+      mma_commit(&accf);
+    }
+  } else {
+    // epilogue: thread = weight row 32*warp + lane, TMEM columns = tokens
+    const int row = warp * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    const bool ok = gb_mbar_wait(&accf, 0);
+    tc_fence_after();
+    if (!ok) {
+      if (lane == 0 && g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
+    } else if (!bad && g.splits > 1) {
+      // this split's fp32 partial: [token][128 columns], the layout splitk_reduce reads
+      float *pt = g.part + ((size_t)blockIdx.x * g.splits + blockIdx.z) * (size_t)(kBM * 128);
+      for (int c = 0; c < NP; c += 16) {
+        float v[16];
+        tmem_ld16(trow + (uint32_t)c, v);
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+          if (c + i < g.T) pt[(size_t)(c + i) * 128 + row] = v[i];
+      }
+    } else if (!bad) {
+      if constexpr (EPI == GB_EPI_SWIGLU) {
+        float *xs = (float *)base;  // [token][64] up values (the ring is idle now)
+        const int n = (int)blockIdx.x * 64 + (row & 63);
+        if (warp >= 2) {
+          for (int c = 0; c < NP; c += 16) {
+            float v[16];
+            tmem_ld16(trow + (uint32_t)c, v);
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+              if (c + i < g.T) xs[(c + i) * 64 + row - 64] = v[i];
+          }
+          __syncwarp();
+          if (lane == 0) gb_mbar_arrive(&xch);
+        } else if (!gb_mbar_wait(&xch, 0)) {
+          if (lane == 0 && g.err) atomicOr(g.err, GB_DEVERR_TIMEOUT);
+        } else {
+          for (int c = 0; c < NP; c += 16) {
+            float gv[16];
+            tmem_ld16(trow + (uint32_t)c, gv);
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              const int t = c + i;
+              if (t < g.T && n < g.rows) {
+                const float u = xs[t * 64 + row];
+                g.act[(size_t)t * g.ld_act + n] = __float2half_rn(gv[i] / (1.f + (float)exp(-(double)gv[i])) * u);  // cpu.SiluMul
+              }
+            }
+          }
+        }
+      } else {
+        const int n = (int)blockIdx.x * 128 + row;
+        for (int c = 0; c < NP; c += 16) {
+          float v[16];
+          tmem_ld16(trow + (uint32_t)c, v);
+          if (n >= g.rows) continue;
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const int t = c + i;
+            if (t >= g.T) break;
+            float *dst = g.y + (size_t)t * g.ldy + n;
+            *dst = EPI == GB_EPI_RESID ? *dst + v[i] : v[i];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols);
+  }
+}
+
+// The binary16 weight copy of one tiled matrix, row-major with K contiguous:
+// element (row, col) is what dequant_chunk gives the GEMM for it, so a GEMM
+// on the copy multiplies the same binary16 numbers. Rows are grouped as the
+// GEMM's CTAs take them: 128 consecutive rows per CTA, for gate/up pairs 64
+// gate rows then the 64 matching up rows. One CTA per (32-row tile, super-
+// block[, gate/up]); thread = (K-stage of 64 columns, row).
+__global__ void f16_weights_kernel(const TcArgs g, __half *w16) {
+  const int t = blockIdx.x, sb = blockIdx.y, up = blockIdx.z, kc = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int typ = -1;
+  const uint8_t *raw = nullptr;
+  if (t < g.ntiles) {
+    const uint8_t *blk = sb_block(g, t, sb, up, typ);
+    raw = blk + (raw_spr(typ) == 1 ? (size_t)kc * raw_unit_bytes(typ) : 0);
+  }
+  const int row = g.pair ? (t >> 1) * 128 + ((t & 1) + 2 * up) * 32 + lane : t * 32 + lane;
+  __half *dst = w16 + (size_t)row * ((size_t)g.nsb * 256) + (size_t)sb * 256 + kc * 64;
+#pragma unroll
+  for (int c = 0; c < 8; c++) *(uint4 *)(dst + c * 8) = dequant_chunk(typ, kc, raw, lane, c);
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -558,12 +758,30 @@ __global__ void embed_rows_kernel(int typ, const uint8_t *tiled, int nsb, int di
 
 // RMSNorm of each row (cpu.RMSNorm, backend/cpu/cpu.go:17: float64 sum of
 // squares, float32 products) to binary16: the GEMM's A operand.
+// Rows whose length is a multiple of 4 (and at most kNormV * 4 * blockDim)
+// keep their elements in registers between the two passes.
+constexpr int kNormV = 4;
 __global__ void rmsnorm_rows_f16_kernel(const float *x, const float *w, int n, float eps, __half *out) {
   const float *xr = x + (size_t)blockIdx.x * n;
   __half *o = out + (size_t)blockIdx.x * n;
   __shared__ double red[32];
   double ss = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ss += (double)xr[i] * (double)xr[i];
+  const bool vec = (n & 3) == 0 && n <= kNormV * 4 * (int)blockDim.x && ((uintptr_t)xr & 15) == 0 &&
+                   ((uintptr_t)w & 15) == 0 && ((uintptr_t)o & 7) == 0;
+  float4 xv[kNormV];
+  if (vec) {
+#pragma unroll
+    for (int j = 0; j < kNormV; j++) {
+      const int i4 = threadIdx.x + j * blockDim.x;
+      xv[j] = i4 < (n >> 2) ? ((const float4 *)xr)[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < kNormV; j++)
+      ss += (double)xv[j].x * (double)xv[j].x + (double)xv[j].y * (double)xv[j].y +
+            (double)xv[j].z * (double)xv[j].z + (double)xv[j].w * (double)xv[j].w;
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += (double)xr[i] * (double)xr[i];
+  }
   for (int k = 16; k > 0; k >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, k);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
@@ -574,7 +792,22 @@ __global__ void rmsnorm_rows_f16_kernel(const float *x, const float *w, int n, f
   }
   __syncthreads();
   const float inv = (float)(1.0 / sqrt(red[0] / (double)n + (double)eps));
-  for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = __float2half_rn(__fmul_rn(__fmul_rn(xr[i], inv), w[i]));
+  if (vec) {
+#pragma unroll
+    for (int j = 0; j < kNormV; j++) {
+      const int i4 = threadIdx.x + j * blockDim.x;
+      if (i4 >= (n >> 2)) break;
+      const float4 wv = ((const float4 *)w)[i4];
+      __half2 h0 = __floats2half2_rn(__fmul_rn(__fmul_rn(xv[j].x, inv), wv.x), __fmul_rn(__fmul_rn(xv[j].y, inv), wv.y));
+      __half2 h1 = __floats2half2_rn(__fmul_rn(__fmul_rn(xv[j].z, inv), wv.z), __fmul_rn(__fmul_rn(xv[j].w, inv), wv.w));
+      uint2 u;
+      u.x = *(uint32_t *)&h0;
+      u.y = *(uint32_t *)&h1;
+      ((uint2 *)o)[i4] = u;
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = __float2half_rn(__fmul_rn(__fmul_rn(xr[i], inv), w[i]));
+  }
 }
 
 // RoPE of q and k rows of every token (cpu.RoPE's float64 rotation with the
@@ -586,7 +819,8 @@ __global__ void rope_kv_kernel(const float *qkv, int ldq, int q_rows, int kv_row
   const float *row = qkv + (size_t)t * ldq;
   const double *cs_row = rope_cs + (size_t)pos * (hd / 2) * 2;
   const int pairs = (q_rows + kv_rows) / 2;
-  for (int i = threadIdx.x; i < pairs + kv_rows; i += blockDim.x) {
+  const int i = blockIdx.y * blockDim.x + threadIdx.x;  // this thread's item
+  if (i < pairs + kv_rows) {
     if (i < pairs) {
       const int r = 2 * i, rr = r < q_rows ? r : r - q_rows, jj = (rr % hd) >> 1;
       const double c = cs_row[2 * jj], s = cs_row[2 * jj + 1];
@@ -951,7 +1185,7 @@ __global__ void splitk_reduce_kernel(const float *part, int S, int MT, int BN, i
 
 // ---- launchers ------------------------------------------------------------------
 
-int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map) {
+int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map, int box_rows) {
   static EncodeTiledFn encode = nullptr;
   if (!encode) {
     void *fn = nullptr;
@@ -964,7 +1198,7 @@ int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map) {
   if (cols % kBK || ((uintptr_t)base & 15)) return gb_fail(GB_ERR_INVALID, "gpu: prefill: bad activation layout");
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -979,6 +1213,17 @@ int gb_tmap_f16_rows(const void *base, int rows, int cols, CUtensorMap *map) {
 GbTcPlan gb_tc_gemm_plan(const GbTcGemm &a, int sms) {
   GbTcPlan p;
   const bool pair = a.epi == GB_EPI_SWIGLU;
+  if (a.w16 && a.a16 && a.T <= kBM) {
+    // gemm_swap_kernel: K splits for about two CTAs per SM, each split at
+    // least four K-stages long
+    const int ntn = (a.rows + (pair ? 63 : 127)) / (pair ? 64 : 128), nu = a.nsb * 4;
+    int S = (2 * sms) / std::max(1, ntn);
+    S = std::max(1, std::min(S, nu / 4));
+    p.swap = true;
+    p.splits = S;
+    p.part_floats = S > 1 ? (size_t)ntn * S * kBM * 128 : 0;
+    return p;
+  }
   const int BN = 128, mt_max = 4, oc = pair ? 64 : 128;
   const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + oc - 1) / oc;
   int mt = 1;
@@ -1029,18 +1274,43 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   g.splits = plan.splits;
   g.part = a.part;
   g.mt = mt;
+  const bool f16w = a.w16 != nullptr;
+  if (plan.swap) {
+    int np = 16;
+    while (np < a.T) np *= 2;
+    g.npad = np;
+    const int nctas = ntn * g.splits;
+    const int resident = std::max(1, std::min(4, (nctas + 147) / 148));  // CTAs an SM holds at once
+    const size_t per_cta = (size_t)233472 / resident - 2048 - 1024;  // minus reserved/static and alignment slack
+    const size_t stage = (size_t)128 * 128 + (size_t)np * 128;
+    const int ns = (int)std::min<size_t>(kMaxStagesSW, per_cta / stage);
+    if (ns < 2) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: stages do not fit");
+    g.nstage = ns;
+    const size_t smem = (size_t)ns * stage + 1024;
+    void (*kern)(TcArgs, CUtensorMap, CUtensorMap) =
+        a.epi == GB_EPI_PLAIN ? gemm_swap_kernel<GB_EPI_PLAIN>
+                              : a.epi == GB_EPI_RESID ? gemm_swap_kernel<GB_EPI_RESID> : gemm_swap_kernel<GB_EPI_SWIGLU>;
+    GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "gpu: GEMM");
+    kern<<<dim3((unsigned)ntn, 1, (unsigned)g.splits), kSwapThreads, smem, st>>>(g, a.tmap_a16, a.tmap_b);
+    GB_CUDA(cudaGetLastError(), "gpu: GEMM");
+  } else {
   const size_t ab = (size_t)kABytes * mt + (size_t)BN * 128, rb = (size_t)NT * g.raw_tile;
   const size_t budget = 227 * 1024 - 1024 - 512;  // dynamic smem minus the alignment slack and statics
   // (A/B slots, raw slots) in order of preference: two raw units in flight
   // keep the copy of the next super-block under the decode of this one
   static const int pref[9][2] = {{4, 3}, {4, 2}, {3, 3}, {3, 2}, {2, 3}, {2, 2}, {4, 1}, {3, 1}, {2, 1}};
   int ns = 0, rsn = 0;
-  for (const auto &p : pref)
-    if (p[0] * ab + p[1] * rb <= budget) {
-      ns = p[0];
-      rsn = p[1];
-      break;
-    }
+  if (f16w) {  // binary16 weights by TMA: every byte of shared memory to the A/B ring
+    ns = (int)std::min<size_t>(kMaxStagesTC, budget / ab);
+    if (ns < 2) ns = 0;
+  } else {
+    for (const auto &p : pref)
+      if (p[0] * ab + p[1] * rb <= budget) {
+        ns = p[0];
+        rsn = p[1];
+        break;
+      }
+  }
   if (!ns) return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: stages do not fit");
   g.nstage = ns;
   g.rstage = rsn;
@@ -1048,16 +1318,23 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   const size_t smem = (size_t)ns * stage + (size_t)rsn * rb + 1024;
   const dim3 grid((unsigned)ntn, (unsigned)((mtiles + mt - 1) / mt), (unsigned)g.splits);
   const dim3 block((unsigned)((kDQ + 3) * 32));
-  void (*kern)(TcArgs, CUtensorMap) = nullptr;
+  void (*kern)(TcArgs, CUtensorMap, CUtensorMap) = nullptr;
   switch (a.epi) {
-    case GB_EPI_PLAIN: kern = gemm_tc_kernel<128, GB_EPI_PLAIN>; break;
-    case GB_EPI_RESID: kern = gemm_tc_kernel<128, GB_EPI_RESID>; break;
-    case GB_EPI_SWIGLU: kern = gemm_tc_kernel<128, GB_EPI_SWIGLU>; break;
+    case GB_EPI_PLAIN:
+      kern = f16w ? gemm_tc_kernel<128, GB_EPI_PLAIN, true> : gemm_tc_kernel<128, GB_EPI_PLAIN, false>;
+      break;
+    case GB_EPI_RESID:
+      kern = f16w ? gemm_tc_kernel<128, GB_EPI_RESID, true> : gemm_tc_kernel<128, GB_EPI_RESID, false>;
+      break;
+    case GB_EPI_SWIGLU:
+      kern = f16w ? gemm_tc_kernel<128, GB_EPI_SWIGLU, true> : gemm_tc_kernel<128, GB_EPI_SWIGLU, false>;
+      break;
     default: return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: epilogue %d", a.epi);
   }
   GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "gpu: prefill GEMM");
-  kern<<<grid, block, smem, st>>>(g, a.tmap_a);
+  kern<<<grid, block, smem, st>>>(g, a.tmap_a, f16w ? a.tmap_b : a.tmap_a);
   GB_CUDA(cudaGetLastError(), "gpu: prefill GEMM");
+  }
   if (g.splits > 1) {
     const dim3 blocks((unsigned)((a.rows + 4 * 128 - 1) / (4 * 128)), (unsigned)a.T);
     switch (a.epi) {
@@ -1078,6 +1355,32 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   return GB_OK;
 }
 
+// Rows of the binary16 weight copy of a GEMM's matrix: 128 per CTA column.
+size_t gb_tc_f16_rows(const GbTcGemm &a) {
+  const bool pair = a.epi == GB_EPI_SWIGLU;
+  return (size_t)((a.rows + (pair ? 63 : 127)) / (pair ? 64 : 128)) * 128;
+}
+
+int gb_tc_f16_weights_launch(const GbTcGemm &a, __half *w16, CUtensorMap *map, cudaStream_t st) {
+  if (a.nsb <= 0 || !gb_tiled_type(a.type_a) || !gb_tiled_type(a.type_b) || ((uintptr_t)w16 & 15))
+    return gb_fail(GB_ERR_UNSUPPORTED, "gpu: binary16 weights: type %d/%d, %d super-blocks", a.type_a, a.type_b,
+                   a.nsb);
+  TcArgs g{};
+  g.w = a.w;
+  g.type_a = a.type_a;
+  g.type_b = a.type_b;
+  g.split_tile = a.split_tile;
+  g.rows = a.rows;
+  g.ntiles = a.ntiles;
+  g.nsb = a.nsb;
+  g.pair = a.epi == GB_EPI_SWIGLU;
+  const size_t rows16 = gb_tc_f16_rows(a);
+  const dim3 grid((unsigned)(rows16 / (g.pair ? 64 : 32)), (unsigned)a.nsb, g.pair ? 2u : 1u);  // (tile, sb, up)
+  f16_weights_kernel<<<grid, 128, 0, st>>>(g, w16);
+  GB_CUDA(cudaGetLastError(), "gpu: binary16 weights");
+  return gb_tmap_f16_rows(w16, (int)rows16, a.nsb * 256, map);
+}
+
 int gb_embed_rows_launch(int typ, const uint8_t *tiled, int nsb, int dim, const int32_t *tokens, int T, int vocab,
                          float *x, int32_t *fed, int pos0, int max_len, unsigned *err, cudaStream_t st) {
   embed_rows_kernel<<<dim3((unsigned)(dim / 256), (unsigned)T), 256, 0, st>>>(typ, tiled, nsb, dim, tokens, T, vocab,
@@ -1088,14 +1391,15 @@ int gb_embed_rows_launch(int typ, const uint8_t *tiled, int nsb, int dim, const 
 
 int gb_rmsnorm_rows_f16_launch(const float *x, const float *w, int rows, int n, float eps, __half *out,
                                cudaStream_t st) {
-  rmsnorm_rows_f16_kernel<<<rows, 256, 0, st>>>(x, w, n, eps, out);
+  rmsnorm_rows_f16_kernel<<<rows, 512, 0, st>>>(x, w, n, eps, out);
   GB_CUDA(cudaGetLastError(), "gpu: prefill RMSNorm");
   return GB_OK;
 }
 
 int gb_rope_kv_launch(const float *qkv, int T, int q_rows, int kv_rows, int hd, const double *rope_cs, int pos0,
                       int max_len, int kv_f16, float *q_out, void *kcache, void *vcache, cudaStream_t st) {
-  rope_kv_kernel<<<T, 256, 0, st>>>(qkv, q_rows + 2 * kv_rows, q_rows, kv_rows, hd, rope_cs, pos0, max_len, kv_f16,
+  const unsigned items = (unsigned)((q_rows + kv_rows) / 2 + kv_rows);
+  rope_kv_kernel<<<dim3((unsigned)T, (items + 255) / 256), 256, 0, st>>>(qkv, q_rows + 2 * kv_rows, q_rows, kv_rows, hd, rope_cs, pos0, max_len, kv_f16,
                                     q_out, kcache, vcache);
   GB_CUDA(cudaGetLastError(), "gpu: prefill RoPE");
   return GB_OK;

@@ -89,7 +89,8 @@ _SIGS = {
     "gb_gpu_peer_resid": (I, [P, P, I, P, P, P, I, I, P, I, P, C.c_uint, P]), "gb_gpu_sample": (I, [P, P, P, I, P, P, I, U64, P]),
     "gb_gpu_attn_decode_paged": (I, [P, P, P, P, P, I, P, P, I, I, I, I, I, I, I, F, P]),
     "gb_model_set_sampler": (I, [P, P]), "gb_model_prefill": (I, [P, P, I, I, P]),
-    "gb_linear_matmul_f16": (I, [P, P, P, I, P]),
+    "gb_model_cache_f16_weights": (I, [P, C.POINTER(S)]),
+    "gb_linear_matmul_f16": (I, [P, P, P, I, P]), "gb_linear_cache_f16_weights": (I, [P, C.POINTER(S)]),
     "gb_engine_create": (I, [P, I, I, I, C.POINTER(P)]), "gb_engine_add": (I, [P, C.POINTER(I)]),
     "gb_engine_release": (I, [P, I]), "gb_engine_seq_len": (I, [P, I]), "gb_engine_free_pages": (I, [P]),
     "gb_engine_step": (I, [P, I, P, P, P, P]), "gb_engine_free": (I, [P]),
@@ -270,6 +271,13 @@ class Linear:
         """y[T][rows] = x16[T][cols] W^T on the tensor cores (x16 binary16, y float32)."""
         _check(lib().gb_linear_matmul_f16(self.h, _stream(stream), _ptr(x16), T, _ptr(y)))
 
+    def cache_f16_weights(self) -> int:
+        """Keep the binary16 copy of the weights for matmul_f16 (bit-identical
+        results); its device bytes."""
+        n = S(0)
+        _check(lib().gb_linear_cache_f16_weights(self.h, C.byref(n)))
+        return n.value
+
     def weight_bytes(self) -> int:
         s = S()
         _check(lib().gb_linear_info(self.h, None, None, None, C.byref(s)))
@@ -340,6 +348,13 @@ class Model:
             out = self._logits
         _check(lib().gb_model_prefill(self.h, t.ctypes.data, t.size, pos0, out.ctypes.data))
         return out
+
+    def cache_f16_weights(self) -> int:
+        """Keep a binary16 copy of every weight matrix for prefill and the
+        engine (bit-identical results); the device bytes it took."""
+        n = S(0)
+        _check(lib().gb_model_cache_f16_weights(self.h, C.byref(n)))
+        return n.value
 
     def set_sampler(self, params: SampleParams | None) -> None:
         """Token rule of next/generate/decode_async: None = greedy argmax."""

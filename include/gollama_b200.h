@@ -208,6 +208,11 @@ int gb_linear_matvec(gb_linear *l, void *stream, const float *x, float *y);
  * kernel (deterministic); their scratch is allocated by the first call that
  * needs it (after a device synchronisation). */
 int gb_linear_matmul_f16(gb_linear *l, void *stream, const uint16_t *x, int T, float *y);
+/* Added: the binary16 copy of the Linear's weights (the values the matmul
+ * decodes them to; 2 bytes per weight) for gb_linear_matmul_f16 to read by
+ * TMA instead of decoding the quantized tiles each call; bit-identical
+ * results. *bytes (may be NULL) receives its size. */
+int gb_linear_cache_f16_weights(gb_linear *l, size_t *bytes);
 /* Bytes of the tiled weight buffer and the type's algorithmic bytes. */
 int gb_linear_info(const gb_linear *l, int *typ, int *rows, int *cols, size_t *weight_bytes);
 int gb_linear_free(gb_linear *l);
@@ -272,6 +277,15 @@ int gb_model_read_tokens(gb_model *m, int pos0, int n, int32_t *out_tokens);
  * parallelism every rank makes the call with the same tokens, the o and down
  * partials are summed by NCCL all-reduces, and rank 0 receives the logits). */
 int gb_model_prefill(gb_model *m, const int32_t *tokens, int n, int pos0, float *host_logits);
+/* Added: keep a binary16 copy of every weight matrix on the device (the
+ * values the tensor-core GEMMs decode the quantized weights to, so results
+ * are bit-identical) and have gb_model_prefill and gb_engine_step read it by
+ * TMA instead of decoding the quantized tiles each call. Costs 2 bytes per
+ * weight of device memory (about 16 GB for an 8B model); *bytes (may be NULL)
+ * receives the amount this call allocated (0 once the copy exists). Fails with GB_ERR_UNSUPPORTED, leaving the model as it
+ * was, when free device memory is short of it plus 1 GiB. The decode step
+ * (gb_model_forward / next / generate) keeps the quantized weights. */
+int gb_model_cache_f16_weights(gb_model *m, size_t *bytes);
 /* ---- continuous batching (added; the reference's roadmap "Paged KV cache
  * plus continuous batching", ROADMAP.md:197-202) ---------------------------
  * An engine over a loaded model (one GPU) decodes many sequences at once.

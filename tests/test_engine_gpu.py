@@ -126,3 +126,33 @@ def test_engine_page_exhaustion_and_errors(gb, cuda):
     assert e.free_pages() == 0
     e.close()
     m.close()
+
+
+def test_engine_f16_weight_copy(gb, cuda):
+    # the engine's GEMMs through the model's binary16 weight copy (the
+    # few-token kernel: the same binary16 products, float32 sums in another
+    # order): every row within float32 accumulation of the decoding GEMM's
+    cfg = MODELS["q5km"]
+    img = gb.SynthImage(gb.synth_spec(**cfg))
+    rng = np.random.default_rng(9)
+    seqs = [[int(t) for t in rng.integers(0, cfg["vocab"], 12)] for _ in range(5)]
+    outs = []
+    for cached in (False, True):
+        m = gb.Model(img, max_len=96)
+        if cached:
+            m.cache_f16_weights()
+        e = gb.Engine(m, page_size=16, n_pages=64, max_batch=8)
+        ids = [e.add() for _ in seqs]
+        rows = []
+        for p in range(12):
+            logits, nxt = e.step(ids, [s[p] for s in seqs])
+            rows.append((logits.copy(), nxt.copy()))
+        e.close()
+        m.close()
+        outs.append(rows)
+    for (la, na), (lb, nb) in zip(*outs):
+        for j in range(len(seqs)):
+            assert rel_err(lb[j], la[j]) < 1e-3
+            top = np.sort(la[j].astype(np.float64))
+            if top[-1] - top[-2] > 2e-3 * np.abs(la[j]).max():
+                assert na[j] == nb[j]
