@@ -23,6 +23,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <map>
 #include <memory>
 #include <string>
 #include <thread>
@@ -1299,20 +1300,30 @@ struct gb_engine {
     std::vector<int> pages;
   };
   std::vector<Seq> seqs;
-  float *attn32 = nullptr, *logits = nullptr, *part = nullptr;
+  float *logits = nullptr, *part = nullptr;
   size_t part_floats = 0;
   unsigned *counter = nullptr;
   int32_t *d_in = nullptr;   // tokens [B] | pos [B] | lens [B] | table [B][max_pages]
   int32_t *h_in = nullptr;   // pinned copy of d_in
   int32_t *d_next = nullptr;
   std::vector<void *> allocs;
+  // one CUDA graph of the step per (rows, attention splits) met so far
+  std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
 };
 
 namespace {
 
+constexpr size_t kEngineGraphs = 64;  // graphs kept before the cache is emptied
+
+void drop_graphs(gb_engine *e) {
+  for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+  e->graphs.clear();
+}
+
 void free_engine(gb_engine *e) {
   if (!e) return;
   if (e->m && e->m->st) cudaStreamSynchronize(e->m->st);
+  drop_graphs(e);
   for (void *p : e->allocs) cudaFree(p);
   if (e->h_in) cudaFreeHost(e->h_in);
   delete e;
@@ -1328,24 +1339,29 @@ int ealloc(gb_engine *e, T **p, size_t n, const char *what) {
   return GB_OK;
 }
 
-int engine_forward(gb_engine *e, int n, int max_len) {
+// Paged attention splits for n rows whose longest sequence has max_len
+// positions: about two CTAs per SM, within the scratch, and no more than
+// give each split's warps one 32-position chunk each.
+int engine_splits(const gb_engine *e, int n, int max_len) {
+  const gb_model *m = e->m;
+  const int hd = m->c.head_dim, nkv = m->kv_local / hd, G = m->c.heads / m->c.kv_heads;
+  long long S = (2LL * m->sms + (long long)nkv * n - 1) / ((long long)nkv * n);
+  S = std::min<long long>(S, std::max(1, (max_len + 32 * 8 - 1) / (32 * 8)));
+  S = std::min<long long>(S, 32);
+  S = std::min<long long>(S, (long long)(e->part_floats / gb_paged_part_floats(n, nkv, 1, G, hd)));
+  return (int)std::max<long long>(S, 1);
+}
+
+int engine_forward(gb_engine *e, int n, int S) {
   gb_model *m = e->m;
   const gb_config &c = m->c;
   cudaStream_t st = m->st;
-  const int hd = c.head_dim, qkv = m->q_local + 2 * m->kv_local, nkv = m->kv_local / hd, G = c.heads / c.kv_heads;
+  const int hd = c.head_dim, qkv = m->q_local + 2 * m->kv_local, nkv = m->kv_local / hd;
   const int32_t *tok = e->d_in, *pos = e->d_in + e->max_batch, *lens = e->d_in + 2 * e->max_batch,
                 *table = e->d_in + 3 * e->max_batch;
   int rc = gb_embed_rows_launch(m->embd_type, m->embd.w, m->embd_nsb, c.dim, tok, n, c.vocab, m->pf_x, nullptr, 0,
                                 c.max_len, m->err, st);
   if (rc) return rc;
-  // paged attention splits: about two CTAs per SM, within the scratch, and
-  // no more than give each split's warps one 32-position chunk each of the
-  // longest sequence
-  long long S = (2LL * m->sms + (long long)nkv * n - 1) / ((long long)nkv * n);
-  S = std::min<long long>(S, std::max(1, (max_len + 32 * 8 - 1) / (32 * 8)));
-  S = std::min<long long>(S, 32);
-  S = std::min<long long>(S, (long long)(e->part_floats / gb_paged_part_floats(n, nkv, 1, G, hd)));
-  S = std::max<long long>(S, 1);
   for (int l = 0; l < c.layers; l++) {
     gb_model::Layer &L = m->layers[(size_t)l];
     if ((rc = gb_rmsnorm_rows_f16_launch(m->pf_x, L.attn_norm, n, c.dim, c.eps, m->pf_a16, st))) return rc;
@@ -1359,9 +1375,8 @@ int engine_forward(gb_engine *e, int n, int max_len) {
       return rc;
     if ((rc = gb_attn_paged_launch(m->pf_q, e->kpool[(size_t)l], e->vpool[(size_t)l], 1, table, lens, n, e->max_pages,
                                    e->n_pages, e->page_size, m->q_local / hd, nkv, hd, 1.f / sqrtf((float)hd),
-                                   e->attn32, e->part, e->counter, (int)S, m->err, st)))
+                                   nullptr, m->pf_a16, e->part, e->counter, (int)S, m->err, st)))
       return rc;
-    if ((rc = gb_f32_to_f16_launch(e->attn32, m->pf_a16, (size_t)n * m->q_local, st))) return rc;
     g = tc_args(L.wo, GB_EPI_RESID, n, m->pf_map_q, m);
     g.y = m->pf_x;
     g.ldy = c.dim;
@@ -1419,8 +1434,7 @@ int gb_engine_create(gb_model *m, int page_size, int n_pages, int max_batch, gb_
         (rc = ealloc(e.get(), &e->vpool[(size_t)l], pool, "engine: KV pool")))
       return rc;
   e->part_floats = gb_paged_part_floats(max_batch, nkv, 4, G, hd);
-  if ((rc = ealloc(e.get(), &e->attn32, (size_t)max_batch * m->q_local, "engine: work")) ||
-      (rc = ealloc(e.get(), &e->logits, (size_t)max_batch * c.vocab, "engine: work")) ||
+  if ((rc = ealloc(e.get(), &e->logits, (size_t)max_batch * c.vocab, "engine: work")) ||
       (rc = ealloc(e.get(), &e->part, e->part_floats, "engine: work")) ||
       (rc = ealloc(e.get(), &e->counter, (size_t)max_batch * nkv, "engine: work")) ||
       (rc = ealloc(e.get(), &e->d_in, (size_t)max_batch * (3 + e->max_pages), "engine: work")) ||
@@ -1507,7 +1521,28 @@ int gb_engine_step(gb_engine *e, int n, const int32_t *seq_ids, const int32_t *t
   }
   GB_CUDA(cudaMemcpyAsync(e->d_in, h, sizeof(int32_t) * (size_t)B * (3 + e->max_pages), cudaMemcpyHostToDevice, m->st),
           "engine: step inputs");
-  int rc = engine_forward(e, n, max_len);
+  // the step's kernels: replayed from the graph of (n, S), captured on first use
+  const int S = engine_splits(e, n, max_len);
+  int rc = GB_OK;
+  if (m->o.use_graph) {
+    auto it = e->graphs.find({n, S});
+    if (it == e->graphs.end()) {
+      if (e->graphs.size() >= kEngineGraphs) drop_graphs(e);
+      cudaGraph_t g = nullptr;
+      cudaGraphExec_t x = nullptr;
+      GB_CUDA(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal), "engine: graph capture");
+      rc = engine_forward(e, n, S);
+      const cudaError_t ce = cudaStreamEndCapture(m->st, &g);
+      if (!rc && ce != cudaSuccess) rc = gb_cuda_fail(ce, "engine: graph capture");
+      if (!rc && cudaGraphInstantiate(&x, g, 0) != cudaSuccess) rc = gb_fail(GB_ERR_CUDA, "engine: graph instantiate");
+      if (g) cudaGraphDestroy(g);
+      if (rc) return rc;
+      it = e->graphs.emplace(std::make_pair(n, S), x).first;
+    }
+    rc = cudaGraphLaunch(it->second, m->st) == cudaSuccess ? GB_OK : gb_fail(GB_ERR_CUDA, "engine: graph launch");
+  } else {
+    rc = engine_forward(e, n, S);
+  }
   if (!rc && host_logits)
     rc = cudaMemcpyAsync(host_logits, e->logits, sizeof(float) * (size_t)n * m->c.vocab, cudaMemcpyDeviceToHost,
                          m->st) == cudaSuccess

@@ -866,7 +866,7 @@ int gb_gpu_attn_decode_paged(gb_kernels *k, void *stream, const float *q, const 
     k->pws_counters = cnt;
   }
   return gb_attn_paged_launch(q, k_pool, v_pool, kv_f16, block_table, seq_lens, batch, max_pages, n_pages, page_size,
-                              n_heads, n_kv, head_dim, scale, out, k->pws, k->pws_counter, (int)S, nullptr,
+                              n_heads, n_kv, head_dim, scale, out, nullptr, k->pws, k->pws_counter, (int)S, nullptr,
                               (cudaStream_t)stream);
 }
 

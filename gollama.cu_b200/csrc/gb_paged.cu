@@ -27,6 +27,8 @@ constexpr int kPW = 8;          // warps per CTA
 constexpr int kPMaxG = 8;       // query heads per KV head
 constexpr int kPMaxHD = 128;    // head_dim
 constexpr int kPDL = kPMaxHD / 32;
+// 16-byte pieces a thread moves per chunk: 2 x 32 rows of up to 512 bytes
+constexpr int kPFetch = 2 * 32 * (kPMaxHD * 4 / 16) / (kPW * 32);
 
 template <bool F16>
 GB_DEV float ld_kv(const void *pool, size_t i) {
@@ -59,137 +61,147 @@ struct PagedArgs {
   int B, n_heads, n_kv, hd, page_size, max_pages, n_pages;
   float scale;
   float *out;               // [B][n_heads][hd]
+  __half *out16;            // or, when set, the output in binary16
   float *part;              // [B][n_kv][S][G][hd + 2] split partials (m, l, acc)
   unsigned *counter;        // [B][n_kv], zero between launches
   int S;                    // splits of the pages
   unsigned *err;
 };
 
+// Bytes of one staged K or V row: the row plus 16 bytes, so that lanes
+// reading rows 16 bytes at a time fall on distinct banks.
 template <bool F16>
-__global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a) {
-  const int h = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
-  const int G = a.n_heads / a.n_kv, hd = a.hd, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  __shared__ float qs[kPMaxG][kPMaxHD];
-  __shared__ float wm[kPW][kPMaxG], wl[kPW][kPMaxG];
-  __shared__ float wacc[kPW][kPMaxG][kPMaxHD];
-  __shared__ unsigned last;
-  const int L = a.seq_lens[b];
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
-    qs[i / hd][i % hd] = a.q[((size_t)b * a.n_heads + (size_t)h * G + i / hd) * hd + i % hd];
-  __syncthreads();
-  // this split's 32-position chunks: [c0, c1)
-  const int nchunk = (L + 31) / 32;
-  const int c0 = (int)((long long)nchunk * sp / a.S), c1 = (int)((long long)nchunk * (sp + 1) / a.S);
-  float m[kPMaxG], l[kPMaxG], acc[kPMaxG][kPDL];
+constexpr int row_stride(int hd) {
+  return hd * (F16 ? 2 : 4) + 16;
+}
+
+// The chunk [ch*32, ch*32+32) of K and V into registers: thread t moves the
+// 16-byte pieces t, t + blockDim, ... of the chunk's 2 x 32 rows (positions
+// at or past L, and pieces past the rows, as zeros).
+template <bool F16>
+GB_DEV void chunk_fetch(const PagedArgs &a, int b, int h, int ch, int L, uint4 (&reg)[kPFetch]) {
+  const int ppr = a.hd * (F16 ? 2 : 4) / 16;  // pieces per row
+  const int32_t *table = a.block_table + (size_t)b * a.max_pages;
 #pragma unroll
-  for (int g = 0; g < kPMaxG; g++) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int d = 0; d < kPDL; d++) acc[g][d] = 0.f;
-  }
-  const int DL = hd / 32;
-  for (int ch = c0 + warp; ch < c1; ch += kPW) {
-    const int p = ch * 32 + lane;  // this lane's position
-    const bool in = p < L;
-    size_t krow = 0;
-    if (in) {
-      const int lp = p / a.page_size, off = p % a.page_size;
-      int phys = a.block_table[(size_t)b * a.max_pages + lp];
+  for (int i = 0; i < kPFetch; i++) {
+    const int piece = (int)threadIdx.x + i * kPW * 32, kv = piece / (32 * ppr), rem = piece % (32 * ppr);
+    const int j = rem / ppr, pc = rem % ppr, p = ch * 32 + j;
+    reg[i] = make_uint4(0, 0, 0, 0);
+    if (kv < 2 && p < L) {
+      int phys = table[p / a.page_size];
       if (phys < 0 || phys >= a.n_pages) {
         if (a.err) atomicOr(a.err, GB_DEVERR_POS);
         phys = 0;
       }
-      krow = (((size_t)phys * a.n_kv + h) * a.page_size + off) * hd;
+      const size_t row = (((size_t)phys * a.n_kv + h) * a.page_size + p % a.page_size) * a.hd;
+      const uint8_t *pool = (const uint8_t *)(kv ? a.v_pool : a.k_pool) + row * (F16 ? 2 : 4);
+      reg[i] = __ldcg((const uint4 *)pool + pc);
     }
-    float s[kPMaxG];
+  }
+}
+template <bool F16>
+GB_DEV void chunk_store(const PagedArgs &a, const uint4 (&reg)[kPFetch], uint8_t *ks, uint8_t *vs) {
+  const int ppr = a.hd * (F16 ? 2 : 4) / 16, rs = row_stride<F16>(a.hd);
 #pragma unroll
-    for (int g = 0; g < kPMaxG; g++) s[g] = 0.f;
-    if (in)
-      for (int d0 = 0; d0 < hd; d0 += 8) {  // this lane's key row, 8 dimensions a load
+  for (int i = 0; i < kPFetch; i++) {
+    const int piece = (int)threadIdx.x + i * kPW * 32, kv = piece / (32 * ppr), rem = piece % (32 * ppr);
+    if (kv < 2) *(uint4 *)((kv ? vs : ks) + (size_t)(rem / ppr) * rs + (rem % ppr) * 16) = reg[i];
+  }
+}
+
+// One CTA per (KV head, sequence, split of the positions); warp g < G owns
+// query head h*G + g. The split's 32-position chunks go through shared memory
+// one after another (the next chunk's loads in flight while this one is
+// used): lane = position for the scores, lane = dimensions lane + 32 i for
+// P V, an online softmax per warp. One split writes the output itself; with
+// several, each writes (m, l, acc) and the last to finish merges them.
+template <bool F16>
+__global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a) {
+  const int h = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
+  const int G = a.n_heads / a.n_kv, hd = a.hd, lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  constexpr int RS = row_stride<F16>(kPMaxHD);
+  __shared__ float qs[kPMaxG][kPMaxHD];
+  __shared__ __align__(16) uint8_t ks[32 * RS], vs[32 * RS];
+  __shared__ unsigned last;
+  const int L = a.seq_lens[b];
+  for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
+    qs[i / hd][i % hd] = a.q[((size_t)b * a.n_heads + (size_t)h * G + i / hd) * hd + i % hd];
+  const int nchunk = (L + 31) / 32;
+  const int c0 = (int)((long long)nchunk * sp / a.S), c1 = (int)((long long)nchunk * (sp + 1) / a.S);
+  const int rs = row_stride<F16>(hd), DL = hd / 32;
+  float m = -INFINITY, l = 0.f, acc[kPDL];
+#pragma unroll
+  for (int d = 0; d < kPDL; d++) acc[d] = 0.f;
+  uint4 reg[kPFetch];
+  if (c0 < c1) chunk_fetch<F16>(a, b, h, c0, L, reg);
+  for (int ch = c0; ch < c1; ch++) {
+    __syncthreads();  // the previous chunk is used up (and q is in place)
+    chunk_store<F16>(a, reg, ks, vs);
+    __syncthreads();
+    if (ch + 1 < c1) chunk_fetch<F16>(a, b, h, ch + 1, L, reg);
+    if (g < G) {
+      const int p = ch * 32 + lane;
+      const bool in = p < L;
+      float sc = 0.f;
+      const uint8_t *kr = ks + (size_t)lane * rs;
+      for (int d0 = 0; d0 < hd; d0 += F16 ? 8 : 4) {
+        const uint4 u = *(const uint4 *)(kr + (F16 ? d0 * 2 : d0 * 4));
         float kv[8];
-        ld8<F16>(a.k_pool, krow + d0, kv);
+        if constexpr (F16) {
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int e = 0; e < 8; e++)
+          for (int e = 0; e < 4; e++) {
+            kv[2 * e] = gb_half_to_float((uint16_t)(w[e] & 0xFFFF));
+            kv[2 * e + 1] = gb_half_to_float((uint16_t)(w[e] >> 16));
+          }
+        } else {
+          kv[0] = __uint_as_float(u.x), kv[1] = __uint_as_float(u.y), kv[2] = __uint_as_float(u.z),
+          kv[3] = __uint_as_float(u.w);
+        }
 #pragma unroll
-          for (int g = 0; g < kPMaxG; g++)
-            if (g < G) s[g] = fmaf(qs[g][d0 + e], kv[e], s[g]);
+        for (int e = 0; e < (F16 ? 8 : 4); e++) sc = fmaf(qs[g][d0 + e], kv[e], sc);
       }
+      const float sv = in ? sc * a.scale : -INFINITY;
+      const float mn = fmaxf(m, gb_warp_max(sv));
+      const float alpha = expf(m - mn), pe = in ? expf(sv - mn) : 0.f;
+      l = l * alpha + gb_warp_sum(pe);
+      m = mn;
 #pragma unroll
-    for (int g = 0; g < kPMaxG; g++) {
-      if (g >= G) break;
-      const float sv = in ? s[g] * a.scale : -INFINITY;
-      const float mn = fmaxf(m[g], gb_warp_max(sv));
-      const float alpha = expf(m[g] - mn), pe = in ? expf(sv - mn) : 0.f;
-      l[g] = l[g] * alpha + gb_warp_sum(pe);
-      m[g] = mn;
+      for (int d = 0; d < kPDL; d++) acc[d] *= alpha;
+      const int jn = min(32, L - ch * 32);
+      for (int j = 0; j < jn; j++) {
+        const float pj = __shfl_sync(0xffffffffu, pe, j);
+        const uint8_t *vr = vs + (size_t)j * rs;
 #pragma unroll
-      for (int d = 0; d < kPDL; d++) acc[g][d] *= alpha;
-      s[g] = pe;
-    }
-    // P V: lane holds dimensions lane + 32 i; position j's V row sits where
-    // lane j's K row does (the pools share one layout), so the V loads of the
-    // 32 positions do not wait on one another
-    const unsigned long long krow_u = krow;
-#pragma unroll 8
-    for (int j = 0; j < 32; j++) {
-      const bool pin = ch * 32 + j < L;
-      const size_t vrow = (size_t)__shfl_sync(0xffffffffu, krow_u, j);
-      float vv[kPDL];
-#pragma unroll
-      for (int d = 0; d < kPDL; d++) vv[d] = pin && d < DL ? ld_kv<F16>(a.v_pool, vrow + lane + 32 * d) : 0.f;
-#pragma unroll
-      for (int g = 0; g < kPMaxG; g++) {
-        if (g >= G) break;
-        const float pg = __shfl_sync(0xffffffffu, s[g], j);
-#pragma unroll
-        for (int d = 0; d < kPDL; d++) acc[g][d] = fmaf(pg, vv[d], acc[g][d]);
+        for (int d = 0; d < kPDL; d++)
+          if (d < DL) {
+            const float v = F16 ? gb_half_to_float(((const uint16_t *)vr)[lane + 32 * d])
+                                : ((const float *)vr)[lane + 32 * d];
+            acc[d] = fmaf(pj, v, acc[d]);
+          }
       }
     }
   }
-  // merge the warps (in warp order)
+  if (a.S == 1) {
+    if (g < G)
 #pragma unroll
-  for (int g = 0; g < kPMaxG; g++) {
-    if (g >= G) break;
-    if (lane == 0) {
-      wm[warp][g] = m[g];
-      wl[warp][g] = l[g];
-    }
-#pragma unroll
-    for (int d = 0; d < kPDL; d++)
-      if (d < DL) wacc[warp][g][lane + 32 * d] = acc[g][d];
-  }
-  __syncthreads();
-  float *dst = a.part + (((size_t)b * a.n_kv + h) * a.S + sp) * G * (hd + 2);
-  if (a.S == 1) {  // one split: its merge is the output (as the split merge below gives it)
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-      const int g = i / hd, d = i % hd;
-      float M = -INFINITY;
-      for (int w = 0; w < kPW; w++) M = fmaxf(M, wm[w][g]);
-      float Lsum = 0.f, A = 0.f;
-      for (int w = 0; w < kPW; w++) {
-        const float f = wm[w][g] == -INFINITY ? 0.f : expf(wm[w][g] - M);
-        Lsum += wl[w][g] * f;
-        A += wacc[w][g][d] * f;
-      }
-      a.out[((size_t)b * a.n_heads + (size_t)h * G + g) * hd + d] = Lsum > 0.f ? A / Lsum : 0.f;
-    }
+      for (int d = 0; d < kPDL; d++)
+        if (d < DL) {
+          const float o = l > 0.f ? acc[d] / l : 0.f;
+          const size_t idx = ((size_t)b * a.n_heads + (size_t)h * G + g) * hd + lane + 32 * d;
+          if (a.out16) a.out16[idx] = __float2half_rn(o);
+          else a.out[idx] = o;
+        }
     return;
   }
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-    const int g = i / hd, d = i % hd;
-    float M = -INFINITY;
-    for (int w = 0; w < kPW; w++) M = fmaxf(M, wm[w][g]);
-    float Lsum = 0.f, A = 0.f;
-    for (int w = 0; w < kPW; w++) {
-      const float f = wm[w][g] == -INFINITY ? 0.f : expf(wm[w][g] - M);
-      Lsum += wl[w][g] * f;
-      A += wacc[w][g][d] * f;
-    }
-    dst[(size_t)g * (hd + 2) + 2 + d] = A;
-    if (d == 0) {
-      dst[(size_t)g * (hd + 2)] = M;
-      dst[(size_t)g * (hd + 2) + 1] = Lsum;
+  float *dst = a.part + (((size_t)b * a.n_kv + h) * a.S + sp) * G * (hd + 2);
+  if (g < G) {
+#pragma unroll
+    for (int d = 0; d < kPDL; d++)
+      if (d < DL) dst[(size_t)g * (hd + 2) + 2 + lane + 32 * d] = acc[d];
+    if (lane == 0) {
+      dst[(size_t)g * (hd + 2)] = m;
+      dst[(size_t)g * (hd + 2) + 1] = l;
     }
   }
   // the last split of (sequence, KV head) merges the splits (in split order)
@@ -201,18 +213,21 @@ __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a)
   __threadfence();
   const float *src = a.part + ((size_t)b * a.n_kv + h) * a.S * G * (hd + 2);
   for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-    const int g = i / hd, d = i % hd;
+    const int gg = i / hd, d = i % hd;
     float M = -INFINITY;
-    for (int s2 = 0; s2 < a.S; s2++) M = fmaxf(M, __ldcg(src + ((size_t)s2 * G + g) * (hd + 2)));
+    for (int s2 = 0; s2 < a.S; s2++) M = fmaxf(M, __ldcg(src + ((size_t)s2 * G + gg) * (hd + 2)));
     float Lsum = 0.f, A = 0.f;
     for (int s2 = 0; s2 < a.S; s2++) {
-      const float *ps = src + ((size_t)s2 * G + g) * (hd + 2);
+      const float *ps = src + ((size_t)s2 * G + gg) * (hd + 2);
       const float ms = __ldcg(ps);
       const float f = ms == -INFINITY ? 0.f : expf(ms - M);
       Lsum += __ldcg(ps + 1) * f;
       A += __ldcg(ps + 2 + d) * f;
     }
-    a.out[((size_t)b * a.n_heads + (size_t)h * G + g) * hd + d] = Lsum > 0.f ? A / Lsum : 0.f;
+    const float o = Lsum > 0.f ? A / Lsum : 0.f;
+    const size_t idx = ((size_t)b * a.n_heads + (size_t)h * G + gg) * hd + d;
+    if (a.out16) a.out16[idx] = __float2half_rn(o);
+    else a.out[idx] = o;
   }
   if (threadIdx.x == 0) a.counter[(size_t)b * a.n_kv + h] = 0u;  // ready for the next launch
 }
@@ -319,8 +334,8 @@ size_t gb_paged_part_floats(int B, int n_kv, int S, int G, int hd) {
 
 int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool, int kv_f16, const int32_t *block_table,
                          const int32_t *seq_lens, int B, int max_pages, int n_pages, int page_size, int n_heads,
-                         int n_kv, int hd, float scale, float *out, float *part, unsigned *counter, int S,
-                         unsigned *err, cudaStream_t st) {
+                         int n_kv, int hd, float scale, float *out, __half *out16, float *part, unsigned *counter,
+                         int S, unsigned *err, cudaStream_t st) {
   if (B <= 0) return GB_OK;
   if (n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > kPMaxG || hd % 32 || hd > kPMaxHD || page_size <= 0)
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: paged attention: %d heads, %d KV heads, head_dim %d, page %d", n_heads,
@@ -340,6 +355,7 @@ int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool,
   a.n_pages = n_pages;
   a.scale = scale;
   a.out = out;
+  a.out16 = out16;
   a.part = part;
   a.counter = counter;
   a.S = S;
