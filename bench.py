@@ -476,10 +476,10 @@ def run_ours(args, cfg, world, rank, local):
                        "parallelism the o/down partials summed by NCCL all-reduces; CUDA events, "
                        f"mean of {reps}, max over ranks"}
 
-    def time_engine(weights):
-        e = gb.Engine(m, page_size=64, n_pages=args.batch * 4, max_batch=args.batch)
-        ids = [e.add() for _ in range(args.batch)]
-        btoks = prompt_tokens(spec, args.batch)
+    def time_engine(weights, batch):
+        e = gb.Engine(m, page_size=64, n_pages=batch * 4, max_batch=batch)
+        ids = [e.add() for _ in range(batch)]
+        btoks = prompt_tokens(spec, batch)
         for _ in range(4):  # warm-up: positions 0..3 of every sequence
             _, btoks = e.step(ids, btoks, logits=False)
         torch.cuda.synchronize()
@@ -493,15 +493,15 @@ def run_ours(args, cfg, world, rank, local):
         wall = time.perf_counter() - w0
         bms = ev0.elapsed_time(ev1) / nsteps
         e.close()
-        return {"batch": args.batch, "value": round(args.batch * nsteps / (bms * nsteps / 1e3), 1), "unit": "tok/s",
-                "ms_per_step": round(bms, 3), "e2e_tok_s": round(args.batch * nsteps / wall, 1),
+        return {"batch": batch, "value": round(batch * nsteps / (bms * nsteps / 1e3), 1), "unit": "tok/s",
+                "ms_per_step": round(bms, 3), "e2e_tok_s": round(batch * nsteps / wall, 1),
                 "positions": f"4..{4 + nsteps - 1}", "weights": weights,
                 "how": "gb_engine_step: B sequences one token each per step through the tensor-core GEMMs and the "
-                       "paged attention; value = CUDA events around 32 steps, each synchronous (ids in, next tokens "
-                       "out, status check), e2e = wall clock of the same loop"}
+                       "paged attention, replayed from a CUDA graph; value = CUDA events around 32 steps, each "
+                       "synchronous (ids in, next tokens out, status check), e2e = wall clock of the same loop"}
 
     prefill = time_prefill("quantized, decoded per call") if args.prefill_tokens > 1 else None
-    batched = time_engine("quantized, decoded per call") if world == 1 and args.batch > 1 else None
+    batched = time_engine("quantized, decoded per call", args.batch) if world == 1 and args.batch > 1 else None
     prefill16 = batched16 = None
     if args.prefill_tokens > 1 or (world == 1 and args.batch > 1):
         try:
@@ -511,7 +511,8 @@ def run_ours(args, cfg, world, rank, local):
         if isinstance(w16, int):
             what = f"binary16 copy ({w16 / 1e9:.2f} GB, gb_model_cache_f16_weights), read by TMA"
             prefill16 = time_prefill(what) if args.prefill_tokens > 1 else None
-            batched16 = time_engine(what) if world == 1 and args.batch > 1 else None
+            batched16 = ([time_engine(what, b) for b in sorted({8, args.batch})]
+                         if world == 1 and args.batch > 1 else None)
         else:
             prefill16 = batched16 = {"unavailable": w16}
 
@@ -703,6 +704,53 @@ def run_reference(args, cfg, world, rank):
           flush=True)
 
 
+def profile_batched(args, cfg):
+    """One engine step (or prefill) of the config's model, with its binary16
+    weight copy, after warm-up, between cudaProfilerStart/Stop: the launch list
+    and kernel captures of the batched paths. The engine runs without its
+    CUDA graphs (use_graph=0), so that ncu sees plain kernel launches. Prints
+    the wall time of the warm steps (not a bench line)."""
+    import torch
+
+    import gollama_b200 as gb
+
+    src, spec = build_image(gb, cfg, 1, 0)
+    m = gb.Model(src, device=0, max_len=max(1024, args.profile_prefill + 1), kv_f16=1, use_graph=0)
+    m.cache_f16_weights()
+    if args.profile_engine:
+        B = args.profile_engine
+        e = gb.Engine(m, page_size=64, n_pages=B * 4, max_batch=B)
+        ids = [e.add() for _ in range(B)]
+        toks = prompt_tokens(spec, B)
+        for _ in range(4):
+            _, toks = e.step(ids, toks, logits=False)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(8):
+            _, toks = e.step(ids, toks, logits=False)
+        ms = (time.perf_counter() - t0) / 8 * 1e3
+        torch.cuda.profiler.start()
+        e.step(ids, toks, logits=False)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        e.close()
+        print(json.dumps({"profile": "engine step", "batch": B, "layers": spec.layers, "ms_per_step_wall": round(ms, 3)}))
+    else:
+        pt = prompt_tokens(spec, args.profile_prefill)
+        for _ in range(2):
+            m.prefill(pt, 0)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        m.prefill(pt, 0)
+        ms = (time.perf_counter() - t0) * 1e3
+        torch.cuda.profiler.start()
+        m.prefill(pt, 0)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profile": "prefill", "tokens": len(pt), "layers": spec.layers, "ms_wall": round(ms, 3)}))
+    m.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -722,6 +770,11 @@ def main():
                     help="run only the GEMV sweep, e.g. q4_k:14336x4096 or all:all (profiling captures)")
     ap.add_argument("--layers", type=int, default=0,
                     help="truncate the model to this many layers (small ncu captures only; not a bench line)")
+    ap.add_argument("--profile-engine", type=int, default=0, metavar="B",
+                    help="one engine step of B sequences through the binary16 weight copy between "
+                         "cudaProfilerStart/Stop (ncu --profile-from-start off); not a bench line")
+    ap.add_argument("--profile-prefill", type=int, default=0, metavar="T",
+                    help="one T-token prefill through the binary16 weight copy between cudaProfilerStart/Stop")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -729,6 +782,9 @@ def main():
     if args.layers:
         cfg["layers"] = args.layers
         cfg["workload"] += f" [truncated to {args.layers} layers for profiling]"
+    if args.profile_engine or args.profile_prefill:
+        profile_batched(args, cfg)
+        return
     if args.sweep_only:
         import torch
 
