@@ -45,11 +45,15 @@ def _rank(rank, world, port, out_dir):
         toks = m.generate(int(np.argmax(logits[-1])), len(TOKENS), 6)
         # batched prefill over both ranks (all-reduced o/down partials)
         pre = m.prefill(PREFILL, 0).copy()
+        # and through each rank's binary16 weight copy (the few-token GEMM)
+        m.cache_f16_weights()
+        pre16 = m.prefill(PREFILL, 0).copy()
         m.close()
         if rank == 0:
             np.save(os.path.join(out_dir, "tp_logits.npy"), np.stack(logits))
             np.save(os.path.join(out_dir, "tp_tokens.npy"), toks)
             np.save(os.path.join(out_dir, "tp_prefill.npy"), pre)
+            np.save(os.path.join(out_dir, "tp_prefill16.npy"), pre16)
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -81,6 +85,8 @@ def test_two_gpu_step_matches_one_gpu_and_cpu(gb, orc, cuda, tmp_path):
     tp_pre = np.load(tmp_path / "tp_prefill.npy")
     rel = lambda a, b: float(np.abs(a.astype(np.float64) - b).max() / np.abs(b).max())
     assert rel(tp_pre, one_pre) < 5e-3, rel(tp_pre, one_pre)
+    tp_pre16 = np.load(tmp_path / "tp_prefill16.npy")
+    assert rel(tp_pre16, one_pre) < 5e-3, rel(tp_pre16, one_pre)
     d = gb.Model(img, max_len=64)
     for p, t in enumerate(PREFILL):
         dec = d.forward(t, p).copy()
