@@ -500,9 +500,37 @@ def run_ours(args, cfg, world, rank, local):
                        "paged attention, replayed from a CUDA graph; value = CUDA events around 32 steps, each "
                        "synchronous (ids in, next tokens out, status check), e2e = wall clock of the same loop"}
 
+    def time_engine_prompt(weights):
+        # a prompt fed to the engine as the rows of one step (chunked prefill
+        # into the paged cache), next to nothing else
+        T = min(args.prefill_tokens, 512)
+        e = gb.Engine(m, page_size=64, n_pages=(T + 63) // 64 + 1, max_batch=T)
+        pt = prompt_tokens(spec, T)
+        for _ in range(2):  # warm-up (captures the step's graph)
+            sid = e.add()
+            e.step([sid] * T, pt, logits=False)
+            e.release(sid)
+        torch.cuda.synchronize()
+        reps, tot = 3, 0.0
+        for _ in range(reps):
+            sid = e.add()
+            ev0.record(stream)
+            e.step([sid] * T, pt, logits=False)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            tot += ev0.elapsed_time(ev1)
+            e.release(sid)
+        e.close()
+        pms = tot / reps
+        return {"tokens": T, "value": round(T / (pms / 1e3), 1), "unit": "tok/s", "ms": round(pms, 3),
+                "weights": weights,
+                "how": "gb_engine_step with one sequence listed T times (its prompt at positions 0..T-1 in one "
+                       "step: the batched GEMMs, paged RoPE/KV append, paged attention per row); CUDA events, "
+                       f"mean of {reps}"}
+
     prefill = time_prefill("quantized, decoded per call") if args.prefill_tokens > 1 else None
     batched = time_engine("quantized, decoded per call", args.batch) if world == 1 and args.batch > 1 else None
-    prefill16 = batched16 = None
+    prefill16 = batched16 = prompt16 = None
     if args.prefill_tokens > 1 or (world == 1 and args.batch > 1):
         try:
             w16 = m.cache_f16_weights()
@@ -513,8 +541,9 @@ def run_ours(args, cfg, world, rank, local):
             prefill16 = time_prefill(what) if args.prefill_tokens > 1 else None
             batched16 = ([time_engine(what, b) for b in sorted({8, args.batch})]
                          if world == 1 and args.batch > 1 else None)
+            prompt16 = time_engine_prompt(what) if world == 1 and args.prefill_tokens > 1 else None
         else:
-            prefill16 = batched16 = {"unavailable": w16}
+            prefill16 = batched16 = prompt16 = {"unavailable": w16}
 
     sweep = gemv_sweep(gb, torch, local, peaks()[0]) if world == 1 and not args.no_sweep else None
     configs = {}
@@ -543,7 +572,7 @@ def run_ours(args, cfg, world, rank, local):
                                    "launches serialized (no PDL overlap), so the classes add up to more than "
                                    "ms_per_step"),
         "prefill": prefill, "prefill_f16w": prefill16,
-        "batched_decode": batched, "batched_decode_f16w": batched16,
+        "batched_decode": batched, "batched_decode_f16w": batched16, "engine_prompt_f16w": prompt16,
         "gemv_sweep": sweep,
         "configs": configs or None,
         "e2e": e2e,

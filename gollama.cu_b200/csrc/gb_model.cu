@@ -1309,6 +1309,7 @@ struct gb_engine {
   std::vector<void *> allocs;
   // one CUDA graph of the step per (rows, attention splits) met so far
   std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+  std::vector<int> row_off;  // per sequence: rows of the current step so far
 };
 
 namespace {
@@ -1484,21 +1485,24 @@ int gb_engine_step(gb_engine *e, int n, const int32_t *seq_ids, const int32_t *t
                    int32_t *next) {
   gb_clear_error();
   if (!e || n <= 0 || !seq_ids || !tokens) return gb_fail(GB_ERR_INVALID, "engine: bad step arguments");
-  if (n > e->max_batch) return gb_fail(GB_ERR_INVALID, "engine: %d sequences, at most %d", n, e->max_batch);
+  if (n > e->max_batch) return gb_fail(GB_ERR_INVALID, "engine: %d rows, at most %d", n, e->max_batch);
   gb_model *m = e->m;
-  // validate every row before touching any state
+  // validate every row before touching any state. A sequence listed k times
+  // feeds k tokens at its next k positions, in the order listed (a prompt
+  // chunk); each row attends to its sequence's positions up to its own.
+  std::vector<int> &off = e->row_off;
+  off.assign(e->seqs.size(), 0);
   int need_pages = 0;
   for (int t = 0; t < n; t++) {
     const int id = seq_ids[t];
     if (id < 0 || id >= (int)e->seqs.size() || !e->seqs[(size_t)id].live)
       return gb_fail(GB_ERR_INVALID, "engine: no sequence %d", id);
-    for (int u = 0; u < t; u++)
-      if (seq_ids[u] == id) return gb_fail(GB_ERR_INVALID, "engine: sequence %d twice in one step", id);
     if (tokens[t] < 0 || tokens[t] >= m->c.vocab)
       return gb_fail(GB_ERR_INVALID, "model: token %d outside the vocabulary", tokens[t]);
-    const int len = e->seqs[(size_t)id].len;
-    if (len >= e->max_pos) return gb_fail(GB_ERR_INVALID, "engine: sequence %d is full (%d positions)", id, len);
-    if ((int)e->seqs[(size_t)id].pages.size() <= len / e->page_size) need_pages++;
+    const gb_engine::Seq &q = e->seqs[(size_t)id];
+    const int pos = q.len + off[(size_t)id]++;
+    if (pos >= e->max_pos) return gb_fail(GB_ERR_INVALID, "engine: sequence %d is full (%d positions)", id, pos);
+    if (pos % e->page_size == 0 && (int)q.pages.size() <= pos / e->page_size) need_pages++;
   }
   if (need_pages > (int)e->free_pages.size())
     return gb_fail(GB_ERR_UNSUPPORTED, "engine: out of KV pages (%d needed, %zu free)", need_pages,
@@ -1506,16 +1510,18 @@ int gb_engine_step(gb_engine *e, int n, const int32_t *seq_ids, const int32_t *t
   int32_t *h = e->h_in;
   const int B = e->max_batch;
   int max_len = 0;
+  off.assign(e->seqs.size(), 0);
   for (int t = 0; t < n; t++) {
     gb_engine::Seq &q = e->seqs[(size_t)seq_ids[t]];
-    max_len = std::max(max_len, q.len + 1);
-    if ((int)q.pages.size() <= q.len / e->page_size) {  // its next position starts a page
+    const int pos = q.len + off[(size_t)seq_ids[t]]++;
+    max_len = std::max(max_len, pos + 1);
+    if ((int)q.pages.size() <= pos / e->page_size) {  // this position starts a page
       q.pages.push_back(e->free_pages.back());
       e->free_pages.pop_back();
     }
     h[t] = tokens[t];
-    h[B + t] = q.len;
-    h[2 * B + t] = q.len + 1;
+    h[B + t] = pos;
+    h[2 * B + t] = pos + 1;
     int32_t *row = h + 3 * B + (size_t)t * e->max_pages;
     for (int i = 0; i < e->max_pages; i++) row[i] = i < (int)q.pages.size() ? q.pages[(size_t)i] : -1;
   }

@@ -434,7 +434,8 @@ class Engine:
         return lib().gb_engine_free_pages(self.h)
 
     def step(self, seq_ids, tokens, logits: bool = True):
-        """One token per sequence; returns (logits [n][vocab] or None, next tokens [n])."""
+        """One row per (sequence, token); a sequence listed k times takes its next k
+        positions in the order listed. Returns (logits [n][vocab] or None, next tokens [n])."""
         ids = np.ascontiguousarray(np.asarray(seq_ids, np.int32))
         toks = np.ascontiguousarray(np.asarray(tokens, np.int32))
         n = ids.size

@@ -309,11 +309,14 @@ int gb_engine_release(gb_engine *e, int seq_id);
 /* Positions fed so far (-1: no such sequence); free pages of the pool. */
 int gb_engine_seq_len(const gb_engine *e, int seq_id);
 int gb_engine_free_pages(const gb_engine *e);
-/* One token for each of seq_ids[0..n) (distinct live sequences). The logits
- * of each row are copied to host_logits[n][vocab] and the first maximum of
- * each row (model.Argmax's rule) to next[n]; either may be NULL. Fails
- * (GB_ERR_UNSUPPORTED) without changing any sequence when the pool has too
- * few free pages for the step. */
+/* Rows (seq_ids[t], tokens[t]) for t in [0, n), n <= max_batch, each a live
+ * sequence. A sequence listed k times feeds k tokens at its next k positions
+ * in the order listed (a prompt chunk in one step); each row attends to its
+ * sequence's positions up to its own. The logits of each row are copied to
+ * host_logits[n][vocab] and the first maximum of each row (model.Argmax's
+ * rule) to next[n]; either may be NULL. Fails (GB_ERR_UNSUPPORTED) without
+ * changing any sequence when the pool has too few free pages for the step,
+ * and (GB_ERR_INVALID) when a sequence would pass the cache's length. */
 int gb_engine_step(gb_engine *e, int n, const int32_t *seq_ids, const int32_t *tokens, float *host_logits,
                    int32_t *next);
 int gb_engine_free(gb_engine *e);

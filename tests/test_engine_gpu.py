@@ -118,14 +118,58 @@ def test_engine_page_exhaustion_and_errors(gb, cuda):
     assert "out of KV pages" in str(err.value)
     assert e.seq_len(a) == 1 and e.seq_len(c) == 0  # nothing changed
     with pytest.raises(gb.GollamaError):
-        e.step([a, a], [1, 1])
-    with pytest.raises(gb.GollamaError):
         e.step([a], [cfg["vocab"]])
     e.release(b)
     e.step([a, c], [3, 4])  # c takes b's page
     assert e.free_pages() == 0
     e.close()
+    # a sequence listed several times takes that many positions: 97 rows
+    # pass the 96-position cache, and nothing changes
+    e = gb.Engine(m, page_size=16, n_pages=16, max_batch=128)
+    a = e.add()
+    with pytest.raises(gb.GollamaError) as err:
+        e.step([a] * 97, [1] * 97)
+    assert "is full" in str(err.value)
+    assert e.seq_len(a) == 0 and e.free_pages() == 16
+    e.step([a] * 96, [1] * 96)
+    assert e.seq_len(a) == 96 and e.free_pages() == 10
+    e.close()
     m.close()
+
+
+def test_engine_prompt_chunk_in_one_step(gb, cuda):
+    # a prompt fed as rows of one step (the batched GEMMs) gives the rows the
+    # same logits as feeding it token by token, next to another sequence that
+    # decodes one token in the same step; decoding then continues from it
+    cfg = MODELS["q4km_hd128"]
+    img = gb.SynthImage(gb.synth_spec(**cfg))
+    rng = np.random.default_rng(21)
+    prompt = [int(t) for t in rng.integers(0, cfg["vocab"], 40)]
+    other = [int(t) for t in rng.integers(0, cfg["vocab"], 8)]
+    m = gb.Model(img, max_len=96)
+    e = gb.Engine(m, page_size=16, n_pages=32, max_batch=64)
+    a, b = e.add(), e.add()
+    for t in other[:4]:
+        e.step([b], [t])
+    logits, nxt = e.step([a] * len(prompt) + [b], prompt + [other[4]])
+    chunk = logits[:len(prompt)].copy()
+    assert e.seq_len(a) == len(prompt) and e.seq_len(b) == 5
+    cont = [e.step([a], [int(nxt[len(prompt) - 1])])[0][0].copy()]
+    e.close()
+    # the same prompt token by token in a fresh engine
+    e = gb.Engine(m, page_size=16, n_pages=32, max_batch=64)
+    a = e.add()
+    rows = [e.step([a], [t])[0][0].copy() for t in prompt]
+    ref_next = int(np.argmax(rows[-1]))
+    cont_ref = e.step([a], [ref_next])[0][0].copy()
+    e.close()
+    m.close()
+    for p in range(len(prompt)):
+        assert rel_err(chunk[p], rows[p]) < 1e-3, f"pos {p}: {rel_err(chunk[p], rows[p]):.3g}"
+    top = np.sort(rows[-1].astype(np.float64))
+    if top[-1] - top[-2] > 2e-3 * np.abs(rows[-1]).max():  # not a near-tie
+        assert int(nxt[len(prompt) - 1]) == ref_next
+        assert rel_err(cont[0], cont_ref) < 1e-3
 
 
 def test_engine_f16_weight_copy(gb, cuda):
