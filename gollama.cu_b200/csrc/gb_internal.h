@@ -211,7 +211,9 @@ size_t gb_paged_part_floats(int B, int n_kv, int S, int G, int hd);
 int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool, int kv_f16, const int32_t *block_table,
                          const int32_t *seq_lens, int B, int max_pages, int n_pages, int page_size, int n_heads,
                          int n_kv, int hd, float scale, float *out, __half *out16, float *part, unsigned *counter,
-                         int S, unsigned *err, cudaStream_t st);
+                         int S, unsigned *err, cudaStream_t st, const int32_t *groups = nullptr, int n_groups = 0);
+// Rows of one sequence a paged-attention row group may hold (query heads per KV head G).
+int gb_attn_paged_group_rows(int G);
 
 int gb_rope_kv_paged_launch(const float *qkv, int T, int q_rows, int kv_rows, int hd, const double *rope_cs,
                             const int32_t *pos, const int32_t *table, int max_pages, int page_size, int n_pages,

@@ -27,6 +27,7 @@
 #include <memory>
 #include <string>
 #include <thread>
+#include <tuple>
 #include <vector>
 
 #include "gb_internal.h"
@@ -1303,12 +1304,12 @@ struct gb_engine {
   float *logits = nullptr, *part = nullptr;
   size_t part_floats = 0;
   unsigned *counter = nullptr;
-  int32_t *d_in = nullptr;   // tokens [B] | pos [B] | lens [B] | table [B][max_pages]
+  int32_t *d_in = nullptr;   // tokens [B] | pos [B] | lens [B] | table [B][max_pages] | groups [B + 1]
   int32_t *h_in = nullptr;   // pinned copy of d_in
   int32_t *d_next = nullptr;
   std::vector<void *> allocs;
-  // one CUDA graph of the step per (rows, attention splits) met so far
-  std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+  // one CUDA graph of the step per (rows, attention splits, row groups) met so far
+  std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;
   std::vector<int> row_off;  // per sequence: rows of the current step so far
 };
 
@@ -1343,23 +1344,24 @@ int ealloc(gb_engine *e, T **p, size_t n, const char *what) {
 // Paged attention splits for n rows whose longest sequence has max_len
 // positions: about two CTAs per SM, within the scratch, and no more than
 // give each split's warps one 32-position chunk each.
-int engine_splits(const gb_engine *e, int n, int max_len) {
+int engine_splits(const gb_engine *e, int n, int ngroups, int max_len) {
   const gb_model *m = e->m;
   const int hd = m->c.head_dim, nkv = m->kv_local / hd, G = m->c.heads / m->c.kv_heads;
-  long long S = (2LL * m->sms + (long long)nkv * n - 1) / ((long long)nkv * n);
+  long long S = (2LL * m->sms + (long long)nkv * ngroups - 1) / ((long long)nkv * ngroups);
   S = std::min<long long>(S, std::max(1, (max_len + 32 * 8 - 1) / (32 * 8)));
   S = std::min<long long>(S, 32);
   S = std::min<long long>(S, (long long)(e->part_floats / gb_paged_part_floats(n, nkv, 1, G, hd)));
   return (int)std::max<long long>(S, 1);
 }
 
-int engine_forward(gb_engine *e, int n, int S) {
+int engine_forward(gb_engine *e, int n, int S, int ngroups) {
   gb_model *m = e->m;
   const gb_config &c = m->c;
   cudaStream_t st = m->st;
   const int hd = c.head_dim, qkv = m->q_local + 2 * m->kv_local, nkv = m->kv_local / hd;
   const int32_t *tok = e->d_in, *pos = e->d_in + e->max_batch, *lens = e->d_in + 2 * e->max_batch,
                 *table = e->d_in + 3 * e->max_batch;
+  const int32_t *groups = ngroups < n ? table + (size_t)e->max_batch * e->max_pages : nullptr;
   int rc = gb_embed_rows_launch(m->embd_type, m->embd.w, m->embd_nsb, c.dim, tok, n, c.vocab, m->pf_x, nullptr, 0,
                                 c.max_len, m->err, st);
   if (rc) return rc;
@@ -1376,7 +1378,7 @@ int engine_forward(gb_engine *e, int n, int S) {
       return rc;
     if ((rc = gb_attn_paged_launch(m->pf_q, e->kpool[(size_t)l], e->vpool[(size_t)l], 1, table, lens, n, e->max_pages,
                                    e->n_pages, e->page_size, m->q_local / hd, nkv, hd, 1.f / sqrtf((float)hd),
-                                   nullptr, m->pf_a16, e->part, e->counter, (int)S, m->err, st)))
+                                   nullptr, m->pf_a16, e->part, e->counter, (int)S, m->err, st, groups, ngroups)))
       return rc;
     g = tc_args(L.wo, GB_EPI_RESID, n, m->pf_map_q, m);
     g.y = m->pf_x;
@@ -1438,10 +1440,10 @@ int gb_engine_create(gb_model *m, int page_size, int n_pages, int max_batch, gb_
   if ((rc = ealloc(e.get(), &e->logits, (size_t)max_batch * c.vocab, "engine: work")) ||
       (rc = ealloc(e.get(), &e->part, e->part_floats, "engine: work")) ||
       (rc = ealloc(e.get(), &e->counter, (size_t)max_batch * nkv, "engine: work")) ||
-      (rc = ealloc(e.get(), &e->d_in, (size_t)max_batch * (3 + e->max_pages), "engine: work")) ||
+      (rc = ealloc(e.get(), &e->d_in, (size_t)max_batch * (4 + e->max_pages) + 1, "engine: work")) ||
       (rc = ealloc(e.get(), &e->d_next, (size_t)max_batch, "engine: work")))
     return rc;
-  GB_CUDA(cudaMallocHost(&e->h_in, sizeof(int32_t) * (size_t)max_batch * (3 + e->max_pages)), "engine: staging");
+  GB_CUDA(cudaMallocHost(&e->h_in, sizeof(int32_t) * ((size_t)max_batch * (4 + e->max_pages) + 1)), "engine: staging");
   for (int p = n_pages - 1; p >= 0; p--) e->free_pages.push_back(p);
   GB_CUDA(cudaStreamSynchronize(m->st), "engine: create");
   *out = e.release();
@@ -1522,32 +1524,44 @@ int gb_engine_step(gb_engine *e, int n, const int32_t *seq_ids, const int32_t *t
     h[t] = tokens[t];
     h[B + t] = pos;
     h[2 * B + t] = pos + 1;
+  }
+  // page tables after the step's allocations (a row attends only up to its
+  // own position, so later pages of its sequence are harmless), and row
+  // groups: consecutive rows of one sequence, up to the attention's group size
+  const int R = gb_attn_paged_group_rows(m->c.heads / m->c.kv_heads);
+  int32_t *grp = h + 3 * B + (size_t)B * e->max_pages;
+  int ngroups = 0;
+  for (int t = 0; t < n; t++) {
+    const gb_engine::Seq &q = e->seqs[(size_t)seq_ids[t]];
     int32_t *row = h + 3 * B + (size_t)t * e->max_pages;
     for (int i = 0; i < e->max_pages; i++) row[i] = i < (int)q.pages.size() ? q.pages[(size_t)i] : -1;
+    if (t == 0 || seq_ids[t] != seq_ids[t - 1] || t - grp[ngroups - 1] >= R) grp[ngroups++] = t;
   }
-  GB_CUDA(cudaMemcpyAsync(e->d_in, h, sizeof(int32_t) * (size_t)B * (3 + e->max_pages), cudaMemcpyHostToDevice, m->st),
+  grp[ngroups] = n;
+  GB_CUDA(cudaMemcpyAsync(e->d_in, h, sizeof(int32_t) * ((size_t)B * (4 + e->max_pages) + 1), cudaMemcpyHostToDevice,
+                          m->st),
           "engine: step inputs");
-  // the step's kernels: replayed from the graph of (n, S), captured on first use
-  const int S = engine_splits(e, n, max_len);
+  // the step's kernels: replayed from the graph of (n, S, groups), captured on first use
+  const int S = engine_splits(e, n, ngroups, max_len);
   int rc = GB_OK;
   if (m->o.use_graph) {
-    auto it = e->graphs.find({n, S});
+    auto it = e->graphs.find(std::make_tuple(n, S, ngroups));
     if (it == e->graphs.end()) {
       if (e->graphs.size() >= kEngineGraphs) drop_graphs(e);
       cudaGraph_t g = nullptr;
       cudaGraphExec_t x = nullptr;
       GB_CUDA(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal), "engine: graph capture");
-      rc = engine_forward(e, n, S);
+      rc = engine_forward(e, n, S, ngroups);
       const cudaError_t ce = cudaStreamEndCapture(m->st, &g);
       if (!rc && ce != cudaSuccess) rc = gb_cuda_fail(ce, "engine: graph capture");
       if (!rc && cudaGraphInstantiate(&x, g, 0) != cudaSuccess) rc = gb_fail(GB_ERR_CUDA, "engine: graph instantiate");
       if (g) cudaGraphDestroy(g);
       if (rc) return rc;
-      it = e->graphs.emplace(std::make_pair(n, S), x).first;
+      it = e->graphs.emplace(std::make_tuple(n, S, ngroups), x).first;
     }
     rc = cudaGraphLaunch(it->second, m->st) == cudaSuccess ? GB_OK : gb_fail(GB_ERR_CUDA, "engine: graph launch");
   } else {
-    rc = engine_forward(e, n, S);
+    rc = engine_forward(e, n, S, ngroups);
   }
   if (!rc && host_logits)
     rc = cudaMemcpyAsync(host_logits, e->logits, sizeof(float) * (size_t)n * m->c.vocab, cudaMemcpyDeviceToHost,

@@ -58,6 +58,7 @@ struct PagedArgs {
   const void *k_pool, *v_pool;
   const int32_t *block_table;  // [B][max_pages]
   const int32_t *seq_lens;     // [B]
+  const int32_t *groups;       // null, or [n_groups + 1] first rows of the row groups
   int B, n_heads, n_kv, hd, page_size, max_pages, n_pages;
   float scale;
   float *out;               // [B][n_heads][hd]
@@ -109,37 +110,49 @@ GB_DEV void chunk_store(const PagedArgs &a, const uint4 (&reg)[kPFetch], uint8_t
   }
 }
 
-// One CTA per (KV head, sequence, split of the positions); warp g < G owns
-// query head h*G + g. The split's 32-position chunks go through shared memory
-// one after another (the next chunk's loads in flight while this one is
-// used): lane = position for the scores, lane = dimensions lane + 32 i for
-// P V, an online softmax per warp. One split writes the output itself; with
-// several, each writes (m, l, acc) and the last to finish merges them.
+// One CTA per (KV head, row group, split of the positions). A row group is
+// one row, or (with `groups`) up to kPW / G consecutive rows of one sequence
+// that share its page table; warp w owns query head h*G + w % G of the
+// group's row w / G. The split's 32-position chunks (up to the group's
+// longest row) go through shared memory one after another, the next chunk's
+// loads in flight while this one is used, so a group's rows read each chunk
+// once: lane = position for the scores (masked at the warp's own row
+// length), lane = dimensions lane + 32 i for P V, an online softmax per warp.
+// One split writes the output itself; with several, each writes (m, l, acc)
+// per row and the last to finish merges them.
 template <bool F16>
 __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a) {
-  const int h = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
-  const int G = a.n_heads / a.n_kv, hd = a.hd, lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int h = blockIdx.x, sp = blockIdx.z;
+  const int G = a.n_heads / a.n_kv, hd = a.hd, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r0 = a.groups ? a.groups[blockIdx.y] : (int)blockIdx.y;
+  const int nr = a.groups ? a.groups[blockIdx.y + 1] - r0 : 1;
+  const int rr = warp / G, g = warp % G, b = r0 + rr;  // this warp's row and head
+  const bool active = rr < nr;
   constexpr int RS = row_stride<F16>(kPMaxHD);
-  __shared__ float qs[kPMaxG][kPMaxHD];
+  __shared__ float qs[kPW][kPMaxHD];
   __shared__ __align__(16) uint8_t ks[32 * RS], vs[32 * RS];
   __shared__ unsigned last;
-  const int L = a.seq_lens[b];
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
-    qs[i / hd][i % hd] = a.q[((size_t)b * a.n_heads + (size_t)h * G + i / hd) * hd + i % hd];
-  const int nchunk = (L + 31) / 32;
+  int Lmax = 0;
+  for (int r = 0; r < nr; r++) Lmax = max(Lmax, a.seq_lens[r0 + r]);
+  const int L = active ? a.seq_lens[b] : 0;
+  for (int i = threadIdx.x; i < nr * G * hd; i += blockDim.x) {
+    const int w = i / hd, d = i % hd;  // warp slot w = row * G + head
+    qs[w][d] = a.q[((size_t)(r0 + w / G) * a.n_heads + (size_t)h * G + w % G) * hd + d];
+  }
+  const int nchunk = (Lmax + 31) / 32;
   const int c0 = (int)((long long)nchunk * sp / a.S), c1 = (int)((long long)nchunk * (sp + 1) / a.S);
   const int rs = row_stride<F16>(hd), DL = hd / 32;
   float m = -INFINITY, l = 0.f, acc[kPDL];
 #pragma unroll
   for (int d = 0; d < kPDL; d++) acc[d] = 0.f;
   uint4 reg[kPFetch];
-  if (c0 < c1) chunk_fetch<F16>(a, b, h, c0, L, reg);
+  if (c0 < c1) chunk_fetch<F16>(a, r0, h, c0, Lmax, reg);
   for (int ch = c0; ch < c1; ch++) {
     __syncthreads();  // the previous chunk is used up (and q is in place)
     chunk_store<F16>(a, reg, ks, vs);
     __syncthreads();
-    if (ch + 1 < c1) chunk_fetch<F16>(a, b, h, ch + 1, L, reg);
-    if (g < G) {
+    if (ch + 1 < c1) chunk_fetch<F16>(a, r0, h, ch + 1, Lmax, reg);
+    if (active && ch * 32 < L) {
       const int p = ch * 32 + lane;
       const bool in = p < L;
       float sc = 0.f;
@@ -159,7 +172,7 @@ __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a)
           kv[3] = __uint_as_float(u.w);
         }
 #pragma unroll
-        for (int e = 0; e < (F16 ? 8 : 4); e++) sc = fmaf(qs[g][d0 + e], kv[e], sc);
+        for (int e = 0; e < (F16 ? 8 : 4); e++) sc = fmaf(qs[warp][d0 + e], kv[e], sc);
       }
       const float sv = in ? sc * a.scale : -INFINITY;
       const float mn = fmaxf(m, gb_warp_max(sv));
@@ -183,7 +196,7 @@ __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a)
     }
   }
   if (a.S == 1) {
-    if (g < G)
+    if (active)
 #pragma unroll
       for (int d = 0; d < kPDL; d++)
         if (d < DL) {
@@ -194,8 +207,8 @@ __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a)
         }
     return;
   }
-  float *dst = a.part + (((size_t)b * a.n_kv + h) * a.S + sp) * G * (hd + 2);
-  if (g < G) {
+  if (active) {
+    float *dst = a.part + (((size_t)b * a.n_kv + h) * a.S + sp) * G * (hd + 2);
 #pragma unroll
     for (int d = 0; d < kPDL; d++)
       if (d < DL) dst[(size_t)g * (hd + 2) + 2 + lane + 32 * d] = acc[d];
@@ -204,16 +217,16 @@ __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a)
       dst[(size_t)g * (hd + 2) + 1] = l;
     }
   }
-  // the last split of (sequence, KV head) merges the splits (in split order)
+  // the last split of (row group, KV head) merges the splits (in split order)
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(a.counter + (size_t)b * a.n_kv + h, 1u) == (unsigned)(a.S - 1);
+  if (threadIdx.x == 0) last = atomicAdd(a.counter + (size_t)r0 * a.n_kv + h, 1u) == (unsigned)(a.S - 1);
   __syncthreads();
   if (!last) return;
   __threadfence();
-  const float *src = a.part + ((size_t)b * a.n_kv + h) * a.S * G * (hd + 2);
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-    const int gg = i / hd, d = i % hd;
+  for (int i = threadIdx.x; i < nr * G * hd; i += blockDim.x) {
+    const int row = r0 + i / (G * hd), gg = (i / hd) % G, d = i % hd;
+    const float *src = a.part + ((size_t)row * a.n_kv + h) * a.S * G * (hd + 2);
     float M = -INFINITY;
     for (int s2 = 0; s2 < a.S; s2++) M = fmaxf(M, __ldcg(src + ((size_t)s2 * G + gg) * (hd + 2)));
     float Lsum = 0.f, A = 0.f;
@@ -225,11 +238,11 @@ __global__ void __launch_bounds__(kPW * 32) attn_paged_kernel(const PagedArgs a)
       A += __ldcg(ps + 2 + d) * f;
     }
     const float o = Lsum > 0.f ? A / Lsum : 0.f;
-    const size_t idx = ((size_t)b * a.n_heads + (size_t)h * G + gg) * hd + d;
+    const size_t idx = ((size_t)row * a.n_heads + (size_t)h * G + gg) * hd + d;
     if (a.out16) a.out16[idx] = __float2half_rn(o);
     else a.out[idx] = o;
   }
-  if (threadIdx.x == 0) a.counter[(size_t)b * a.n_kv + h] = 0u;  // ready for the next launch
+  if (threadIdx.x == 0) a.counter[(size_t)r0 * a.n_kv + h] = 0u;  // ready for the next launch
 }
 
 // ---- batched decode helpers (one row per sequence) --------------------------
@@ -332,10 +345,12 @@ size_t gb_paged_part_floats(int B, int n_kv, int S, int G, int hd) {
   return (size_t)B * n_kv * S * G * (hd + 2);
 }
 
+int gb_attn_paged_group_rows(int G) { return G >= 1 && G <= kPW ? kPW / G : 1; }
+
 int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool, int kv_f16, const int32_t *block_table,
                          const int32_t *seq_lens, int B, int max_pages, int n_pages, int page_size, int n_heads,
                          int n_kv, int hd, float scale, float *out, __half *out16, float *part, unsigned *counter,
-                         int S, unsigned *err, cudaStream_t st) {
+                         int S, unsigned *err, cudaStream_t st, const int32_t *groups, int n_groups) {
   if (B <= 0) return GB_OK;
   if (n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > kPMaxG || hd % 32 || hd > kPMaxHD || page_size <= 0)
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: paged attention: %d heads, %d KV heads, head_dim %d, page %d", n_heads,
@@ -346,6 +361,7 @@ int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool,
   a.v_pool = v_pool;
   a.block_table = block_table;
   a.seq_lens = seq_lens;
+  a.groups = groups;
   a.B = B;
   a.n_heads = n_heads;
   a.n_kv = n_kv;
@@ -360,7 +376,7 @@ int gb_attn_paged_launch(const float *q, const void *k_pool, const void *v_pool,
   a.counter = counter;
   a.S = S;
   a.err = err;
-  const dim3 grid((unsigned)n_kv, (unsigned)B, (unsigned)S);
+  const dim3 grid((unsigned)n_kv, (unsigned)(groups ? n_groups : B), (unsigned)S);
   if (kv_f16)
     attn_paged_kernel<true><<<grid, kPW * 32, 0, st>>>(a);
   else
