@@ -311,7 +311,7 @@ __global__ void __launch_bounds__((kDQ + 3) * 32, 1)
   const int ABytes = kABytes * MT;          // the stage's activation tiles
   // first weight tile: 4 per CTA, or for gate/up pairs 2 of each half (B rows
   // 0..63 gate, 64..127 up; TMEM columns likewise)
-  const int tile0 = blockIdx.x * (g.pair ? 2 : 4);
+  const int tile0 = blockIdx.x * (g.pair ? NT / 2 : NT);
   // [NS] A tiles | [NS] B tiles (1024-aligned) | [RS][NT] raw units
   uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *A0 = base, *B0 = base + (size_t)NS * ABytes, *R0 = B0 + (size_t)NS * BBytes;
@@ -352,7 +352,10 @@ __global__ void __launch_bounds__((kDQ + 3) * 32, 1)
           break;
         }
         gb_mbar_expect_tx(&bfull[s], (uint32_t)BBytes);
-        tma_load_2d(B0 + (size_t)s * BBytes, &tmap_b, (k0 + kl) * kBK, (int)blockIdx.x * BN, &bfull[s]);
+#pragma unroll
+        for (int hb = 0; hb < BN / 128; hb++)  // 128-row boxes
+          tma_load_2d(B0 + (size_t)s * BBytes + (size_t)hb * 128 * 128, &tmap_b, (k0 + kl) * kBK,
+                      (int)blockIdx.x * BN + hb * 128, &bfull[s]);
         b_issued = kl + 1;
       }
       for (int j = b_issued > NS ? b_issued - NS : 0; j < b_issued; j++) (void)gb_mbar_wait(&bfull[j % NS], (j / NS) & 1);
@@ -497,12 +500,13 @@ __global__ void __launch_bounds__((kDQ + 3) * 32, 1)
       const int m = m0 + mt * kBM + quarter * 32 + lane;
       const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mt * BN);
       if constexpr (EPI == GB_EPI_SWIGLU) {
-        {
-          const int cc = cq * 16;  // gate columns cc..cc+15, up columns 64+cc..
+        // each 128 columns: gate columns 0..63 then the up columns of the same outputs
+        for (int hb = 0; hb < BN / 128; hb++) {
+          const int cc = hb * 128 + cq * 16;  // gate columns cc..cc+15, up columns 64+cc..
           float gv[16], uv[16];
           tmem_ld16(trow + cc, gv);
           tmem_ld16(trow + 64 + cc, uv);
-          const int n = tile0 * 32 + cc;
+          const int n = tile0 * 32 + hb * 64 + cq * 16;
           if (m < g.T && n < g.rows) {
             uint4 o[2];
             uint32_t *ow = (uint32_t *)o;
@@ -1156,8 +1160,10 @@ __global__ void splitk_reduce_kernel(const float *part, int S, int MT, int BN, i
   if (n >= rows) return;
   const size_t tile = (size_t)MT * kBM * BN;
   const int mg = m / (MT * kBM), rl = m % (MT * kBM);
-  const int oc = EPI == GB_EPI_SWIGLU ? 64 : 128;  // output columns of one weight tile group
-  const float *p = part + ((size_t)mg * ntn + n / oc) * S * tile + (size_t)rl * BN + (n % oc);
+  const int oc = EPI == GB_EPI_SWIGLU ? BN / 2 : BN;  // outputs of one CTA column
+  // the column of output n in its CTA's tile (gate/up: per 128 columns, 64 gate then 64 up)
+  const int col = EPI == GB_EPI_SWIGLU ? (n % oc) / 64 * 128 + n % 64 : n % oc;
+  const float *p = part + ((size_t)mg * ntn + n / oc) * S * tile + (size_t)rl * BN + col;
   float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = v;
   for (int z = 0; z < S; z++) {
     const float4 a = __ldcg((const float4 *)(p + z * tile));
@@ -1224,7 +1230,11 @@ GbTcPlan gb_tc_gemm_plan(const GbTcGemm &a, int sms) {
     p.part_floats = S > 1 ? (size_t)ntn * S * kBM * 128 : 0;
     return p;
   }
-  const int BN = 128, mt_max = 4, oc = pair ? 64 : 128;
+  // with the binary16 copy: 256 weight rows and up to 2 token tiles per CTA
+  // (a stage of 32 KB activations + 32 KB weights, three stages), else 128 rows
+  // and up to 4 token tiles (the dequant warps' width)
+  const bool wide = a.w16 != nullptr;
+  const int BN = wide ? 256 : 128, mt_max = wide ? 2 : 4, oc = pair ? BN / 2 : BN;
   const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + oc - 1) / oc;
   int mt = 1;
   while (mt * 2 <= mt_max && mt * 2 <= mtiles) mt *= 2;
@@ -1263,8 +1273,9 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   if (raw_spr(a.type_a) != raw_spr(a.type_b))
     return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: mixed quantized and float tiles");
   g.raw_tile = (std::max(raw_unit_bytes(a.type_a), raw_unit_bytes(a.type_b)) + 127) & ~127;
-  const int BN = 128, NT = BN / 32;
-  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + (g.pair ? 63 : 127)) / (g.pair ? 64 : 128);
+  const bool f16w = a.w16 != nullptr;
+  const int BN = f16w ? 256 : 128, NT = BN / 32, oc = g.pair ? BN / 2 : BN;
+  const int mtiles = (a.T + kBM - 1) / kBM, ntn = (a.rows + oc - 1) / oc;
   GbTcPlan plan = gb_tc_gemm_plan(a, 148);
   if (plan.splits > 1 && (!a.part || a.part_floats < plan.part_floats)) {  // no room for partials: one split
     plan.splits = 1;
@@ -1274,12 +1285,15 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   g.splits = plan.splits;
   g.part = a.part;
   g.mt = mt;
-  const bool f16w = a.w16 != nullptr;
+  int rbn = BN, rntn = ntn;  // the partials' tile width and CTA columns, for the reduce
   if (plan.swap) {
     int np = 16;
     while (np < a.T) np *= 2;
     g.npad = np;
-    const int nctas = ntn * g.splits;
+    const int sw_ntn = (a.rows + (g.pair ? 63 : 127)) / (g.pair ? 64 : 128);  // 128 weight rows per CTA
+    const int nctas = sw_ntn * g.splits;
+    rbn = 128;
+    rntn = sw_ntn;
     const int resident = std::max(1, std::min(4, (nctas + 147) / 148));  // CTAs an SM holds at once
     const size_t per_cta = (size_t)233472 / resident - 2048 - 1024;  // minus reserved/static and alignment slack
     const size_t stage = (size_t)128 * 128 + (size_t)np * 128;
@@ -1291,7 +1305,7 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
         a.epi == GB_EPI_PLAIN ? gemm_swap_kernel<GB_EPI_PLAIN>
                               : a.epi == GB_EPI_RESID ? gemm_swap_kernel<GB_EPI_RESID> : gemm_swap_kernel<GB_EPI_SWIGLU>;
     GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem), "gpu: GEMM");
-    kern<<<dim3((unsigned)ntn, 1, (unsigned)g.splits), kSwapThreads, smem, st>>>(g, a.tmap_a16, a.tmap_b);
+    kern<<<dim3((unsigned)sw_ntn, 1, (unsigned)g.splits), kSwapThreads, smem, st>>>(g, a.tmap_a16, a.tmap_b);
     GB_CUDA(cudaGetLastError(), "gpu: GEMM");
   } else {
   const size_t ab = (size_t)kABytes * mt + (size_t)BN * 128, rb = (size_t)NT * g.raw_tile;
@@ -1321,13 +1335,13 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
   void (*kern)(TcArgs, CUtensorMap, CUtensorMap) = nullptr;
   switch (a.epi) {
     case GB_EPI_PLAIN:
-      kern = f16w ? gemm_tc_kernel<128, GB_EPI_PLAIN, true> : gemm_tc_kernel<128, GB_EPI_PLAIN, false>;
+      kern = f16w ? gemm_tc_kernel<256, GB_EPI_PLAIN, true> : gemm_tc_kernel<128, GB_EPI_PLAIN, false>;
       break;
     case GB_EPI_RESID:
-      kern = f16w ? gemm_tc_kernel<128, GB_EPI_RESID, true> : gemm_tc_kernel<128, GB_EPI_RESID, false>;
+      kern = f16w ? gemm_tc_kernel<256, GB_EPI_RESID, true> : gemm_tc_kernel<128, GB_EPI_RESID, false>;
       break;
     case GB_EPI_SWIGLU:
-      kern = f16w ? gemm_tc_kernel<128, GB_EPI_SWIGLU, true> : gemm_tc_kernel<128, GB_EPI_SWIGLU, false>;
+      kern = f16w ? gemm_tc_kernel<256, GB_EPI_SWIGLU, true> : gemm_tc_kernel<128, GB_EPI_SWIGLU, false>;
       break;
     default: return gb_fail(GB_ERR_UNSUPPORTED, "gpu: prefill: epilogue %d", a.epi);
   }
@@ -1339,15 +1353,15 @@ int gb_tc_gemm_launch(const GbTcGemm &a, cudaStream_t st) {
     const dim3 blocks((unsigned)((a.rows + 4 * 128 - 1) / (4 * 128)), (unsigned)a.T);
     switch (a.epi) {
       case GB_EPI_PLAIN:
-        splitk_reduce_kernel<GB_EPI_PLAIN><<<blocks, 128, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows, a.y,
+        splitk_reduce_kernel<GB_EPI_PLAIN><<<blocks, 128, 0, st>>>(a.part, g.splits, mt, rbn, rntn, a.T, a.rows, a.y,
                                                                    a.ldy, nullptr, 0);
         break;
       case GB_EPI_RESID:
-        splitk_reduce_kernel<GB_EPI_RESID><<<blocks, 128, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows, a.y,
+        splitk_reduce_kernel<GB_EPI_RESID><<<blocks, 128, 0, st>>>(a.part, g.splits, mt, rbn, rntn, a.T, a.rows, a.y,
                                                                    a.ldy, nullptr, 0);
         break;
       default:
-        splitk_reduce_kernel<GB_EPI_SWIGLU><<<blocks, 128, 0, st>>>(a.part, g.splits, mt, BN, ntn, a.T, a.rows,
+        splitk_reduce_kernel<GB_EPI_SWIGLU><<<blocks, 128, 0, st>>>(a.part, g.splits, mt, rbn, rntn, a.T, a.rows,
                                                                     nullptr, 0, a.act, a.ld_act);
     }
     GB_CUDA(cudaGetLastError(), "gpu: prefill split-K reduce");

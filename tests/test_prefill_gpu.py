@@ -162,29 +162,24 @@ def test_prefill_rejects_bad_arguments(gb, cuda):
                                          (256, 512, 512), (4096, 14336, 8)])
 @pytest.mark.parametrize("typ", [Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, F16, BF16, F32])
 def test_matmul_f16_weight_copy(gb, orc, cuda, typ, rows, cols, T):
-    # The binary16 weight copy holds the values the GEMM decodes to. Above 128
-    # token rows the GEMM reading it by TMA is the decoding GEMM's kernel with
-    # the same K splits: bit-identical results. At up to 128 rows the
-    # few-token kernel (tokens as the MMA's N) runs with its own K splits:
-    # the same binary16 products, float32 sums in another order, so it is
-    # held to the float32-accumulation bound against the float64 product.
+    # The binary16 weight copy holds the values the decoding GEMM produces, so
+    # the GEMMs over it multiply the same binary16 products; they run other
+    # kernel shapes (256 weight rows per CTA above 128 token rows, tokens as
+    # the MMA's N below) and so other K splits: float32 sums in another
+    # order, held to the float32-accumulation bound against the float64
+    # product, like the decoding GEMM itself.
     rng = np.random.default_rng(rows * 7 + cols + T + typ)
     w = weight_bytes(rng, typ, rows, cols)
     x16 = rng.standard_normal((T, cols)).astype(np.float16)
     dx = torch.from_numpy(x16.view(np.uint16).copy()).cuda()
     lin = gb.Linear(typ, w, rows, cols)
-    want = torch.full((T, rows), float("nan"), device="cuda")
-    lin.matmul_f16(dx, T, want)
     n = lin.cache_f16_weights()
     assert n == ((rows + 127) // 128) * 128 * cols * 2
     got = torch.full((T, rows), float("nan"), device="cuda")
     lin.matmul_f16(dx, T, got)
     torch.cuda.synchronize()
     lin.close()
-    assert torch.isfinite(want).all() and torch.isfinite(got).all()
-    if T > 128:
-        assert torch.equal(got, want)
-        return
+    assert torch.isfinite(got).all()
     w16 = orc.dequantize(typ, w, rows * cols).reshape(rows, cols).astype(np.float16).astype(np.float64)
     ref = x16.astype(np.float64) @ w16.T
     bound = np.abs(x16.astype(np.float64)) @ np.abs(w16).T
@@ -194,10 +189,10 @@ def test_matmul_f16_weight_copy(gb, orc, cuda, typ, rows, cols, T):
 
 @pytest.mark.parametrize("name", ["q4km_hd64", "q40_tied", "q4k_all", "q80_all", "f16_all", "q5km"])
 def test_prefill_f16_weight_copy(gb, cuda, name):
-    # prefill through the model's binary16 weight copy: at 199 batched tokens
-    # (the decoding GEMM's kernel) the same logits and KV cache bit for bit;
-    # at 60 (the few-token kernel, float32 sums in another order) within
-    # float32 accumulation of them
+    # prefill through the model's binary16 weight copy, at 199 batched tokens
+    # (256-row CTAs) and at 60 (the few-token kernel): the same binary16
+    # products as the decoding GEMM with float32 sums in another order, so
+    # logits and KV cache within float32 accumulation of it
     cfg = dict(MODELS[name], ctx_len=256)
     img = gb.SynthImage(gb.synth_spec(**cfg))
     for n in (200, 61):
@@ -212,12 +207,7 @@ def test_prefill_f16_weight_copy(gb, cuda, name):
         got = b.prefill(toks, 0).copy()
         kv_got = read_kv(b, cfg, n)
         b.close()
-        if n - 1 > 128:
-            assert np.array_equal(got, want)
-            for (kg, vg), (kw, vw) in zip(kv_got, kv_want):
-                assert np.array_equal(kg, kw) and np.array_equal(vg, vw)
-        else:
-            assert rel_err(got, want) < 1e-3, rel_err(got, want)
-            for (kg, vg), (kw, vw) in zip(kv_got, kv_want):
-                for g_, w_ in ((kg, kw), (vg, vw)):
-                    assert rms_err(g_, w_) < 1e-3 and rel_err(g_, w_) < 1e-2
+        assert rel_err(got, want) < 1e-3, (n, rel_err(got, want))
+        for (kg, vg), (kw, vw) in zip(kv_got, kv_want):
+            for g_, w_ in ((kg, kw), (vg, vw)):
+                assert rms_err(g_, w_) < 1e-3 and rel_err(g_, w_) < 1e-2
