@@ -1114,7 +1114,9 @@ int gb_gemv_launch(const GbGemvArgs &a, const GbGemvPlan &plan, cudaStream_t st,
   p.upr = p.half ? 2 * a.nsb : a.nsb;
   p.units = (unsigned)p.nrb * (unsigned)p.upr;
   const int ub = p.rb * std::max(gb_tiled_sb_bytes(ta), gb_tiled_sb_bytes(tb));  // largest unit
-  const int nsm = sms();
+  // SMs a launch spreads over (GB_GEMV_SMS overrides, for sweeps)
+  int nsm = sms();
+  if (const char *e = getenv("GB_GEMV_SMS")) nsm = std::max(1, std::min(nsm, atoi(e)));
   const long long cap = smem_optin();
   static const char *epi_names[] = {"PLAIN", "QKV", "RESID", "SWIGLU", "LOGITS", "PARTIAL"};
   // Paired launch: two 8-warp CTAs per SM, so that a matrix of up to twice as
