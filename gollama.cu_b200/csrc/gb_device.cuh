@@ -190,6 +190,17 @@ GB_DEV void gb_st_release_sys(unsigned *p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// 64-bit accesses that other GPUs read over NVLink while this one writes them
+// (aligned 64-bit scalar accesses are single-copy atomic).
+GB_DEV void gb_st_relaxed_sys_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+GB_DEV unsigned long long gb_ld_relaxed_sys_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Streaming 16-byte global load that does not allocate in L1.
 GB_DEV uint4 gb_ld_stream16(const void *p) {
   uint4 v;

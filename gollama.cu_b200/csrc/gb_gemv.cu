@@ -399,21 +399,14 @@ GB_DEV void epilogue(const Kp &p, int rbk, float y0, float y1, const double *rop
       }
     }
   } else if constexpr (EPI == GB_EPI_PARTIAL) {
-    // this rank's partial of rows r into its own slot; the row-block that
-    // completes the vector publishes the step's flag (the other ranks read
-    // both over NVLink)
+    // this rank's partial of rows r into its own slot as tagged words
+    // ((step + 1) << 32 | float bits): the other ranks read them over NVLink
+    // and know each word is this step's by its tag, so no fence, counter or
+    // flag is needed here
     const GbPeer &P = e.peer;
-    P.my_buf[(size_t)e.peer_slot * P.dim + rbk * 32 + lane] = y0;
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) {
-      const unsigned done = atomicAdd(P.done + e.peer_slot, 1u) + 1u;
-      if (done == (unsigned)p.nrb) {
-        P.done[e.peer_slot] = 0u;
-        __threadfence();
-        gb_st_release_sys(P.my_flag + e.peer_slot, *P.epoch + 1u);
-      }
-    }
+    const unsigned long long tag = (unsigned long long)(__ldcg(P.epoch) + 1u) << 32;
+    gb_st_relaxed_sys_u64(P.my_tbuf + (size_t)e.peer_slot * P.dim + rbk * 32 + lane,
+                          tag | (unsigned long long)__float_as_uint(y0));
   } else if constexpr (EPI == GB_EPI_LOGITS) {
     int r = rbk * 32 + lane;
     uint32_t gidx = (uint32_t)(e.row_offset + r);

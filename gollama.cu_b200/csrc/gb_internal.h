@@ -51,6 +51,9 @@ struct GbPeer {
   unsigned *my_flag = nullptr;            // this rank's flags [slots]
   unsigned *done = nullptr;               // [slots] local row-block counters (zero between launches)
   const unsigned *epoch = nullptr;        // device step counter
+  // this rank's partials of the row-split GEMVs as tagged words [slots][dim]:
+  // (step + 1) << 32 | float bits, read by the peers with no flag
+  unsigned long long *my_tbuf = nullptr;
   unsigned wait_limit = 1u << 22;         // polls of a peer flag (~100 ns each) before a wait gives up
 };
 
@@ -152,6 +155,15 @@ int gb_add_launch(const float *a, const float *b, float *out, int n, cudaStream_
 // Tensor parallel: wait for every rank's partial in peer slot `slot`, then
 // x += sum of the partials (rank order, identical on every rank) with per-32
 // sums of squares.
+// Every rank's tagged partial buffer (this rank's own and the peers' mapped
+// ones), passed by value so the exchange kernel reads the pointers from its
+// parameters.
+constexpr int kGbMaxWorld = 32;
+struct GbTagTable {
+  const unsigned long long *w[kGbMaxWorld];
+};
+int gb_peer_resid_tagged_launch(const GbTagTable &t, int world, const unsigned *step, unsigned wait_limit, int slot,
+                                int dim, float *x, int n, float *ssq, unsigned *err, cudaStream_t st, bool pdl);
 int gb_peer_resid_launch(const GbPeer &p, int slot, float *x, int n, float *ssq, unsigned *err,
                          cudaStream_t st, bool pdl);
 // Tensor parallel: wait for every rank's argmax key in peer slot `slot` and

@@ -199,6 +199,7 @@ struct gb_model {
   // tensor parallel: peer exchange (receive buffers mapped by every rank)
   GbPeer peer;
   std::vector<void *> ipc_opened;  // peers' buffers and flags mapped into this process
+  GbTagTable ttab = {};            // every rank's tagged partials (the o/down exchanges)
   unsigned *done = nullptr;
   int attn_splits = 1;
   GbGemvPlan plan_plain, plan_gu;
@@ -346,26 +347,30 @@ int upload_tiles(const GbTensor *t, int r0, int nr, int c0, int nc, uint8_t *dst
   return GB_OK;
 }
 
-// Tensor parallel: every rank allocates a buffer [slots][dim] floats for its
-// partials and flags [slots] (slots: o and down of every layer, plus the
-// lm_head's argmax key), exports them with CUDA IPC, gathers every rank's
-// handles over NCCL (once, at load) and maps the peers' buffers, so that the
-// step's kernels exchange partial sums with loads over NVLink and
-// system-scope flags instead of collectives.
+// Tensor parallel: every rank allocates a buffer [slots][dim] of tagged
+// 64-bit words for the partials of its row-split GEMVs (slots: o and down of
+// every layer), a float buffer and flags [slots] for the lm_head's argmax key,
+// exports them with CUDA IPC, gathers every rank's handles over NCCL (once,
+// at load) and maps the peers' buffers, so that the step's kernels exchange
+// partial sums with loads over NVLink instead of collectives.
 int setup_peers(gb_model *m) {
   const gb_config &c = m->c;
   const int N = c.tp_world, R = c.tp_rank, slots = 2 * c.layers + 1;
   const int dim = std::max(c.dim, 2);
   float *buf = nullptr;
   unsigned *flag = nullptr, *done = nullptr, *epoch = nullptr;
+  unsigned long long *tbuf = nullptr;
   int rc;
+  if (N > kGbMaxWorld) return gb_fail(GB_ERR_UNSUPPORTED, "model: %d ranks (%d at most)", N, kGbMaxWorld);
+  if ((rc = dalloc(m, &tbuf, (size_t)slots * dim, "model: peer buffers"))) return rc;
   if ((rc = dalloc(m, &buf, (size_t)slots * dim, "model: peer buffers")) ||
       (rc = dalloc(m, &flag, (size_t)slots, "model: peer flags")) ||
       (rc = dalloc(m, &done, (size_t)slots, "model: peer counters")) || (rc = dalloc(m, &epoch, 1, "model: step counter")))
     return rc;
   struct Handles {
-    cudaIpcMemHandle_t buf, flag;
+    cudaIpcMemHandle_t buf, flag, tbuf;
   } mine;
+  GB_CUDA(cudaIpcGetMemHandle(&mine.tbuf, tbuf), "model: IPC handle");
   GB_CUDA(cudaIpcGetMemHandle(&mine.buf, buf), "model: IPC handle");
   GB_CUDA(cudaIpcGetMemHandle(&mine.flag, flag), "model: IPC handle");
   uint8_t *dh = nullptr;
@@ -388,9 +393,13 @@ int setup_peers(gb_model *m) {
     if (q == R) {
       bufs[q] = buf;
       flags[q] = flag;
+      m->ttab.w[q] = tbuf;
       continue;
     }
-    void *pb = nullptr, *pf = nullptr;
+    void *pb = nullptr, *pf = nullptr, *pt = nullptr;
+    GB_CUDA(cudaIpcOpenMemHandle(&pt, all[q].tbuf, cudaIpcMemLazyEnablePeerAccess), "model: map peer buffer");
+    m->ipc_opened.push_back(pt);
+    m->ttab.w[q] = (const unsigned long long *)pt;
     GB_CUDA(cudaIpcOpenMemHandle(&pb, all[q].buf, cudaIpcMemLazyEnablePeerAccess), "model: map peer buffer");
     m->ipc_opened.push_back(pb);
     GB_CUDA(cudaIpcOpenMemHandle(&pf, all[q].flag, cudaIpcMemLazyEnablePeerAccess), "model: map peer flags");
@@ -414,6 +423,7 @@ int setup_peers(gb_model *m) {
   P.flags = dflags;
   P.my_buf = buf;
   P.my_flag = flag;
+  P.my_tbuf = tbuf;
   P.done = done;
   P.epoch = epoch;
   return GB_OK;
@@ -557,7 +567,9 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook, bool sample = false) 
       a.e.peer = m->peer;
       a.e.peer_slot = 2 * l;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_O))) return rc;
-      if ((rc = gb_peer_resid_launch(m->peer, 2 * l, m->x, c.dim, m->ssq, m->err, st, pdl)) || (rc = mark(K_OTHER)))
+      if ((rc = gb_peer_resid_tagged_launch(m->ttab, c.tp_world, m->peer.epoch, m->peer.wait_limit, 2 * l,
+                                            m->peer.dim, m->x, c.dim, m->ssq, m->err, st, pdl)) ||
+          (rc = mark(K_OTHER)))
         return rc;
     }
     // FFN RMSNorm in the prologue; gate/up + SwiGLU
@@ -575,7 +587,8 @@ int enqueue_step(gb_model *m, cudaStream_t st, Hook *hook, bool sample = false) 
       a.e.peer = m->peer;
       a.e.peer_slot = 2 * l + 1;
       if ((rc = gb_gemv_launch(a, m->plan_plain, st, pdl)) || (rc = mark(K_DOWN))) return rc;
-      if ((rc = gb_peer_resid_launch(m->peer, 2 * l + 1, m->x, c.dim, m->ssq, m->err, st, pdl)) ||
+      if ((rc = gb_peer_resid_tagged_launch(m->ttab, c.tp_world, m->peer.epoch, m->peer.wait_limit, 2 * l + 1,
+                                            m->peer.dim, m->x, c.dim, m->ssq, m->err, st, pdl)) ||
           (rc = mark(K_OTHER)))
         return rc;
     }

@@ -259,6 +259,52 @@ __global__ void peer_resid_kernel(GbPeer p, int slot, float *x, int n, float *ss
 
 // The token from every rank's argmax key in peer slot `slot` (the largest
 // key: larger value, then lower index, as model.Argmax).
+// The exchange of the model's row-split GEMVs. Rank q's partial of element c
+// is the 64-bit word t.w[q][slot*dim + c] = (step + 1) << 32 | float bits,
+// stored by that rank's GEMV epilogue with no fence or flag. Each thread
+// loads its element's word from every rank at once (one NVLink round trip
+// once they have landed), polls again only words whose tag is still an older
+// step (bounded: wait_limit polls each, ~100 ns apart), then adds the values
+// in rank order, so every rank computes the same bits. A wait that runs out
+// leaves x[c] as it was and sets GB_DEVERR_TIMEOUT.
+constexpr int kTagBatch = 8;
+__global__ void peer_resid_tagged_kernel(const __grid_constant__ GbTagTable t, int world, const unsigned *step,
+                                         unsigned wait_limit, int slot, int dim, float *x, int n, float *ssq,
+                                         unsigned *err) {
+  gb_grid_dep_launch();
+  gb_grid_dep_wait();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x, lane = threadIdx.x & 31;
+  if (c >= n) return;  // n is a multiple of 32: whole warps leave together
+  const unsigned ep = __ldcg(step) + 1u;
+  const size_t off = (size_t)slot * dim + c;
+  float sum = 0.f;
+  bool ok = true;
+  for (int q0 = 0; q0 < world && ok; q0 += kTagBatch) {
+    unsigned long long w[kTagBatch];
+#pragma unroll
+    for (int i = 0; i < kTagBatch; i++)
+      if (q0 + i < world) w[i] = gb_ld_relaxed_sys_u64(t.w[q0 + i] + off);
+#pragma unroll
+    for (int i = 0; i < kTagBatch; i++) {
+      if (q0 + i >= world || !ok) continue;
+      for (unsigned k = 0; (unsigned)(w[i] >> 32) != ep; k++) {
+        if (k >= wait_limit) {
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+        w[i] = gb_ld_relaxed_sys_u64(t.w[q0 + i] + off);
+      }
+      sum += __uint_as_float((unsigned)(w[i] & 0xFFFFFFFFull));
+    }
+  }
+  if (!ok && err) atomicOr(err, GB_DEVERR_TIMEOUT);
+  const float xn = ok ? x[c] + sum : x[c];
+  x[c] = xn;
+  const float ss = gb_warp_sum(xn * xn);
+  if (lane == 0) ssq[c / 32] = ss;
+}
+
 __global__ void peer_argmax_kernel(GbPeer p, int slot, int32_t *token, int32_t *hist, const int32_t *pos,
                                    int max_len, unsigned *err) {
   gb_grid_dep_launch();
@@ -415,6 +461,14 @@ int gb_peer_resid_launch(const GbPeer &p, int slot, float *x, int n, float *ssq,
   return GB_OK;
 }
 
+int gb_peer_resid_tagged_launch(const GbTagTable &t, int world, const unsigned *step, unsigned wait_limit, int slot,
+                                int dim, float *x, int n, float *ssq, unsigned *err, cudaStream_t st, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_cfg(dim3((n + 255) / 256), dim3(256), st, attr, pdl);
+  GB_CUDA(cudaLaunchKernelEx(&cfg, peer_resid_tagged_kernel, t, world, step, wait_limit, slot, dim, x, n, ssq, err),
+          "gpu: peer residual");
+  return GB_OK;
+}
 int gb_peer_argmax_launch(const GbPeer &p, int slot, int32_t *token, int32_t *hist, const int32_t *pos,
                           int max_len, unsigned *err, cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];
@@ -816,6 +870,35 @@ int gb_gpu_peer_resid(gb_kernels *k, void *stream, int world, const float *const
     GB_CUDA(cudaMemsetAsync(k->status, 0, sizeof h, st), "gpu: peer residual");
     GB_CUDA(cudaStreamSynchronize(st), "gpu: peer residual");
     return gb_fail(GB_ERR_TIMEOUT, "gpu: peer residual: a rank's flag did not arrive within %u polls", p.wait_limit);
+  }
+  return GB_OK;
+}
+
+int gb_gpu_peer_resid_tagged(gb_kernels *k, void *stream, int world, const unsigned long long *const *bufs,
+                             const unsigned *step, int slot, int dim, float *x, int n, float *ssq,
+                             unsigned wait_limit, unsigned *status) {
+  gb_clear_error();
+  GB_NEED(k);
+  if (world < 1 || world > kGbMaxWorld || !bufs || !step || slot < 0 || !x || !ssq || n <= 0 || n % 32 || n > dim)
+    return gb_fail(GB_ERR_INVALID, "gpu: peer residual: bad arguments");
+  GbTagTable t = {};
+  for (int q = 0; q < world; q++) {
+    if (!bufs[q]) return gb_fail(GB_ERR_INVALID, "gpu: peer residual: rank %d has no buffer", q);
+    t.w[q] = bufs[q];
+  }
+  const unsigned limit = wait_limit ? wait_limit : GbPeer().wait_limit;
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned *word = status ? status : k->status;
+  int rc = gb_peer_resid_tagged_launch(t, world, step, limit, slot, dim, x, n, ssq, word, st, false);
+  if (rc || status) return rc;
+  // no status word of the caller's: wait for the call and report its outcome
+  unsigned h = 0;
+  GB_CUDA(cudaMemcpyAsync(&h, k->status, sizeof h, cudaMemcpyDeviceToHost, st), "gpu: peer residual");
+  GB_CUDA(cudaStreamSynchronize(st), "gpu: peer residual");
+  if (h) {
+    GB_CUDA(cudaMemsetAsync(k->status, 0, sizeof h, st), "gpu: peer residual");
+    GB_CUDA(cudaStreamSynchronize(st), "gpu: peer residual");
+    return gb_fail(GB_ERR_TIMEOUT, "gpu: peer residual: a rank's partial did not arrive within %u polls", limit);
   }
   return GB_OK;
 }

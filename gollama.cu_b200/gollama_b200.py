@@ -86,7 +86,8 @@ _SIGS = {
     "gb_gpu_matvec_q": (I, [P, P, I, P, P, P, I, I, I]), "gb_gpu_ones": (I, [I, C.POINTER(P)]),
     "gb_free": (I, [P]), "gb_gpu_dequant_rows": (I, [P, P, I, P, I, I, I, I, P]),
     "gb_gpu_argmax": (I, [P, P, P, I, P]),
-    "gb_gpu_peer_resid": (I, [P, P, I, P, P, P, I, I, P, I, P, C.c_uint, P]), "gb_gpu_sample": (I, [P, P, P, I, P, P, I, U64, P]),
+    "gb_gpu_peer_resid": (I, [P, P, I, P, P, P, I, I, P, I, P, C.c_uint, P]),
+    "gb_gpu_peer_resid_tagged": (I, [P, P, I, P, P, I, I, P, I, P, C.c_uint, P]), "gb_gpu_sample": (I, [P, P, P, I, P, P, I, U64, P]),
     "gb_gpu_attn_decode_paged": (I, [P, P, P, P, P, I, P, P, I, I, I, I, I, I, I, F, P]),
     "gb_model_set_sampler": (I, [P, P]), "gb_model_prefill": (I, [P, P, I, I, P]),
     "gb_model_cache_f16_weights": (I, [P, C.POINTER(S)]),
@@ -243,6 +244,14 @@ class Kernels:
         bufs / flags: device arrays of `world` device pointers."""
         _check(lib().gb_gpu_peer_resid(self.h, _stream(stream), world, _ptr(bufs), _ptr(flags), _ptr(step), slot,
                                        dim, _ptr(x), n, _ptr(ssq), wait_limit, _ptr(status)))
+
+    def peer_resid_tagged(self, world, bufs, step, slot, dim, x, n, ssq, wait_limit=0, status=None, stream=None):
+        """gb_gpu_peer_resid_tagged: x += the ranks' partials of `slot` once every rank's word of an
+        element carries the tag *step + 1. bufs: `world` device pointers (ints) to the ranks'
+        [slots][dim] arrays of 64-bit tagged words."""
+        arr = (C.c_uint64 * world)(*[int(b) for b in bufs])
+        _check(lib().gb_gpu_peer_resid_tagged(self.h, _stream(stream), world, C.cast(arr, P), _ptr(step), slot,
+                                              dim, _ptr(x), n, _ptr(ssq), wait_limit, _ptr(status)))
 
     def attn_decode_paged(self, q, k_pool, v_pool, kv_f16, block_table, seq_lens, batch, max_pages, n_pages,
                           page_size, n_heads, n_kv, head_dim, scale, out, stream=None):

@@ -151,6 +151,21 @@ int gb_gpu_argmax(gb_kernels *k, void *stream, const float *x, int n, int32_t *o
 int gb_gpu_peer_resid(gb_kernels *k, void *stream, int world, const float *const *bufs,
                       const unsigned *const *flags, const unsigned *step, int slot, int dim, float *x, int n,
                       float *ssq, unsigned wait_limit, unsigned *status);
+/* Added (tensor parallelism; no reference interface): the exchange the model
+ * itself runs after each row-split GEMV. bufs is a HOST array of `world`
+ * device pointers (this rank's buffer and the peers' buffers mapped into this
+ * process): word bufs[q][slot*dim + c] is rank q's partial of element c as a
+ * 64-bit word ((*step + 1) << 32 | the float's bits), written by that rank
+ * with no flag. Each element waits (bounded by wait_limit polls of ~100 ns
+ * each, 0: the default) until every rank's word carries the tag *step + 1,
+ * then x[c] += the values summed in rank order; ssq[n/32] receives the per-32
+ * sums of squares of the new x. An element whose wait runs out keeps its x
+ * and ORs GB_DEVERR_TIMEOUT (4) into *status (a device word); status NULL:
+ * the call waits for the stream and returns GB_ERR_TIMEOUT. n is a multiple
+ * of 32, n <= dim, world <= 32. */
+int gb_gpu_peer_resid_tagged(gb_kernels *k, void *stream, int world, const unsigned long long *const *bufs,
+                             const unsigned *step, int slot, int dim, float *x, int n, float *ssq,
+                             unsigned wait_limit, unsigned *status);
 
 /* ---- sampling (added; the reference's roadmap item, ROADMAP.md:42-45) ----
  * One token from a logits vector on the device:
