@@ -125,3 +125,25 @@ def test_tagged_stale_word_times_out_and_device_stays_usable(gb, kernels):
     torch.cuda.synchronize()
     want = x0 + (np.float32(0) + parts[0][slot * dim:slot * dim + n] + parts[1][slot * dim:slot * dim + n])
     assert np.array_equal(x.cpu().numpy(), want.astype(np.float32))
+
+
+def test_tagged_exchange_ten_ranks_ragged(gb, kernels):
+    """Ten ranks (two batches of eight words per element) and n not a multiple of
+    the 256-thread CTA: the sum is the rank-order float32 sum, elements past n
+    are untouched."""
+    world, dim, slot, n, slots = 10, 800, 2, 672, 4
+    rng = np.random.default_rng(7)
+    parts = [rng.standard_normal(slots * dim).astype(np.float32) for _ in range(world)]
+    step = torch.tensor([41], dtype=torch.int32, device="cuda")
+    bufs = [tagged(p, 42) for p in parts]
+    x = torch.randn(dim, device="cuda")
+    x0 = x.cpu().numpy().copy()
+    ssq = torch.zeros(dim // 32, device="cuda")
+    kernels.peer_resid_tagged(world, [b.data_ptr() for b in bufs], step, slot, dim, x, n, ssq)
+    torch.cuda.synchronize()
+    acc = np.zeros(n, dtype=np.float32)
+    for p in parts:
+        acc = (acc + p[slot * dim:slot * dim + n]).astype(np.float32)
+    got = x.cpu().numpy()
+    assert np.array_equal(got[:n], (x0[:n] + acc).astype(np.float32))
+    assert np.array_equal(got[n:], x0[n:])
