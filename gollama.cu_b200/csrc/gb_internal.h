@@ -49,7 +49,6 @@ struct GbPeer {
   const unsigned *const *flags = nullptr; // device array [world]: every rank's flags
   float *my_buf = nullptr;                // this rank's partials [slots][dim]
   unsigned *my_flag = nullptr;            // this rank's flags [slots]
-  unsigned *done = nullptr;               // [slots] local row-block counters (zero between launches)
   const unsigned *epoch = nullptr;        // device step counter
   // this rank's partials of the row-split GEMVs as tagged words [slots][dim]:
   // (step + 1) << 32 | float bits, read by the peers with no flag

@@ -358,14 +358,13 @@ int setup_peers(gb_model *m) {
   const int N = c.tp_world, R = c.tp_rank, slots = 2 * c.layers + 1;
   const int dim = std::max(c.dim, 2);
   float *buf = nullptr;
-  unsigned *flag = nullptr, *done = nullptr, *epoch = nullptr;
+  unsigned *flag = nullptr, *epoch = nullptr;
   unsigned long long *tbuf = nullptr;
   int rc;
   if (N > kGbMaxWorld) return gb_fail(GB_ERR_UNSUPPORTED, "model: %d ranks (%d at most)", N, kGbMaxWorld);
   if ((rc = dalloc(m, &tbuf, (size_t)slots * dim, "model: peer buffers"))) return rc;
   if ((rc = dalloc(m, &buf, (size_t)slots * dim, "model: peer buffers")) ||
-      (rc = dalloc(m, &flag, (size_t)slots, "model: peer flags")) ||
-      (rc = dalloc(m, &done, (size_t)slots, "model: peer counters")) || (rc = dalloc(m, &epoch, 1, "model: step counter")))
+      (rc = dalloc(m, &flag, (size_t)slots, "model: peer flags")) || (rc = dalloc(m, &epoch, 1, "model: step counter")))
     return rc;
   struct Handles {
     cudaIpcMemHandle_t buf, flag, tbuf;
@@ -424,7 +423,6 @@ int setup_peers(gb_model *m) {
   P.my_buf = buf;
   P.my_flag = flag;
   P.my_tbuf = tbuf;
-  P.done = done;
   P.epoch = epoch;
   return GB_OK;
 }
