@@ -34,15 +34,16 @@ enum GbEpi {
   GB_EPI_RESID = 2,   // x[r] += y; per-32 sums of squares for the next RMSNorm
   GB_EPI_SWIGLU = 3,  // gate/up pairs -> act = silu(g)*u
   GB_EPI_LOGITS = 4,  // logits[r] = y; argmax candidates; last CTA -> token
-  GB_EPI_PARTIAL = 5, // tensor parallel: this rank's partial y into every rank's peer slot
+  GB_EPI_PARTIAL = 5, // tensor parallel: this rank's partial y, tagged with the step, into its peer slot
 };
 
-// Tensor-parallel exchange over peer memory. Every rank owns a buffer
-// [slots][dim] floats for its own partials and flags [slots], mapped into the
-// other ranks' address spaces (CUDA IPC). A rank stores its partial of slot s
-// locally and publishes flag[s] = epoch+1 (system-scope release) once all its
-// row-blocks are stored; a reducer reads every rank's flag and partial over
-// NVLink. `epoch` counts decode steps and is the same on every rank.
+// Tensor-parallel exchange over peer memory; every buffer is mapped into the
+// other ranks' address spaces (CUDA IPC). The row-split GEMVs' partials go to
+// `my_tbuf` as 64-bit words tagged with epoch + 1, which the peers read with no
+// flag (peer_resid_tagged_kernel). The lm_head's argmax key goes to `my_buf`
+// and is published by flag[s] = epoch + 1 (system-scope release); the per-op
+// flag exchange (gb_gpu_peer_resid) uses the same pair. `epoch` counts decode
+// steps, only grows, and is the same on every rank.
 struct GbPeer {
   int world = 1, rank = 0, dim = 0;
   const float *const *bufs = nullptr;     // device array [world]: every rank's partials
